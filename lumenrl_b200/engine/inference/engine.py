@@ -1,0 +1,258 @@
+"""Native rollout engine: batched sampling with a paged KV cache.
+
+Replaces the reference's external engines (vLLM/ATOM subprocesses driven over
+FIFOs, ``lumenrl/engine/inference/{vllm,atom}_engine.py``) with an in-process
+engine on the trainer's own weights:
+
+* GRPO prefix sharing: each prompt is prefilled ONCE; its ``n`` samples share
+  the prompt's full KV blocks (reference counted) and copy only the partial
+  tail block, so prefill work and prompt KV memory drop by ``n``.
+* Static batches up to ``max_num_seqs``; larger requests run in waves.
+  Finished rows keep a fixed slot (masked), so the decode step has static
+  shapes and is replayed from a CUDA graph.
+* Returns token ids, per-token rollout log-probs (under softmax(logits/T),
+  the quantity TIS/MIS rollout correction needs) and, for MoE models, the
+  routed expert ids per generated token (R3).
+* ``sleep()``/``wake()`` free and re-create the KV pool for colocated
+  training; ``update_weights`` is a no-op in colocated mode (the engine reads
+  the trainer's flat bf16 buffer directly) and a copy otherwise.
+"""
+
+from __future__ import annotations
+
+import logging
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from lumenrl_b200.engine.inference.kv_cache import KVSpec, PagedKVCache
+from lumenrl_b200.engine.inference.runner import DecodeGraph, ModelRunner
+from lumenrl_b200.models.qwen3 import Qwen3Model
+
+logger = logging.getLogger(__name__)
+
+
+@dataclass
+class SamplingParams:
+    max_new_tokens: int = 1024
+    temperature: float = 1.0
+    top_p: float = 1.0
+    n: int = 1
+    seed: int = 0
+    eos_token_id: Optional[int] = 2
+    stop_at_eos: bool = True
+
+
+@dataclass
+class GenerationOutput:
+    prompts: list[list[int]]
+    responses: Tensor          # [N, max_new] int64, pad_id after the end
+    response_lengths: Tensor   # [N] int64
+    logprobs: Tensor           # [N, max_new] fp32 (0 past the end)
+    prompt_index: Tensor       # [N] which prompt each row came from
+    routed_experts: list = field(default_factory=list)  # per row: [len, layers, k] int16 (MoE only)
+    stats: dict = field(default_factory=dict)
+
+
+class _RoutingRecorder:
+    def __init__(self, layers: list[int]) -> None:
+        self.layers = layers
+        self.buf: dict[int, Tensor] = {}
+
+    def record(self, layer: int, ids: Tensor) -> None:
+        self.buf[layer] = ids.to(torch.int16)
+
+    def take(self) -> Tensor:
+        return torch.stack([self.buf[l] for l in self.layers], dim=1)  # [B, layers, k]
+
+
+class RolloutEngine:
+    def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
+                 kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
+                 use_cuda_graph: bool = True, pad_token_id: int = 0) -> None:
+        self.model = model
+        self.args = model.args
+        self.device = model.flat.device
+        self.max_num_seqs = max_num_seqs
+        self.max_model_len = max_model_len
+        self.block_size = block_size
+        self.pad_token_id = pad_token_id
+        self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda" and self.args.num_experts == 0
+        spec = KVSpec(self.args.num_layers, self.args.num_kv_heads, self.args.head_dim, block_size, kv_dtype)
+        self.max_blocks_per_seq = math.ceil(max_model_len / block_size) + 1
+        if kv_cache_bytes is None:
+            nblocks = max_num_seqs * self.max_blocks_per_seq + 1
+        else:
+            nblocks = PagedKVCache.blocks_for_budget(spec, kv_cache_bytes)
+        self.cache = PagedKVCache(spec, nblocks, self.device)
+        self.runner = ModelRunner(model, self.cache)
+        self._graphs: dict[tuple, DecodeGraph] = {}
+        self.weight_version = 0
+
+    # -- lifecycle ---------------------------------------------------------------
+    def sleep(self) -> None:
+        self._graphs.clear()
+        self.cache.sleep()
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def wake(self) -> None:
+        self.cache.wake()
+
+    def update_weights(self, flat: Optional[Tensor] = None, version: Optional[int] = None) -> None:
+        """Colocated: the engine aliases the trainer buffer, nothing to move.
+        Separated: copy a full bf16 flat buffer in (one contiguous copy)."""
+        if flat is not None and flat.data_ptr() != self.model.flat.data_ptr():
+            self.model.flat.copy_(flat, non_blocking=True)
+        self.weight_version = self.weight_version + 1 if version is None else version
+
+    # -- generation ------------------------------------------------------------------
+    def _graph(self, batch: int, sp: SamplingParams) -> DecodeGraph:
+        key = (batch, sp.temperature, sp.top_p)
+        g = self._graphs.get(key)
+        if g is None:
+            g = DecodeGraph(self.runner, batch, self.max_blocks_per_seq, sp.temperature, sp.top_p,
+                            self.use_cuda_graph)
+            self._graphs[key] = g
+        return g
+
+    @torch.no_grad()
+    def generate(self, prompts: list[list[int]], sp: SamplingParams) -> GenerationOutput:
+        if not self.cache.awake:
+            self.wake()
+        rows_per_prompt = sp.n
+        per_wave = max(1, self.max_num_seqs // rows_per_prompt)
+        outs = []
+        for w0 in range(0, len(prompts), per_wave):
+            outs.append(self._generate_wave(prompts[w0: w0 + per_wave], sp, w0))
+        if len(outs) == 1:
+            return outs[0]
+        width = max(o.responses.shape[1] for o in outs)
+
+        def padw(t: Tensor, fill) -> Tensor:
+            return torch.nn.functional.pad(t, (0, width - t.shape[1]), value=fill)
+        return GenerationOutput(
+            prompts=[p for o in outs for p in o.prompts],
+            responses=torch.cat([padw(o.responses, self.pad_token_id) for o in outs]),
+            response_lengths=torch.cat([o.response_lengths for o in outs]),
+            logprobs=torch.cat([padw(o.logprobs, 0.0) for o in outs]),
+            prompt_index=torch.cat([o.prompt_index for o in outs]),
+            routed_experts=[r for o in outs for r in o.routed_experts],
+            stats={k: sum(o.stats.get(k, 0) for o in outs) for k in outs[0].stats})
+
+    def _generate_wave(self, prompts: list[list[int]], sp: SamplingParams, prompt_offset: int) -> GenerationOutput:
+        dev, bs, n = self.device, self.block_size, sp.n
+        P = len(prompts)
+        B = P * n
+        alloc = self.cache.allocator
+        max_new = min(sp.max_new_tokens, self.max_model_len - max(len(p) for p in prompts))
+        if max_new <= 0:
+            raise ValueError("prompt longer than max_model_len")
+        # 1) blocks: prompt blocks per prompt, per-row private tail + generation blocks
+        tables: list[list[int]] = []
+        owned: list[list[int]] = []
+        prompt_blocks: list[list[int]] = []
+        for p in prompts:
+            L = len(p)
+            prompt_blocks.append(alloc.alloc(math.ceil(L / bs)))
+        # 2) prefill unique prompts
+        ids = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device=dev)
+        pos = torch.cat([torch.arange(len(p), device=dev) for p in prompts])
+        lens = torch.tensor([len(p) for p in prompts], device=dev)
+        cu = torch.zeros(P + 1, dtype=torch.int32, device=dev)
+        cu[1:] = torch.cumsum(lens, 0)
+        slots = torch.tensor([prompt_blocks[i][j // bs] * bs + j % bs for i, p in enumerate(prompts)
+                              for j in range(len(p))], dtype=torch.long, device=dev)
+        recorder = None
+        moe_layers = [i for i in range(self.args.num_layers) if self.args.is_moe_layer(i)]
+        if moe_layers:
+            recorder = _RoutingRecorder(moe_layers)
+            self.runner.routing_recorder = recorder
+        logits = self.runner.prefill(ids, pos, cu, int(lens.max()), slots)
+        prompt_routes = recorder.take() if recorder else None   # [sumL, layers, k]
+        for i, p in enumerate(prompts):
+            L = len(p)
+            full = L // bs
+            need = math.ceil((L + max_new) / bs)
+            for _ in range(n):
+                shared = alloc.share(prompt_blocks[i][:full])
+                private = alloc.alloc(need - full)
+                if L % bs:
+                    self.cache.copy_block(prompt_blocks[i][full], private[0])
+                tables.append(shared + private)
+                owned.append(shared + private)
+        alloc.release([b for pb in prompt_blocks for b in pb])   # rows hold their own references now
+        # 3) first token from the prefill logits (row r samples prompt r // n)
+        row_logits = logits.repeat_interleave(n, dim=0)
+        g = self._graph(B, sp)
+        g.row_seed.copy_(torch.arange(B, device=dev) + (sp.seed * 1_000_003 + prompt_offset * n) )
+        g.step.fill_(0)
+        from lumenrl_b200 import ops
+        tok, lp = ops.sample_tokens_device(row_logits, sp.temperature, sp.top_p, g.row_seed, g.step)
+        out_tok = torch.full((B, max_new), self.pad_token_id, dtype=torch.long, device=dev)
+        out_lp = torch.zeros(B, max_new, dtype=torch.float32, device=dev)
+        out_tok[:, 0], out_lp[:, 0] = tok, lp
+        bt = torch.zeros(B, self.max_blocks_per_seq, dtype=torch.int32, device=dev)
+        for r, t in enumerate(tables):
+            bt[r, : len(t)] = torch.tensor(t, dtype=torch.int32)
+        g.block_table.copy_(bt)
+        plen = torch.tensor([len(p) for p in prompts], device=dev).repeat_interleave(n)
+        g.positions.copy_(plen)
+        g.tokens.copy_(tok)
+        routes_rows: list[list[Tensor]] = [[] for _ in range(B)]
+        if recorder:
+            self.runner.routing_recorder = recorder
+        finished = torch.zeros(B, dtype=torch.bool, device=dev)
+        eos = sp.eos_token_id if sp.stop_at_eos else None
+        if eos is not None:
+            finished |= tok == eos
+        lengths = torch.full((B,), max_new, dtype=torch.long, device=dev)
+        steps = 1
+        check_every = 16
+        for t in range(1, max_new):
+            g.step.fill_(t)
+            tok, lp = g.run()
+            if recorder:
+                step_routes = recorder.take()
+                for r in range(B):
+                    routes_rows[r].append(step_routes[r])
+            out_tok[:, t] = tok
+            out_lp[:, t] = lp
+            g.tokens.copy_(tok)
+            g.positions.add_(1)
+            steps += 1
+            if eos is not None:
+                newly = (~finished) & (tok == eos)
+                lengths = torch.where(newly, torch.full_like(lengths, t + 1), lengths)
+                finished |= newly
+                if t % check_every == 0 and bool(finished.all()):
+                    break
+        if eos is not None:
+            first = (out_tok[:, 0] == eos)
+            lengths = torch.where(first, torch.ones_like(lengths), lengths)
+        lengths = lengths.clamp(max=steps)
+        ar = torch.arange(out_tok.shape[1], device=dev).unsqueeze(0)
+        valid = ar < lengths.unsqueeze(1)
+        out_tok = torch.where(valid, out_tok, torch.full_like(out_tok, self.pad_token_id))[:, :steps]
+        out_lp = torch.where(valid, out_lp, torch.zeros_like(out_lp))[:, :steps]
+        for t in owned:
+            alloc.release(t)
+        routed = []
+        if recorder:
+            self.runner.routing_recorder = None
+            offs = [0] + torch.cumsum(lens, 0).tolist()
+            lens_host = lengths.tolist()
+            for r in range(B):
+                i = r // n
+                pr = prompt_routes[offs[i]: offs[i + 1]]
+                gen = torch.stack(routes_rows[r]) if routes_rows[r] else pr[:0]
+                # routes of prompt tokens + tokens that were fed back (all but the last sample)
+                routed.append(torch.cat([pr, gen[: max(lens_host[r] - 1, 0)]]).cpu())
+        return GenerationOutput(
+            prompts=[p for p in prompts for _ in range(n)], responses=out_tok, response_lengths=lengths,
+            logprobs=out_lp, prompt_index=torch.arange(P, device=dev).repeat_interleave(n) + prompt_offset,
+            routed_experts=routed,
+            stats={"decode_steps": steps, "prefill_tokens": int(lens.sum()), "gen_tokens": int(lengths.sum())})

@@ -1,0 +1,148 @@
+"""Forward passes of the rollout engine over the paged KV cache.
+
+* ``prefill``: packed prompts, causal varlen attention over the prompt itself,
+  K/V written into the cache, logits of each prompt's last token.
+* ``decode``: one token per sequence; QK-norm+RoPE, KV append and paged
+  attention per layer, then the LM head.  Shapes are static, so the whole step
+  is captured once per batch size into a CUDA graph (``DecodeGraph``): a
+  ~36-layer step is ~400 launches that the graph replays with one.
+
+The math is the training model's (same kernels for RMSNorm, QK-norm+RoPE,
+SwiGLU), which keeps rollout and training log-probs consistent.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from lumenrl_b200 import ops
+from lumenrl_b200.engine.inference.kv_cache import PagedKVCache
+from lumenrl_b200.models.qwen3 import Qwen3Model
+
+
+class ModelRunner:
+    def __init__(self, model: Qwen3Model, cache: PagedKVCache) -> None:
+        self.model = model
+        self.cache = cache
+        self.args = model.args
+        self.scale = 1.0 / math.sqrt(self.args.head_dim)
+        self.routing_recorder = None
+
+    def _w(self, name: str) -> Tensor:
+        return self.model.p(name).detach()
+
+    def _mlp(self, i: int, h: Tensor) -> Tensor:
+        if self.args.is_moe_layer(i):
+            from lumenrl_b200.models.moe import moe_forward
+            prev = getattr(self.model, "routing_recorder", None)
+            self.model.routing_recorder = self.routing_recorder
+            try:
+                out, _ = moe_forward(self.model, i, h)
+            finally:
+                self.model.routing_recorder = prev
+            return out
+        return ops.linear(ops.swiglu(ops.linear(h, self._w(f"layers.{i}.w13"))), self._w(f"layers.{i}.w2"))
+
+    def _qkv(self, i: int, h: Tensor, positions: Tensor):
+        a = self.args
+        qkv = ops.linear(h, self._w(f"layers.{i}.wqkv"))
+        qn = self._w(f"layers.{i}.q_norm") if a.qk_norm else None
+        kn = self._w(f"layers.{i}.k_norm") if a.qk_norm else None
+        return ops.qk_norm_rope(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
+                                a.head_dim, a.rms_norm_eps)
+
+    @torch.no_grad()
+    def prefill(self, ids: Tensor, positions: Tensor, cu_seqlens: Tensor, max_len: int, slots: Tensor) -> Tensor:
+        a, c = self.args, self.cache
+        x = torch.nn.functional.embedding(ids, self._w("embed"))
+        res = None
+        for i in range(a.num_layers):
+            h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
+            q, k, v = self._qkv(i, h, positions)
+            ops.kv_cache_append(k, v, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
+            o = ops.attention_varlen(q, k, v, cu_seqlens, max_len, causal=True, scale=self.scale)
+            x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
+            h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
+            x = self._mlp(i, h)
+        last = cu_seqlens[1:] - 1
+        h, _ = ops.add_rmsnorm(x[last], res[last], self._w("norm"), a.rms_norm_eps)
+        return ops.linear(h, self.model.lm_head.detach())
+
+    @torch.no_grad()
+    def decode(self, ids: Tensor, positions: Tensor, slots: Tensor, block_table: Tensor, seq_lens: Tensor) -> Tensor:
+        a, c = self.args, self.cache
+        x = torch.nn.functional.embedding(ids, self._w("embed"))
+        res = None
+        for i in range(a.num_layers):
+            h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
+            q, k, v = self._qkv(i, h, positions)
+            ops.kv_cache_append(k, v, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
+            o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
+                                           c.k_scale[i], c.v_scale[i])
+            x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
+            h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
+            x = self._mlp(i, h)
+        h, _ = ops.add_rmsnorm(x, res, self._w("norm"), a.rms_norm_eps)
+        return ops.linear(h, self.model.lm_head.detach())
+
+
+class DecodeGraph:
+    """Static-shape decode step + sampling, captured into one CUDA graph.
+
+    Inputs live in static buffers that the caller updates in place
+    (``tokens``, ``positions``, ``block_table``, ``row_seed``, ``step``);
+    ``seq_lens`` and ``slots`` are derived inside the graph."""
+
+    def __init__(self, runner: ModelRunner, batch: int, max_blocks: int, temperature: float, top_p: float,
+                 use_graph: bool) -> None:
+        dev = runner.cache.device
+        self.runner = runner
+        self.B = batch
+        self.bs = runner.cache.spec.block_size
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.positions = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.block_table = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
+        self.row_seed = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.step = torch.zeros(1, dtype=torch.long, device=dev)
+        self.temperature, self.top_p = temperature, top_p
+        self.out_tokens: Optional[Tensor] = None
+        self.out_logp: Optional[Tensor] = None
+        self.graph = None
+        if use_graph and dev.type == "cuda":
+            self._capture()
+
+    def _body(self) -> None:
+        pos = self.positions
+        blk = self.block_table.gather(1, (pos // self.bs).unsqueeze(1).to(torch.long)).squeeze(1).to(torch.long)
+        slots = blk * self.bs + pos % self.bs
+        seq_lens = (pos + 1).to(torch.int32)
+        logits = self.runner.decode(self.tokens, pos, slots, self.block_table, seq_lens)
+        tok, lp = ops.sample_tokens_device(logits, self.temperature, self.top_p, self.row_seed, self.step)
+        if self.out_tokens is None:
+            self.out_tokens, self.out_logp = tok, lp
+        else:
+            self.out_tokens.copy_(tok)
+            self.out_logp.copy_(lp)
+
+    def _capture(self) -> None:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._body()
+        self.graph = g
+
+    def run(self) -> tuple[Tensor, Tensor]:
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._body()
+        return self.out_tokens, self.out_logp

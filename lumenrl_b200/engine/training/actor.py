@@ -1,0 +1,194 @@
+"""Training engine for the policy (and reference / critic) model.
+
+Replaces the reference's FSDP2 engine + actor worker hot path
+(``lumenrl/engine/training/fsdp_engine.py:63-722``,
+``lumenrl/workers/actor_worker.py:290-792``):
+
+* ``compute_log_probs``: no-grad packed forward in token-budget micro
+  batches, fused LM-head log-prob (+ entropy), scattered to ``[B, R]``.
+* ``update_policy``: for each mini-batch and PPO epoch, packed forward with
+  grad per micro-batch, the clipped-ratio loss on the flat stream of scored
+  tokens (one fused kernel), backward accumulating fp32 ``main_grad``, then
+  one sharded AdamW step.  Loss normalisation is the global token mean
+  (``token-mean``): each rank divides its token sum by the token count of the
+  whole mini-batch over all ranks, and gradients are SUM-reduced.
+* Activation recomputation per decoder layer is on when
+  ``policy.training.megatron_cfg.recompute_granularity`` or HF
+  gradient-checkpointing asks for it (``gradient_checkpointing=True``).
+"""
+
+from __future__ import annotations
+
+import logging
+import math
+import time
+from typing import Any, Optional
+
+import torch
+from torch import Tensor
+
+from lumenrl_b200 import ops
+from lumenrl_b200.core.protocol import DataProto
+from lumenrl_b200.engine.training.lr_scheduler import LRSchedule
+from lumenrl_b200.engine.training.optimizer import ShardedFlatAdamW
+from lumenrl_b200.engine.training.packing import PackedBatch, make_micro_batches, pack_from_grid
+from lumenrl_b200.models.config import ModelArgs
+from lumenrl_b200.models.qwen3 import FlatLayout, Qwen3Model, param_specs
+from lumenrl_b200.parallel.dist import ParallelState, all_reduce_sum
+
+logger = logging.getLogger(__name__)
+
+
+def padded_numel(args: ModelArgs, world: int) -> int:
+    n = FlatLayout(param_specs(args)).numel
+    q = world * 128
+    return (n + q - 1) // q * q
+
+
+class ActorEngine:
+    def __init__(self, args: ModelArgs, state: ParallelState, *, lr: float = 1e-6, betas=(0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 0.01, max_grad_norm: float = 1.0, seed: int = 0,
+                 dtype: Optional[torch.dtype] = None, trainable: bool = True, gradient_checkpointing: bool = False,
+                 total_steps: int = 1000, warmup_steps: int = 0, lr_style: str = "constant", min_lr_ratio: float = 0.0,
+                 comm=None, init: bool = True) -> None:
+        self.args = args
+        self.state = state
+        self.device = state.device
+        if dtype is None:
+            dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+        flat = torch.zeros(padded_numel(args, state.world_size if trainable else 1), dtype=dtype, device=self.device)
+        self.model = Qwen3Model(args, device=self.device, dtype=dtype, flat=flat, requires_grad=trainable)
+        if init:
+            self.model.init_weights(seed)
+        self.model.gradient_checkpointing = gradient_checkpointing
+        self.trainable = trainable
+        self.opt: Optional[ShardedFlatAdamW] = None
+        self.sched: Optional[LRSchedule] = None
+        if trainable:
+            self.opt = ShardedFlatAdamW(flat, state.world_size, state.rank, lr=lr, betas=betas, eps=eps,
+                                        weight_decay=weight_decay, max_grad_norm=max_grad_norm, comm=comm)
+            self.model.attach_main_grad(self.opt.grad)
+            self.sched = LRSchedule(lr, total_steps, warmup_steps, lr_style, min_lr_ratio)
+
+    # ------------------------------------------------------------------ scoring
+    def _forward_scored(self, pb: PackedBatch, temperature: float, want_entropy: bool):
+        h = self.model.forward_packed(pb.input_ids, pb.positions, pb.cu_seqlens, pb.max_seqlen)
+        hs = h.index_select(0, pb.score_index)
+        return ops.token_logprob(hs, self.model.lm_head, pb.targets, temperature=temperature,
+                                 want_entropy=want_entropy)
+
+    @torch.no_grad()
+    def compute_log_probs(self, batch: DataProto, temperature: float = 1.0, token_budget: int = 16384,
+                          want_entropy: bool = True) -> tuple[Tensor, Optional[Tensor]]:
+        t = batch.tensors
+        B, R = t["responses"].shape
+        lens = (t["prompt_lengths"] + t["response_lengths"]).tolist()
+        logp = torch.zeros(B, R, dtype=torch.float32, device=self.device)
+        ent = torch.zeros(B, R, dtype=torch.float32, device=self.device) if want_entropy else None
+        for rows in make_micro_batches(lens, token_budget=token_budget):
+            pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
+                                self.device)
+            self._set_replay(batch, pb)
+            lp, e = self._forward_scored(pb, temperature, want_entropy)
+            rows_t = torch.as_tensor(rows, device=self.device)[pb.out_row]
+            logp[rows_t, pb.out_col] = lp
+            if want_entropy:
+                ent[rows_t, pb.out_col] = e
+        self.model.routing_replay = None
+        return logp, ent
+
+    def _set_replay(self, batch: DataProto, pb: PackedBatch) -> None:
+        if self.args.num_experts == 0 or "routed_experts" not in batch.ragged:
+            self.model.routing_replay = None
+            return
+        from lumenrl_b200.moe.r3 import RoutingReplay
+        self.model.routing_replay = RoutingReplay.from_rows(
+            [batch.ragged["routed_experts"][r] for r in pb.rows],
+            (pb.cu_seqlens[1:] - pb.cu_seqlens[:-1]).tolist(), self.args, self.device)
+
+    # ------------------------------------------------------------------ training
+    def update_policy(self, batch: DataProto, algo_cfg, algorithm: str = "grpo", rows_per_micro: int = 4,
+                      token_budget: int = 0, num_mini_batches: int = 1, num_epochs: int = 1,
+                      temperature: float = 1.0) -> dict[str, float]:
+        assert self.opt is not None
+        t = batch.tensors
+        B = t["responses"].shape[0]
+        lens = (t["prompt_lengths"] + t["response_lengths"]).tolist()
+        mask_grid = t["response_mask"].float()
+        if "dapo_sample_mask" in t:
+            mask_grid = mask_grid * t["dapo_sample_mask"].float().reshape(-1, 1)
+        metrics: dict[str, float] = {}
+        sums = {"pg_loss": 0.0, "ppo_kl": 0.0, "clipfrac": 0.0, "tok": 0.0, "entropy": 0.0}
+        t_fwd_bwd = 0.0
+        opt_stats = {}
+        for _epoch in range(num_epochs):
+            mini_size = math.ceil(B / num_mini_batches)
+            for m0 in range(0, B, mini_size):
+                mini_rows = list(range(m0, min(B, m0 + mini_size)))
+                local_tok = float(mask_grid[mini_rows].sum())
+                global_tok = max(all_reduce_sum(local_tok), 1.0)
+                micro = make_micro_batches([lens[r] for r in mini_rows], rows_per_micro=rows_per_micro,
+                                           token_budget=token_budget)
+                t0 = time.perf_counter()
+                for mb in micro:
+                    rows = [mini_rows[i] for i in mb]
+                    stats = self._micro_step(batch, rows, mask_grid, algo_cfg, algorithm, global_tok, temperature)
+                    for k in sums:
+                        sums[k] += stats.get(k, 0.0)
+                t_fwd_bwd += time.perf_counter() - t0
+                lr = self.sched.current if self.sched else None
+                opt_stats = self.opt.step(lr)
+                if self.sched:
+                    self.sched.step()
+        tok = max(sums["tok"], 1.0)
+        metrics.update({
+            "actor/pg_loss": sums["pg_loss"], "actor/ppo_kl": sums["ppo_kl"] / tok,
+            "actor/pg_clipfrac": sums["clipfrac"] / tok, "actor/grad_norm": opt_stats.get("grad_norm", 0.0),
+            "actor/lr": opt_stats.get("lr", 0.0), "actor/update_skipped": opt_stats.get("skipped", 0.0),
+            "timing/fwd_bwd_s": t_fwd_bwd,
+        })
+        return metrics
+
+    def _micro_step(self, batch: DataProto, rows: list[int], mask_grid: Tensor, algo_cfg, algorithm: str,
+                    global_tok: float, temperature: float) -> dict[str, float]:
+        t = batch.tensors
+        pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
+                            self.device)
+        self._set_replay(batch, pb)
+        logp, _ = self._forward_scored(pb, temperature, want_entropy=False)
+        r_idx = torch.as_tensor(rows, device=self.device)[pb.out_row]
+        c_idx = pb.out_col
+        old = t["old_log_probs"][r_idx, c_idx].float()
+        adv = t["advantages"]
+        adv = adv[r_idx] if adv.dim() == 1 else adv[r_idx, c_idx]
+        mask = mask_grid[r_idx, c_idx]
+        isw = t["rollout_is_weights"][r_idx, c_idx].float() if "rollout_is_weights" in t else None
+        if algorithm == "dapo":
+            lo, hi, c = float(algo_cfg.clip_ratio_low), float(algo_cfg.clip_ratio_high), float(algo_cfg.clip_ratio_c)
+        else:
+            lo = hi = float(getattr(algo_cfg, "clip_ratio", 0.2))
+            c, isw = 0.0, (isw if algorithm == "grpo_tis" else None)
+        loss = ops.ppo_clip_loss(logp, old, adv.float(), mask, lo, hi, c, isw, denom=global_tok)
+        kl_c = float(getattr(algo_cfg, "kl_coeff", 0.0))
+        if kl_c > 0 and "ref_log_probs" in t:
+            ref_lp = t["ref_log_probs"][r_idx, c_idx].float()
+            loss = loss + kl_c * ((ref_lp - logp) * mask).sum() / global_tok
+        for aux in self.model.aux_losses:
+            loss = loss + aux * (float(mask.sum()) / global_tok)
+        loss.backward()
+        self.model.routing_replay = None
+        with torch.no_grad():
+            d = logp.detach() - old
+            ratio = torch.exp(d.clamp(-20, 20))
+            clipped = ((ratio < 1 - lo) | (ratio > 1 + hi)).float()
+            return {"pg_loss": float(loss.detach()), "ppo_kl": float(((-d) * mask).sum()),
+                    "clipfrac": float((clipped * mask).sum()), "tok": float(mask.sum())}
+
+    # ------------------------------------------------------------------ state
+    def state_dict(self) -> dict[str, Any]:
+        sd: dict[str, Any] = {"args": self.args.to_dict()}
+        if self.opt is not None:
+            sd["optimizer"] = self.opt.state_dict()
+        if self.sched is not None:
+            sd["scheduler"] = self.sched.state_dict()
+        return sd

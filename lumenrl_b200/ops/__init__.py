@@ -1,0 +1,401 @@
+"""Custom ops: one function per hot op, autograd-aware.
+
+On CUDA tensors every op here runs a hand-written sm_100a kernel from the
+in-tree extension ``lumenrl_b200._C`` (sources under ``csrc/``); if the
+extension is missing on a GPU machine the call raises instead of silently
+falling back.  CPU tensors use the fp32 PyTorch definitions in
+``ops.reference`` (these are also the oracles of the kernel tests).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from lumenrl_b200.ops import reference as ref
+from lumenrl_b200.ops.ext import ext, has_ext  # noqa: F401
+
+__all__ = [
+    "rmsnorm", "add_rmsnorm", "qk_norm_rope", "swiglu", "linear", "attention_varlen", "paged_decode_attention",
+    "token_logprob", "group_advantage", "ppo_clip_loss", "sample_tokens", "sample_tokens_device", "kv_cache_append", "embedding",
+]
+
+
+def _cuda(*ts) -> bool:
+    return any(t is not None and t.is_cuda for t in ts)
+
+
+# ---------------------------------------------------------------------------
+# gradient sinks: weights keep an fp32 ``main_grad`` view into the flat fp32
+# gradient buffer; kernels and GEMMs accumulate straight into it.
+# ---------------------------------------------------------------------------
+
+def _accum_main_grad(w: Tensor, g: Tensor) -> None:
+    mg = getattr(w, "main_grad", None)
+    if mg is None:
+        if w.grad is None:
+            w.grad = g.to(w.dtype)
+        else:
+            w.grad += g.to(w.dtype)
+    else:
+        mg += g.to(mg.dtype)
+
+
+# ---------------------------------------------------------------------------
+# Linear: y = x @ W^T, wgrad accumulated in fp32 into W.main_grad
+# ---------------------------------------------------------------------------
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, w: Tensor, w_handle: Tensor):
+        ctx.save_for_backward(x, w)
+        ctx.w_handle = w_handle
+        return x @ w.t()
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):
+        x, w = ctx.saved_tensors
+        dx = dy @ w
+        wh = ctx.w_handle
+        mg = getattr(wh, "main_grad", None)
+        dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
+        if mg is not None and dy.is_cuda:
+            # cuBLAS bf16 x bf16 -> fp32 accumulate (beta = 1) into the flat
+            # gradient buffer: no bf16 weight-grad tensor is ever allocated.
+            torch.addmm(mg, dy2.t(), x2, out_dtype=torch.float32, out=mg)
+        else:
+            _accum_main_grad(wh, dy2.t().float() @ x2.float())
+        return dx, None, None
+
+
+def linear(x: Tensor, w: Tensor) -> Tensor:
+    if not torch.is_grad_enabled() or not w.requires_grad:
+        return x @ w.t()
+    return _Linear.apply(x, w.detach(), w)
+
+
+class _LinearFP32(torch.autograd.Function):
+    """fp32 y = x @ W^T (router gates); wgrad accumulated into main_grad."""
+
+    @staticmethod
+    def forward(ctx, x, w, w_handle):
+        xf, wf = x.float(), w.float()
+        ctx.save_for_backward(xf, wf)
+        ctx.w_handle, ctx.x_dtype = w_handle, x.dtype
+        return xf @ wf.t()
+
+    @staticmethod
+    def backward(ctx, dy):
+        xf, wf = ctx.saved_tensors
+        dy = dy.float()
+        _accum_main_grad(ctx.w_handle, dy.reshape(-1, dy.shape[-1]).t() @ xf.reshape(-1, xf.shape[-1]))
+        return (dy @ wf).to(ctx.x_dtype), None, None
+
+
+def linear_fp32(x: Tensor, w: Tensor) -> Tensor:
+    if not torch.is_grad_enabled() or not w.requires_grad:
+        return x.float() @ w.float().t()
+    return _LinearFP32.apply(x, w.detach(), w)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm (optionally fused with the residual add that precedes it)
+# ---------------------------------------------------------------------------
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, w: Tensor, w_handle: Tensor, eps: float):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        y, rstd = ext().rmsnorm_fwd(x2, w, eps)
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.w_handle, ctx.shape = w_handle, shape
+        return y.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):
+        x2, w, rstd = ctx.saved_tensors
+        dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        dx = ext().rmsnorm_bwd(dy.reshape(x2.shape).contiguous(), x2, w, rstd, dw)
+        _accum_main_grad(ctx.w_handle, dw)
+        return dx.view(ctx.shape), None, None, None
+
+
+def rmsnorm(x: Tensor, w: Tensor, eps: float) -> Tensor:
+    if not _cuda(x):
+        return ref.rmsnorm(x, w, eps)
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad):
+        return _RMSNorm.apply(x, w.detach(), w, eps)
+    shape = x.shape
+    y, _ = ext().rmsnorm_fwd(x.reshape(-1, shape[-1]).contiguous(), w, eps)
+    return y.view(shape)
+
+
+def add_rmsnorm(x: Tensor, residual: Optional[Tensor], w: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    """Returns (rmsnorm(x + residual), x + residual); ``residual`` may be None."""
+    if residual is None:
+        return rmsnorm(x, w, eps), x
+    if _cuda(x) and not (torch.is_grad_enabled() and (x.requires_grad or residual.requires_grad)):
+        shape = x.shape
+        y, s = ext().add_rmsnorm_fwd(x.reshape(-1, shape[-1]), residual.reshape(-1, shape[-1]), w, eps)
+        return y.view(shape), s.view(shape)
+    s = x + residual
+    return rmsnorm(s, w, eps), s
+
+
+# ---------------------------------------------------------------------------
+# QK-RMSNorm + RoPE on a fused QKV projection output
+# ---------------------------------------------------------------------------
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, qw, kw, qw_h, kw_h, positions, inv_freq, nh, nkv, hd, eps):
+        q, k, v, rq, rk = ext().qk_norm_rope_fwd(qkv, qw, kw, positions, inv_freq, nh, nkv, hd, eps)
+        ctx.save_for_backward(qkv, qw, kw, positions, inv_freq, rq, rk)
+        ctx.meta = (qw_h, kw_h, nh, nkv, hd, eps)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, qw, kw, positions, inv_freq, rq, rk = ctx.saved_tensors
+        qw_h, kw_h, nh, nkv, hd, eps = ctx.meta
+        has_norm = qw.numel() > 0
+        dqw = torch.zeros(max(qw.numel(), 1), dtype=torch.float32, device=qkv.device)
+        dkw = torch.zeros(max(kw.numel(), 1), dtype=torch.float32, device=qkv.device)
+        dqkv = ext().qk_norm_rope_bwd(dq.contiguous(), dk.contiguous(), dv.contiguous(), qkv, qw, kw, positions,
+                                      inv_freq, rq, rk, dqw, dkw, nh, nkv, hd, eps)
+        if has_norm:
+            _accum_main_grad(qw_h, dqw)
+            _accum_main_grad(kw_h, dkw)
+        return dqkv, None, None, None, None, None, None, None, None, None, None
+
+
+def qk_norm_rope(qkv: Tensor, qw: Optional[Tensor], kw: Optional[Tensor], positions: Tensor, inv_freq: Tensor,
+                 nh: int, nkv: int, hd: int, eps: float) -> tuple[Tensor, Tensor, Tensor]:
+    """qkv [T, (nh+2nkv)*hd] -> q [T,nh,hd], k [T,nkv,hd], v [T,nkv,hd]."""
+    if not _cuda(qkv):
+        ang = positions.float().unsqueeze(-1) * inv_freq.float().to(positions.device).unsqueeze(0)
+        return ref.qk_norm_rope(qkv, qw, kw, ang.cos(), ang.sin(), nh, nkv, hd, eps)
+    empty = qkv.new_empty(0)
+    qw_d = qw.detach() if qw is not None else empty
+    kw_d = kw.detach() if kw is not None else empty
+    if torch.is_grad_enabled() and qkv.requires_grad:
+        return _QKNormRope.apply(qkv, qw_d, kw_d, qw, kw, positions, inv_freq, nh, nkv, hd, eps)
+    q, k, v, _, _ = ext().qk_norm_rope_fwd(qkv, qw_d, kw_d, positions, inv_freq, nh, nkv, hd, eps)
+    return q, k, v
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        return ext().swiglu_fwd(gu)
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gu,) = ctx.saved_tensors
+        return ext().swiglu_bwd(dh.contiguous(), gu)
+
+
+def swiglu(gate_up: Tensor) -> Tensor:
+    if not _cuda(gate_up):
+        return ref.swiglu(gate_up)
+    gu = gate_up.contiguous()
+    if torch.is_grad_enabled() and gu.requires_grad:
+        return _SwiGLU.apply(gu)
+    return ext().swiglu_fwd(gu)
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+
+def attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_seqlen: int,
+                     causal: bool = True, scale: Optional[float] = None) -> Tensor:
+    """Packed causal attention, q [T,Hq,D], k/v [T,Hk,D]."""
+    if not _cuda(q):
+        return ref.attention_varlen(q, k, v, cu_seqlens, causal, scale)
+    from lumenrl_b200.ops.attention import flash_attention_varlen
+    return flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale)
+
+
+def paged_decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_table: Tensor, seq_lens: Tensor,
+                           scale: float, k_scale: float = 1.0, v_scale: float = 1.0) -> Tensor:
+    if not _cuda(q):
+        return ref.paged_decode_attention(q, k_cache.to(q.dtype) * k_scale if k_cache.dtype != q.dtype else k_cache,
+                                          v_cache.to(q.dtype) * v_scale if v_cache.dtype != q.dtype else v_cache,
+                                          block_table, seq_lens, scale)
+    return ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale)
+
+
+def kv_cache_append(k: Tensor, v: Tensor, k_cache: Tensor, v_cache: Tensor, slots: Tensor,
+                    k_scale: float = 1.0, v_scale: float = 1.0) -> None:
+    """Write k/v rows [T,Hk,D] into the paged caches at flat slot indices."""
+    if not _cuda(k):
+        bs = k_cache.shape[1]
+        flat_k = k_cache.view(-1, *k_cache.shape[2:])
+        flat_v = v_cache.view(-1, *v_cache.shape[2:])
+        flat_k[slots.long()] = (k.float() / k_scale).to(k_cache.dtype)
+        flat_v[slots.long()] = (v.float() / v_scale).to(v_cache.dtype)
+        return
+    ext().kv_append(k, v, k_cache, v_cache, slots, 1.0 / k_scale, 1.0 / v_scale)
+
+
+# ---------------------------------------------------------------------------
+# Token log-prob (+ entropy) from hidden states and the LM head, chunked so
+# full logits never exist; backward recomputes each chunk.
+# ---------------------------------------------------------------------------
+
+class _TokenLogProb(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden, w, w_handle, targets, inv_temp, chunk, want_entropy):
+        T = hidden.shape[0]
+        logp = torch.empty(T, dtype=torch.float32, device=hidden.device)
+        ent = torch.empty(T, dtype=torch.float32, device=hidden.device)
+        lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
+        for a in range(0, T, chunk):
+            b = min(T, a + chunk)
+            logits = hidden[a:b] @ w.t()
+            ext().logprob_fwd(logits, targets[a:b], inv_temp, logp[a:b], ent[a:b], lse[a:b])
+        ctx.save_for_backward(hidden, w, targets, lse)
+        ctx.meta = (w_handle, inv_temp, chunk, want_entropy)
+        return logp, ent
+
+    @staticmethod
+    def backward(ctx, dlogp, dent):
+        hidden, w, targets, lse = ctx.saved_tensors
+        w_handle, inv_temp, chunk, want_entropy = ctx.meta
+        T = hidden.shape[0]
+        dh = torch.empty_like(hidden)
+        dlogp = dlogp.float().contiguous() if dlogp is not None else torch.zeros(T, device=hidden.device)
+        dent = dent.float().contiguous() if (dent is not None and want_entropy) else None
+        mg = getattr(w_handle, "main_grad", None)
+        for a in range(0, T, chunk):
+            b = min(T, a + chunk)
+            logits = hidden[a:b] @ w.t()
+            # in place: logits -> dL/dlogits (bf16)
+            ext().logprob_bwd(logits, targets[a:b], lse[a:b], dlogp[a:b],
+                              dent[a:b] if dent is not None else None, inv_temp)
+            dh[a:b] = logits @ w
+            if mg is not None:
+                torch.addmm(mg, logits.t(), hidden[a:b], out_dtype=torch.float32, out=mg)
+            else:
+                _accum_main_grad(w_handle, logits.t().float() @ hidden[a:b].float())
+        return dh, None, None, None, None, None, None
+
+
+def token_logprob(hidden: Tensor, lm_head: Tensor, targets: Tensor, temperature: float = 1.0,
+                  chunk: int = 2048, want_entropy: bool = True) -> tuple[Tensor, Optional[Tensor]]:
+    """log softmax(hidden @ W^T / T)[target] and the entropy, per row."""
+    if not _cuda(hidden):
+        logits = hidden @ lm_head.t()
+        return ref.token_logprob_from_logits(logits, targets, temperature, want_entropy)
+    inv_t = 1.0 / float(temperature)
+    if torch.is_grad_enabled() and (hidden.requires_grad or lm_head.requires_grad):
+        logp, ent = _TokenLogProb.apply(hidden, lm_head.detach(), lm_head, targets.contiguous(), inv_t, chunk,
+                                        want_entropy)
+        return logp, (ent if want_entropy else None)
+    T = hidden.shape[0]
+    logp = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    ent = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    for a in range(0, T, chunk):
+        b = min(T, a + chunk)
+        ext().logprob_fwd(hidden[a:b] @ lm_head.t(), targets[a:b].contiguous(), inv_t, logp[a:b], ent[a:b], lse[a:b])
+    return logp, (ent if want_entropy else None)
+
+
+# ---------------------------------------------------------------------------
+# RL math kernels
+# ---------------------------------------------------------------------------
+
+def group_advantage(rewards: Tensor, group: int, unbiased: bool = False, eps: float = 1e-8) -> Tensor:
+    if not _cuda(rewards):
+        return ref.group_advantage(rewards, group, unbiased, eps)
+    if rewards.shape[0] % group:
+        raise ValueError(f"Batch size {rewards.shape[0]} not divisible by num_generations={group}.")
+    return ext().group_adv(rewards.float().contiguous(), group, unbiased, eps)
+
+
+class _PPOClip(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logp, old, adv, mask, is_w, clip_low, clip_high, clip_c, denom):
+        loss, dlogp = ext().ppo_clip_fwd_bwd(logp.contiguous(), old.float().contiguous(), adv.float().contiguous(),
+                                             mask.float().contiguous(), is_w, clip_low, clip_high, clip_c, denom)
+        ctx.save_for_backward(dlogp)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        (dlogp,) = ctx.saved_tensors
+        return dlogp * g, None, None, None, None, None, None, None, None
+
+
+def ppo_clip_loss(logp: Tensor, old: Tensor, adv: Tensor, mask: Tensor, clip_low: float, clip_high: float,
+                  clip_c: float = 0.0, is_w: Optional[Tensor] = None, denom: Optional[float] = None) -> Tensor:
+    """DAPO token-level clipped surrogate: sum(masked per-token loss) / denom
+    (denom defaults to the mask count).  Forward computes d(loss)/d(logp) in
+    the same pass; backward is a scale."""
+    if not _cuda(logp):
+        return ref.ppo_clip_token_loss(logp, old, adv, mask, clip_low, clip_high, clip_c, is_w, denom)
+    if denom is None:
+        denom = -1.0
+    isw = is_w.float().contiguous() if is_w is not None else None
+    return _PPOClip.apply(logp, old, adv, mask, isw, float(clip_low), float(clip_high), float(clip_c), float(denom))
+
+
+def sample_tokens_device(logits: Tensor, temperature: float, top_p: float, row_seed: Tensor,
+                         step: Tensor) -> tuple[Tensor, Tensor]:
+    """Sample one token per row from softmax(logits / T) restricted to the
+    top-p nucleus; returns (token ids int64, log-prob of the sampled token
+    under softmax(logits / T)).
+
+    Randomness is a counter-based stream keyed by (row_seed[row], step[0],
+    vocab index), so a row's draw does not depend on batch composition and
+    the call can live inside a CUDA graph (seed/step are device tensors)."""
+    inv_t = 1.0 / max(float(temperature), 1e-6)
+    if not _cuda(logits):
+        z = logits.float() * inv_t
+        lp = torch.log_softmax(z, -1)
+        toks = []
+        for r in range(z.shape[0]):
+            g = torch.Generator(device="cpu").manual_seed(int(row_seed[r]) * 1000003 + int(step[0]))
+            row = lp[r]
+            if top_p < 1.0:
+                srt, idx = torch.sort(row, descending=True)
+                p = srt.exp()
+                keep = (p.cumsum(-1) - p) < top_p
+                probs = torch.where(keep, p, torch.zeros_like(p))
+                pick = torch.multinomial(probs / probs.sum(), 1, generator=g)
+                toks.append(idx[pick])
+            else:
+                toks.append(torch.multinomial(row.exp(), 1, generator=g))
+        tok = torch.cat(toks).long()
+        return tok, lp.gather(-1, tok.unsqueeze(-1)).squeeze(-1)
+    tok, lp = ext().sample(logits.contiguous(), inv_t, float(top_p), row_seed, step)
+    return tok, lp
+
+
+def sample_tokens(logits: Tensor, temperature: float, top_p: float, seed: int, offset: int) -> tuple[Tensor, Tensor]:
+    rows = torch.arange(logits.shape[0], device=logits.device, dtype=torch.long) + int(seed) * 65536
+    step = torch.full((1,), int(offset), device=logits.device, dtype=torch.long)
+    return sample_tokens_device(logits, temperature, top_p, rows, step)
+
+
+def embedding(ids: Tensor, table: Tensor) -> Tensor:
+    return torch.nn.functional.embedding(ids, table)
+
+
+def inv_freq_table(head_dim: int, theta: float, scaling: dict | None, device) -> Tensor:
+    return ref.rope_inv_freq(head_dim, theta, scaling).to(device)
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

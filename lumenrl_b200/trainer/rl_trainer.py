@@ -1,0 +1,224 @@
+"""Synchronous RL trainer (GRPO / DAPO / PPO), colocated or separated.
+
+Per step (reference hot loop ``lumenrl/trainer/rl_trainer.py:3003-3522``):
+
+1. rollout: every rank generates ``prompts_per_rank x n`` samples with the
+   native engine on the policy's own bf16 weights (data-parallel rollout,
+   groups never straddle ranks, so advantages need no communication);
+2. rewards (programmatic function, or reward model);
+3. DAPO dynamic sampling: groups with equal rewards are dropped;
+4. old log-probs (skipped in bypass mode) and, when ``kl_coeff > 0``, reference
+   log-probs from a frozen copy;
+5. advantages (estimator registry) and rollout correction (TIS/MIS/RS);
+6. policy update (sharded AdamW), whose final all-gather leaves every GPU with
+   the new bf16 weights: that is the weight sync in colocated mode;
+7. metrics with the reference's names (``timing/*``, ``perf/throughput``,
+   ``rollout_corr/*``, ``actor/*``).
+
+Every phase is timed on the device (CUDA events) when running on GPU.
+"""
+
+from __future__ import annotations
+
+import logging
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable, Optional
+
+import torch
+
+from lumenrl_b200.algorithms import rollout_correction as rc
+from lumenrl_b200.core.config import LumenRLConfig
+from lumenrl_b200.core.protocol import DataProto
+from lumenrl_b200.core.registry import ALGORITHM_REGISTRY
+from lumenrl_b200.data.synthetic import SyntheticPrompts
+from lumenrl_b200.engine.inference.engine import RolloutEngine, SamplingParams
+from lumenrl_b200.engine.training.actor import ActorEngine
+from lumenrl_b200.models.config import ModelArgs, resolve_model
+from lumenrl_b200.parallel.dist import ParallelState, all_reduce_max, all_reduce_sum, get_state, init_distributed
+from lumenrl_b200.rewards import get_reward_fn
+from lumenrl_b200.utils.timers import PhaseTimer
+
+logger = logging.getLogger(__name__)
+
+
+@dataclass
+class RLRunSpec:
+    """Workload knobs that the YAML schema does not carry (synthetic runs)."""
+    prompts_per_step: int = 8            # global prompts per step
+    prompt_len: int = 32
+    prompt_low: int = 3
+    prompt_high: int = 2048
+    max_new_tokens: int = 32
+    eos_token_id: Optional[int] = 2
+    reward: str = "contains_token"
+    reward_kwargs: dict = field(default_factory=dict)
+    rows_per_micro: int = 4
+    logprob_token_budget: int = 16384
+    kv_cache_bytes: Optional[int] = None
+    use_cuda_graph: bool = True
+    gradient_checkpointing: bool = False
+
+
+class RLTrainer:
+    def __init__(self, config: LumenRLConfig, model_args: Optional[ModelArgs] = None,
+                 spec: Optional[RLRunSpec] = None, state: Optional[ParallelState] = None) -> None:
+        self.config = config
+        self.spec = spec or RLRunSpec()
+        self.model_args = model_args or resolve_model(config.policy.model_name or "tiny-llama")
+        self.state = state
+        self.callbacks: list = []
+        self.global_step = 0
+        self.history: list[dict] = []
+
+    # ------------------------------------------------------------------ setup
+    def setup(self) -> "RLTrainer":
+        c = self.config
+        if self.state is None:
+            self.state = get_state() if get_state().world_size > 1 or get_state().device.type == "cuda" \
+                else init_distributed()
+        st = self.state
+        algo = c.algorithm.name.lower()
+        self.algorithm_name = algo
+        self.algorithm = ALGORITHM_REGISTRY.get(algo)(c)
+        self.algo_cfg = getattr(c.algorithm, algo)
+        self.group = int(getattr(self.algo_cfg, "num_generations", 1) or 1)
+        p = c.policy
+        self.actor = ActorEngine(
+            self.model_args, st, lr=p.learning_rate, betas=(p.adam_beta1, p.adam_beta2), eps=p.adam_eps,
+            weight_decay=p.weight_decay, max_grad_norm=p.max_grad_norm, seed=c.seed,
+            gradient_checkpointing=self.spec.gradient_checkpointing, total_steps=c.num_training_steps,
+            warmup_steps=p.lr_warmup_steps, lr_style=p.lr_decay_style,
+            min_lr_ratio=(p.min_lr / p.learning_rate if p.learning_rate else 0.0))
+        self.ref = None
+        if float(getattr(self.algo_cfg, "kl_coeff", 0.0)) > 0:
+            self.ref = ActorEngine(self.model_args, st, seed=c.seed, trainable=False, init=False)
+            self.ref.model.flat.copy_(self.actor.model.flat)
+        vc = p.generation.vllm_cfg
+        self.temperature = float(vc.temperature)
+        self.top_p = float(vc.top_p)
+        max_len = self.spec.prompt_len + self.spec.max_new_tokens
+        prompts_per_rank = max(1, self.spec.prompts_per_step // st.world_size)
+        self.prompts_per_rank = prompts_per_rank
+        kv_dtype = torch.float8_e4m3fn if str(vc.kv_cache_dtype).startswith("fp8") else torch.bfloat16
+        self.rollout = RolloutEngine(self.actor.model, max_num_seqs=prompts_per_rank * self.group,
+                                     max_model_len=max_len, kv_cache_bytes=self.spec.kv_cache_bytes,
+                                     use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype)
+        self.data = SyntheticPrompts(self.spec.prompt_len, self.spec.prompt_low, self.spec.prompt_high, c.seed)
+        self.reward_fn = get_reward_fn(self.spec.reward)
+        self.timer = PhaseTimer(st.device)
+        return self
+
+    # ------------------------------------------------------------------ step
+    def _rollout(self, step: int) -> DataProto:
+        st, sp = self.state, self.spec
+        prompts = self.data.batch(self.prompts_per_rank, step, st.rank)
+        params = SamplingParams(max_new_tokens=sp.max_new_tokens, temperature=self.temperature, top_p=self.top_p,
+                                n=self.group, seed=self.config.seed * 7919 + step * 131 + st.rank,
+                                eos_token_id=sp.eos_token_id)
+        self.rollout.wake()
+        out = self.rollout.generate(prompts, params)
+        self.rollout.sleep()
+        dev = st.device
+        B = out.responses.shape[0]
+        plens = torch.tensor([len(p) for p in out.prompts], device=dev)
+        P = int(plens.max())
+        pgrid = torch.zeros(B, P, dtype=torch.long, device=dev)
+        for i, pr in enumerate(out.prompts):
+            pgrid[i, : len(pr)] = torch.tensor(pr, device=dev)
+        R = out.responses.shape[1]
+        rmask = (torch.arange(R, device=dev).unsqueeze(0) < out.response_lengths.unsqueeze(1)).float()
+        batch = DataProto(
+            tensors={"prompt_ids": pgrid, "prompt_lengths": plens, "responses": out.responses,
+                     "response_lengths": out.response_lengths, "response_mask": rmask,
+                     "rollout_log_probs": out.logprobs},
+            meta={"num_generations": self.group,
+                  "uid": [f"{step}-{st.rank}-{int(i)}" for i in out.prompt_index.tolist()],
+                  "response_lengths": out.response_lengths.tolist(), "gen_stats": out.stats})
+        if out.routed_experts:
+            batch.ragged["routed_experts"] = out.routed_experts
+        return batch
+
+    def step(self) -> dict[str, Any]:
+        c, st = self.config, self.state
+        step = self.global_step
+        m: dict[str, Any] = {}
+        self.timer.start("step")
+        self.timer.start("gen")
+        batch = self._rollout(step)
+        self.timer.stop("gen")
+        rewards = self.reward_fn(batch["responses"], None, lengths=batch["response_lengths"], **self.spec.reward_kwargs)
+        batch["rewards"] = rewards.to(st.device).float()
+        if self.algorithm_name == "dapo" and c.algorithm.dapo.filter_groups.enable:
+            from lumenrl_b200.algorithms.dapo_sampling import filter_groups_keep_mask
+            keep, _ = filter_groups_keep_mask(batch["rewards"].cpu(), batch.meta["uid"])
+            m["dapo/kept_frac"] = float(keep.float().mean())
+        rcfg = c.quantization.rollout_correction
+        self.timer.start("old_log_prob")
+        if rcfg.bypass_mode:
+            rc.apply_bypass_mode(batch, rcfg)
+        else:
+            lp, ent = self.actor.compute_log_probs(batch, self.temperature, self.spec.logprob_token_budget)
+            batch["old_log_probs"] = lp
+            mask = batch["response_mask"]
+            m["actor/entropy"] = float((ent * mask).sum() / mask.sum().clamp(min=1))
+        self.timer.stop("old_log_prob")
+        if self.ref is not None:
+            self.timer.start("ref")
+            batch["ref_log_probs"], _ = self.ref.compute_log_probs(batch, self.temperature,
+                                                                   self.spec.logprob_token_budget, want_entropy=False)
+            self.timer.stop("ref")
+        self.timer.start("adv")
+        self.algorithm.compute_advantages(batch)
+        if rcfg.rollout_is or rcfg.rollout_rs:
+            batch, corr = rc.compute_rollout_correction_and_add_to_batch(batch, rcfg)
+            m.update(corr)
+        else:
+            m.update(rc.compute_rollout_corr_metrics_from_logprobs(batch["old_log_probs"], batch["rollout_log_probs"],
+                                                                   batch["response_mask"]))
+        self.timer.stop("adv")
+        self.timer.start("train")
+        pol = c.algorithm.dapo if self.algorithm_name == "dapo" else self.algo_cfg
+        tm = self.actor.update_policy(batch, pol, self.algorithm_name, rows_per_micro=self.spec.rows_per_micro,
+                                      num_mini_batches=int(getattr(self.algo_cfg, "num_mini_batches", 1)),
+                                      num_epochs=int(getattr(self.algo_cfg, "num_ppo_epochs", 1)),
+                                      temperature=self.temperature)
+        self.timer.stop("train")
+        self.timer.start("weight_sync")
+        self.rollout.update_weights()
+        self.timer.stop("weight_sync")
+        self.timer.stop("step")
+        times = self.timer.collect()
+        m.update(tm)
+        tokens_local = float(batch["prompt_lengths"].sum() + batch["response_lengths"].sum())
+        tokens = all_reduce_sum(tokens_local)
+        step_s = all_reduce_max(times["step"])
+        m.update({f"timing/{k}_s": all_reduce_max(v) for k, v in times.items()})
+        m["perf/total_num_tokens"] = tokens
+        m["perf/step_tokens_per_s"] = tokens / step_s
+        m["perf/throughput"] = tokens / (step_s * st.world_size)
+        m["perf/gen_tokens_per_s"] = all_reduce_sum(float(batch["response_lengths"].sum())) / max(
+            all_reduce_max(times["gen"]), 1e-9)
+        m["reward/mean"] = all_reduce_sum(float(batch["rewards"].sum())) / all_reduce_sum(float(len(batch)))
+        m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
+            float(len(batch)))
+        m["weight_sync/ms"] = times["weight_sync"] * 1e3
+        m["step"] = step + 1
+        self.global_step += 1
+        self.history.append(m)
+        for cb in self.callbacks:
+            cb.on_step_end(self, m)
+        return m
+
+    def train(self) -> list[dict]:
+        for cb in self.callbacks:
+            cb.on_train_begin(self)
+        for _ in range(self.global_step, self.config.num_training_steps):
+            self.step()
+        for cb in self.callbacks:
+            cb.on_train_end(self)
+        return self.history
+
+    def cleanup(self) -> None:
+        self.rollout.sleep()

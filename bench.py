@@ -1,0 +1,233 @@
+"""Headline benchmark: GRPO step tokens/s (rollout + train), Qwen3-8B, B200.
+
+    python bench.py --gpus N --steps K --warmup W          # N=1
+    torchrun --nproc-per-node N bench.py --gpus N ...       # N>1, one rank per GPU
+    python bench.py --impl reference ...                    # the reference's own arm
+
+Workload (BASELINE config "Qwen3-8B architecture, bf16, random init, GRPO
+colocated"), weak scaling: every GPU runs 8 prompts x group 8 = 64 sequences
+(so N=8 is the named 64 x 8 batch); prompts are 512 uniform-random token ids
+from [0, 151643) by seed; responses up to 1024 tokens at temperature 1.0;
+parity reward; micro-batch 4; one AdamW step per GRPO step; the updated bf16
+weights reach the rollout engine every step (full weight sync).
+
+A step is everything: rollout (prefill + decode), rewards, old log-probs,
+advantages, fwd+bwd of every micro-batch, the optimizer step and the weight
+sync.  `value` is total tokens (prompt + response, all ranks) / device time of
+K steps (CUDA events, barrier + synchronize on both sides, max over ranks).
+`e2e` repeats K steps through the public trainer API on the wall clock, each
+step including the pinned host->device copy of its prompts and a
+device->host read of its metrics.  The model weights (16 GB) dwarf the 126 MB
+L2, so every step streams its inputs from HBM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+METRIC = "GRPO step tokens/s (rollout+train) Qwen3-8B at 1/2/4/8 B200; weight-sync ms"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--prompts-per-gpu", type=int, default=8)
+    ap.add_argument("--group", type=int, default=8)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--max-new", type=int, default=1024)
+    ap.add_argument("--micro", type=int, default=4)
+    ap.add_argument("--recompute", choices=["auto", "on", "off"], default="auto")
+    ap.add_argument("--no-graph", action="store_true")
+    return ap.parse_args()
+
+
+def reference_arm(args) -> None:
+    here = os.path.dirname(os.path.abspath(__file__))
+    ref = os.path.join(here, "baseline", "_ref")
+    why = None
+    if not os.path.isdir(os.path.join(ref, "lumenrl")):
+        why = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import lumenrl.trainer.rl_trainer  # noqa: F401
+        except Exception as e:  # the ROCm stack (ATOM/AITER/vLLM-ROCm, Ray, OmegaConf) is absent
+            why = f"reference trainer import failed: {type(e).__name__}: {str(e).splitlines()[0][:160]}"
+    if why is None:
+        why = ("reference GRPO path needs the ATOM/AITER/MORI ROCm submodules and Ray, none of which exist "
+               "for NVIDIA GPUs offline")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": why}))
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of the GPUs in use during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, n: int) -> None:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        self.ids = vis.split(",")[:n] if vis else [str(i) for i in range(n)]
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(self.ids)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from lumenrl_b200.core.config import LumenRLConfig
+    from lumenrl_b200.models.config import resolve_model
+    from lumenrl_b200.ops.ext import LAUNCHES, ext
+    from lumenrl_b200.parallel.dist import init_distributed
+    from lumenrl_b200.trainer.rl_trainer import RLRunSpec, RLTrainer
+
+    st = init_distributed(timeout_s=900)
+    ext()  # the kernels must be there
+    world, rank = st.world_size, st.rank
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    margs = resolve_model(args.model)
+    recompute = args.recompute == "on" or (args.recompute == "auto" and world == 1)
+    cfg = LumenRLConfig.from_dict({
+        "policy": {"model_name": margs.name, "learning_rate": 1e-6, "lr_warmup_steps": 0,
+                   "lr_decay_style": "constant", "train_micro_batch_size": args.micro,
+                   "max_grad_norm": 1.0, "weight_decay": 0.01,
+                   "generation": {"vllm_cfg": {"temperature": 1.0, "top_p": 1.0}}},
+        "algorithm": {"name": "grpo", "grpo": {"num_generations": args.group, "kl_coeff": 0.0, "clip_ratio": 0.2}},
+        "num_training_steps": args.warmup + 2 * args.steps, "seed": 1234})
+    spec = RLRunSpec(prompts_per_step=args.prompts_per_gpu * world, prompt_len=args.prompt_len, prompt_low=0,
+                     prompt_high=151643, max_new_tokens=args.max_new, eos_token_id=151645, reward="parity",
+                     rows_per_micro=args.micro, use_cuda_graph=not args.no_graph,
+                     gradient_checkpointing=recompute)
+    tr = RLTrainer(cfg, margs, spec, st).setup()
+
+    def sync():
+        if dist.is_initialized():
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        tr.step()
+    # ---- device-timed region ----
+    clocks = ClockSampler(world) if rank == 0 else None
+    sync()
+    if clocks:
+        clocks.start()
+    l0 = LAUNCHES[0]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    toks = 0.0
+    hist = []
+    for _ in range(args.steps):
+        m = tr.step()
+        hist.append(m)
+        toks += m["perf/total_num_tokens"]
+    e1.record()
+    sync()
+    launches = LAUNCHES[0] - l0
+    dev_s = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([dev_s], device=st.device, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_s = float(t.item())
+    clk = clocks.stop() if clocks else None
+    # ---- end-to-end region: public API, pinned H2D in, D2H of metrics out ----
+    sync()
+    w0 = time.perf_counter()
+    toks_e2e = 0.0
+    for _ in range(args.steps):
+        m = tr.step()           # copies the pinned prompt batch H2D inside
+        toks_e2e += float(m["perf/total_num_tokens"])   # metrics are host values (D2H inside step)
+    sync()
+    wall = time.perf_counter() - w0
+    tw = torch.tensor([wall], device=st.device, dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(tw, op=dist.ReduceOp.MAX)
+    wall = float(tw.item())
+    if rank == 0:
+        last = hist[-1]
+        B = args.prompts_per_gpu * args.group
+        out = {
+            "metric": METRIC, "value": toks / dev_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_s / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: uniform-random prompt ids [0,151643) by seed, random-init weights N(0,0.02)",
+            "config": {"model": "Qwen3-8B (36L, h4096, 32q/8kv, hd128, ffn12288, vocab151936, qk-norm)",
+                       "global_batch": B * world, "prompts": args.prompts_per_gpu * world, "group": args.group,
+                       "seq_len": args.prompt_len + args.max_new, "prompt_len": args.prompt_len,
+                       "max_new_tokens": args.max_new, "micro_batch": args.micro,
+                       "parallelism": f"dp{world} (sharded AdamW, resident bf16 weights; rollout TP=1 per GPU)",
+                       "recompute": recompute, "cache": "inputs larger than L2 (16 GB of weights per step)"},
+            "clocks": clk,
+            "e2e": {"value": toks_e2e / wall, "unit": "tokens/s", "h2d_bytes_per_step": tr.io_bytes["h2d"] * world,
+                    "d2h_bytes_per_step": tr.io_bytes.get("d2h", 0) * world},
+            "gpu_launches": launches,
+            "breakdown_s": {k.replace("timing/", ""): v for k, v in last.items() if k.startswith("timing/")},
+            "weight_sync_ms": last.get("weight_sync/ms"),
+            "gen_tokens_per_s": last.get("perf/gen_tokens_per_s"),
+            "mean_response_len": last.get("response_length/mean"),
+        }
+        print(json.dumps(out))
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,60 @@
+// Python bindings of the lumenrl_b200._C extension.
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace lrl {
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw);
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                                            torch::Tensor inv_freq, int64_t nh, int64_t nkv, int64_t hd, double eps);
+torch::Tensor qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
+                               torch::Tensor qw, torch::Tensor kw, torch::Tensor pos, torch::Tensor inv_freq,
+                               torch::Tensor rq, torch::Tensor rk, torch::Tensor dqw, torch::Tensor dkw, int64_t nh,
+                               int64_t nkv, int64_t hd, double eps);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor dh, torch::Tensor gu);
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, torch::Tensor w16, double lr,
+                double b1, double b2, double eps, double wd, int64_t step, double clip);
+torch::Tensor sumsq(torch::Tensor x);
+torch::Tensor group_adv(torch::Tensor r, int64_t G, bool unbiased, double eps);
+std::vector<torch::Tensor> ppo_clip_fwd_bwd(torch::Tensor logp, torch::Tensor old, torch::Tensor adv,
+                                            torch::Tensor mask, c10::optional<torch::Tensor> isw, double lo, double hi,
+                                            double cc, double denom);
+void logprob_fwd(torch::Tensor logits, torch::Tensor targets, double inv_t, torch::Tensor logp, torch::Tensor ent,
+                 torch::Tensor lse);
+void logprob_bwd(torch::Tensor logits, torch::Tensor targets, torch::Tensor lse, torch::Tensor dlogp,
+                 c10::optional<torch::Tensor> dent, double inv_t, c10::optional<torch::Tensor> ent);
+std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top_p, torch::Tensor row_seed,
+                                  torch::Tensor step);
+torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_table,
+                                torch::Tensor seq_lens, double scale, double k_scale, double v_scale,
+                                int64_t max_len_hint);
+void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots,
+               double inv_ks, double inv_vs);
+}  // namespace lrl
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "lumenrl_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &lrl::rmsnorm_fwd);
+  m.def("add_rmsnorm_fwd", &lrl::add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &lrl::rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &lrl::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &lrl::qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &lrl::swiglu_fwd);
+  m.def("swiglu_bwd", &lrl::swiglu_bwd);
+  m.def("adamw_step", &lrl::adamw_step);
+  m.def("sumsq", &lrl::sumsq);
+  m.def("group_adv", &lrl::group_adv);
+  m.def("ppo_clip_fwd_bwd", &lrl::ppo_clip_fwd_bwd, py::arg("logp"), py::arg("old"), py::arg("adv"), py::arg("mask"),
+        py::arg("isw"), py::arg("lo"), py::arg("hi"), py::arg("cc"), py::arg("denom"));
+  m.def("logprob_fwd", &lrl::logprob_fwd);
+  m.def("logprob_bwd", &lrl::logprob_bwd, py::arg("logits"), py::arg("targets"), py::arg("lse"), py::arg("dlogp"),
+        py::arg("dent"), py::arg("inv_t"), py::arg("ent") = py::none());
+  m.def("sample", &lrl::sample);
+  m.def("paged_decode_attn", &lrl::paged_decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"),
+        py::arg("block_table"), py::arg("seq_lens"), py::arg("scale"), py::arg("k_scale") = 1.0,
+        py::arg("v_scale") = 1.0, py::arg("max_len_hint") = 0);
+  m.def("kv_append", &lrl::kv_append);
+}

@@ -1,0 +1,410 @@
+// RMSNorm (+ fused residual add) and QK-RMSNorm + rotary embedding, forward
+// and backward.  Row kernels keep the row in registers (one 16-byte access
+// per 8 elements); weight gradients accumulate in registers across many rows
+// and hit global fp32 memory with one atomic per column per CTA.
+#include "../common.cuh"
+
+namespace lrl {
+
+constexpr int kMaxChunks = 4;  // 8-element chunks per thread => H <= 32768 at 1024 threads
+
+// ---------------------------------------------------------------- RMSNorm fwd
+template <bool kResidual>
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
+                                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                                   __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
+                                   float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int64_t base = int64_t(row) * H;
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * blockDim.x + threadIdx.x) * 8;
+    if (col < H) {
+      load8(x + base + col, v[c]);
+      if (kResidual) {
+        float r[8];
+        load8(res + base + col, r);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = __bfloat162float(__float2bfloat16(v[c][i] + r[i]));
+        // the residual stream is bf16: the sum is rounded as the unfused path does
+        store8(sum_out + base + col, v[c]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * blockDim.x + threadIdx.x) * 8;
+    if (col < H) {
+      float wf[8], o[8];
+      load8(w + col, wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * r * wf[i];
+      store8(y + base + col, o);
+    }
+  }
+}
+
+static int row_threads(int H) {
+  int t = (H / 8 + kMaxChunks - 1) / kMaxChunks;
+  t = ((t + 31) / 32) * 32;
+  return t < 32 ? 32 : (t > 1024 ? 1024 : t);
+}
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+  LRL_CHECK(x);
+  LRL_CHECK(w);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "rmsnorm: bf16 only");
+  const int H = x.size(-1);
+  const int64_t T = x.numel() / H;
+  TORCH_CHECK(H % 8 == 0 && H <= 1024 * 8 * kMaxChunks, "rmsnorm: H must be a multiple of 8 and <= 32768");
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {y, rstd};
+  rmsnorm_fwd_kernel<false><<<T, row_threads(H), 0, stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+      nullptr, rstd.data_ptr<float>(), H, (float)eps);
+  return {y, rstd};
+}
+
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps) {
+  x = x.contiguous();
+  res = res.contiguous();
+  LRL_CHECK(w);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "add_rmsnorm: bf16 only");
+  const int H = x.size(-1);
+  const int64_t T = x.numel() / H;
+  TORCH_CHECK(H % 8 == 0 && H <= 1024 * 8 * kMaxChunks, "add_rmsnorm: bad H");
+  auto y = torch::empty_like(x);
+  auto s = torch::empty_like(x);
+  if (T == 0) return {y, s};
+  rmsnorm_fwd_kernel<true><<<T, row_threads(H), 0, stream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)res.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+      (__nv_bfloat16*)y.data_ptr(), (__nv_bfloat16*)s.data_ptr(), nullptr, H, (float)eps);
+  return {y, s};
+}
+
+// ---------------------------------------------------------------- RMSNorm bwd
+// dx = r * (g - xh * mean(g * xh)),  g = w * dy,  xh = x * r;  dw += dy * xh
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int64_t T, int H,
+                                   int rows_per_cta) {
+  __shared__ float red[32];
+  float acc[kMaxChunks][8];
+  float wf[kMaxChunks][8];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * blockDim.x + threadIdx.x) * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
+    if (col < H) load8(w + col, wf[c]);
+  }
+  const int64_t r0 = int64_t(blockIdx.x) * rows_per_cta;
+  for (int64_t row = r0; row < r0 + rows_per_cta && row < T; ++row) {
+    const int64_t base = row * H;
+    const float r = rstd[row];
+    float xh[kMaxChunks][8], g[kMaxChunks][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * blockDim.x + threadIdx.x) * 8;
+      if (col < H) {
+        float d[8];
+        load8(x + base + col, xh[c]);
+        load8(dy + base + col, d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          xh[c][i] *= r;
+          g[c][i] = d[i] * wf[c][i];
+          dot += g[c][i] * xh[c][i];
+          acc[c][i] += d[i] * xh[c][i];
+        }
+      }
+    }
+    dot = block_sum(dot, red) / H;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * blockDim.x + threadIdx.x) * 8;
+      if (col < H) {
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = r * (g[c][i] - xh[c][i] * dot);
+        store8(dx + base + col, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * blockDim.x + threadIdx.x) * 8;
+    if (col < H) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) atomicAdd(dw + col + i, acc[c][i]);
+    }
+  }
+}
+
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw) {
+  LRL_CHECK(dy);
+  LRL_CHECK(x);
+  LRL_CHECK(w);
+  LRL_CHECK(rstd);
+  LRL_CHECK(dw);
+  TORCH_CHECK(dw.scalar_type() == at::kFloat, "dw accumulator must be fp32");
+  const int H = x.size(-1);
+  const int64_t T = x.numel() / H;
+  auto dx = torch::empty_like(x);
+  if (T == 0) return dx;
+  const int rows = 32;
+  const int64_t grid = (T + rows - 1) / rows;
+  rmsnorm_bwd_kernel<<<grid, row_threads(H), 0, stream()>>>(
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), T, H, rows);
+  return dx;
+}
+
+// ------------------------------------------------------- QK-RMSNorm + RoPE
+// One warp per (token, head).  Lane l owns P = hd/64 consecutive elements of
+// each half: [l*P, l*P+P) and [hd/2 + l*P, ...), so rotate-half pairs are
+// lane-local.  kind: 0 = q heads, 1 = k heads, 2 = v heads (copy only).
+template <int P>
+__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+                                       const __nv_bfloat16* __restrict__ kw, const int64_t* __restrict__ pos,
+                                       const float* __restrict__ inv_freq, __nv_bfloat16* __restrict__ q,
+                                       __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v,
+                                       float* __restrict__ rq, float* __restrict__ rk, int64_t T, int nh, int nkv,
+                                       float eps, int has_norm) {
+  constexpr int HD = 64 * P, HALF = 32 * P;
+  const int lane = threadIdx.x & 31;
+  const int kind = blockIdx.y;
+  const int nheads = kind == 0 ? nh : nkv;
+  const int col0 = kind == 0 ? 0 : (kind == 1 ? nh * HD : (nh + nkv) * HD);
+  const int stride_in = (nh + 2 * nkv) * HD;
+  __nv_bfloat16* out = kind == 0 ? q : (kind == 1 ? k : v);
+  const __nv_bfloat16* nw = kind == 0 ? qw : kw;
+  float* rs = kind == 0 ? rq : rk;
+  float wlo[P], whi[P], fr[P];
+  if (kind < 2) {
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      wlo[i] = has_norm ? __bfloat162float(nw[lane * P + i]) : 1.f;
+      whi[i] = has_norm ? __bfloat162float(nw[HALF + lane * P + i]) : 1.f;
+      fr[i] = inv_freq[lane * P + i];
+    }
+  }
+  const int64_t total = T * nheads;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < total; p += warps) {
+    const int64_t t = p / nheads;
+    const int h = p % nheads;
+    const __nv_bfloat16* src = qkv + t * stride_in + col0 + h * HD;
+    __nv_bfloat16* dst = out + (t * nheads + h) * HD;
+    float lo[P], hi[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      lo[i] = __bfloat162float(src[lane * P + i]);
+      hi[i] = __bfloat162float(src[HALF + lane * P + i]);
+    }
+    if (kind == 2) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        dst[lane * P + i] = __float2bfloat16(lo[i]);
+        dst[HALF + lane * P + i] = __float2bfloat16(hi[i]);
+      }
+      continue;
+    }
+    if (has_norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < P; ++i) ss += lo[i] * lo[i] + hi[i] * hi[i];
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / HD + eps);
+      if (lane == 0) rs[t * nheads + h] = r;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        lo[i] *= r * wlo[i];
+        hi[i] *= r * whi[i];
+      }
+    }
+    const float ps = (float)pos[t];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float s, c;
+      sincosf(ps * fr[i], &s, &c);
+      const float a = lo[i] * c - hi[i] * s;
+      const float b = hi[i] * c + lo[i] * s;
+      dst[lane * P + i] = __float2bfloat16(a);
+      dst[HALF + lane * P + i] = __float2bfloat16(b);
+    }
+  }
+}
+
+template <int P>
+__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, const __nv_bfloat16* __restrict__ dk,
+                                       const __nv_bfloat16* __restrict__ dv, const __nv_bfloat16* __restrict__ qkv,
+                                       const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+                                       const int64_t* __restrict__ pos, const float* __restrict__ inv_freq,
+                                       const float* __restrict__ rq, const float* __restrict__ rk,
+                                       __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqw,
+                                       float* __restrict__ dkw, int64_t T, int nh, int nkv, int has_norm) {
+  constexpr int HD = 64 * P, HALF = 32 * P;
+  const int lane = threadIdx.x & 31;
+  const int kind = blockIdx.y;
+  const int nheads = kind == 0 ? nh : nkv;
+  const int col0 = kind == 0 ? 0 : (kind == 1 ? nh * HD : (nh + nkv) * HD);
+  const int stride = (nh + 2 * nkv) * HD;
+  const __nv_bfloat16* dout = kind == 0 ? dq : (kind == 1 ? dk : dv);
+  const __nv_bfloat16* nw = kind == 0 ? qw : kw;
+  const float* rs = kind == 0 ? rq : rk;
+  float* dwp = kind == 0 ? dqw : dkw;
+  float wlo[P], whi[P], fr[P], alo[P], ahi[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    alo[i] = ahi[i] = 0.f;
+    if (kind < 2) {
+      wlo[i] = has_norm ? __bfloat162float(nw[lane * P + i]) : 1.f;
+      whi[i] = has_norm ? __bfloat162float(nw[HALF + lane * P + i]) : 1.f;
+      fr[i] = inv_freq[lane * P + i];
+    }
+  }
+  const int64_t total = T * nheads;
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < total; p += warps) {
+    const int64_t t = p / nheads;
+    const int h = p % nheads;
+    const __nv_bfloat16* g = dout + (t * nheads + h) * HD;
+    __nv_bfloat16* dst = dqkv + t * stride + col0 + h * HD;
+    float glo[P], ghi[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      glo[i] = __bfloat162float(g[lane * P + i]);
+      ghi[i] = __bfloat162float(g[HALF + lane * P + i]);
+    }
+    if (kind == 2) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        dst[lane * P + i] = __float2bfloat16(glo[i]);
+        dst[HALF + lane * P + i] = __float2bfloat16(ghi[i]);
+      }
+      continue;
+    }
+    // inverse rotation
+    const float ps = (float)pos[t];
+    float ulo[P], uhi[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float s, c;
+      sincosf(ps * fr[i], &s, &c);
+      ulo[i] = glo[i] * c + ghi[i] * s;
+      uhi[i] = ghi[i] * c - glo[i] * s;
+    }
+    if (!has_norm) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        dst[lane * P + i] = __float2bfloat16(ulo[i]);
+        dst[HALF + lane * P + i] = __float2bfloat16(uhi[i]);
+      }
+      continue;
+    }
+    const __nv_bfloat16* src = qkv + t * stride + col0 + h * HD;
+    const float r = rs[t * nheads + h];
+    float xlo[P], xhi[P];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      xlo[i] = __bfloat162float(src[lane * P + i]) * r;
+      xhi[i] = __bfloat162float(src[HALF + lane * P + i]) * r;
+      alo[i] += ulo[i] * xlo[i];
+      ahi[i] += uhi[i] * xhi[i];
+      ulo[i] *= wlo[i];
+      uhi[i] *= whi[i];
+      dot += ulo[i] * xlo[i] + uhi[i] * xhi[i];
+    }
+    dot = warp_sum(dot) / HD;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      dst[lane * P + i] = __float2bfloat16(r * (ulo[i] - xlo[i] * dot));
+      dst[HALF + lane * P + i] = __float2bfloat16(r * (uhi[i] - xhi[i] * dot));
+    }
+  }
+  if (kind < 2 && has_norm) {
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      atomicAdd(dwp + lane * P + i, alo[i]);
+      atomicAdd(dwp + HALF + lane * P + i, ahi[i]);
+    }
+  }
+}
+
+static int qk_grid(int64_t pairs) {
+  int64_t blocks = (pairs + 7) / 8;
+  const int64_t cap = int64_t(num_sms()) * 8;
+  return (int)(blocks < cap ? (blocks < 1 ? 1 : blocks) : cap);
+}
+
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                                            torch::Tensor inv_freq, int64_t nh, int64_t nkv, int64_t hd, double eps) {
+  LRL_CHECK(qkv);
+  LRL_CHECK(pos);
+  LRL_CHECK(inv_freq);
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16, "qk_norm_rope: bf16 qkv");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && inv_freq.scalar_type() == at::kFloat, "pos int64, inv_freq fp32");
+  TORCH_CHECK(hd == 64 || hd == 128 || hd == 256, "head_dim must be 64, 128 or 256");
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(qkv.size(1) == (nh + 2 * nkv) * hd, "qkv width mismatch");
+  const bool has_norm = qw.numel() > 0;
+  auto opts = qkv.options();
+  auto q = torch::empty({T, nh, hd}, opts), k = torch::empty({T, nkv, hd}, opts), v = torch::empty({T, nkv, hd}, opts);
+  auto rq = torch::empty({T, nh}, opts.dtype(at::kFloat)), rk = torch::empty({T, nkv}, opts.dtype(at::kFloat));
+  if (T == 0) return {q, k, v, rq, rk};
+  dim3 grid(qk_grid(T * nh), 3);
+  auto qwp = has_norm ? (const __nv_bfloat16*)qw.data_ptr() : nullptr;
+  auto kwp = has_norm ? (const __nv_bfloat16*)kw.data_ptr() : nullptr;
+#define LAUNCH(PP)                                                                                              \
+  qk_norm_rope_fwd_kernel<PP><<<grid, 256, 0, stream()>>>(                                                      \
+      (const __nv_bfloat16*)qkv.data_ptr(), qwp, kwp, pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),     \
+      (__nv_bfloat16*)q.data_ptr(), (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(),                \
+      rq.data_ptr<float>(), rk.data_ptr<float>(), T, (int)nh, (int)nkv, (float)eps, has_norm ? 1 : 0)
+  if (hd == 64) LAUNCH(1);
+  else if (hd == 128) LAUNCH(2);
+  else LAUNCH(4);
+#undef LAUNCH
+  return {q, k, v, rq, rk};
+}
+
+torch::Tensor qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
+                               torch::Tensor qw, torch::Tensor kw, torch::Tensor pos, torch::Tensor inv_freq,
+                               torch::Tensor rq, torch::Tensor rk, torch::Tensor dqw, torch::Tensor dkw, int64_t nh,
+                               int64_t nkv, int64_t hd, double eps) {
+  LRL_CHECK(dq);
+  LRL_CHECK(dk);
+  LRL_CHECK(dv);
+  LRL_CHECK(qkv);
+  const int64_t T = qkv.size(0);
+  const bool has_norm = qw.numel() > 0;
+  auto dqkv = torch::empty_like(qkv);
+  if (T == 0) return dqkv;
+  dim3 grid(qk_grid(T * nh), 3);
+  auto qwp = has_norm ? (const __nv_bfloat16*)qw.data_ptr() : nullptr;
+  auto kwp = has_norm ? (const __nv_bfloat16*)kw.data_ptr() : nullptr;
+#define LAUNCH(PP)                                                                                               \
+  qk_norm_rope_bwd_kernel<PP><<<grid, 256, 0, stream()>>>(                                                       \
+      (const __nv_bfloat16*)dq.data_ptr(), (const __nv_bfloat16*)dk.data_ptr(), (const __nv_bfloat16*)dv.data_ptr(), \
+      (const __nv_bfloat16*)qkv.data_ptr(), qwp, kwp, pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),      \
+      rq.data_ptr<float>(), rk.data_ptr<float>(), (__nv_bfloat16*)dqkv.data_ptr(), dqw.data_ptr<float>(),       \
+      dkw.data_ptr<float>(), T, (int)nh, (int)nkv, has_norm ? 1 : 0)
+  if (hd == 64) LAUNCH(1);
+  else if (hd == 128) LAUNCH(2);
+  else LAUNCH(4);
+#undef LAUNCH
+  return dqkv;
+}
+
+}  // namespace lrl

@@ -89,6 +89,7 @@ class RolloutEngine:
             nblocks = PagedKVCache.blocks_for_budget(spec, kv_cache_bytes)
         self.cache = PagedKVCache(spec, nblocks, self.device)
         self.runner = ModelRunner(model, self.cache)
+        self.runner.max_len = max_model_len
         self._graphs: dict[tuple, DecodeGraph] = {}
         self.weight_version = 0
 
@@ -120,7 +121,9 @@ class RolloutEngine:
         return g
 
     @torch.no_grad()
-    def generate(self, prompts: list[list[int]], sp: SamplingParams) -> GenerationOutput:
+    def generate(self, prompts, sp: SamplingParams) -> GenerationOutput:
+        """``prompts``: list of token-id lists, or an int64 tensor [P, L] of
+        equal-length prompts (already on the device for the fast path)."""
         if not self.cache.awake:
             self.wake()
         rows_per_prompt = sp.n
@@ -135,7 +138,8 @@ class RolloutEngine:
         def padw(t: Tensor, fill) -> Tensor:
             return torch.nn.functional.pad(t, (0, width - t.shape[1]), value=fill)
         return GenerationOutput(
-            prompts=[p for o in outs for p in o.prompts],
+            prompts=(torch.cat(list(o.prompts for o in outs)) if isinstance(outs[0].prompts, Tensor)
+                     else [p for o in outs for p in o.prompts]),
             responses=torch.cat([padw(o.responses, self.pad_token_id) for o in outs]),
             response_lengths=torch.cat([o.response_lengths for o in outs]),
             logprobs=torch.cat([padw(o.logprobs, 0.0) for o in outs]),
@@ -143,29 +147,33 @@ class RolloutEngine:
             routed_experts=[r for o in outs for r in o.routed_experts],
             stats={k: sum(o.stats.get(k, 0) for o in outs) for k in outs[0].stats})
 
-    def _generate_wave(self, prompts: list[list[int]], sp: SamplingParams, prompt_offset: int) -> GenerationOutput:
+    def _generate_wave(self, prompts, sp: SamplingParams, prompt_offset: int) -> GenerationOutput:
         dev, bs, n = self.device, self.block_size, sp.n
         P = len(prompts)
         B = P * n
         alloc = self.cache.allocator
-        max_new = min(sp.max_new_tokens, self.max_model_len - max(len(p) for p in prompts))
+        as_tensor = isinstance(prompts, Tensor)
+        plens = [int(prompts.shape[1])] * P if as_tensor else [len(p) for p in prompts]
+        max_new = min(sp.max_new_tokens, self.max_model_len - max(plens))
         if max_new <= 0:
             raise ValueError("prompt longer than max_model_len")
         # 1) blocks: prompt blocks per prompt, per-row private tail + generation blocks
         tables: list[list[int]] = []
         owned: list[list[int]] = []
         prompt_blocks: list[list[int]] = []
-        for p in prompts:
-            L = len(p)
+        for L in plens:
             prompt_blocks.append(alloc.alloc(math.ceil(L / bs)))
         # 2) prefill unique prompts
-        ids = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device=dev)
-        pos = torch.cat([torch.arange(len(p), device=dev) for p in prompts])
-        lens = torch.tensor([len(p) for p in prompts], device=dev)
+        if as_tensor:
+            ids = prompts.to(dev, torch.long).reshape(-1)
+        else:
+            ids = torch.tensor([t for p in prompts for t in p], dtype=torch.long, device=dev)
+        pos = torch.cat([torch.arange(L, device=dev) for L in plens])
+        lens = torch.tensor(plens, device=dev)
         cu = torch.zeros(P + 1, dtype=torch.int32, device=dev)
         cu[1:] = torch.cumsum(lens, 0)
-        slots = torch.tensor([prompt_blocks[i][j // bs] * bs + j % bs for i, p in enumerate(prompts)
-                              for j in range(len(p))], dtype=torch.long, device=dev)
+        slots = torch.tensor([prompt_blocks[i][j // bs] * bs + j % bs for i, L in enumerate(plens)
+                              for j in range(L)], dtype=torch.long, device=dev)
         recorder = None
         moe_layers = [i for i in range(self.args.num_layers) if self.args.is_moe_layer(i)]
         if moe_layers:
@@ -173,8 +181,7 @@ class RolloutEngine:
             self.runner.routing_recorder = recorder
         logits = self.runner.prefill(ids, pos, cu, int(lens.max()), slots)
         prompt_routes = recorder.take() if recorder else None   # [sumL, layers, k]
-        for i, p in enumerate(prompts):
-            L = len(p)
+        for i, L in enumerate(plens):
             full = L // bs
             need = math.ceil((L + max_new) / bs)
             for _ in range(n):
@@ -199,7 +206,7 @@ class RolloutEngine:
         for r, t in enumerate(tables):
             bt[r, : len(t)] = torch.tensor(t, dtype=torch.int32)
         g.block_table.copy_(bt)
-        plen = torch.tensor([len(p) for p in prompts], device=dev).repeat_interleave(n)
+        plen = lens.repeat_interleave(n)
         g.positions.copy_(plen)
         g.tokens.copy_(tok)
         routes_rows: list[list[Tensor]] = [[] for _ in range(B)]
@@ -252,7 +259,8 @@ class RolloutEngine:
                 # routes of prompt tokens + tokens that were fed back (all but the last sample)
                 routed.append(torch.cat([pr, gen[: max(lens_host[r] - 1, 0)]]).cpu())
         return GenerationOutput(
-            prompts=[p for p in prompts for _ in range(n)], responses=out_tok, response_lengths=lengths,
+            prompts=(prompts.repeat_interleave(n, 0) if as_tensor else [p for p in prompts for _ in range(n)]),
+            responses=out_tok, response_lengths=lengths,
             logprobs=out_lp, prompt_index=torch.arange(P, device=dev).repeat_interleave(n) + prompt_offset,
             routed_experts=routed,
             stats={"decode_steps": steps, "prefill_tokens": int(lens.sum()), "gen_tokens": int(lengths.sum())})

@@ -31,6 +31,7 @@ class ModelRunner:
         self.args = model.args
         self.scale = 1.0 / math.sqrt(self.args.head_dim)
         self.routing_recorder = None
+        self.max_len = 0   # static bound on context length (set by the engine)
 
     def _w(self, name: str) -> Tensor:
         return self.model.p(name).detach()
@@ -82,7 +83,7 @@ class ModelRunner:
             q, k, v = self._qkv(i, h, positions)
             ops.kv_cache_append(k, v, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
             o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
-                                           c.k_scale[i], c.v_scale[i])
+                                           c.k_scale[i], c.v_scale[i], self.max_len)
             x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h)
@@ -135,14 +136,19 @@ class DecodeGraph:
             for _ in range(2):
                 self._body()
         torch.cuda.current_stream().wait_stream(s)
+        from lumenrl_b200.ops.ext import LAUNCHES
         g = torch.cuda.CUDAGraph()
+        before = LAUNCHES[0]
         with torch.cuda.graph(g):
             self._body()
         self.graph = g
+        self.launches_per_replay = LAUNCHES[0] - before
 
     def run(self) -> tuple[Tensor, Tensor]:
         if self.graph is not None:
+            from lumenrl_b200.ops.ext import LAUNCHES
             self.graph.replay()
+            LAUNCHES[0] += self.launches_per_replay
         else:
             self._body()
         return self.out_tokens, self.out_logp

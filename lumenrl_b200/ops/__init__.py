@@ -227,12 +227,15 @@ def attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_se
 
 
 def paged_decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_table: Tensor, seq_lens: Tensor,
-                           scale: float, k_scale: float = 1.0, v_scale: float = 1.0) -> Tensor:
+                           scale: float, k_scale: float = 1.0, v_scale: float = 1.0, max_len: int = 0) -> Tensor:
+    """q [B,Hq,D] against the paged caches; ``max_len`` (static upper bound of
+    seq_lens, 0 = block-table capacity) sizes the context split without a
+    device->host read, so the call is CUDA-graph safe."""
     if not _cuda(q):
         return ref.paged_decode_attention(q, k_cache.to(q.dtype) * k_scale if k_cache.dtype != q.dtype else k_cache,
                                           v_cache.to(q.dtype) * v_scale if v_cache.dtype != q.dtype else v_cache,
                                           block_table, seq_lens, scale)
-    return ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale)
+    return ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale, max_len)
 
 
 def kv_cache_append(k: Tensor, v: Tensor, k_cache: Tensor, v_cache: Tensor, slots: Tensor,
@@ -264,13 +267,13 @@ class _TokenLogProb(torch.autograd.Function):
             b = min(T, a + chunk)
             logits = hidden[a:b] @ w.t()
             ext().logprob_fwd(logits, targets[a:b], inv_temp, logp[a:b], ent[a:b], lse[a:b])
-        ctx.save_for_backward(hidden, w, targets, lse)
+        ctx.save_for_backward(hidden, w, targets, lse, ent)
         ctx.meta = (w_handle, inv_temp, chunk, want_entropy)
         return logp, ent
 
     @staticmethod
     def backward(ctx, dlogp, dent):
-        hidden, w, targets, lse = ctx.saved_tensors
+        hidden, w, targets, lse, ent = ctx.saved_tensors
         w_handle, inv_temp, chunk, want_entropy = ctx.meta
         T = hidden.shape[0]
         dh = torch.empty_like(hidden)
@@ -282,7 +285,8 @@ class _TokenLogProb(torch.autograd.Function):
             logits = hidden[a:b] @ w.t()
             # in place: logits -> dL/dlogits (bf16)
             ext().logprob_bwd(logits, targets[a:b], lse[a:b], dlogp[a:b],
-                              dent[a:b] if dent is not None else None, inv_temp)
+                              dent[a:b] if dent is not None else None, inv_temp,
+                              ent[a:b] if dent is not None else None)
             dh[a:b] = logits @ w
             if mg is not None:
                 torch.addmm(mg, logits.t(), hidden[a:b], out_dtype=torch.float32, out=mg)

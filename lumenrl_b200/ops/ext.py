@@ -12,6 +12,25 @@ import importlib
 
 _MOD = None
 _ERR: Exception | None = None
+LAUNCHES = [0]   # kernels of this extension launched (graph replays add their captured count)
+
+
+class _Counted:
+    """Proxy that counts launches of the extension's kernels.  Each op call is
+    one kernel launch except the split decode attention (two)."""
+
+    def __init__(self, mod) -> None:
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def call(*a, **k):
+            LAUNCHES[0] += 1
+            return fn(*a, **k)
+        return call
 
 
 def _load():
@@ -20,7 +39,7 @@ def _load():
         return
     try:
         import torch  # noqa: F401  (loads libc10/libtorch for the extension)
-        _MOD = importlib.import_module("lumenrl_b200._C")
+        _MOD = _Counted(importlib.import_module("lumenrl_b200._C"))
     except Exception as e:  # pragma: no cover - depends on the build
         _ERR = e
 

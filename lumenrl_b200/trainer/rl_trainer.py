@@ -108,12 +108,15 @@ class RLTrainer:
         self.data = SyntheticPrompts(self.spec.prompt_len, self.spec.prompt_low, self.spec.prompt_high, c.seed)
         self.reward_fn = get_reward_fn(self.spec.reward)
         self.timer = PhaseTimer(st.device)
+        self.io_bytes = {"h2d": 0, "d2h": 0}
         return self
 
     # ------------------------------------------------------------------ step
     def _rollout(self, step: int) -> DataProto:
         st, sp = self.state, self.spec
-        prompts = self.data.batch(self.prompts_per_rank, step, st.rank)
+        host = self.data.batch_tensor(self.prompts_per_rank, step, st.rank, pin=st.device.type == "cuda")
+        prompts = host.to(st.device, non_blocking=True)
+        self.io_bytes["h2d"] = host.numel() * host.element_size()
         params = SamplingParams(max_new_tokens=sp.max_new_tokens, temperature=self.temperature, top_p=self.top_p,
                                 n=self.group, seed=self.config.seed * 7919 + step * 131 + st.rank,
                                 eos_token_id=sp.eos_token_id)
@@ -122,11 +125,8 @@ class RLTrainer:
         self.rollout.sleep()
         dev = st.device
         B = out.responses.shape[0]
-        plens = torch.tensor([len(p) for p in out.prompts], device=dev)
-        P = int(plens.max())
-        pgrid = torch.zeros(B, P, dtype=torch.long, device=dev)
-        for i, pr in enumerate(out.prompts):
-            pgrid[i, : len(pr)] = torch.tensor(pr, device=dev)
+        pgrid = out.prompts
+        plens = torch.full((B,), pgrid.shape[1], dtype=torch.long, device=dev)
         R = out.responses.shape[1]
         rmask = (torch.arange(R, device=dev).unsqueeze(0) < out.response_lengths.unsqueeze(1)).float()
         batch = DataProto(
@@ -204,6 +204,8 @@ class RLTrainer:
         m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
             float(len(batch)))
         m["weight_sync/ms"] = times["weight_sync"] * 1e3
+        host_result = batch["rewards"].to("cpu")          # the step's result read back to the host
+        self.io_bytes["d2h"] = host_result.numel() * host_result.element_size()
         m["step"] = step + 1
         self.global_step += 1
         self.history.append(m)

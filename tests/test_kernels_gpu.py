@@ -1,0 +1,222 @@
+"""Each sm_100a kernel against the fp32 PyTorch definition of the same op."""
+
+import math
+
+import pytest
+import torch
+
+from lumenrl_b200 import ops
+from lumenrl_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def close(a, b, atol, rtol=0.0):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    tol = atol + rtol * b.abs().max().item()
+    assert err <= tol, f"max abs err {err} > {tol}"
+
+
+@pytest.mark.parametrize("T,H", [(1, 256), (37, 4096), (129, 1000 * 8)])
+def test_rmsnorm_fwd_bwd(cuda, T, H):
+    torch.manual_seed(0)
+    x = torch.randn(T, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(H, device=cuda)).to(torch.bfloat16)
+    wp = torch.nn.Parameter(w.clone())
+    wp.main_grad = torch.zeros(H, device=cuda)
+    y = ops.rmsnorm(x, wp, 1e-6)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    close(y, yr, 2e-2, 1e-2)
+    g = torch.randn_like(yr)
+    y.backward(g.to(torch.bfloat16))
+    yr.backward(g)
+    close(x.grad, xr.grad, 3e-2, 2e-2)
+    close(wp.main_grad, wr.grad, 0.5, 1e-2)
+
+
+def test_add_rmsnorm(cuda):
+    torch.manual_seed(0)
+    x = torch.randn(64, 4096, device=cuda, dtype=torch.bfloat16)
+    r = torch.randn(64, 4096, device=cuda, dtype=torch.bfloat16)
+    w = torch.randn(4096, device=cuda).to(torch.bfloat16)
+    with torch.no_grad():
+        y, s = ops.add_rmsnorm(x, r, w, 1e-6)
+    s_ref = (x + r)
+    close(s, s_ref, 0.0)
+    close(y, ref.rmsnorm(s_ref.float(), w.float(), 1e-6), 3e-2, 1e-2)
+
+
+@pytest.mark.parametrize("hd,nh,nkv,norm", [(128, 32, 8, True), (64, 4, 2, False), (128, 4, 4, True)])
+def test_qk_norm_rope(cuda, hd, nh, nkv, norm):
+    torch.manual_seed(0)
+    T = 77
+    qkv = torch.randn(T, (nh + 2 * nkv) * hd, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    pos = torch.randint(0, 4000, (T,), device=cuda)
+    inv = ops.inv_freq_table(hd, 1e6, None, cuda)
+    qw = torch.nn.Parameter((1 + 0.1 * torch.randn(hd, device=cuda)).to(torch.bfloat16)) if norm else None
+    kw = torch.nn.Parameter((1 + 0.1 * torch.randn(hd, device=cuda)).to(torch.bfloat16)) if norm else None
+    if norm:
+        qw.main_grad = torch.zeros(hd, device=cuda)
+        kw.main_grad = torch.zeros(hd, device=cuda)
+    q, k, v = ops.qk_norm_rope(qkv, qw, kw, pos, inv, nh, nkv, hd, 1e-6)
+    # fp32 reference with autograd
+    xr = qkv.detach().float().requires_grad_(True)
+    qwr = qw.detach().float().requires_grad_(True) if norm else None
+    kwr = kw.detach().float().requires_grad_(True) if norm else None
+    ang = pos.float().unsqueeze(-1) * inv.unsqueeze(0)
+    cos, sin = ang.cos(), ang.sin()
+
+    def nrm(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * w if w is not None else t
+
+    def rope(t):
+        d = t.shape[-1] // 2
+        c, s = cos.unsqueeze(1), sin.unsqueeze(1)
+        return torch.cat([t[..., :d] * c - t[..., d:] * s, t[..., d:] * c + t[..., :d] * s], -1)
+    qr = rope(nrm(xr[:, : nh * hd].view(T, nh, hd), qwr))
+    kr = rope(nrm(xr[:, nh * hd:(nh + nkv) * hd].view(T, nkv, hd), kwr))
+    vr = xr[:, (nh + nkv) * hd:].view(T, nkv, hd)
+    close(q, qr, 3e-2, 1e-2)
+    close(k, kr, 3e-2, 1e-2)
+    close(v, vr, 0.0)
+    gq, gk, gv = torch.randn_like(qr), torch.randn_like(kr), torch.randn_like(vr)
+    torch.autograd.backward([q, k, v], [gq.bfloat16(), gk.bfloat16(), gv.bfloat16()])
+    torch.autograd.backward([qr, kr, vr], [gq, gk, gv])
+    close(qkv.grad, xr.grad, 5e-2, 2e-2)
+    if norm:
+        close(qw.main_grad, qwr.grad, 0.5, 2e-2)
+        close(kw.main_grad, kwr.grad, 0.5, 2e-2)
+
+
+def test_swiglu(cuda):
+    torch.manual_seed(0)
+    gu = torch.randn(33, 2 * 688, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    h = ops.swiglu(gu)
+    gr = gu.detach().float().requires_grad_(True)
+    hr = torch.nn.functional.silu(gr[:, :688]) * gr[:, 688:]
+    close(h, hr, 3e-2, 1e-2)
+    g = torch.randn_like(hr)
+    h.backward(g.bfloat16())
+    hr.backward(g)
+    close(gu.grad, gr.grad, 5e-2, 1e-2)
+
+
+@pytest.mark.parametrize("V,temp", [(2048, 1.0), (151936, 0.7)])
+def test_token_logprob_fwd_bwd(cuda, V, temp):
+    torch.manual_seed(0)
+    N, H = 70, 256
+    hidden = (0.5 * torch.randn(N, H, device=cuda)).to(torch.bfloat16).requires_grad_(True)
+    W = torch.nn.Parameter((0.05 * torch.randn(V, H, device=cuda)).to(torch.bfloat16))
+    W.main_grad = torch.zeros(V, H, device=cuda)
+    tgt = torch.randint(0, V, (N,), device=cuda)
+    lp, ent = ops.token_logprob(hidden, W, tgt, temperature=temp, chunk=32)
+    hr = hidden.detach().float().requires_grad_(True)
+    Wr = W.detach().float().requires_grad_(True)
+    z = (hr @ Wr.t()) / temp
+    lpr = z.log_softmax(-1).gather(-1, tgt.unsqueeze(-1)).squeeze(-1)
+    p = z.softmax(-1)
+    entr = -(p * z.log_softmax(-1)).sum(-1)
+    close(lp, lpr, 2e-2, 1e-3)
+    close(ent, entr, 2e-2, 1e-3)
+    g1, g2 = torch.randn(N, device=cuda), torch.randn(N, device=cuda)
+    torch.autograd.backward([lp, ent], [g1, g2])
+    torch.autograd.backward([lpr, entr], [g1, g2])
+    close(hidden.grad, hr.grad, 2e-2, 2e-2)
+    close(W.main_grad, Wr.grad, 2e-2, 2e-2)
+
+
+def test_group_advantage(cuda):
+    r = torch.randint(0, 2, (64,), device=cuda).float()
+    for unb in (False, True):
+        close(ops.group_advantage(r, 8, unb), ref.group_advantage(r.cpu(), 8, unb, 1e-8), 1e-5)
+
+
+@pytest.mark.parametrize("clip_c,with_w", [(0.0, False), (3.0, True)])
+def test_ppo_clip_loss(cuda, clip_c, with_w):
+    torch.manual_seed(0)
+    n = 5000
+    old = -torch.rand(n, device=cuda) * 3
+    logp = (old + 0.3 * torch.randn(n, device=cuda)).requires_grad_(True)
+    adv = torch.randn(n, device=cuda)
+    mask = (torch.rand(n, device=cuda) > 0.2).float()
+    w = torch.rand(n, device=cuda) * 2 if with_w else None
+    loss = ops.ppo_clip_loss(logp, old, adv, mask, 0.2, 0.28, clip_c, w, denom=1234.0)
+    lr = logp.detach().clone().requires_grad_(True)
+    loss_r = ref.ppo_clip_token_loss(lr, old, adv, mask, 0.2, 0.28, clip_c, w, 1234.0)
+    close(loss, loss_r, 1e-4, 1e-5)
+    loss.backward()
+    loss_r.backward()
+    close(logp.grad, lr.grad, 1e-6, 1e-5)
+
+
+def test_adamw_matches_reference(cuda):
+    torch.manual_seed(0)
+    n = 4096 * 3
+    p = torch.randn(n, device=cuda)
+    g = torch.randn(n, device=cuda)
+    m, v = torch.zeros(n, device=cuda), torch.zeros(n, device=cuda)
+    w16 = torch.empty(n, device=cuda, dtype=torch.bfloat16)
+    pr, mr, vr = p.cpu().clone(), m.cpu().clone(), v.cpu().clone()
+    from lumenrl_b200.ops.ext import ext
+    for step in (1, 2, 3):
+        ext().adamw_step(p, g, m, v, w16, 1e-3, 0.9, 0.95, 1e-8, 0.01, step, 0.5)
+        ref.adamw_reference(pr, g.cpu(), mr, vr, 1e-3, 0.9, 0.95, 1e-8, 0.01, step, 0.5)
+    close(p, pr, 1e-5, 1e-5)
+    close(w16, pr, 1e-2, 4e-3)
+    close(ext().sumsq(g), (g.double() ** 2).sum(), 1e-1, 1e-5)
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("B,Hq,Hk,bs,maxlen", [(3, 32, 8, 64, 700), (64, 32, 8, 64, 1536), (5, 4, 2, 16, 90)])
+def test_paged_decode_attention(cuda, kv_dtype, B, Hq, Hk, bs, maxlen):
+    torch.manual_seed(0)
+    D = 128
+    lens = torch.randint(1, maxlen + 1, (B,), device=cuda, dtype=torch.int32)
+    lens[0] = maxlen
+    mb = (maxlen + bs - 1) // bs
+    nblocks = B * mb + 3
+    perm = torch.randperm(nblocks - 1, device=cuda)[: B * mb] + 1
+    bt = perm.view(B, mb).to(torch.int32)
+    kc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(kv_dtype)
+    vc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(kv_dtype)
+    q = torch.randn(B, Hq, D, device=cuda, dtype=torch.bfloat16)
+    ks, vs = (0.5, 2.0) if kv_dtype != torch.bfloat16 else (1.0, 1.0)
+    out = ops.paged_decode_attention(q, kc, vc, bt, lens, 1 / math.sqrt(D), ks, vs, maxlen)
+    out_r = ref.paged_decode_attention(q.cpu(), kc.float().cpu() * ks, vc.float().cpu() * vs, bt.cpu(), lens.cpu(),
+                                       1 / math.sqrt(D))
+    close(out, out_r, 2e-2, 2e-2)
+
+
+def test_kv_append_roundtrip(cuda):
+    T, Hk, D, bs = 50, 8, 128, 16
+    kc = torch.zeros(10, bs, Hk, D, device=cuda, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    k = torch.randn(T, Hk, D, device=cuda, dtype=torch.bfloat16)
+    v = torch.randn(T, Hk, D, device=cuda, dtype=torch.bfloat16)
+    slots = torch.randperm(10 * bs, device=cuda)[:T]
+    ops.kv_cache_append(k, v, kc, vc, slots)
+    close(kc.view(-1, Hk, D)[slots], k, 0.0)
+    close(vc.view(-1, Hk, D)[slots], v, 0.0)
+
+
+def test_sampler_distribution(cuda):
+    torch.manual_seed(0)
+    V = 50
+    logits = torch.randn(1, V, device=cuda).repeat(4096, 1)
+    seeds = torch.arange(4096, device=cuda)
+    step = torch.zeros(1, dtype=torch.long, device=cuda)
+    tok, lp = ops.sample_tokens_device(logits, 1.0, 1.0, seeds, step)
+    p = torch.softmax(logits[0].float(), -1)
+    freq = torch.bincount(tok, minlength=V).float() / 4096
+    assert (freq - p).abs().max().item() < 0.03
+    close(lp, torch.log(p)[tok], 1e-4)
+    # same seed + step -> same draw; top-p keeps only the nucleus
+    tok2, _ = ops.sample_tokens_device(logits, 1.0, 1.0, seeds, step)
+    assert torch.equal(tok, tok2)
+    tk, _ = ops.sample_tokens_device(logits, 1.0, 0.5, seeds, step)
+    srt, idx = torch.sort(p, descending=True)
+    keep = set(idx[: int((torch.cumsum(srt, 0) < 0.5).sum()) + 1].tolist())
+    assert set(tk.tolist()) <= keep

@@ -89,13 +89,15 @@ def tiny_llama(vocab: int = 2048) -> ModelArgs:
 
 
 def tiny_qwen3(vocab: int = 2048, layers: int = 2) -> ModelArgs:
+    """Qwen3 block structure at toy size; head_dim 128 like the real model so
+    every GPU kernel (decode attention included) runs its production shape."""
     return ModelArgs(name="tiny-qwen3", vocab_size=vocab, hidden_size=256, num_layers=layers, num_heads=4,
-                     num_kv_heads=2, head_dim=64, intermediate_size=512, qk_norm=True, max_position_embeddings=4096)
+                     num_kv_heads=2, head_dim=128, intermediate_size=512, qk_norm=True, max_position_embeddings=4096)
 
 
 def tiny_qwen3_moe(vocab: int = 2048) -> ModelArgs:
     return ModelArgs(name="tiny-qwen3-moe", vocab_size=vocab, hidden_size=256, num_layers=2, num_heads=4,
-                     num_kv_heads=2, head_dim=64, intermediate_size=512, num_experts=8, num_experts_per_tok=2,
+                     num_kv_heads=2, head_dim=128, intermediate_size=512, num_experts=8, num_experts_per_tok=2,
                      moe_intermediate_size=128, router_aux_loss_coef=1e-3, max_position_embeddings=4096)
 
 

@@ -1,0 +1,112 @@
+"""Micro-benchmarks of the hot paths on one GPU (random weights).
+
+    python -m lumenrl_b200.utils.microbench decode --batch 64 --ctx 1024 --steps 20
+    python -m lumenrl_b200.utils.microbench train  --rows 4 --seq 1536 --steps 3
+    python -m lumenrl_b200.utils.microbench logprob --rows 8 --seq 1536
+
+Each prints one JSON line with CUDA-event timings (warm-up first).  They run
+the production code paths (engine decode graph, packed fwd/bwd, fused
+log-prob) and are the commands the ncu summaries under profiles/ were made
+with.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+
+def _model(name: str, trainable: bool):
+    from lumenrl_b200.models.config import resolve_model
+    from lumenrl_b200.models.qwen3 import Qwen3Model
+    args = resolve_model(name)
+    m = Qwen3Model(args, device="cuda", dtype=torch.bfloat16, requires_grad=trainable)
+    m.init_weights(0)
+    return m
+
+
+def _time(fn, steps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def bench_decode(ns) -> dict:
+    from lumenrl_b200.engine.inference.engine import RolloutEngine
+    from lumenrl_b200.engine.inference.runner import DecodeGraph
+    m = _model(ns.model, False)
+    B, ctx = ns.batch, ns.ctx
+    eng = RolloutEngine(m, max_num_seqs=B, max_model_len=ctx + 64, use_cuda_graph=not ns.no_graph)
+    g = DecodeGraph(eng.runner, B, eng.max_blocks_per_seq, 1.0, 1.0, not ns.no_graph)
+    nb = math.ceil((ctx + 64) / eng.block_size)
+    blocks = torch.arange(1, 1 + B * nb, dtype=torch.int32, device="cuda").view(B, nb)
+    g.block_table[:, :nb].copy_(blocks)
+    g.positions.fill_(ctx)
+    g.tokens.random_(0, m.args.vocab_size)
+    ms = _time(g.run, ns.steps, ns.warmup)
+    wbytes = m.flat.numel() * 2
+    kvbytes = B * ctx * m.args.kv_bytes_per_token()
+    return {"op": "decode_step", "batch": B, "ctx": ctx, "ms": ms,
+            "weights_GB": wbytes / 1e9, "kv_GB": kvbytes / 1e9, "achieved_TBps": (wbytes + kvbytes) / ms / 1e9}
+
+
+def bench_train(ns) -> dict:
+    from lumenrl_b200 import ops
+    m = _model(ns.model, True)
+    m.gradient_checkpointing = ns.recompute
+    grad = torch.zeros(m.flat.numel(), dtype=torch.float32, device="cuda")
+    m.attach_main_grad(grad)
+    T = ns.rows * ns.seq
+    ids = torch.randint(0, m.args.vocab_size, (T,), device="cuda")
+    pos = torch.arange(ns.seq, device="cuda").repeat(ns.rows)
+    cu = torch.arange(0, T + 1, ns.seq, dtype=torch.int32, device="cuda")
+
+    def step():
+        h = m.forward_packed(ids, pos, cu, ns.seq)
+        lp, _ = ops.token_logprob(h, m.lm_head, ids, want_entropy=False)
+        lp.sum().backward()
+    ms = _time(step, ns.steps, ns.warmup)
+    flops = (8 if ns.recompute else 6) * m.args.num_params() * T
+    return {"op": "train_micro_step", "tokens": T, "ms": ms, "tflops": flops / ms / 1e9, "recompute": ns.recompute}
+
+
+def bench_logprob(ns) -> dict:
+    from lumenrl_b200 import ops
+    m = _model(ns.model, False)
+    T = ns.rows * ns.seq
+    h = torch.randn(T, m.args.hidden_size, device="cuda", dtype=torch.bfloat16)
+    tgt = torch.randint(0, m.args.vocab_size, (T,), device="cuda")
+    ms = _time(lambda: ops.token_logprob(h, m.lm_head, tgt), ns.steps, ns.warmup)
+    return {"op": "lmhead_logprob", "tokens": T, "ms": ms,
+            "tflops": 2 * T * m.args.vocab_size * m.args.hidden_size / ms / 1e9}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["decode", "train", "logprob"])
+    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--rows", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=1536)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--recompute", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    ns = ap.parse_args(argv)
+    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob}[ns.what]
+    print(json.dumps(fn(ns)))
+
+
+if __name__ == "__main__":
+    main()

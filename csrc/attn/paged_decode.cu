@@ -421,3 +421,125 @@ void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor
 }
 
 }  // namespace lrl
+
+// ============================================================================
+// Scratch-free C entry point (declared in paged_decode_noalloc.h; it has no
+// counterpart in the reference).  The split-K partials live in a file-scope
+// device array instead of allocator memory.
+// ============================================================================
+#include <mutex>
+#include <cstdio>
+
+#include "paged_decode_noalloc.h"
+
+namespace lrl {
+namespace {
+
+constexpr size_t kNoAllocFloats = LRL_DECODE_NOALLOC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_decode_noalloc_scratch[kNoAllocFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+thread_local char g_noalloc_err[256] = "";
+
+int noalloc_fail(cudaError_t code, const char* msg) {
+  snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s", msg);
+  return (int)code;
+}
+
+}  // namespace
+
+// Device address of this device's scratch array.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+static cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+static int paged_decode_noalloc_impl(const void* q, const void* kc, const void* vc, const int* block_table,
+                                     const int* seq_lens, void* out, int B, int Hq, int Hk, int bs, int max_blocks,
+                                     int kv_fp8, float scale, float k_scale, float v_scale, int max_len_hint,
+                                     cudaStream_t st) {
+  if (!q || !kc || !vc || !block_table || !seq_lens || !out) return noalloc_fail(cudaErrorInvalidValue, "null pointer");
+  if (B <= 0 || Hq <= 0 || Hk <= 0 || bs <= 0 || max_blocks <= 0)
+    return noalloc_fail(cudaErrorInvalidValue, "sizes must be positive");
+  if (Hq % Hk != 0 || Hq / Hk > 16) return noalloc_fail(cudaErrorInvalidValue, "GQA group must divide and be <= 16");
+  const int64_t max_len = max_len_hint > 0 ? max_len_hint : (int64_t)max_blocks * bs;
+  const int64_t max_tiles = (max_len + kTile - 1) / kTile;
+  const int nsplit = decode_num_splits(B, Hk, max_tiles);
+  const int tps = (int)((max_tiles + nsplit - 1) / nsplit);
+  float* po = nullptr;
+  float* pl = nullptr;
+  if (nsplit > 1) {
+    const size_t need = (size_t)nsplit * B * Hq * (kHD + 1);
+    if (need > kNoAllocFloats) {
+      char msg[200];
+      snprintf(msg, sizeof(msg), "split-K scratch of %zu bytes exceeds the %u-byte static array", need * 4,
+               (unsigned)LRL_DECODE_NOALLOC_SCRATCH_BYTES);
+      return noalloc_fail(cudaErrorInvalidValue, msg);
+    }
+    float* base = nullptr;
+    cudaError_t e = noalloc_scratch(&base);
+    if (e != cudaSuccess) return noalloc_fail(e, "cudaGetSymbolAddress of the scratch array failed");
+    po = base;
+    pl = base + (size_t)nsplit * B * Hq * kHD;
+  }
+  const size_t smem = 4 * kTileBytes;
+  const float sl2 = scale * k_scale * 1.4426950408889634f;
+  dim3 grid(nsplit, Hk, B);
+  cudaError_t e;
+  if (kv_fp8) {
+    auto kern = paged_decode_kernel<__nv_fp8_e4m3>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
+    kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_fp8_e4m3*)kc, (const __nv_fp8_e4m3*)vc,
+                                       block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
+                                       tps, sl2, v_scale);
+  } else {
+    auto kern = paged_decode_kernel<__nv_bfloat16>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
+    kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
+                                       block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
+                                       tps, sl2, v_scale);
+  }
+  if (nsplit > 1) {
+    decode_combine_kernel<<<dim3(B, Hq), kHD, 0, st>>>(po, pl, (__nv_bfloat16*)out, nsplit, B, Hq);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(e, "kernel launch failed");
+  g_noalloc_err[0] = '\0';
+  return 0;
+}
+
+}  // namespace lrl
+
+extern "C" __attribute__((visibility("default"))) int lrl_paged_decode_attn_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int* block_table, const int* seq_lens, void* out,
+    int batch, int num_q_heads, int num_kv_heads, int block_size, int max_blocks, int kv_fp8, float scale,
+    float k_scale, float v_scale, int max_len_hint, cudaStream_t stream) {
+  return lrl::paged_decode_noalloc_impl(q, k_cache, v_cache, block_table, seq_lens, out, batch, num_q_heads,
+                                        num_kv_heads, block_size, max_blocks, kv_fp8, scale, k_scale, v_scale,
+                                        max_len_hint, stream);
+}
+
+extern "C" __attribute__((visibility("default"))) const char* lrl_decode_noalloc_last_error(void) {
+  return lrl::g_noalloc_err;
+}
+
+extern "C" __attribute__((visibility("default"))) size_t lrl_decode_noalloc_scratch_bytes(void) {
+  return LRL_DECODE_NOALLOC_SCRATCH_BYTES;
+}

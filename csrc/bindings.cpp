@@ -33,6 +33,8 @@ torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor
                                 int64_t max_len_hint);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots,
                double inv_ks, double inv_vs);
+torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
+int64_t tc_gemm_status();
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -57,4 +59,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_table"), py::arg("seq_lens"), py::arg("scale"), py::arg("k_scale") = 1.0,
         py::arg("v_scale") = 1.0, py::arg("max_len_hint") = 0);
   m.def("kv_append", &lrl::kv_append);
+  m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,
+        py::arg("bn") = 0);
+  m.def("tc_gemm_status", &lrl::tc_gemm_status);
 }

@@ -403,3 +403,28 @@ def inv_freq_table(head_dim: int, theta: float, scaling: dict | None, device) ->
 
 def softmax_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 GEMM (hand-written sm_100a kernel)
+# ---------------------------------------------------------------------------
+
+def tc_gemm(a: Tensor, b: Tensor, out: Optional[Tensor] = None, accumulate: bool = False,
+            out_dtype: torch.dtype = torch.bfloat16, bn: int = 0) -> Tensor:
+    """C = a @ b.T with a [M,K], b [N,K] bf16 on the tensor cores (TMA + tcgen05
+    + TMEM).  ``accumulate``: out (fp32 [M,N]) += a @ b.T."""
+    if not _cuda(a):
+        r = a.float() @ b.float().t()
+        if accumulate:
+            out += r
+            return out
+        return r.to(out_dtype)
+    if accumulate:
+        return ext().tc_gemm(a, b, out, 2, bn)
+    return ext().tc_gemm(a, b, None, 0 if out_dtype == torch.bfloat16 else 1, bn)
+
+
+def tc_gemm_status() -> int:
+    """Error word of the tcgen05 GEMMs since the last call (0 = no error); a
+    non-zero value names the role whose bounded wait expired."""
+    return int(ext().tc_gemm_status())

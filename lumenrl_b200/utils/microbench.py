@@ -91,9 +91,27 @@ def bench_logprob(ns) -> dict:
             "tflops": 2 * T * m.args.vocab_size * m.args.hidden_size / ms / 1e9}
 
 
+def bench_gemm(ns) -> dict:
+    """tcgen05 GEMM vs cuBLAS (torch.matmul) on the model's GEMM shapes."""
+    from lumenrl_b200 import ops
+    shapes = [(6144, 6144, 4096), (6144, 24576, 4096), (6144, 4096, 12288), (6144, 4096, 4096),
+              (4096, 151936, 4096), (8192, 8192, 8192), (64, 24576, 4096), (64, 6144, 4096)]
+    out = []
+    for M, N, K in shapes:
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        b = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        t_tc = _time(lambda: ops.tc_gemm(a, b), ns.steps, ns.warmup)
+        t_cb = _time(lambda: a @ b.t(), ns.steps, ns.warmup)
+        fl = 2 * M * N * K
+        out.append({"M": M, "N": N, "K": K, "tc_ms": t_tc, "cublas_ms": t_cb, "tc_tflops": fl / t_tc / 1e9,
+                    "cublas_tflops": fl / t_cb / 1e9})
+    st = ops.tc_gemm_status()
+    return {"op": "gemm", "status": st, "shapes": out}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "train", "logprob"])
+    ap.add_argument("what", choices=["decode", "train", "logprob", "gemm"])
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=1024)
@@ -104,7 +122,7 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
-    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob}[ns.what]
+    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm}[ns.what]
     print(json.dumps(fn(ns)))
 
 

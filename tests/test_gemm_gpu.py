@@ -1,0 +1,39 @@
+"""Hand-written tcgen05 GEMM against an fp32 matmul of the same bf16 inputs."""
+
+import pytest
+import torch
+
+from lumenrl_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(128, 128, 64, 128), (256, 512, 256, 128), (300, 640, 4096, 0),
+                                      (64, 6144, 4096, 0), (1024, 2048, 512, 256), (77, 1000 * 8, 136, 128),
+                                      (4096, 4096, 4096, 0)])
+def test_tc_gemm_bf16(cuda, M, N, K, bn):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=cuda) / K ** 0.5).to(torch.bfloat16)
+    c = ops.tc_gemm(a, b, bn=bn)
+    torch.cuda.synchronize()
+    assert ops.tc_gemm_status() == 0
+    ref = a.float() @ b.float().t()
+    err = (c.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), err
+
+
+def test_tc_gemm_fp32_accumulate(cuda):
+    torch.manual_seed(1)
+    M, N, K = 384, 768, 1024
+    a = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    b = torch.randn(N, K, device=cuda).to(torch.bfloat16)
+    c = torch.randn(M, N, device=cuda)
+    c0 = c.clone()
+    ops.tc_gemm(a, b, out=c, accumulate=True)
+    f = ops.tc_gemm(a, b, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.tc_gemm_status() == 0
+    ref = a.float() @ b.float().t()
+    assert (f - ref).abs().max().item() < 1e-2
+    assert (c - (c0 + ref)).abs().max().item() < 1e-2

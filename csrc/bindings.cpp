@@ -35,6 +35,18 @@ void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor
                double inv_ks, double inv_vs);
 torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
 int64_t tc_gemm_status();
+std::vector<int64_t> symm_malloc(int64_t nbytes);
+int64_t symm_open(std::vector<int64_t> handle_words);
+void symm_close(int64_t ptr);
+void symm_free(int64_t ptr);
+torch::Tensor symm_tensor(int64_t ptr, int64_t numel, torch::ScalarType dtype);
+int64_t symm_signal_words();
+void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+             torch::Tensor out, int64_t epoch, torch::Tensor status);
+void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+              torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
+              double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
+              torch::Tensor norm_out);
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -62,4 +74,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,
         py::arg("bn") = 0);
   m.def("tc_gemm_status", &lrl::tc_gemm_status);
+  m.def("symm_malloc", &lrl::symm_malloc);
+  m.def("symm_open", &lrl::symm_open);
+  m.def("symm_close", &lrl::symm_close);
+  m.def("symm_free", &lrl::symm_free);
+  m.def("symm_tensor", &lrl::symm_tensor);
+  m.def("symm_signal_words", &lrl::symm_signal_words);
+  m.def("rs_norm", &lrl::rs_norm);
+  m.def("adamw_ag", &lrl::adamw_ag);
 }

@@ -50,13 +50,21 @@ class ActorEngine:
                  eps: float = 1e-8, weight_decay: float = 0.01, max_grad_norm: float = 1.0, seed: int = 0,
                  dtype: Optional[torch.dtype] = None, trainable: bool = True, gradient_checkpointing: bool = False,
                  total_steps: int = 1000, warmup_steps: int = 0, lr_style: str = "constant", min_lr_ratio: float = 0.0,
-                 comm=None, init: bool = True) -> None:
+                 comm=None, init: bool = True, fused_comm: bool = True) -> None:
         self.args = args
         self.state = state
         self.device = state.device
         if dtype is None:
             dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
-        flat = torch.zeros(padded_numel(args, state.world_size if trainable else 1), dtype=dtype, device=self.device)
+        numel = padded_numel(args, state.world_size if trainable else 1)
+        if comm is None and trainable and state.world_size > 1 and self.device.type == "cuda" and fused_comm:
+            from lumenrl_b200.parallel.symm import NVLinkOptimizerComm
+            comm = NVLinkOptimizerComm(numel, state.rank, state.world_size, dtype)
+        if comm is not None and hasattr(comm, "weights"):
+            flat = comm.weights.tensor      # resident weights live in NVLink-mapped memory
+        else:
+            flat = torch.zeros(numel, dtype=dtype, device=self.device)
+        self.comm = comm
         self.model = Qwen3Model(args, device=self.device, dtype=dtype, flat=flat, requires_grad=trainable)
         if init:
             self.model.init_weights(seed)

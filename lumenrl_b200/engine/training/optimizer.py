@@ -47,9 +47,11 @@ class ShardedFlatAdamW:
         self.master = w16[self.lo: self.hi].float().clone()
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
-        self.grad = torch.zeros(n, dtype=grad_dtype, device=dev)
+        fused = comm is not None and hasattr(comm, "fused_step")
+        self.grad = comm.grads.tensor if fused else torch.zeros(n, dtype=grad_dtype, device=dev)
         self.grad_shard = self.grad[self.lo: self.hi] if world == 1 else torch.zeros(self.shard, dtype=torch.float32,
                                                                                      device=dev)
+        self.fused = fused
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.step_count = 0
@@ -60,7 +62,7 @@ class ShardedFlatAdamW:
     def _reduce_scatter(self) -> None:
         if self.world == 1:
             return
-        if self.comm is not None:
+        if self.comm is not None and hasattr(self.comm, "reduce_scatter_sum"):
             self.comm.reduce_scatter_sum(self.grad, self.grad_shard)
         elif self.grad.is_cuda:
             dist.reduce_scatter_tensor(self.grad_shard, self.grad)
@@ -71,7 +73,7 @@ class ShardedFlatAdamW:
     def _all_gather(self) -> None:
         if self.world == 1:
             return
-        if self.comm is not None:
+        if self.comm is not None and hasattr(self.comm, "all_gather"):
             self.comm.all_gather(self.w16, self.lo, self.hi)
         elif self.w16.is_cuda:
             dist.all_gather_into_tensor(self.w16, self.w16[self.lo: self.hi].clone())
@@ -94,6 +96,17 @@ class ShardedFlatAdamW:
     @torch.no_grad()
     def step(self, lr: Optional[float] = None) -> dict[str, float]:
         lr = self.lr if lr is None else lr
+        if self.fused:
+            # one kernel pair over NVLink peer memory: reduce-scatter + norm, then
+            # clip + AdamW + bf16 broadcast into every rank's resident weights
+            norm, skipped = self.comm.fused_step(self.lo, self.shard, self.master, self.grad_shard, self.m, self.v,
+                                                 lr, self.betas, self.eps, self.wd, self.step_count + 1,
+                                                 self.max_grad_norm)
+            if not skipped:
+                self.step_count += 1
+            self.grad.zero_()
+            clip = min(1.0, self.max_grad_norm / (norm + 1e-6)) if self.max_grad_norm else 1.0
+            return {"grad_norm": norm, "skipped": float(skipped), "lr": lr, "clip_coef": clip}
         t0 = time.perf_counter()
         self._reduce_scatter()
         norm = self._global_norm()

@@ -1,0 +1,61 @@
+"""Multi-GPU: the fused NVLink optimizer step (peer-load reduce-scatter +
+norm, clip + AdamW + bf16 peer-store broadcast) against the NCCL path, as
+2 processes on 2 GPUs.  Skips with fewer than 2 GPUs."""
+
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.engine.training.optimizer import ShardedFlatAdamW
+    from lumenrl_b200.parallel.symm import NVLinkOptimizerComm
+    n = 128 * world * 1000
+    torch.manual_seed(0)
+    w0 = torch.randn(n, device="cuda").to(torch.bfloat16)
+    comm = NVLinkOptimizerComm(n, rank, world)
+    comm.weights.tensor.copy_(w0)
+    fused = ShardedFlatAdamW(comm.weights.tensor, world, rank, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1,
+                             max_grad_norm=1.0, comm=comm)
+    plain_w = w0.clone()
+    plain = ShardedFlatAdamW(plain_w, world, rank, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+    norms = []
+    for step in range(3):
+        g = torch.randn(n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(10 * step + rank))
+        fused.grad.copy_(g)
+        plain.grad.copy_(g)
+        a = fused.step()
+        b = plain.step()
+        norms.append((a["grad_norm"], b["grad_norm"]))
+    torch.cuda.synchronize()
+    err = (comm.weights.tensor.float() - plain_w.float()).abs().max().item()
+    q.put((rank, err, norms))
+    comm.close()
+    dist.destroy_process_group()
+
+
+def test_fused_optimizer_step_matches_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + os.getpid() % 200
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err, norms in res:
+        assert err <= 1e-2, (rank, err)
+        for a, b in norms:
+            assert abs(a - b) <= 1e-3 * max(1.0, b), (a, b)

@@ -42,11 +42,11 @@ void symm_free(int64_t ptr);
 torch::Tensor symm_tensor(int64_t ptr, int64_t numel, torch::ScalarType dtype);
 int64_t symm_signal_words();
 void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-             torch::Tensor out, int64_t epoch, torch::Tensor status);
+             torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
               torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
               double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
-              torch::Tensor norm_out);
+              torch::Tensor norm_out, int64_t wait_cycles);
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

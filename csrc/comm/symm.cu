@@ -25,7 +25,6 @@ namespace lrl {
 
 namespace {
 
-constexpr long long kCommWaitCycles = 2000000000LL;
 constexpr int kMaxRanks = 8;
 constexpr int kSlots = 8;        // barrier slots
 // signal area layout (uint32 words): flags[kSlots][kMaxRanks] | norms[kMaxRanks] (float) | pad
@@ -50,7 +49,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
 // peer's row for `slot`; every block's thread 0 waits (bounded) until all W
 // announcements for this epoch are visible in the local row.
 __device__ bool rank_barrier(const PeerPtrs& sig, uint32_t* my_sig, int rank, int W, int slot, uint32_t epoch,
-                             int* status) {
+                             int* status, long long wait_cycles) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
@@ -62,7 +61,7 @@ __device__ bool rank_barrier(const PeerPtrs& sig, uint32_t* my_sig, int rank, in
     const long long t0 = clock64();
     for (int r = 0; r < W && ok; ++r) {
       while (ld_acquire_sys(my_sig + kSigFlags + slot * kMaxRanks + r) < epoch) {
-        if (clock64() - t0 > kCommWaitCycles || *reinterpret_cast<volatile int*>(status) != 0) {
+        if (clock64() - t0 > wait_cycles || *reinterpret_cast<volatile int*>(status) != 0) {
           atomicCAS(status, 0, 100 + slot);
           ok = 0;
           break;
@@ -75,8 +74,9 @@ __device__ bool rank_barrier(const PeerPtrs& sig, uint32_t* my_sig, int rank, in
 }
 
 __global__ void rs_norm_kernel(PeerPtrs grads, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t lo,
-                               int64_t n, float* __restrict__ out, uint32_t epoch, int* status) {
-  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status)) return;
+                               int64_t n, float* __restrict__ out, uint32_t epoch, int* status,
+                               long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles)) return;
   __shared__ float red[32];
   float ss = 0.f;
   const int64_t n4 = n / 4;
@@ -113,8 +113,9 @@ __global__ void rs_norm_kernel(PeerPtrs grads, PeerPtrs sig, uint32_t* my_sig, i
 __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t lo,
                                 int64_t n, float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                                 float* __restrict__ v, float lr, float b1, float b2, float eps, float wd, float bc1,
-                                float bc2, float max_norm, uint32_t epoch, int* status, float* norm_out) {
-  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status)) return;
+                                float bc2, float max_norm, uint32_t epoch, int* status, float* norm_out,
+                                long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles)) return;
   float sq = 0.f;
   for (int r = 0; r < W; ++r) sq += reinterpret_cast<volatile float*>(my_sig + kSigNorms)[r];
   const float norm = sqrtf(sq);
@@ -171,7 +172,7 @@ __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig
       const long long t0 = clock64();
       for (int r = 0; r < W; ++r) {
         while (ld_acquire_sys(my_sig + kSigFlags + 2 * kMaxRanks + r) < epoch) {
-          if (clock64() - t0 > kCommWaitCycles) {
+          if (clock64() - t0 > wait_cycles) {
             atomicCAS(status, 0, 102);
             break;
           }
@@ -226,19 +227,19 @@ int64_t symm_signal_words() { return kSigWords; }
 
 // ---- fused optimizer collectives ----------------------------------------------
 void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-             torch::Tensor out, int64_t epoch, torch::Tensor status) {
+             torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles) {
   TORCH_CHECK(n % 4 == 0 && lo % 4 == 0, "rs_norm: 16-byte aligned shards");
   const int W = grad_ptrs.size();
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   rs_norm_kernel<<<comm_grid(), 512, 0, stream()>>>(to_peers(grad_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W, lo,
                                                     n, out.data_ptr<float>(), (uint32_t)epoch,
-                                                    status.data_ptr<int>());
+                                                    status.data_ptr<int>(), (long long)wait_cycles);
 }
 
 void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
               torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
               double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
-              torch::Tensor norm_out) {
+              torch::Tensor norm_out, int64_t wait_cycles) {
   TORCH_CHECK(n % 4 == 0 && lo % 4 == 0, "adamw_ag: aligned shards");
   const int W = weight_ptrs.size();
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
@@ -246,7 +247,8 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
   adamw_ag_kernel<<<comm_grid(), 512, 0, stream()>>>(
       to_peers(weight_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W, lo, n, p.data_ptr<float>(),
       g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
-      (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(), norm_out.data_ptr<float>());
+      (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(), norm_out.data_ptr<float>(),
+      (long long)wait_cycles);
 }
 
 }  // namespace lrl

@@ -68,8 +68,11 @@ class SymmetricBuffer:
 class NVLinkOptimizerComm:
     """Fused reduce-scatter / AdamW / all-gather over NVLink peer memory."""
 
-    def __init__(self, numel: int, rank: int, world: int, weight_dtype=torch.bfloat16, group=None) -> None:
-        self.rank, self.world = rank, world
+    def __init__(self, numel: int, rank: int, world: int, weight_dtype=torch.bfloat16, group=None,
+                 wait_seconds: float = 10.0) -> None:
+        self.rank, self.world, self.group = rank, world, group
+        # in-kernel spin bound, in SM clock cycles at boost clock
+        self.wait_cycles = int(wait_seconds * 2.0e9)
         self.weights = SymmetricBuffer(numel, weight_dtype, rank, world, group)
         self.grads = SymmetricBuffer(numel, torch.float32, rank, world, group)
         self.signals = SymmetricBuffer(int(ext().symm_signal_words()), torch.int32, rank, world, group)
@@ -77,17 +80,23 @@ class NVLinkOptimizerComm:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.norm = torch.zeros(1, dtype=torch.float32, device=dev)
         self.epoch = 0
+        self._rendezvous = torch.zeros(1, dtype=torch.int32, device=dev)
         dist.barrier(group=group)
 
     def fused_step(self, shard_lo: int, shard_n: int, master, grad_shard, m, v, lr: float, betas, eps: float,
-                   wd: float, step: int, max_norm: float) -> tuple[float, bool]:
+                   wd: float, step: int, max_norm: float, rendezvous: bool = True) -> tuple[float, bool]:
         self.epoch += 1
         e = ext()
+        # stream-ordered rendezvous (4 bytes over NCCL, control plane only): ranks
+        # whose backward finished at different times meet here, so the in-kernel
+        # flag barriers below only order memory and never wait long
+        if rendezvous:
+            dist.all_reduce(self._rendezvous, group=self.group)
         e.rs_norm(self.grads.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, grad_shard, self.epoch,
-                  self.status)
+                  self.status, self.wait_cycles)
         e.adamw_ag(self.weights.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, master, grad_shard, m, v, lr,
                    betas[0], betas[1], eps, wd, step, max_norm if max_norm else 0.0, self.epoch, self.status,
-                   self.norm)
+                   self.norm, self.wait_cycles)
         vals = torch.cat([self.norm, self.status.float()]).cpu()   # one device->host read per step
         norm, status = float(vals[0]), int(vals[1])
         if status:

@@ -59,3 +59,42 @@ def test_fused_optimizer_step_matches_nccl():
         assert err <= 1e-2, (rank, err)
         for a, b in norms:
             assert abs(a - b) <= 1e-3 * max(1.0, b), (a, b)
+
+
+def _dead_peer_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.parallel.symm import CommTimeout, NVLinkOptimizerComm
+    n = 128 * world * 64
+    comm = NVLinkOptimizerComm(n, rank, world, wait_seconds=0.5)
+    shard = n // world
+    master = torch.zeros(shard, device="cuda")
+    gs, m, v = torch.zeros_like(master), torch.zeros_like(master), torch.zeros_like(master)
+    result = "no-error"
+    if rank == 0:   # rank 1 "dies" before the step: it never enters the kernels
+        try:
+            comm.fused_step(0, shard, master, gs, m, v, 1e-3, (0.9, 0.95), 1e-8, 0.0, 1, 1.0, rendezvous=False)
+        except CommTimeout:
+            result = "timeout"
+    torch.cuda.synchronize()
+    q.put((rank, result))
+    dist.barrier()           # both ranks leave between steps, nothing in flight
+    comm.close()
+    dist.destroy_process_group()
+
+
+def test_dead_peer_becomes_comm_timeout():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29900 + os.getpid() % 90
+    procs = [ctx.Process(target=_dead_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "timeout"

@@ -109,9 +109,49 @@ def bench_gemm(ns) -> dict:
     return {"op": "gemm", "status": st, "shapes": out}
 
 
+def bench_comm(ns) -> dict:
+    """Fused NVLink optimizer step vs the NCCL path on a Qwen3-8B-sized flat
+    buffer (launch under torchrun, one rank per GPU)."""
+    import torch.distributed as dist
+    from lumenrl_b200.engine.training.optimizer import ShardedFlatAdamW
+    from lumenrl_b200.parallel.dist import init_distributed
+    from lumenrl_b200.parallel.symm import NVLinkOptimizerComm
+    st = init_distributed()
+    W, r = st.world_size, st.rank
+    n = (ns.numel // (W * 128)) * W * 128
+    comm = NVLinkOptimizerComm(n, r, W)
+    fused = ShardedFlatAdamW(comm.weights.tensor, W, r, lr=1e-6, comm=comm)
+    fused.grad.normal_()
+
+    def fstep():
+        fused.comm.fused_step(fused.lo, fused.shard, fused.master, fused.grad_shard, fused.m, fused.v, 1e-6,
+                              fused.betas, fused.eps, fused.wd, 1, 1.0)
+    t_f = _time(fstep, ns.steps, ns.warmup)
+    del fused
+    plain_w = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
+    plain = ShardedFlatAdamW(plain_w, W, r, lr=1e-6)
+
+    def pstep():
+        plain.grad.normal_() if False else None
+        plain._reduce_scatter()
+        plain._global_norm()
+        from lumenrl_b200.ops.ext import ext
+        ext().adamw_step(plain.master, plain.grad_shard, plain.m, plain.v, plain.w16[plain.lo: plain.hi], 1e-6,
+                         0.9, 0.999, 1e-8, 0.01, 1, 1.0)
+        plain._all_gather()
+    t_p = _time(pstep, ns.steps, ns.warmup)
+    t = torch.tensor([t_f, t_p], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    comm.close()
+    grad_bytes, w_bytes = n * 4, n * 2
+    return {"op": "optimizer_collective", "world": W, "numel": n, "fused_ms": float(t[0]), "nccl_ms": float(t[1]),
+            "nvlink_bytes_per_gpu": (W - 1) / W * (grad_bytes + w_bytes)}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "train", "logprob", "gemm"])
+    ap.add_argument("what", choices=["decode", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("--numel", type=int, default=8_200_000_000)
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=1024)
@@ -122,8 +162,12 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
-    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm}[ns.what]
-    print(json.dumps(fn(ns)))
+    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
+          "comm": bench_comm}[ns.what]
+    res = fn(ns)
+    import os
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(res))
 
 
 if __name__ == "__main__":

@@ -143,7 +143,7 @@ def main() -> None:
     world, rank = st.world_size, st.rank
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
     margs = resolve_model(args.model)
-    recompute = args.recompute == "on" or (args.recompute == "auto" and world == 1)
+    recompute = {"on": True, "off": False, "auto": "auto"}[args.recompute]
     cfg = LumenRLConfig.from_dict({
         "policy": {"model_name": margs.name, "learning_rate": 1e-6, "lr_warmup_steps": 0,
                    "lr_decay_style": "constant", "train_micro_batch_size": args.micro,

@@ -310,8 +310,10 @@ __global__ void decode_combine_kernel(const float* __restrict__ part_o, const fl
 }  // namespace
 
 int decode_num_splits(int64_t B, int64_t Hk, int64_t max_tiles) {
+  // aim for >= 4 CTAs per SM (3 are resident at a time), so the last wave is
+  // a small fraction of the work
   const int64_t ctas = B * Hk;
-  int64_t want = (2 * (int64_t)num_sms() + ctas - 1) / ctas;
+  int64_t want = (4 * (int64_t)num_sms() + ctas - 1) / ctas;
   if (want > max_tiles) want = max_tiles;
   if (want > 32) want = 32;
   return (int)(want < 1 ? 1 : want);

@@ -180,7 +180,8 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
                                        const float* __restrict__ inv_freq, __nv_bfloat16* __restrict__ q,
                                        __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v,
                                        float* __restrict__ rq, float* __restrict__ rk, int64_t T, int nh, int nkv,
-                                       float eps, int has_norm) {
+                                       float eps, int has_norm, void* __restrict__ kc, void* __restrict__ vc,
+                                       const int64_t* __restrict__ slots, int cache_fp8, float inv_ks, float inv_vs) {
   constexpr int HD = 64 * P, HALF = 32 * P;
   const int lane = threadIdx.x & 31;
   const int kind = blockIdx.y;
@@ -188,6 +189,17 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
   const int col0 = kind == 0 ? 0 : (kind == 1 ? nh * HD : (nh + nkv) * HD);
   const int stride_in = (nh + 2 * nkv) * HD;
   __nv_bfloat16* out = kind == 0 ? q : (kind == 1 ? k : v);
+  // optional paged-KV write of k and v (decode and prefill skip a separate append)
+  void* cache = kind == 1 ? kc : (kind == 2 ? vc : nullptr);
+  const float cinv = kind == 1 ? inv_ks : inv_vs;
+  auto cache_put = [&](int64_t t, int h, int d, float val) {
+    if (cache == nullptr) return;
+    const int64_t slot = slots[t];
+    if (slot < 0) return;
+    const int64_t off = (slot * nkv + h) * HD + d;
+    if (cache_fp8) reinterpret_cast<__nv_fp8_e4m3*>(cache)[off] = __nv_fp8_e4m3(val * cinv);
+    else reinterpret_cast<__nv_bfloat16*>(cache)[off] = __float2bfloat16(val);
+  };
   const __nv_bfloat16* nw = kind == 0 ? qw : kw;
   float* rs = kind == 0 ? rq : rk;
   float wlo[P], whi[P], fr[P];
@@ -217,6 +229,8 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
       for (int i = 0; i < P; ++i) {
         dst[lane * P + i] = __float2bfloat16(lo[i]);
         dst[HALF + lane * P + i] = __float2bfloat16(hi[i]);
+        cache_put(t, h, lane * P + i, lo[i]);
+        cache_put(t, h, HALF + lane * P + i, hi[i]);
       }
       continue;
     }
@@ -242,6 +256,9 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
       const float b = hi[i] * c + lo[i] * s;
       dst[lane * P + i] = __float2bfloat16(a);
       dst[HALF + lane * P + i] = __float2bfloat16(b);
+      // the cache holds the bf16-rounded value the attention reads in training
+      cache_put(t, h, lane * P + i, __bfloat162float(__float2bfloat16(a)));
+      cache_put(t, h, HALF + lane * P + i, __bfloat162float(__float2bfloat16(b)));
     }
   }
 }
@@ -350,7 +367,9 @@ static int qk_grid(int64_t pairs) {
 }
 
 std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
-                                            torch::Tensor inv_freq, int64_t nh, int64_t nkv, int64_t hd, double eps) {
+                                            torch::Tensor inv_freq, int64_t nh, int64_t nkv, int64_t hd, double eps,
+                                            c10::optional<torch::Tensor> kc, c10::optional<torch::Tensor> vc,
+                                            c10::optional<torch::Tensor> slots, double inv_ks, double inv_vs) {
   LRL_CHECK(qkv);
   LRL_CHECK(pos);
   LRL_CHECK(inv_freq);
@@ -367,11 +386,27 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
   dim3 grid(qk_grid(T * nh), 3);
   auto qwp = has_norm ? (const __nv_bfloat16*)qw.data_ptr() : nullptr;
   auto kwp = has_norm ? (const __nv_bfloat16*)kw.data_ptr() : nullptr;
+  const bool to_cache = slots.has_value() && slots->defined();
+  void* kcp = nullptr;
+  void* vcp = nullptr;
+  const int64_t* sp = nullptr;
+  int fp8 = 0;
+  if (to_cache) {
+    LRL_CHECK((*kc));
+    LRL_CHECK((*vc));
+    LRL_CHECK((*slots));
+    TORCH_CHECK(slots->scalar_type() == at::kLong && kc->size(2) == nkv && kc->size(3) == hd, "cache layout");
+    kcp = kc->data_ptr();
+    vcp = vc->data_ptr();
+    sp = slots->data_ptr<int64_t>();
+    fp8 = kc->scalar_type() == at::kFloat8_e4m3fn ? 1 : 0;
+  }
 #define LAUNCH(PP)                                                                                              \
   qk_norm_rope_fwd_kernel<PP><<<grid, 256, 0, stream()>>>(                                                      \
       (const __nv_bfloat16*)qkv.data_ptr(), qwp, kwp, pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),     \
       (__nv_bfloat16*)q.data_ptr(), (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(),                \
-      rq.data_ptr<float>(), rk.data_ptr<float>(), T, (int)nh, (int)nkv, (float)eps, has_norm ? 1 : 0)
+      rq.data_ptr<float>(), rk.data_ptr<float>(), T, (int)nh, (int)nkv, (float)eps, has_norm ? 1 : 0, kcp, vcp, \
+      sp, fp8, (float)inv_ks, (float)inv_vs)
   if (hd == 64) LAUNCH(1);
   else if (hd == 128) LAUNCH(2);
   else LAUNCH(4);

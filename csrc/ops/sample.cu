@@ -111,6 +111,76 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const void* __re
   }
 }
 
+// ---- split-row path (top-p = 1): many CTAs per row ---------------------------
+// Pass 1: CTA (row, c) scans a contiguous vocab chunk and writes its partial
+// (max, sum exp relative to it, best Gumbel score, its index).  Pass 2 merges
+// a row's partials into the sampled token and its log-prob.
+struct SamplePart {
+  float m, s, best;
+  int idx;
+};
+
+constexpr int kSplitThreads = 256;
+
+__global__ void __launch_bounds__(kSplitThreads) sample_part_kernel(const __nv_bfloat16* __restrict__ logits, int V,
+                                                                    int chunk, float inv_t,
+                                                                    const int64_t* __restrict__ row_seed,
+                                                                    const int64_t* __restrict__ step,
+                                                                    SamplePart* __restrict__ parts) {
+  __shared__ float redf[32];
+  __shared__ MaxIdx redm[32];
+  const int64_t row = blockIdx.y;
+  const int c = blockIdx.x;
+  const int v0 = c * chunk, v1 = min(V, v0 + chunk);
+  const __nv_bfloat16* z = logits + row * V;
+  const uint64_t seed = (uint64_t)row_seed[row];
+  const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  const uint64_t st = (uint64_t)step[0];
+  float m = -INFINITY;
+  for (int v = v0 + threadIdx.x; v < v1; v += kSplitThreads) m = fmaxf(m, __bfloat162float(z[v]) * inv_t);
+  m = block_max(m, redf);
+  float sum = 0.f;
+  MaxIdx best{-INFINITY, 0x7fffffff};
+  for (int v = v0 + threadIdx.x; v < v1; v += kSplitThreads) {
+    const float zz = __bfloat162float(z[v]) * inv_t;
+    sum += __expf(zz - m);
+    best = better(best, MaxIdx{zz + gumbel_at(key, (uint32_t)st, (uint32_t)(st >> 32), v), v});
+  }
+  sum = block_sum(sum, redf);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    MaxIdx o{__shfl_xor_sync(0xffffffffu, best.v, off), __shfl_xor_sync(0xffffffffu, best.i, off)};
+    best = better(best, o);
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) redm[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    MaxIdx b = redm[0];
+    for (int w = 1; w < kSplitThreads / 32; ++w) b = better(b, redm[w]);
+    parts[row * gridDim.x + c] = SamplePart{m, sum, b.v, b.i};
+  }
+}
+
+__global__ void sample_merge_kernel(const __nv_bfloat16* __restrict__ logits, int V, int nparts, float inv_t,
+                                    const SamplePart* __restrict__ parts, int64_t* __restrict__ out_tok,
+                                    float* __restrict__ out_logp) {
+  const int64_t row = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  const SamplePart* p = parts + row * nparts;
+  float m = -INFINITY;
+  for (int i = 0; i < nparts; ++i) m = fmaxf(m, p[i].m);
+  float s = 0.f;
+  MaxIdx b{-INFINITY, 0x7fffffff};
+  for (int i = 0; i < nparts; ++i) {
+    if (p[i].m != -INFINITY) s += p[i].s * __expf(p[i].m - m);
+    b = better(b, MaxIdx{p[i].best, p[i].idx});
+  }
+  if (b.i < 0 || b.i >= V) b.i = 0;
+  out_tok[row] = b.i;
+  out_logp[row] = __bfloat162float(logits[row * V + b.i]) * inv_t - (m + logf(s));
+}
+
 std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top_p, torch::Tensor row_seed,
                                   torch::Tensor step) {
   LRL_CHECK(logits);
@@ -124,6 +194,19 @@ std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top
   auto tok = torch::empty({B}, logits.options().dtype(at::kLong));
   auto lp = torch::empty({B}, logits.options().dtype(at::kFloat));
   if (B == 0) return {tok, lp};
+  const int V = logits.size(1);
+  if (top_p >= 1.0 && logits.scalar_type() == at::kBFloat16 && V >= 16384) {
+    const int chunk = 8192;
+    const int nparts = (V + chunk - 1) / chunk;
+    auto parts = torch::empty({B, nparts, (int64_t)(sizeof(SamplePart) / 4)}, logits.options().dtype(at::kFloat));
+    sample_part_kernel<<<dim3(nparts, B), kSplitThreads, 0, stream()>>>(
+        (const __nv_bfloat16*)logits.data_ptr(), V, chunk, (float)inv_t, row_seed.data_ptr<int64_t>(),
+        step.data_ptr<int64_t>(), reinterpret_cast<SamplePart*>(parts.data_ptr()));
+    sample_merge_kernel<<<B, 32, 0, stream()>>>((const __nv_bfloat16*)logits.data_ptr(), V, nparts, (float)inv_t,
+                                                reinterpret_cast<const SamplePart*>(parts.data_ptr()),
+                                                tok.data_ptr<int64_t>(), lp.data_ptr<float>());
+    return {tok, lp};
+  }
   sample_kernel<<<B, kSampleThreads, 0, stream()>>>(logits.data_ptr(), logits.scalar_type() == at::kBFloat16,
                                                     logits.size(1), (float)inv_t, (float)top_p,
                                                     row_seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(),

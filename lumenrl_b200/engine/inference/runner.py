@@ -48,13 +48,13 @@ class ModelRunner:
             return out
         return ops.linear(ops.swiglu(ops.linear(h, self._w(f"layers.{i}.w13"))), self._w(f"layers.{i}.w2"))
 
-    def _qkv(self, i: int, h: Tensor, positions: Tensor):
-        a = self.args
+    def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor):
+        a, c = self.args, self.cache
         qkv = ops.linear(h, self._w(f"layers.{i}.wqkv"))
         qn = self._w(f"layers.{i}.q_norm") if a.qk_norm else None
         kn = self._w(f"layers.{i}.k_norm") if a.qk_norm else None
-        return ops.qk_norm_rope(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
-                                a.head_dim, a.rms_norm_eps)
+        return ops.qk_norm_rope_cache(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
+                                      a.head_dim, a.rms_norm_eps, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
 
     @torch.no_grad()
     def prefill(self, ids: Tensor, positions: Tensor, cu_seqlens: Tensor, max_len: int, slots: Tensor) -> Tensor:
@@ -63,8 +63,7 @@ class ModelRunner:
         res = None
         for i in range(a.num_layers):
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
-            q, k, v = self._qkv(i, h, positions)
-            ops.kv_cache_append(k, v, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
+            q, k, v = self._qkv(i, h, positions, slots)
             o = ops.attention_varlen(q, k, v, cu_seqlens, max_len, causal=True, scale=self.scale)
             x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
@@ -80,8 +79,7 @@ class ModelRunner:
         res = None
         for i in range(a.num_layers):
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
-            q, k, v = self._qkv(i, h, positions)
-            ops.kv_cache_append(k, v, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
+            q, k, v = self._qkv(i, h, positions, slots)
             o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
                                            c.k_scale[i], c.v_scale[i], self.max_len)
             x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))

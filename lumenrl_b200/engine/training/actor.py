@@ -68,7 +68,8 @@ class ActorEngine:
         self.model = Qwen3Model(args, device=self.device, dtype=dtype, flat=flat, requires_grad=trainable)
         if init:
             self.model.init_weights(seed)
-        self.model.gradient_checkpointing = gradient_checkpointing
+        self.model.gradient_checkpointing = gradient_checkpointing is True
+        self.recompute_policy = "auto" if gradient_checkpointing == "auto" else None
         self.trainable = trainable
         self.opt: Optional[ShardedFlatAdamW] = None
         self.sched: Optional[LRSchedule] = None
@@ -126,6 +127,10 @@ class ActorEngine:
         if "dapo_sample_mask" in t:
             mask_grid = mask_grid * t["dapo_sample_mask"].float().reshape(-1, 1)
         metrics: dict[str, float] = {}
+        if self.recompute_policy == "auto" and self.device.type == "cuda":
+            rows = rows_per_micro or B
+            tok = max(sum(sorted(lens, reverse=True)[:rows]), 1)
+            metrics["actor/recompute_layers"] = float(self.plan_recompute(tok))
         sums = {"pg_loss": 0.0, "ppo_kl": 0.0, "clipfrac": 0.0, "tok": 0.0, "entropy": 0.0}
         t_fwd_bwd = 0.0
         opt_stats = {}
@@ -156,6 +161,20 @@ class ActorEngine:
             "timing/fwd_bwd_s": t_fwd_bwd,
         })
         return metrics
+
+    def plan_recompute(self, tokens_per_micro: int, margin_bytes: int = 8 << 30) -> int:
+        """Recompute as few decoder layers as the free memory allows: keep the
+        activations of as many layers as fit into what is free after the
+        resident state (weights, fp32 grads, optimizer shards), less a margin
+        for the LM-head chunks, GEMM workspaces and fragmentation."""
+        free, _ = torch.cuda.mem_get_info(self.device)
+        free += torch.cuda.memory_reserved(self.device) - torch.cuda.memory_allocated(self.device)
+        per_layer = int(self.model.activation_bytes_per_token_layer() * tokens_per_micro * 1.1)
+        L = self.args.num_layers
+        keep = max(0, min(L, (free - margin_bytes) // max(per_layer, 1)))
+        n = L - keep
+        self.model.recompute_layers = set(range(n))
+        return n
 
     def _micro_step(self, batch: DataProto, rows: list[int], mask_grid: Tensor, algo_cfg, algorithm: str,
                     global_tok: float, temperature: float) -> dict[str, float]:

@@ -147,6 +147,7 @@ class Qwen3Model(nn.Module):
         self.register_buffer("inv_freq", ops.inv_freq_table(args.head_dim, args.rope_theta, args.rope_scaling,
                                                             flat.device), persistent=False)
         self.gradient_checkpointing = False
+        self.recompute_layers: set[int] = set()   # per-layer activation recomputation (memory budget)
         self.routing_replay = None   # set by moe.r3 for rollout routing replay
         self.aux_losses: list[Tensor] = []
 
@@ -223,7 +224,7 @@ class Qwen3Model(nn.Module):
         taps: list[Tensor] = []
         want = set(output_hidden_layers or [])
         for i in range(self.args.num_layers):
-            if self.gradient_checkpointing and torch.is_grad_enabled():
+            if (self.gradient_checkpointing or i in self.recompute_layers) and torch.is_grad_enabled():
                 x = _ckpt(self._layer, i, x, positions, cu_seqlens, max_seqlen, use_reentrant=False)
             else:
                 x = self._layer(i, x, positions, cu_seqlens, max_seqlen)
@@ -233,6 +234,15 @@ class Qwen3Model(nn.Module):
         if output_hidden_layers is not None:
             return h, taps
         return h
+
+    def activation_bytes_per_token_layer(self) -> int:
+        """bf16 bytes autograd keeps per token per decoder layer without
+        recomputation: block inputs and norm outputs, qkv, q/k/v, attention
+        output (kept twice: by attention and by the output projection),
+        gate/up and the SwiGLU product."""
+        a = self.args
+        F = a.moe_intermediate_size * a.num_experts_per_tok if a.num_experts else a.intermediate_size
+        return 2 * (4 * a.hidden_size + 2 * a.qkv_dim + 2 * a.q_dim + 3 * F)
 
     def logits(self, hidden: Tensor) -> Tensor:
         return hidden @ self.lm_head.t()

@@ -188,6 +188,22 @@ def qk_norm_rope(qkv: Tensor, qw: Optional[Tensor], kw: Optional[Tensor], positi
     return q, k, v
 
 
+def qk_norm_rope_cache(qkv: Tensor, qw: Optional[Tensor], kw: Optional[Tensor], positions: Tensor,
+                       inv_freq: Tensor, nh: int, nkv: int, hd: int, eps: float, k_cache: Tensor, v_cache: Tensor,
+                       slots: Tensor, k_scale: float = 1.0, v_scale: float = 1.0) -> tuple[Tensor, Tensor, Tensor]:
+    """Inference path: QK-norm + RoPE that also writes k/v into the paged
+    caches at ``slots`` in the same kernel (no separate append)."""
+    if not _cuda(qkv):
+        q, k, v = qk_norm_rope(qkv, qw, kw, positions, inv_freq, nh, nkv, hd, eps)
+        kv_cache_append(k, v, k_cache, v_cache, slots, k_scale, v_scale)
+        return q, k, v
+    empty = qkv.new_empty(0)
+    q, k, v, _, _ = ext().qk_norm_rope_fwd(qkv, qw if qw is not None else empty, kw if kw is not None else empty,
+                                           positions, inv_freq, nh, nkv, hd, eps, k_cache, v_cache, slots,
+                                           1.0 / k_scale, 1.0 / v_scale)
+    return q, k, v
+
+
 # ---------------------------------------------------------------------------
 # SwiGLU
 # ---------------------------------------------------------------------------

@@ -58,7 +58,7 @@ class RLRunSpec:
     logprob_token_budget: int = 16384
     kv_cache_bytes: Optional[int] = None
     use_cuda_graph: bool = True
-    gradient_checkpointing: bool = False
+    gradient_checkpointing: object = False   # True (every layer), False, or "auto" (memory-budgeted)
 
 
 class RLTrainer:

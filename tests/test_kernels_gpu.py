@@ -220,3 +220,36 @@ def test_sampler_distribution(cuda):
     srt, idx = torch.sort(p, descending=True)
     keep = set(idx[: int((torch.cumsum(srt, 0) < 0.5).sum()) + 1].tolist())
     assert set(tk.tolist()) <= keep
+
+
+def test_sampler_split_rows_large_vocab(cuda):
+    torch.manual_seed(0)
+    V = 151936
+    base = torch.full((V,), -30.0, device=cuda)
+    hot = torch.randint(0, V, (40,), device=cuda).unique()
+    base[hot] = torch.randn(hot.numel(), device=cuda)
+    logits = base.to(torch.bfloat16).unsqueeze(0).repeat(4096, 1)
+    tok, lp = ops.sample_tokens_device(logits, 1.0, 1.0, torch.arange(4096, device=cuda),
+                                      torch.zeros(1, dtype=torch.long, device=cuda))
+    p = torch.softmax(logits[0].float(), -1)
+    freq = torch.bincount(tok, minlength=V).float() / 4096
+    assert (freq - p).abs().max().item() < 0.03
+    close(lp, torch.log(p)[tok], 1e-3)
+
+
+def test_qk_norm_rope_cache_write(cuda):
+    torch.manual_seed(0)
+    T, nh, nkv, hd, bs = 9, 8, 2, 128, 16
+    qkv = torch.randn(T, (nh + 2 * nkv) * hd, device=cuda, dtype=torch.bfloat16)
+    pos = torch.arange(T, device=cuda) + 5
+    inv = ops.inv_freq_table(hd, 1e6, None, cuda)
+    qw = (1 + 0.1 * torch.randn(hd, device=cuda)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(hd, device=cuda)).to(torch.bfloat16)
+    kc = torch.zeros(4, bs, nkv, hd, device=cuda, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(4 * bs, device=cuda)[:T]
+    q, k, v = ops.qk_norm_rope_cache(qkv, qw, kw, pos, inv, nh, nkv, hd, 1e-6, kc, vc, slots)
+    q2, k2, v2 = ops.qk_norm_rope(qkv, qw, kw, pos, inv, nh, nkv, hd, 1e-6)
+    close(q, q2, 0.0)
+    close(kc.view(-1, nkv, hd)[slots], k2, 0.0)
+    close(vc.view(-1, nkv, hd)[slots], v2, 0.0)

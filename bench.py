@@ -219,6 +219,7 @@ def main() -> None:
                     "d2h_bytes_per_step": tr.io_bytes.get("d2h", 0) * world},
             "gpu_launches": launches,
             "breakdown_s": {k.replace("timing/", ""): v for k, v in last.items() if k.startswith("timing/")},
+            "recompute_layers": last.get("actor/recompute_layers"),
             "weight_sync_ms": last.get("weight_sync/ms"),
             "gen_tokens_per_s": last.get("perf/gen_tokens_per_s"),
             "mean_response_len": last.get("response_length/mean"),

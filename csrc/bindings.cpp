@@ -49,6 +49,9 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
               torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
               double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
               torch::Tensor norm_out, int64_t wait_cycles);
+std::vector<torch::Tensor> quant_act_1x128(torch::Tensor x, bool e5m2);
+std::vector<torch::Tensor> quant_weight_128x128(torch::Tensor w, bool e5m2);
+torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err);
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -86,4 +89,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_signal_words", &lrl::symm_signal_words);
   m.def("rs_norm", &lrl::rs_norm);
   m.def("adamw_ag", &lrl::adamw_ag);
+  m.def("quant_act_1x128", &lrl::quant_act_1x128);
+  m.def("quant_weight_128x128", &lrl::quant_weight_128x128);
+  m.def("fp8_gemm", &lrl::fp8_gemm);
 }

@@ -1,0 +1,254 @@
+// Block-scaled FP8 GEMM on the 5th-generation tensor cores (kind::f8f6f4).
+//
+//   C[M, N] (bf16) = sum_kb  (A[M, kb] @ B[N, kb]^T) * sa[M, kb] * sb[N/128, kb]
+//
+// A: E4M3 activations with one fp32 scale per 1x128 block (row, K block);
+// B: E4M3 weights with one fp32 scale per 128x128 block.  Scales change with
+// every 128-wide K block, so each K block is accumulated on its own in TMEM
+// (two buffers, ping-pong) and the epilogue warps "promote" it: read it with
+// tcgen05.ld, multiply by sa*sb and add into fp32 registers, while the MMA
+// warp already fills the other buffer with the next K block.  At the end of a
+// tile the registers are written as bf16.
+//
+// Roles per CTA (192 threads): warp 0 TMA producer (128x128-byte A and B
+// boxes, 128-byte swizzle, kStages ring), warp 1 TMEM owner + single-thread
+// tcgen05.mma issuer (M=128, N=128, K=32 per instruction, 4 per K block),
+// warps 2-5 promotion + epilogue (one TMEM lane / output row per thread).
+// All mbarrier waits are bounded (tc_gemm.cuh).
+#include "../common.cuh"
+#include "tc_gemm.cuh"
+
+namespace lrl {
+
+using namespace tc;
+
+namespace {
+
+constexpr int kFBM = 128, kFBN = 128, kFBK = 128;  // K block = one scale block
+constexpr int kFStages = 6;
+constexpr int kFABytes = kFBM * kFBK, kFBBytes = kFBN * kFBK;
+constexpr int kFStageBytes = kFABytes + kFBBytes;  // 32 KB
+constexpr int kFSmem = kFStages * kFStageBytes + 1024 + 256;
+constexpr int kFThreads = 192;
+
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  // c_format F32 (bit 4); a/b format E4M3 = 0; K-major; N>>3 at 17, M>>4 at 24
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const float* __restrict__ sa, const float* __restrict__ sb, __nv_bfloat16* __restrict__ C, int M,
+                    int N, int K, int* err_out) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kFStages * kFABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kFStages * kFStageBytes);
+  uint64_t* empty = full + kFStages;
+  uint64_t* kfull = empty + kFStages;   // a K block's partial is in TMEM buffer b
+  uint64_t* kempty = kfull + 2;         // the epilogue has consumed buffer b
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kempty + 2);
+  volatile int* err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + kFBM - 1) / kFBM, num_n = (N + kFBN - 1) / kFBN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + kFBK - 1) / kFBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&kfull[b], 1);
+      mbar_init(&kempty[b], 128);
+    }
+    *err = kErrNone;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * kFBN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int mb = t % num_m, nb = t / num_m;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % kFStages;
+          if (!mbar_wait(&empty[s], ((it / kFStages) & 1) ^ 1, err, kErrProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], kFStageBytes);
+          tma_load_2d(sA + s * kFABytes, &tmA, &full[s], kb * kFBK, mb * kFBM);
+          tma_load_2d(sB + s * kFBBytes, &tmB, &full[s], kb * kFBK, nb * kFBN);
+        }
+      }
+      if (!ok || *err != kErrNone) {
+        for (int j = it - 1; j >= 0 && j >= it - kFStages; --j) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&full[j % kFStages], (j / kFStages) & 1))
+            if (clock64() - t0 > kWaitCycles) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_e4m3_f32(kFBM, kFBN);
+      int it = 0, kc = 0;  // kc: K blocks issued by this CTA (selects the TMEM buffer)
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it, ++kc) {
+          const int buf = kc & 1;
+          if (!mbar_wait(&kempty[buf], ((kc >> 1) & 1) ^ 1, err, kErrMma)) {
+            ok = false;
+            break;
+          }
+          const int s = it % kFStages;
+          if (!mbar_wait(&full[s], (it / kFStages) & 1, err, kErrMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(smem_addr(sA + s * kFABytes));
+          const uint64_t bd = sw128_kmajor_desc(smem_addr(sB + s * kFBBytes));
+#pragma unroll
+          for (int k = 0; k < kFBK / 32; ++k) umma_f8(tmem + buf * kFBN, ad + 2 * k, bd + 2 * k, idesc, k != 0);
+          umma_commit(&empty[s]);
+          umma_commit(&kfull[buf]);
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    int kc = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int mb = t % num_m, nb = t / num_m;
+      const int row = mb * kFBM + q * 32 + lane;
+      const int rs = row < M ? row : M - 1;
+      float acc[kFBN];
+#pragma unroll
+      for (int i = 0; i < kFBN; ++i) acc[i] = 0.f;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb, ++kc) {
+        const int buf = kc & 1;
+        if (!mbar_wait(&kfull[buf], (kc >> 1) & 1, err, kErrEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float scale = sa[(int64_t)rs * kblocks + kb] * sb[(int64_t)nb * kblocks + kb];
+#pragma unroll
+        for (int c = 0; c < kFBN / 32; ++c) {
+          float v[32];
+          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i] * scale;
+        }
+        tc_fence_before();
+        mbar_arrive(&kempty[buf]);
+      }
+      if (!ok) break;
+      if (row < M) {
+        __nv_bfloat16* p = C + (int64_t)row * N + nb * kFBN;
+        const int ncols = min(kFBN, N - nb * kFBN);
+        if (ncols == kFBN) {
+#pragma unroll
+          for (int i = 0; i < kFBN / 8; ++i) {
+            float tmp[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tmp[j] = acc[8 * i + j];
+            store8(p + 8 * i, tmp);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < kFBN; ++i)
+            if (i < ncols) p[i] = __float2bfloat16(acc[i]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * kFBN);
+  }
+  if (threadIdx.x == 0 && *err != kErrNone) atomicExch(err_out, *err);
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+CUtensorMap make_fp8_map(const void* ptr, int64_t rows, int64_t K, int64_t ld) {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && p,
+                "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 16 == 0, "fp8 TMA: 16-byte alignment");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)kFBK, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp8) failed: ", (int)r);
+  return m;
+}
+
+}  // namespace
+
+int64_t tc_gemm_status();
+
+// a [M, K] e4m3 + sa [M, K/128]; b [N, K] e4m3 + sb [ceil(N/128), K/128] -> bf16 [M, N]
+torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err) {
+  LRL_CHECK(a);
+  LRL_CHECK(b);
+  LRL_CHECK(sa);
+  LRL_CHECK(sb);
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "fp8_gemm: e4m3");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K && K % 16 == 0, "fp8_gemm: K mismatch / alignment");
+  const int64_t kb = (K + kFBK - 1) / kFBK;
+  TORCH_CHECK(sa.size(0) == M && sa.size(1) == kb && sb.size(0) == (N + 127) / 128 && sb.size(1) == kb,
+              "fp8_gemm: scale shapes");
+  auto c = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
+  if (M == 0 || N == 0) return c;
+  const CUtensorMap ma = make_fp8_map(a.data_ptr(), M, K, K);
+  const CUtensorMap mb = make_fp8_map(b.data_ptr(), N, K, K);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
+    attr = true;
+  }
+  const int tiles = (int)(((M + kFBM - 1) / kFBM) * ((N + kFBN - 1) / kFBN));
+  fp8_gemm_kernel<<<std::min(tiles, num_sms()), kFThreads, kFSmem, stream()>>>(
+      ma, mb, sa.data_ptr<float>(), sb.data_ptr<float>(), (__nv_bfloat16*)c.data_ptr(), (int)M, (int)N, (int)K,
+      err.data_ptr<int>());
+  return c;
+}
+
+}  // namespace lrl

@@ -48,14 +48,21 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 }
 
 template <int EPI>
-__device__ __forceinline__ void store_row32(void* C, int row, int col, int N, int64_t ldc, const float* v) {
+__device__ __forceinline__ void store_row32(void* C, int row, int col, int N, int64_t ldc, const float (&v)[32]) {
   if constexpr (EPI == kEpiBF16) {
     __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)row * ldc + col;
     if (col + 32 <= N) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) store8(p + 8 * i, v + 8 * i);
+      for (int i = 0; i < 4; ++i) {
+        float tmp[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tmp[j] = v[8 * i + j];
+        store8(p + 8 * i, tmp);
+      }
     } else {
-      for (int i = 0; i < 32 && col + i < N; ++i) p[i] = __float2bfloat16(v[i]);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) p[i] = __float2bfloat16(v[i]);
     }
   } else {
     float* p = reinterpret_cast<float*>(C) + (int64_t)row * ldc + col;
@@ -73,7 +80,9 @@ __device__ __forceinline__ void store_row32(void* C, int row, int col, int N, in
         reinterpret_cast<float4*>(p)[i] = o;
       }
     } else {
-      for (int i = 0; i < 32 && col + i < N; ++i) p[i] = (EPI == kEpiAccF32 ? p[i] : 0.f) + v[i];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) p[i] = (EPI == kEpiAccF32 ? p[i] : 0.f) + v[i];
     }
   }
 }

@@ -94,10 +94,13 @@ class RolloutEngine:
         self.weight_version = 0
 
     # -- lifecycle ---------------------------------------------------------------
-    def sleep(self) -> None:
+    def sleep(self, release_memory: bool = False) -> None:
+        """Free the KV pool.  The block stays in the caching allocator (so the
+        trainer's activations reuse it and the next wake is a cache hit)
+        unless ``release_memory`` returns it to the driver."""
         self._graphs.clear()
         self.cache.sleep()
-        if self.device.type == "cuda":
+        if release_memory and self.device.type == "cuda":
             torch.cuda.empty_cache()
 
     def wake(self) -> None:
@@ -147,8 +150,16 @@ class RolloutEngine:
             routed_experts=[r for o in outs for r in o.routed_experts],
             stats={k: sum(o.stats.get(k, 0) for o in outs) for k in outs[0].stats})
 
+    def _ev(self):
+        if self.device.type != "cuda":
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
     def _generate_wave(self, prompts, sp: SamplingParams, prompt_offset: int) -> GenerationOutput:
         dev, bs, n = self.device, self.block_size, sp.n
+        ev0 = self._ev()
         P = len(prompts)
         B = P * n
         alloc = self.cache.allocator
@@ -180,6 +191,7 @@ class RolloutEngine:
             recorder = _RoutingRecorder(moe_layers)
             self.runner.routing_recorder = recorder
         logits = self.runner.prefill(ids, pos, cu, int(lens.max()), slots)
+        ev1 = self._ev()
         prompt_routes = recorder.take() if recorder else None   # [sumL, layers, k]
         for i, L in enumerate(plens):
             full = L // bs
@@ -195,6 +207,7 @@ class RolloutEngine:
         # 3) first token from the prefill logits (row r samples prompt r // n)
         row_logits = logits.repeat_interleave(n, dim=0)
         g = self._graph(B, sp)
+        ev2 = self._ev()
         g.row_seed.copy_(torch.arange(B, device=dev) + (sp.seed * 1_000_003 + prompt_offset * n) )
         g.step.fill_(0)
         from lumenrl_b200 import ops
@@ -237,6 +250,7 @@ class RolloutEngine:
                 finished |= newly
                 if t % check_every == 0 and bool(finished.all()):
                     break
+        ev3 = self._ev()
         if eos is not None:
             first = (out_tok[:, 0] == eos)
             lengths = torch.where(first, torch.ones_like(lengths), lengths)
@@ -263,4 +277,6 @@ class RolloutEngine:
             responses=out_tok, response_lengths=lengths,
             logprobs=out_lp, prompt_index=torch.arange(P, device=dev).repeat_interleave(n) + prompt_offset,
             routed_experts=routed,
-            stats={"decode_steps": steps, "prefill_tokens": int(lens.sum()), "gen_tokens": int(lengths.sum())})
+            stats={"decode_steps": steps, "prefill_tokens": int(lens.sum()), "gen_tokens": int(lengths.sum()),
+                   **({"prefill_ms": ev0.elapsed_time(ev1), "setup_ms": ev1.elapsed_time(ev2),
+                       "decode_ms": ev2.elapsed_time(ev3)} if ev0 is not None else {})})

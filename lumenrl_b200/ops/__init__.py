@@ -444,3 +444,32 @@ def tc_gemm_status() -> int:
     """Error word of the tcgen05 GEMMs since the last call (0 = no error); a
     non-zero value names the role whose bounded wait expired."""
     return int(ext().tc_gemm_status())
+
+
+_FP8_ERR: dict = {}
+
+
+def fp8_gemm_blockwise(x: Tensor, qw: Tensor, sw: Tensor, qx: Optional[Tensor] = None,
+                       sx: Optional[Tensor] = None) -> Tensor:
+    """W8A8 block-scaled GEMM: bf16 x [M,K] (quantised here to E4M3 with 1x128
+    scales unless given) times E4M3 weights qw [N,K] with 128x128 scales sw,
+    on the tcgen05 kind::f8f6f4 kernel; returns bf16 [M, N]."""
+    if qx is None:
+        from lumenrl_b200.quant.fp8 import quant_act_1x128
+        qx, sx = quant_act_1x128(x.reshape(-1, x.shape[-1]).contiguous())
+    if not _cuda(qx):
+        from lumenrl_b200.quant.fp8 import dequant_128x128, dequant_1x128
+        return (dequant_1x128(qx, sx) @ dequant_128x128(qw, sw).t()).to(torch.bfloat16)
+    dev = qx.device
+    if dev not in _FP8_ERR:
+        _FP8_ERR[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ext().fp8_gemm(qx, sx.contiguous(), qw, sw.contiguous(), _FP8_ERR[dev])
+    return out.view(*x.shape[:-1], qw.shape[0]) if x is not None else out
+
+
+def fp8_gemm_status() -> int:
+    v = 0
+    for t in _FP8_ERR.values():
+        v = max(v, int(t.item()))
+        t.zero_()
+    return v

@@ -204,6 +204,9 @@ class RLTrainer:
         m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
             float(len(batch)))
         m["weight_sync/ms"] = times["weight_sync"] * 1e3
+        for k in ("prefill_ms", "setup_ms", "decode_ms"):
+            if k in batch.meta.get("gen_stats", {}):
+                m[f"timing/gen_{k}"] = batch.meta["gen_stats"][k]
         host_result = batch["rewards"].to("cpu")          # the step's result read back to the host
         self.io_bytes["d2h"] = host_result.numel() * host_result.element_size()
         m["step"] = step + 1

@@ -37,6 +37,7 @@ void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor
                double inv_ks, double inv_vs);
 torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
 int64_t tc_gemm_status();
+torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
 void symm_close(int64_t ptr);
@@ -81,6 +82,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,
         py::arg("bn") = 0);
   m.def("tc_gemm_status", &lrl::tc_gemm_status);
+  m.def("tc_gemm_splitk", &lrl::tc_gemm_splitk, py::arg("a"), py::arg("b"), py::arg("splits") = 0);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);
   m.def("symm_close", &lrl::symm_close);

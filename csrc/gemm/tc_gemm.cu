@@ -25,7 +25,7 @@ namespace {
 constexpr int kBM = 128, kBK = 64, kGroupM = 8;
 constexpr int kThreadsGemm = 192;
 
-enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiAccF32 = 2 };
+enum Epi : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiAccF32 = 2, kEpiAtomicF32 = 3 };
 
 template <int BN>
 struct Cfg {
@@ -64,6 +64,12 @@ __device__ __forceinline__ void store_row32(void* C, int row, int col, int N, in
       for (int i = 0; i < 32; ++i)
         if (col + i < N) p[i] = __float2bfloat16(v[i]);
     }
+  } else if constexpr (EPI == kEpiAtomicF32) {
+    // split-K partial: add into the zero-initialised fp32 output
+    float* p = reinterpret_cast<float*>(C) + (int64_t)row * ldc + col;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (col + i < N) atomicAdd(p + i, v[i]);
   } else {
     float* p = reinterpret_cast<float*>(C) + (int64_t)row * ldc + col;
     if (col + 32 <= N) {
@@ -90,7 +96,7 @@ __device__ __forceinline__ void store_row32(void* C, int row, int col, int N, in
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C, int M,
-                   int N, int K, int64_t ldc, int* err_out) {
+                   int N, int K, int64_t ldc, int splits, int* err_out) {
   using G = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -105,8 +111,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + kBM - 1) / kBM, num_n = (N + BN - 1) / BN;
-  const int tiles = num_m * num_n;
-  const int kblocks = (K + kBK - 1) / kBK;
+  // work unit = (output tile, K split); splits > 1 only with the atomic epilogue
+  const int tiles = num_m * num_n * splits;
+  const int kblocks_total = (K + kBK - 1) / kBK;
+  const int kps = (kblocks_total + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < G::kStages; ++s) {
@@ -136,8 +144,9 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        tile_coords(t / splits, num_m, num_n, mb, nb);
+        const int k0 = (t % splits) * kps, k1 = min(kblocks_total, k0 + kps);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % G::kStages;
           const uint32_t ph = (it / G::kStages) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, err, kErrProducer)) {
@@ -175,7 +184,8 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
         if (!mbar_wait(&tempty[buf], tph ^ 1, err, kErrMma)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        const int k0 = (t % splits) * kps, k1 = min(kblocks_total, k0 + kps);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % G::kStages;
           if (!mbar_wait(&full[s], (it / G::kStages) & 1, err, kErrMma)) {
             ok = false;
@@ -185,7 +195,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
           const uint64_t ad = sw128_kmajor_desc(smem_addr(sa + s * G::kABytes));
           const uint64_t bd = sw128_kmajor_desc(smem_addr(sb + s * G::kBBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) umma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < kBK / 16; ++k) umma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, ((kb - k0) | k) != 0);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&tfull[buf]);
@@ -196,7 +206,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
     int tc = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t / splits, num_m, num_n, mb, nb);
       const int buf = tc & 1;
       if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue)) break;
       tc_fence_after();
@@ -273,16 +283,45 @@ int64_t tc_gemm_status() {
 }
 
 template <int BN, int EPI>
-static void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int64_t ldc) {
+static void launch(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int64_t ldc,
+                   int splits = 1) {
   auto kern = tc_gemm_kernel<BN, EPI>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::kSmem);
     attr = true;
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN) * splits;
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreadsGemm, Cfg<BN>::kSmem, stream()>>>(ma, mb, c, M, N, K, ldc, gemm_err_word().data_ptr<int>());
+  kern<<<grid, kThreadsGemm, Cfg<BN>::kSmem, stream()>>>(ma, mb, c, M, N, K, ldc, splits,
+                                                         gemm_err_word().data_ptr<int>());
+}
+
+// Small-M (decode) GEMM: the K range is split so enough CTAs stream the
+// weights; partial tiles are added into a zeroed fp32 [M, N] buffer, which
+// is returned (the caller casts or consumes it).
+torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits) {
+  LRL_CHECK_CUDA(a);
+  LRL_CHECK_CUDA(b);
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.stride(1) == 1 &&
+                  b.stride(1) == 1 && a.size(1) == b.size(1),
+              "tc_gemm_splitk: bf16 K-major operands");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(K % 8 == 0, "tc_gemm_splitk: K % 8");
+  auto out = torch::zeros({M, N}, a.options().dtype(at::kFloat));
+  if (M == 0 || N == 0) return out;
+  const int64_t kblocks = (K + kBK - 1) / kBK;
+  if (splits <= 0) {
+    const int64_t tiles = ((M + kBM - 1) / kBM) * ((N + 127) / 128);
+    splits = std::max<int64_t>(1, std::min<int64_t>(kblocks, (2 * num_sms() + tiles - 1) / tiles));
+  }
+  // no empty K ranges: every split gets at least one K block
+  const int64_t kps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kps - 1) / kps;
+  const CUtensorMap ma = make_kmajor_map(a.data_ptr(), M, K, a.stride(0), kBM);
+  const CUtensorMap mb = make_kmajor_map(b.data_ptr(), N, K, b.stride(0), 128);
+  launch<128, kEpiAtomicF32>(ma, mb, out.data_ptr(), (int)M, (int)N, (int)K, out.stride(0), (int)splits);
+  return out;
 }
 
 // a [M, K], b [N, K] (bf16, unit inner stride); epi 0: returns bf16 C,

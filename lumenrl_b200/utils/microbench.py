@@ -105,6 +105,14 @@ def bench_gemm(ns) -> dict:
         fl = 2 * M * N * K
         out.append({"M": M, "N": N, "K": K, "tc_ms": t_tc, "cublas_ms": t_cb, "tc_tflops": fl / t_tc / 1e9,
                     "cublas_tflops": fl / t_cb / 1e9})
+    from lumenrl_b200.ops.ext import ext
+    for M, N, K in [(64, 6144, 4096), (64, 4096, 4096), (64, 24576, 4096), (64, 4096, 12288), (64, 151936, 4096)]:
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        b = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        t_sk = _time(lambda: ext().tc_gemm_splitk(a, b, 0).to(torch.bfloat16), ns.steps, ns.warmup)
+        t_cb = _time(lambda: a @ b.t(), ns.steps, ns.warmup)
+        out.append({"M": M, "N": N, "K": K, "splitk_ms": t_sk, "cublas_ms": t_cb,
+                    "splitk_TBps": N * K * 2 / t_sk / 1e9, "cublas_TBps": N * K * 2 / t_cb / 1e9})
     st = ops.tc_gemm_status()
     return {"op": "gemm", "status": st, "shapes": out}
 

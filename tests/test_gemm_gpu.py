@@ -37,3 +37,17 @@ def test_tc_gemm_fp32_accumulate(cuda):
     ref = a.float() @ b.float().t()
     assert (f - ref).abs().max().item() < 1e-2
     assert (c - (c0 + ref)).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 6144, 4096), (3, 1000 * 8, 520), (128, 512, 4096)])
+def test_tc_gemm_splitk(cuda, M, N, K):
+    from lumenrl_b200.ops.ext import ext
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=cuda) / K ** 0.5).to(torch.bfloat16)
+    for splits in (0, 3, 100):
+        c = ext().tc_gemm_splitk(a, b, splits)
+        torch.cuda.synchronize()
+        assert ops.tc_gemm_status() == 0
+        ref = a.float() @ b.float().t()
+        assert (c - ref).abs().max().item() <= 1e-2 * max(1.0, ref.abs().max().item())

@@ -120,7 +120,8 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
     const int* __restrict__ block_table, const int* __restrict__ seq_lens, __nv_bfloat16* __restrict__ out,
     float* __restrict__ part_o, float* __restrict__ part_lse, int Hq, int Hk, int bs, int max_blocks,
-    int tiles_per_split, float scale_log2, float v_scale) {
+    int tiles_per_split, float scale_log2, float v_scale, const int* __restrict__ kv_start, int force_partial,
+    int part_offset) {
   extern __shared__ __align__(128) uint8_t smem[];
   __nv_bfloat16* kbuf = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* vbuf = reinterpret_cast<__nv_bfloat16*>(smem + 2 * kTileBytes);
@@ -130,7 +131,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int g = lane >> 2, c4 = lane & 3;
   const int L = seq_lens[b];
-  const int t_begin = split * tiles_per_split * kTile;
+  // kv_start (optional): first token of this row's range (the shared-prefix
+  // path runs the private suffix only)
+  const int t0 = kv_start ? kv_start[b] : 0;
+  const int t_begin = t0 + split * tiles_per_split * kTile;
   const int t_end = min(L, t_begin + tiles_per_split * kTile);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
   const int* bt = block_table + (int64_t)b * max_blocks;
@@ -280,10 +284,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     }
     const int qh = h * G + row;
     const float val = lsum > 0.f ? acc / lsum * v_scale : 0.f;
-    if (nsplit == 1) {
+    if (nsplit == 1 && !force_partial) {
       out[((int64_t)b * Hq + qh) * kHD + col] = __float2bfloat16(val);
     } else {
-      const int64_t pi = ((int64_t)split * gridDim.z + b) * Hq + qh;
+      const int64_t pi = ((int64_t)(part_offset + split) * gridDim.z + b) * Hq + qh;
       part_o[pi * kHD + col] = val;
       if (col == 0) part_lse[pi] = lsum > 0.f ? mstar + log2f(lsum) : -INFINITY;
     }
@@ -358,7 +362,7 @@ torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor
                                              seq_lens.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(),          \
                                              nsplit > 1 ? po.data_ptr<float>() : nullptr,                       \
                                              nsplit > 1 ? pl.data_ptr<float>() : nullptr, (int)Hq, (int)Hk,     \
-                                             (int)bs, (int)max_blocks, tps, sl2, (float)v_scale);              \
+                                             (int)bs, (int)max_blocks, tps, sl2, (float)v_scale, nullptr, 0, 0); \
   } while (0)
   if (fp8) LAUNCH(__nv_fp8_e4m3);
   else LAUNCH(__nv_bfloat16);
@@ -367,6 +371,276 @@ torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor
     decode_combine_kernel<<<dim3(B, Hq), kHD, 0, stream()>>>(po.data_ptr<float>(), pl.data_ptr<float>(),
                                                              (__nv_bfloat16*)out.data_ptr(), nsplit, (int)B, (int)Hq);
   }
+  return out;
+}
+
+// ------------------------------------------------ shared-prefix (cascade) part
+// GRPO rows of one prompt share its whole KV blocks.  One CTA per (split, kv
+// head, group): the group's n rows x G query heads form MT = ceil(n*G/16) MMA
+// row tiles, so each shared K/V tile is read from HBM once per group instead
+// of once per row.  Warps split as (MT row tiles) x (4/MT token slices of
+// each 64-token stage).  Writes (o, lse) partials for the combine kernel.
+namespace {
+
+template <typename CacheT, int MT>
+__global__ void __launch_bounds__(kThreads) prefix_attn_kernel(
+    const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
+    const int* __restrict__ block_table, const int* __restrict__ prefix_len, float* __restrict__ part_o,
+    float* __restrict__ part_lse, int B, int Hq, int Hk, int bs, int max_blocks, int group, int tiles_per_split,
+    float scale_log2, float v_scale) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __nv_bfloat16* kbuf = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* vbuf = reinterpret_cast<__nv_bfloat16*>(smem + 2 * kTileBytes);
+  constexpr int kSlices = kWarps / MT;             // warps sharing one row tile
+  constexpr int kChunks = (kTile / 16) / kSlices;  // 16-token chunks per warp per stage
+  const int split = blockIdx.x, h = blockIdx.y, g = blockIdx.z;
+  const int G = Hq / Hk;
+  const int rows = group * G;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int mt = w % MT, slice = w / MT;
+  const int gq = lane >> 2, c4 = lane & 3;
+  const int row0 = g * group;  // first sequence of the group
+  const int P = prefix_len[row0];
+  const int t_begin = split * tiles_per_split * kTile;
+  const int t_end = min(P, t_begin + tiles_per_split * kTile);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
+  const int* bt = block_table + (int64_t)row0 * max_blocks;
+
+  // group row r -> (sequence row0 + r / G, query head h*G + r % G)
+  auto qptr = [&](int r) -> const __nv_bfloat16* {
+    return q + ((int64_t)(row0 + r / G) * Hq + (int64_t)h * G + (r % G)) * kHD;
+  };
+  uint32_t qa[8][4];
+  const int ra = mt * 16 + gq, rb = ra + 8;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int d0 = 16 * s + 2 * c4;
+    qa[s][0] = ra < rows ? ld_bf16x2(qptr(ra) + d0) : 0u;
+    qa[s][1] = rb < rows ? ld_bf16x2(qptr(rb) + d0) : 0u;
+    qa[s][2] = ra < rows ? ld_bf16x2(qptr(ra) + d0 + 8) : 0u;
+    qa[s][3] = rb < rows ? ld_bf16x2(qptr(rb) + d0 + 8) : 0u;
+  }
+  float o[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  if (ntiles > 0) {
+    stage_tile<CacheT>(kc, vc, bt, bs, Hk, h, t_begin, t_end, kbuf, vbuf);
+    cp_commit();
+  }
+  const int mi = lane >> 3, rr = lane & 7;
+  for (int it = 0; it < ntiles; ++it) {
+    const int cur = it & 1;
+    if (it + 1 < ntiles) {
+      stage_tile<CacheT>(kc, vc, bt, bs, Hk, h, t_begin + (it + 1) * kTile, t_end,
+                         kbuf + (cur ^ 1) * (kTileBytes / 2), vbuf + (cur ^ 1) * (kTileBytes / 2));
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    const __nv_bfloat16* ks = kbuf + cur * (kTileBytes / 2);
+    const __nv_bfloat16* vs = vbuf + cur * (kTileBytes / 2);
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      const int tok0 = (slice * kChunks + ch) * 16;  // chunk start within the stage
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(ks + swz(tok0 + 8 * (mi >> 1) + rr, 2 * s + (mi & 1)) * 8), b0, b1, b2, b3);
+        mma16816(sacc[0], qa[s], b0, b1);
+        mma16816(sacc[1], qa[s], b2, b3);
+      }
+      const int tbase = t_begin + it * kTile + tok0;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool ok = tbase + 8 * j + 2 * c4 + e < t_end;
+          sacc[j][e] = ok ? sacc[j][e] * scale_log2 : -INFINITY;
+          sacc[j][2 + e] = ok ? sacc[j][2 + e] * scale_log2 : -INFINITY;
+          mx0 = fmaxf(mx0, sacc[j][e]);
+          mx1 = fmaxf(mx1, sacc[j][2 + e]);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+      const float base0 = nm0 == -INFINITY ? 0.f : nm0, base1 = nm1 == -INFINITY ? 0.f : nm1;
+      const float corr0 = exp2f(m0 - base0), corr1 = exp2f(m1 - base1);
+      m0 = nm0;
+      m1 = nm1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sacc[j][e] = exp2f(sacc[j][e] - base0);
+          sacc[j][2 + e] = exp2f(sacc[j][2 + e] - base1);
+          ps0 += sacc[j][e];
+          ps1 += sacc[j][2 + e];
+        }
+      }
+      l0 = l0 * corr0 + ps0;
+      l1 = l1 * corr1 + ps1;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        o[d][0] *= corr0;
+        o[d][1] *= corr0;
+        o[d][2] *= corr1;
+        o[d][3] *= corr1;
+      }
+      uint32_t pa[4];
+      pa[0] = pack_bf16(sacc[0][0], sacc[0][1]);
+      pa[1] = pack_bf16(sacc[0][2], sacc[0][3]);
+      pa[2] = pack_bf16(sacc[1][0], sacc[1][1]);
+      pa[3] = pack_bf16(sacc[1][2], sacc[1][3]);
+#pragma unroll
+      for (int d = 0; d < 16; d += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(vs + swz(tok0 + 8 * (mi & 1) + rr, d + (mi >> 1)) * 8), b0, b1, b2, b3);
+        mma16816(o[d], pa, b0, b1);
+        mma16816(o[d + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  // merge the token slices of each row tile through shared memory
+  float* sm_o = reinterpret_cast<float*>(smem);  // [warps][16][128]
+  float* sm_ml = sm_o + kWarps * 16 * kHD;       // [warps][16][2]
+#pragma unroll
+  for (int d = 0; d < 16; ++d) {
+    const int col = 8 * d + 2 * c4;
+    sm_o[(w * 16 + gq) * kHD + col] = o[d][0];
+    sm_o[(w * 16 + gq) * kHD + col + 1] = o[d][1];
+    sm_o[(w * 16 + gq + 8) * kHD + col] = o[d][2];
+    sm_o[(w * 16 + gq + 8) * kHD + col + 1] = o[d][3];
+  }
+  if (c4 == 0) {
+    sm_ml[(w * 16 + gq) * 2] = m0;
+    sm_ml[(w * 16 + gq) * 2 + 1] = l0;
+    sm_ml[(w * 16 + gq + 8) * 2] = m1;
+    sm_ml[(w * 16 + gq + 8) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rows * kHD; idx += kThreads) {
+    const int r = idx / kHD, col = idx % kHD;
+    const int t = r / 16, rl = r % 16;
+    float mstar = -INFINITY;
+#pragma unroll
+    for (int sl = 0; sl < kSlices; ++sl) mstar = fmaxf(mstar, sm_ml[((sl * MT + t) * 16 + rl) * 2]);
+    float lsum = 0.f, acc = 0.f;
+    if (mstar != -INFINITY) {
+#pragma unroll
+      for (int sl = 0; sl < kSlices; ++sl) {
+        const int ww = sl * MT + t;
+        const float f = exp2f(sm_ml[(ww * 16 + rl) * 2] - mstar);
+        lsum += sm_ml[(ww * 16 + rl) * 2 + 1] * f;
+        acc += sm_o[(ww * 16 + rl) * kHD + col] * f;
+      }
+    }
+    const int brow = row0 + r / G, qh = h * G + r % G;
+    const int64_t pi = ((int64_t)split * B + brow) * Hq + qh;
+    part_o[pi * kHD + col] = lsum > 0.f ? acc / lsum * v_scale : 0.f;
+    if (col == 0) part_lse[pi] = lsum > 0.f ? mstar + log2f(lsum) : -INFINITY;
+  }
+}
+
+}  // namespace
+
+// Decode attention for GRPO groups that share a prompt: rows [g*group,
+// (g+1)*group) share their first prefix_len[row] tokens (the same whole KV
+// blocks).  The prefix runs once per group (prefix_attn_kernel), each row's
+// private suffix through paged_decode_kernel from kv_start = prefix_len, and
+// decode_combine_kernel merges all (o, lse) partials.  max_prefix_hint and
+// max_suffix_hint are static upper bounds (0 = block-table capacity), so no
+// device value is read on the host.
+torch::Tensor paged_decode_attn_shared(torch::Tensor q, torch::Tensor kc, torch::Tensor vc,
+                                       torch::Tensor block_table, torch::Tensor seq_lens, torch::Tensor prefix_len,
+                                       int64_t group, double scale, double k_scale, double v_scale,
+                                       int64_t max_prefix_hint, int64_t max_suffix_hint) {
+  LRL_CHECK(q);
+  LRL_CHECK(kc);
+  LRL_CHECK(vc);
+  LRL_CHECK(block_table);
+  LRL_CHECK(seq_lens);
+  LRL_CHECK(prefix_len);
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.size(2) == kHD, "q [B, Hq, 128] bf16");
+  TORCH_CHECK(prefix_len.scalar_type() == at::kInt && seq_lens.scalar_type() == at::kInt &&
+                  block_table.scalar_type() == at::kInt,
+              "shared decode: int32 prefix_len / seq_lens / block_table");
+  const bool fp8 = kc.scalar_type() == at::kFloat8_e4m3fn;
+  const int64_t B = q.size(0), Hq = q.size(1), Hk = kc.size(2), bs = kc.size(1);
+  TORCH_CHECK(Hk > 0 && Hq % Hk == 0 && Hq / Hk <= 16, "shared decode: GQA group must be <= 16");
+  TORCH_CHECK(group >= 1 && B % group == 0, "shared decode: batch must be a multiple of group");
+  const int64_t G = Hq / Hk;
+  const int64_t rows = group * G;
+  TORCH_CHECK(rows <= 64, "shared decode: group * GQA group must be <= 64");
+  const int MT = rows <= 16 ? 1 : (rows <= 32 ? 2 : 4);
+  const int64_t max_blocks = block_table.size(1);
+  const int64_t cap = max_blocks * bs;
+  const int64_t max_prefix = max_prefix_hint > 0 ? std::min(max_prefix_hint, cap) : cap;
+  const int64_t max_suffix = max_suffix_hint > 0 ? std::min(max_suffix_hint, cap) : cap;
+  const int64_t groups = B / group;
+  auto out = torch::empty_like(q);
+  if (B == 0) return out;
+  // prefix: enough CTAs for ~4 per SM
+  const int64_t ptiles = std::max<int64_t>(1, (max_prefix + kTile - 1) / kTile);
+  int64_t psplit = std::min<int64_t>(ptiles, std::max<int64_t>(1, (4 * num_sms() + groups * Hk - 1) / (groups * Hk)));
+  const int ptps = (int)((ptiles + psplit - 1) / psplit);
+  psplit = (ptiles + ptps - 1) / ptps;
+  // suffix: at most max_suffix tokens from kv_start
+  const int64_t stiles = std::max<int64_t>(1, (max_suffix + kTile - 1) / kTile);
+  const int ssplit = decode_num_splits(B, Hk, stiles);
+  const int stps = (int)((stiles + ssplit - 1) / ssplit);
+  const int total = (int)psplit + ssplit;
+  auto po = torch::empty({total, B, Hq, kHD}, q.options().dtype(at::kFloat));
+  auto pl = torch::empty({total, B, Hq}, q.options().dtype(at::kFloat));
+  const size_t smem = 4 * kTileBytes;
+  const float sl2 = (float)(scale * k_scale * 1.4426950408889634);
+#define PREFIX(T, M)                                                                                             \
+  do {                                                                                                           \
+    auto kern = prefix_attn_kernel<T, M>;                                                                        \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
+    kern<<<dim3(psplit, Hk, groups), kThreads, smem, stream()>>>(                                                \
+        (const __nv_bfloat16*)q.data_ptr(), (const T*)kc.data_ptr(), (const T*)vc.data_ptr(),                   \
+        block_table.data_ptr<int>(), prefix_len.data_ptr<int>(), po.data_ptr<float>(), pl.data_ptr<float>(),     \
+        (int)B, (int)Hq, (int)Hk, (int)bs, (int)max_blocks, (int)group, ptps, sl2, (float)v_scale);            \
+  } while (0)
+#define SUFFIX(T)                                                                                                \
+  do {                                                                                                           \
+    auto kern = paged_decode_kernel<T>;                                                                          \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
+    kern<<<dim3(ssplit, Hk, B), kThreads, smem, stream()>>>(                                                     \
+        (const __nv_bfloat16*)q.data_ptr(), (const T*)kc.data_ptr(), (const T*)vc.data_ptr(),                   \
+        block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(),                 \
+        po.data_ptr<float>(), pl.data_ptr<float>(), (int)Hq, (int)Hk, (int)bs, (int)max_blocks, stps, sl2,      \
+        (float)v_scale, prefix_len.data_ptr<int>(), 1, (int)psplit);                                            \
+  } while (0)
+  if (fp8) {
+    if (MT == 1) PREFIX(__nv_fp8_e4m3, 1);
+    else if (MT == 2) PREFIX(__nv_fp8_e4m3, 2);
+    else PREFIX(__nv_fp8_e4m3, 4);
+    SUFFIX(__nv_fp8_e4m3);
+  } else {
+    if (MT == 1) PREFIX(__nv_bfloat16, 1);
+    else if (MT == 2) PREFIX(__nv_bfloat16, 2);
+    else PREFIX(__nv_bfloat16, 4);
+    SUFFIX(__nv_bfloat16);
+  }
+#undef PREFIX
+#undef SUFFIX
+  decode_combine_kernel<<<dim3(B, Hq), kHD, 0, stream()>>>(po.data_ptr<float>(), pl.data_ptr<float>(),
+                                                           (__nv_bfloat16*)out.data_ptr(), total, (int)B, (int)Hq);
   return out;
 }
 
@@ -509,14 +783,14 @@ static int paged_decode_noalloc_impl(const void* q, const void* kc, const void* 
     if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
     kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_fp8_e4m3*)kc, (const __nv_fp8_e4m3*)vc,
                                        block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
-                                       tps, sl2, v_scale);
+                                       tps, sl2, v_scale, nullptr, 0, 0);
   } else {
     auto kern = paged_decode_kernel<__nv_bfloat16>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
     kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
                                        block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
-                                       tps, sl2, v_scale);
+                                       tps, sl2, v_scale, nullptr, 0, 0);
   }
   if (nsplit > 1) {
     decode_combine_kernel<<<dim3(B, Hq), kHD, 0, st>>>(po, pl, (__nv_bfloat16*)out, nsplit, B, Hq);

@@ -33,6 +33,10 @@ std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top
 torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_table,
                                 torch::Tensor seq_lens, double scale, double k_scale, double v_scale,
                                 int64_t max_len_hint);
+torch::Tensor paged_decode_attn_shared(torch::Tensor q, torch::Tensor kc, torch::Tensor vc,
+                                       torch::Tensor block_table, torch::Tensor seq_lens, torch::Tensor prefix_len,
+                                       int64_t group, double scale, double k_scale, double v_scale,
+                                       int64_t max_prefix_hint, int64_t max_suffix_hint);
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots,
                double inv_ks, double inv_vs);
 torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
@@ -44,6 +48,9 @@ void symm_close(int64_t ptr);
 void symm_free(int64_t ptr);
 torch::Tensor symm_tensor(int64_t ptr, int64_t numel, torch::ScalarType dtype);
 int64_t symm_signal_words();
+void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_t epoch, torch::Tensor counter);
+void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles);
+void p2p_signal(int64_t flag_ptr, int64_t epoch);
 void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
              torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
@@ -78,6 +85,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attn", &lrl::paged_decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"),
         py::arg("block_table"), py::arg("seq_lens"), py::arg("scale"), py::arg("k_scale") = 1.0,
         py::arg("v_scale") = 1.0, py::arg("max_len_hint") = 0);
+  m.def("paged_decode_attn_shared", &lrl::paged_decode_attn_shared, py::arg("q"), py::arg("kc"), py::arg("vc"),
+        py::arg("block_table"), py::arg("seq_lens"), py::arg("prefix_len"), py::arg("group"), py::arg("scale"),
+        py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0, py::arg("max_prefix_hint") = 0,
+        py::arg("max_suffix_hint") = 0);
   m.def("kv_append", &lrl::kv_append);
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,
         py::arg("bn") = 0);
@@ -89,6 +100,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &lrl::symm_free);
   m.def("symm_tensor", &lrl::symm_tensor);
   m.def("symm_signal_words", &lrl::symm_signal_words);
+  m.def("p2p_push", &lrl::p2p_push);
+  m.def("p2p_wait", &lrl::p2p_wait);
+  m.def("p2p_signal", &lrl::p2p_signal);
   m.def("rs_norm", &lrl::rs_norm);
   m.def("adamw_ag", &lrl::adamw_ag);
   m.def("quant_act_1x128", &lrl::quant_act_1x128);

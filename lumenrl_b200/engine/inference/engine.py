@@ -72,7 +72,7 @@ class _RoutingRecorder:
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
-                 use_cuda_graph: bool = True, pad_token_id: int = 0) -> None:
+                 use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True) -> None:
         self.model = model
         self.args = model.args
         self.device = model.flat.device
@@ -80,6 +80,7 @@ class RolloutEngine:
         self.max_model_len = max_model_len
         self.block_size = block_size
         self.pad_token_id = pad_token_id
+        self.shared_prefix_attention = shared_prefix_attention
         self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda" and self.args.num_experts == 0
         spec = KVSpec(self.args.num_layers, self.args.num_kv_heads, self.args.head_dim, block_size, kv_dtype)
         self.max_blocks_per_seq = math.ceil(max_model_len / block_size) + 1
@@ -114,12 +115,12 @@ class RolloutEngine:
         self.weight_version = self.weight_version + 1 if version is None else version
 
     # -- generation ------------------------------------------------------------------
-    def _graph(self, batch: int, sp: SamplingParams) -> DecodeGraph:
-        key = (batch, sp.temperature, sp.top_p)
+    def _graph(self, batch: int, sp: SamplingParams, share: Optional[tuple] = None) -> DecodeGraph:
+        key = (batch, sp.temperature, sp.top_p, share)
         g = self._graphs.get(key)
         if g is None:
             g = DecodeGraph(self.runner, batch, self.max_blocks_per_seq, sp.temperature, sp.top_p,
-                            self.use_cuda_graph)
+                            self.use_cuda_graph, share)
             self._graphs[key] = g
         return g
 
@@ -206,7 +207,18 @@ class RolloutEngine:
         alloc.release([b for pb in prompt_blocks for b in pb])   # rows hold their own references now
         # 3) first token from the prefill logits (row r samples prompt r // n)
         row_logits = logits.repeat_interleave(n, dim=0)
-        g = self._graph(B, sp)
+        share = None
+        group = 1
+        if self.shared_prefix_attention and n > 1:
+            from lumenrl_b200 import ops
+            group = ops.shared_prefix_group(n, self.args.num_heads // self.args.num_kv_heads)
+        if group > 1 and max(plens) >= bs:
+            # static bounds, bucketed so graphs are reused: the shared whole
+            # prompt blocks, and the private part (partial block + generation)
+            max_prefix = -(-max((L // bs) * bs for L in plens) // 256) * 256
+            max_suffix = -(-(bs + max_new) // 256) * 256
+            share = (group, max_prefix, max_suffix)
+        g = self._graph(B, sp, share)
         ev2 = self._ev()
         g.row_seed.copy_(torch.arange(B, device=dev) + (sp.seed * 1_000_003 + prompt_offset * n) )
         g.step.fill_(0)
@@ -221,6 +233,7 @@ class RolloutEngine:
         g.block_table.copy_(bt)
         plen = lens.repeat_interleave(n)
         g.positions.copy_(plen)
+        g.prefix_len.copy_(((plen // bs) * bs).to(torch.int32))
         g.tokens.copy_(tok)
         routes_rows: list[list[Tensor]] = [[] for _ in range(B)]
         if recorder:

@@ -73,15 +73,23 @@ class ModelRunner:
         return ops.linear(h, self.model.lm_head.detach())
 
     @torch.no_grad()
-    def decode(self, ids: Tensor, positions: Tensor, slots: Tensor, block_table: Tensor, seq_lens: Tensor) -> Tensor:
+    def decode(self, ids: Tensor, positions: Tensor, slots: Tensor, block_table: Tensor, seq_lens: Tensor,
+               shared: Optional[tuple] = None) -> Tensor:
+        """``shared = (prefix_len [B] int32, group, max_prefix, max_suffix)``:
+        rows of each group of ``group`` share their first ``prefix_len``
+        tokens' KV blocks, and attention reads those once per group."""
         a, c = self.args, self.cache
         x = torch.nn.functional.embedding(ids, self._w("embed"))
         res = None
         for i in range(a.num_layers):
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
             q, k, v = self._qkv(i, h, positions, slots)
-            o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
-                                           c.k_scale[i], c.v_scale[i], self.max_len)
+            if shared is not None:
+                o = ops.paged_decode_attention_shared(q, c.k[i], c.v[i], block_table, seq_lens, shared[0], shared[1],
+                                                      self.scale, c.k_scale[i], c.v_scale[i], shared[2], shared[3])
+            else:
+                o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
+                                               c.k_scale[i], c.v_scale[i], self.max_len)
             x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h)
@@ -93,11 +101,13 @@ class DecodeGraph:
     """Static-shape decode step + sampling, captured into one CUDA graph.
 
     Inputs live in static buffers that the caller updates in place
-    (``tokens``, ``positions``, ``block_table``, ``row_seed``, ``step``);
-    ``seq_lens`` and ``slots`` are derived inside the graph."""
+    (``tokens``, ``positions``, ``block_table``, ``row_seed``, ``step``,
+    ``prefix_len``); ``seq_lens`` and ``slots`` are derived inside the graph.
+    ``share = (group, max_prefix, max_suffix)`` selects shared-prefix
+    attention with those static bounds."""
 
     def __init__(self, runner: ModelRunner, batch: int, max_blocks: int, temperature: float, top_p: float,
-                 use_graph: bool) -> None:
+                 use_graph: bool, share: Optional[tuple] = None) -> None:
         dev = runner.cache.device
         self.runner = runner
         self.B = batch
@@ -107,6 +117,8 @@ class DecodeGraph:
         self.block_table = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
         self.row_seed = torch.zeros(batch, dtype=torch.long, device=dev)
         self.step = torch.zeros(1, dtype=torch.long, device=dev)
+        self.prefix_len = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.share = share
         self.temperature, self.top_p = temperature, top_p
         self.out_tokens: Optional[Tensor] = None
         self.out_logp: Optional[Tensor] = None
@@ -119,7 +131,8 @@ class DecodeGraph:
         blk = self.block_table.gather(1, (pos // self.bs).unsqueeze(1).to(torch.long)).squeeze(1).to(torch.long)
         slots = blk * self.bs + pos % self.bs
         seq_lens = (pos + 1).to(torch.int32)
-        logits = self.runner.decode(self.tokens, pos, slots, self.block_table, seq_lens)
+        shared = (self.prefix_len, *self.share) if self.share is not None else None
+        logits = self.runner.decode(self.tokens, pos, slots, self.block_table, seq_lens, shared)
         tok, lp = ops.sample_tokens_device(logits, self.temperature, self.top_p, self.row_seed, self.step)
         if self.out_tokens is None:
             self.out_tokens, self.out_logp = tok, lp

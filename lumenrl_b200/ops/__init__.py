@@ -254,6 +254,32 @@ def paged_decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_ta
     return ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale, max_len)
 
 
+def shared_prefix_group(n: int, gqa: int, limit: int = 64) -> int:
+    """Largest divisor of the GRPO group size ``n`` whose rows x GQA heads fit
+    one shared-prefix attention CTA (<= ``limit`` MMA rows); 1 = no sharing."""
+    for g in range(n, 0, -1):
+        if n % g == 0 and g * gqa <= limit:
+            return g
+    return 1
+
+
+def paged_decode_attention_shared(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_table: Tensor,
+                                  seq_lens: Tensor, prefix_len: Tensor, group: int, scale: float,
+                                  k_scale: float = 1.0, v_scale: float = 1.0, max_prefix: int = 0,
+                                  max_suffix: int = 0) -> Tensor:
+    """Decode attention where rows ``[g*group, (g+1)*group)`` share their first
+    ``prefix_len[row]`` tokens (the same whole KV blocks, e.g. a GRPO prompt).
+    The shared part is read from HBM once per group instead of once per row;
+    the result equals ``paged_decode_attention``.  ``max_prefix`` /
+    ``max_suffix`` are static upper bounds of ``prefix_len`` and
+    ``seq_lens - prefix_len`` (0 = block-table capacity), so the call reads no
+    device value on the host and is CUDA-graph safe."""
+    if not _cuda(q):
+        return paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale)
+    return ext().paged_decode_attn_shared(q, k_cache, v_cache, block_table, seq_lens, prefix_len, group, scale,
+                                          k_scale, v_scale, max_prefix, max_suffix)
+
+
 def kv_cache_append(k: Tensor, v: Tensor, k_cache: Tensor, v_cache: Tensor, slots: Tensor,
                     k_scale: float = 1.0, v_scale: float = 1.0) -> None:
     """Write k/v rows [T,Hk,D] into the paged caches at flat slot indices."""

@@ -28,6 +28,11 @@ def _model(name: str, trainable: bool):
     return m
 
 
+def _model_args(name: str):
+    from lumenrl_b200.models.config import resolve_model
+    return resolve_model(name)
+
+
 def _time(fn, steps: int, warmup: int) -> float:
     for _ in range(warmup):
         fn()
@@ -58,6 +63,42 @@ def bench_decode(ns) -> dict:
     kvbytes = B * ctx * m.args.kv_bytes_per_token()
     return {"op": "decode_step", "batch": B, "ctx": ctx, "ms": ms,
             "weights_GB": wbytes / 1e9, "kv_GB": kvbytes / 1e9, "achieved_TBps": (wbytes + kvbytes) / ms / 1e9}
+
+
+def bench_attn(ns) -> dict:
+    """Decode attention of one layer (the model's heads): the per-row paged
+    kernel vs the shared-prefix kernel on GRPO-shaped rows (``--group``
+    samples share a ``--prefix``-token prompt, each with ``--ctx`` private
+    tokens).  Bytes are the K/V bytes each variant must read."""
+    from lumenrl_b200 import ops
+    args = _model_args(ns.model)
+    B, Hq, Hk, D, bs = ns.batch, args.num_heads, args.num_kv_heads, args.head_dim, 64
+    n, P, S = ns.group, ns.prefix, ns.ctx
+    groups = B // n
+    pb, sb = P // bs, (S + bs - 1) // bs
+    nblocks = 1 + groups * pb + B * sb
+    kc = torch.randn(nblocks, bs, Hk, D, device="cuda").to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    ar_p = torch.arange(pb, dtype=torch.int32, device="cuda")
+    ar_s = torch.arange(sb, dtype=torch.int32, device="cuda")
+    bt = torch.zeros(B, pb + sb, dtype=torch.int32, device="cuda")
+    for r in range(B):
+        bt[r, :pb] = 1 + (r // n) * pb + ar_p
+        bt[r, pb:] = 1 + groups * pb + r * sb + ar_s
+    lens = torch.full((B,), P + S, dtype=torch.int32, device="cuda")
+    pre = torch.full((B,), P, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, Hq, D, device="cuda").to(torch.bfloat16)
+    sc = D ** -0.5
+    grp = ops.shared_prefix_group(n, Hq // Hk)
+    t_plain = _time(lambda: ops.paged_decode_attention(q, kc, vc, bt, lens, sc, max_len=P + S), ns.steps, ns.warmup)
+    t_shared = _time(lambda: ops.paged_decode_attention_shared(q, kc, vc, bt, lens, pre, grp, sc, max_prefix=P,
+                                                               max_suffix=S), ns.steps, ns.warmup)
+    tok = Hk * D * 2 * 2
+    plain_bytes = B * (P + S) * tok
+    shared_bytes = (groups * P + B * S) * tok
+    return {"op": "decode_attention", "batch": B, "group": n, "prefix": P, "suffix": S,
+            "plain_ms": t_plain, "shared_ms": t_shared, "speedup": t_plain / t_shared,
+            "plain_TBps": plain_bytes / t_plain / 1e9, "shared_TBps": shared_bytes / t_shared / 1e9}
 
 
 def bench_train(ns) -> dict:
@@ -158,7 +199,9 @@ def bench_comm(ns) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("what", choices=["decode", "attn", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("--group", type=int, default=8)
+    ap.add_argument("--prefix", type=int, default=512)
     ap.add_argument("--numel", type=int, default=8_200_000_000)
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--batch", type=int, default=64)
@@ -170,7 +213,7 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
-    fn = {"decode": bench_decode, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
+    fn = {"decode": bench_decode, "attn": bench_attn, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
           "comm": bench_comm}[ns.what]
     res = fn(ns)
     import os

@@ -77,3 +77,20 @@ def test_packing_and_micro_batches():
     bins = make_micro_batches([10, 8, 6, 4, 2], token_budget=12)
     assert sorted(i for b in bins for i in b) == [0, 1, 2, 3, 4]
     assert all(sum([10, 8, 6, 4, 2][i] for i in b) <= 12 or len(b) == 1 for b in bins)
+
+
+def test_shared_prefix_group_and_fallback():
+    assert ops.shared_prefix_group(8, 4) == 8
+    assert ops.shared_prefix_group(32, 4) == 16
+    assert ops.shared_prefix_group(6, 16) == 3
+    assert ops.shared_prefix_group(5, 16) == 1
+    # the CPU path of the shared-prefix call is plain paged attention
+    torch.manual_seed(0)
+    B, Hq, Hk, D, bs = 4, 4, 2, 16, 8
+    kc, vc = torch.randn(9, bs, Hk, D), torch.randn(9, bs, Hk, D)
+    bt = torch.tensor([[1, 2, 3, 4], [1, 2, 5, 6], [1, 2, 7, 8], [1, 2, 3, 4]], dtype=torch.int32)
+    lens = torch.tensor([20, 25, 17, 32], dtype=torch.int32)
+    q = torch.randn(B, Hq, D)
+    a = ops.paged_decode_attention_shared(q, kc, vc, bt, lens, torch.full((B,), 16, dtype=torch.int32), 2, 0.25)
+    b = ops.paged_decode_attention(q, kc, vc, bt, lens, 0.25)
+    assert torch.allclose(a, b)

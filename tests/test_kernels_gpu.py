@@ -190,6 +190,45 @@ def test_paged_decode_attention(cuda, kv_dtype, B, Hq, Hk, bs, maxlen):
     close(out, out_r, 2e-2, 2e-2)
 
 
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("n,Hq,Hk,bs,plen,maxnew", [(8, 32, 8, 16, 512, 300), (4, 32, 8, 16, 100, 70),
+                                                    (16, 16, 4, 16, 200, 129), (8, 32, 8, 16, 8, 64),
+                                                    (2, 8, 1, 32, 96, 33)])
+def test_paged_decode_attention_shared_prefix(cuda, kv_dtype, n, Hq, Hk, bs, plen, maxnew):
+    """Rows of a group share the prompt's whole KV blocks; the shared-prefix
+    kernel must equal the fp32 reference of plain paged attention."""
+    torch.manual_seed(1)
+    D, P = 128, 3
+    B = P * n
+    full = plen // bs                         # shared whole blocks
+    need = (plen + maxnew + bs - 1) // bs
+    nblocks = 1 + P * full + B * (need - full) + 2
+    perm = (torch.randperm(nblocks - 1) + 1).tolist()
+    bt = torch.zeros(B, need, dtype=torch.int32)
+    for i in range(P):
+        shared = [perm.pop() for _ in range(full)]
+        for j in range(n):
+            bt[i * n + j, :full] = torch.tensor(shared, dtype=torch.int32)
+            bt[i * n + j, full:] = torch.tensor([perm.pop() for _ in range(need - full)], dtype=torch.int32)
+    bt = bt.to(cuda)
+    lens = (plen + torch.randint(1, maxnew + 1, (B,))).to(torch.int32)
+    lens[0] = plen + maxnew
+    lens = lens.to(cuda)
+    prefix = torch.full((B,), full * bs, dtype=torch.int32, device=cuda)
+    kc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(kv_dtype)
+    vc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(kv_dtype)
+    q = torch.randn(B, Hq, D, device=cuda, dtype=torch.bfloat16)
+    ks, vs = (0.5, 2.0) if kv_dtype != torch.bfloat16 else (1.0, 1.0)
+    grp = ops.shared_prefix_group(n, Hq // Hk)
+    out = ops.paged_decode_attention_shared(q, kc, vc, bt, lens, prefix, grp, 1 / math.sqrt(D), ks, vs,
+                                            full * bs, maxnew + bs)
+    out_r = ref.paged_decode_attention(q.cpu(), kc.float().cpu() * ks, vc.float().cpu() * vs, bt.cpu(), lens.cpu(),
+                                       1 / math.sqrt(D))
+    close(out, out_r, 2e-2, 2e-2)
+    plain = ops.paged_decode_attention(q, kc, vc, bt, lens, 1 / math.sqrt(D), ks, vs, plen + maxnew)
+    close(out, plain, 2e-2, 2e-2)
+
+
 def test_kv_append_roundtrip(cuda):
     T, Hk, D, bs = 50, 8, 128, 16
     kc = torch.zeros(10, bs, Hk, D, device=cuda, dtype=torch.bfloat16)

@@ -98,3 +98,57 @@ def test_dead_peer_becomes_comm_timeout():
     for p in procs:
         p.join(timeout=60)
     assert res[0] == "timeout"
+
+
+def _ring_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.parallel.symm import CommTimeout
+    from lumenrl_b200.transfer.p2p_ring import HiddenStateRing
+    T, D = 2048, 4 * 1024   # one 16 MiB batch of bf16 hidden rows
+    ring = HiddenStateRing(producer=0, consumer=1, slot_bytes=T * D * 2, nslots=2, wait_seconds=2.0)
+    errs = []
+    for i in range(5):   # more batches than slots: the producer waits for released slots
+        x = torch.randn(T, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(i)).to(torch.bfloat16)
+        if rank == 0:
+            ring.put(x)
+        else:
+            y = ring.get((T, D), torch.bfloat16)
+            errs.append((y.float() - x.float()).abs().max().item())
+            ring.release()
+    torch.cuda.synchronize()
+    ring.check()
+    dist.barrier()
+    # a batch the producer never pushes: the consumer's bounded wait expires
+    timeout = "no-error"
+    if rank == 1:
+        ring.get((T, D), torch.bfloat16)
+        torch.cuda.synchronize()
+        try:
+            ring.check()
+        except CommTimeout:
+            timeout = "timeout"
+        ring._held = None
+    q.put((rank, errs, timeout))
+    dist.barrier()
+    ring.close()
+    dist.destroy_process_group()
+
+
+def test_hidden_state_ring_nvlink():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29990 + os.getpid() % 9
+    procs = [ctx.Process(target=_ring_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (e, t) for r, e, t in (q.get(timeout=300) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+    errs, timeout = res[1]
+    assert len(errs) == 5 and max(errs) == 0.0
+    assert timeout == "timeout"

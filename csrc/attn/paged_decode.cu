@@ -115,18 +115,17 @@ __device__ __forceinline__ void stage_tile(const CacheT* __restrict__ kc, const 
   }
 }
 
+// One (context split, kv head, sequence) work item; `nrows` is the batch.
 template <typename CacheT>
-__global__ void __launch_bounds__(kThreads) paged_decode_kernel(
+__device__ __forceinline__ void decode_body(
     const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
     const int* __restrict__ block_table, const int* __restrict__ seq_lens, __nv_bfloat16* __restrict__ out,
     float* __restrict__ part_o, float* __restrict__ part_lse, int Hq, int Hk, int bs, int max_blocks,
     int tiles_per_split, float scale_log2, float v_scale, const int* __restrict__ kv_start, int force_partial,
-    int part_offset) {
+    int part_offset, int split, int h, int b, int nsplit, int nrows) {
   extern __shared__ __align__(128) uint8_t smem[];
   __nv_bfloat16* kbuf = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* vbuf = reinterpret_cast<__nv_bfloat16*>(smem + 2 * kTileBytes);
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int nsplit = gridDim.x;
   const int G = Hq / Hk;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int g = lane >> 2, c4 = lane & 3;
@@ -287,11 +286,23 @@ __global__ void __launch_bounds__(kThreads) paged_decode_kernel(
     if (nsplit == 1 && !force_partial) {
       out[((int64_t)b * Hq + qh) * kHD + col] = __float2bfloat16(val);
     } else {
-      const int64_t pi = ((int64_t)(part_offset + split) * gridDim.z + b) * Hq + qh;
+      const int64_t pi = ((int64_t)(part_offset + split) * nrows + b) * Hq + qh;
       part_o[pi * kHD + col] = val;
       if (col == 0) part_lse[pi] = lsum > 0.f ? mstar + log2f(lsum) : -INFINITY;
     }
   }
+}
+
+template <typename CacheT>
+__global__ void __launch_bounds__(kThreads) paged_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
+    const int* __restrict__ block_table, const int* __restrict__ seq_lens, __nv_bfloat16* __restrict__ out,
+    float* __restrict__ part_o, float* __restrict__ part_lse, int Hq, int Hk, int bs, int max_blocks,
+    int tiles_per_split, float scale_log2, float v_scale, const int* __restrict__ kv_start, int force_partial,
+    int part_offset) {
+  decode_body<CacheT>(q, kc, vc, block_table, seq_lens, out, part_o, part_lse, Hq, Hk, bs, max_blocks,
+                      tiles_per_split, scale_log2, v_scale, kv_start, force_partial, part_offset, blockIdx.x,
+                      blockIdx.y, blockIdx.z, gridDim.x, gridDim.z);
 }
 
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
@@ -380,20 +391,20 @@ torch::Tensor paged_decode_attn(torch::Tensor q, torch::Tensor kc, torch::Tensor
 // row tiles, so each shared K/V tile is read from HBM once per group instead
 // of once per row.  Warps split as (MT row tiles) x (4/MT token slices of
 // each 64-token stage).  Writes (o, lse) partials for the combine kernel.
+// (Device function; launched inside cascade_decode_kernel.)
 namespace {
 
 template <typename CacheT, int MT>
-__global__ void __launch_bounds__(kThreads) prefix_attn_kernel(
+__device__ __forceinline__ void prefix_body(
     const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
     const int* __restrict__ block_table, const int* __restrict__ prefix_len, float* __restrict__ part_o,
     float* __restrict__ part_lse, int B, int Hq, int Hk, int bs, int max_blocks, int group, int tiles_per_split,
-    float scale_log2, float v_scale) {
+    float scale_log2, float v_scale, int split, int h, int g) {
   extern __shared__ __align__(128) uint8_t smem[];
   __nv_bfloat16* kbuf = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* vbuf = reinterpret_cast<__nv_bfloat16*>(smem + 2 * kTileBytes);
   constexpr int kSlices = kWarps / MT;             // warps sharing one row tile
   constexpr int kChunks = (kTile / 16) / kSlices;  // 16-token chunks per warp per stage
-  const int split = blockIdx.x, h = blockIdx.y, g = blockIdx.z;
   const int G = Hq / Hk;
   const int rows = group * G;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -555,12 +566,36 @@ __global__ void __launch_bounds__(kThreads) prefix_attn_kernel(
   }
 }
 
+// One launch for both parts: blocks [0, NP) are shared-prefix work items
+// (split, kv head, group), the rest are per-row suffix items (split, kv head,
+// row) starting at kv_start = prefix_len.  Prefix items are scheduled first
+// and overlap the suffix stream instead of running as a separate, short,
+// latency-bound launch.
+template <typename CacheT, int MT>
+__global__ void __launch_bounds__(kThreads) cascade_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, const CacheT* __restrict__ kc, const CacheT* __restrict__ vc,
+    const int* __restrict__ block_table, const int* __restrict__ seq_lens, const int* __restrict__ prefix_len,
+    float* __restrict__ part_o, float* __restrict__ part_lse, int B, int Hq, int Hk, int bs, int max_blocks,
+    int group, int psplit, int ptps, int ssplit, int stps, float scale_log2, float v_scale) {
+  const int NP = psplit * Hk * (B / group);
+  const int idx = blockIdx.x;
+  if (idx < NP) {
+    prefix_body<CacheT, MT>(q, kc, vc, block_table, prefix_len, part_o, part_lse, B, Hq, Hk, bs, max_blocks, group,
+                            ptps, scale_log2, v_scale, idx % psplit, (idx / psplit) % Hk, idx / (psplit * Hk));
+  } else {
+    const int j = idx - NP;
+    decode_body<CacheT>(q, kc, vc, block_table, seq_lens, nullptr, part_o, part_lse, Hq, Hk, bs, max_blocks, stps,
+                        scale_log2, v_scale, prefix_len, 1, psplit, j % ssplit, (j / ssplit) % Hk, j / (ssplit * Hk),
+                        ssplit, B);
+  }
+}
+
 }  // namespace
 
 // Decode attention for GRPO groups that share a prompt: rows [g*group,
 // (g+1)*group) share their first prefix_len[row] tokens (the same whole KV
-// blocks).  The prefix runs once per group (prefix_attn_kernel), each row's
-// private suffix through paged_decode_kernel from kv_start = prefix_len, and
+// blocks).  One cascade_decode_kernel launch runs the prefix once per group
+// and each row's private suffix from kv_start = prefix_len;
 // decode_combine_kernel merges all (o, lse) partials.  max_prefix_hint and
 // max_suffix_hint are static upper bounds (0 = block-table capacity), so no
 // device value is read on the host.
@@ -593,52 +628,40 @@ torch::Tensor paged_decode_attn_shared(torch::Tensor q, torch::Tensor kc, torch:
   const int64_t groups = B / group;
   auto out = torch::empty_like(q);
   if (B == 0) return out;
-  // prefix: enough CTAs for ~4 per SM
-  const int64_t ptiles = std::max<int64_t>(1, (max_prefix + kTile - 1) / kTile);
-  int64_t psplit = std::min<int64_t>(ptiles, std::max<int64_t>(1, (4 * num_sms() + groups * Hk - 1) / (groups * Hk)));
-  const int ptps = (int)((ptiles + psplit - 1) / psplit);
-  psplit = (ptiles + ptps - 1) / ptps;
-  // suffix: at most max_suffix tokens from kv_start
+  // suffix: at most max_suffix tokens from kv_start, split for >= 4 CTAs per
+  // SM; prefix items take the same number of tiles each
   const int64_t stiles = std::max<int64_t>(1, (max_suffix + kTile - 1) / kTile);
   const int ssplit = decode_num_splits(B, Hk, stiles);
   const int stps = (int)((stiles + ssplit - 1) / ssplit);
-  const int total = (int)psplit + ssplit;
+  const int64_t ptiles = std::max<int64_t>(1, (max_prefix + kTile - 1) / kTile);
+  const int ptps = stps;
+  const int psplit = (int)((ptiles + ptps - 1) / ptps);
+  const int total = psplit + ssplit;
   auto po = torch::empty({total, B, Hq, kHD}, q.options().dtype(at::kFloat));
   auto pl = torch::empty({total, B, Hq}, q.options().dtype(at::kFloat));
   const size_t smem = 4 * kTileBytes;
   const float sl2 = (float)(scale * k_scale * 1.4426950408889634);
-#define PREFIX(T, M)                                                                                             \
+  const int64_t nblocks = (int64_t)psplit * Hk * groups + (int64_t)ssplit * Hk * B;
+#define CASCADE(T, M)                                                                                            \
   do {                                                                                                           \
-    auto kern = prefix_attn_kernel<T, M>;                                                                        \
+    auto kern = cascade_decode_kernel<T, M>;                                                                     \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
-    kern<<<dim3(psplit, Hk, groups), kThreads, smem, stream()>>>(                                                \
+    kern<<<(unsigned)nblocks, kThreads, smem, stream()>>>(                                                      \
         (const __nv_bfloat16*)q.data_ptr(), (const T*)kc.data_ptr(), (const T*)vc.data_ptr(),                   \
-        block_table.data_ptr<int>(), prefix_len.data_ptr<int>(), po.data_ptr<float>(), pl.data_ptr<float>(),     \
-        (int)B, (int)Hq, (int)Hk, (int)bs, (int)max_blocks, (int)group, ptps, sl2, (float)v_scale);            \
-  } while (0)
-#define SUFFIX(T)                                                                                                \
-  do {                                                                                                           \
-    auto kern = paged_decode_kernel<T>;                                                                          \
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                         \
-    kern<<<dim3(ssplit, Hk, B), kThreads, smem, stream()>>>(                                                     \
-        (const __nv_bfloat16*)q.data_ptr(), (const T*)kc.data_ptr(), (const T*)vc.data_ptr(),                   \
-        block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), (__nv_bfloat16*)out.data_ptr(),                 \
-        po.data_ptr<float>(), pl.data_ptr<float>(), (int)Hq, (int)Hk, (int)bs, (int)max_blocks, stps, sl2,      \
-        (float)v_scale, prefix_len.data_ptr<int>(), 1, (int)psplit);                                            \
+        block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), prefix_len.data_ptr<int>(), po.data_ptr<float>(), \
+        pl.data_ptr<float>(), (int)B, (int)Hq, (int)Hk, (int)bs, (int)max_blocks, (int)group, psplit, ptps,      \
+        ssplit, stps, sl2, (float)v_scale);                                                                      \
   } while (0)
   if (fp8) {
-    if (MT == 1) PREFIX(__nv_fp8_e4m3, 1);
-    else if (MT == 2) PREFIX(__nv_fp8_e4m3, 2);
-    else PREFIX(__nv_fp8_e4m3, 4);
-    SUFFIX(__nv_fp8_e4m3);
+    if (MT == 1) CASCADE(__nv_fp8_e4m3, 1);
+    else if (MT == 2) CASCADE(__nv_fp8_e4m3, 2);
+    else CASCADE(__nv_fp8_e4m3, 4);
   } else {
-    if (MT == 1) PREFIX(__nv_bfloat16, 1);
-    else if (MT == 2) PREFIX(__nv_bfloat16, 2);
-    else PREFIX(__nv_bfloat16, 4);
-    SUFFIX(__nv_bfloat16);
+    if (MT == 1) CASCADE(__nv_bfloat16, 1);
+    else if (MT == 2) CASCADE(__nv_bfloat16, 2);
+    else CASCADE(__nv_bfloat16, 4);
   }
-#undef PREFIX
-#undef SUFFIX
+#undef CASCADE
   decode_combine_kernel<<<dim3(B, Hq), kHD, 0, stream()>>>(po.data_ptr<float>(), pl.data_ptr<float>(),
                                                            (__nv_bfloat16*)out.data_ptr(), total, (int)B, (int)Hq);
   return out;

@@ -51,6 +51,12 @@ int64_t symm_signal_words();
 void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_t epoch, torch::Tensor counter);
 void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles);
 void p2p_signal(int64_t flag_ptr, int64_t epoch);
+void tp_publish(std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch);
+torch::Tensor ag_gemm(std::vector<int64_t> shard_ptrs, int64_t Ml, torch::Tensor b, std::vector<int64_t> sig_ptrs,
+                      int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
+torch::Tensor gemm_rs(torch::Tensor a, torch::Tensor b, std::vector<int64_t> recv_ptrs,
+                      std::vector<int64_t> sig_ptrs, torch::Tensor counter, int64_t rank, int64_t slot, int64_t epoch,
+                      torch::Tensor status, int64_t wait_cycles);
 void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
              torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
@@ -103,6 +109,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_push", &lrl::p2p_push);
   m.def("p2p_wait", &lrl::p2p_wait);
   m.def("p2p_signal", &lrl::p2p_signal);
+  m.def("tp_publish", &lrl::tp_publish);
+  m.def("ag_gemm", &lrl::ag_gemm);
+  m.def("gemm_rs", &lrl::gemm_rs);
   m.def("rs_norm", &lrl::rs_norm);
   m.def("adamw_ag", &lrl::adamw_ag);
   m.def("quant_act_1x128", &lrl::quant_act_1x128);

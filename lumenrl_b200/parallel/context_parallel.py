@@ -1,0 +1,243 @@
+"""Context parallelism: zigzag sequence split and ring attention
+(reference ``engine/training/megatron_native_engine.py:1065-1351``: zigzag
+``2*CP`` chunks, TE ring attention over ``thd``, log-probs rebuilt with a
+differentiable all-reduce).
+
+* ``zigzag_indices(S, cp, rank)``: a sequence is cut into ``2*cp`` equal
+  chunks and rank r keeps chunks ``r`` and ``2*cp-1-r``, so every rank gets
+  the same amount of causal attention work.
+* ``ring_attention(q, k, v, cp_group)``: causal attention of this rank's two
+  query chunks against the whole sequence.  The K/V chunks travel round the
+  ring (``cp - 1`` point-to-point exchanges, each posted before the block
+  computation so the transfer overlaps it); blocks are merged with their
+  log-sum-exp.  Per (query chunk, key chunk) pair the mask is all, nothing
+  or the causal diagonal, because chunks are ordered.  Backward runs the ring
+  again, recomputing each block's probabilities from the global LSE and
+  sending each block's dK/dV back with it, so every rank ends with the
+  gradient of its own K/V.
+* ``gather_seq`` / ``scatter_seq``: put per-rank token tensors back in
+  sequence order (all-gather) differentiably, e.g. for log-probs.
+
+Block math: on CUDA the per-block forward/backward are the flash-attention
+kernels behind ``torch.nn.functional.scaled_dot_product_attention`` (which
+return the LSE); on CPU an fp32 restatement is used.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+
+def zigzag_indices(S: int, cp: int, rank: int, device=None) -> Tensor:
+    if S % (2 * cp):
+        raise ValueError(f"sequence length {S} must be a multiple of 2 * cp = {2 * cp}")
+    c = S // (2 * cp)
+    a = torch.arange(rank * c, (rank + 1) * c, device=device)
+    b = torch.arange((2 * cp - 1 - rank) * c, (2 * cp - rank) * c, device=device)
+    return torch.cat([a, b])
+
+
+def _chunk_ids(cp: int, rank: int) -> tuple[int, int]:
+    return rank, 2 * cp - 1 - rank
+
+
+# --------------------------------------------------------------------- block kernels
+def _expand(k: Tensor, hq: int) -> Tensor:
+    return k if k.shape[1] == hq else k.repeat_interleave(hq // k.shape[1], dim=1)
+
+
+def _block_fwd(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: float) -> tuple[Tensor, Tensor]:
+    """q [B,H,Tq,D], k/v [B,Hk,Tk,D] -> (o [B,H,Tq,D] in q's dtype, lse [B,H,Tq] fp32)."""
+    H = q.shape[1]
+    k, v = _expand(k, H), _expand(v, H)
+    if q.is_cuda:
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        out = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, causal, False, scale=scale)
+        return out[0], out[1].float()
+    s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    if causal:
+        Tq, Tk = s.shape[-2], s.shape[-1]
+        s = s.masked_fill(torch.ones(Tq, Tk, dtype=torch.bool).triu(1 + Tk - Tq), float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    o = torch.exp(s - lse.unsqueeze(-1)) @ v.float()
+    return o.to(q.dtype), lse
+
+
+def _block_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, lse: Tensor, causal: bool,
+               scale: float) -> tuple[Tensor, Tensor, Tensor]:
+    """Gradients of one block given the GLOBAL output ``o`` and ``lse``."""
+    H, Hk = q.shape[1], k.shape[1]
+    ke, ve = _expand(k, H), _expand(v, H)
+    if q.is_cuda:
+        B, _, Tq, _ = q.shape
+        Tk = k.shape[2]
+        do, q, ke, ve, o = do.contiguous(), q.contiguous(), ke.contiguous(), ve.contiguous(), o.contiguous()
+        empty = torch.empty(0, device=q.device, dtype=torch.int64)
+        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
+            do, q, ke, ve, o, lse.to(torch.float32), empty, empty, Tq, Tk, 0.0, causal,
+            torch.zeros((), dtype=torch.int64, device=q.device), torch.zeros((), dtype=torch.int64, device=q.device),
+            scale=scale)
+    else:
+        s = (q.float() @ ke.float().transpose(-1, -2)) * scale
+        if causal:
+            Tq, Tk = s.shape[-2], s.shape[-1]
+            s = s.masked_fill(torch.ones(Tq, Tk, dtype=torch.bool).triu(1 + Tk - Tq), float("-inf"))
+        p = torch.exp(s - lse.unsqueeze(-1))
+        dof = do.float()
+        dv = p.transpose(-1, -2) @ dof
+        dp = dof @ ve.float().transpose(-1, -2)
+        delta = (dof * o.float()).sum(-1, keepdim=True)
+        ds = p * (dp - delta) * scale
+        dq = ds @ ke.float()
+        dk = ds.transpose(-1, -2) @ q.float()
+    if Hk != H:
+        g = H // Hk
+        dk = dk.view(dk.shape[0], Hk, g, *dk.shape[2:]).sum(2)
+        dv = dv.view(dv.shape[0], Hk, g, *dv.shape[2:]).sum(2)
+    return dq.float(), dk.float(), dv.float()
+
+
+def _merge(o: Optional[Tensor], lse: Optional[Tensor], ob: Tensor, lb: Tensor) -> tuple[Tensor, Tensor]:
+    if o is None:
+        return ob.float(), lb
+    m = torch.maximum(lse, lb)
+    m = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+    a, b = torch.exp(lse - m), torch.exp(lb - m)
+    new = torch.log(a + b) + m
+    wa = (a / (a + b)).unsqueeze(-1)
+    return o * wa + ob.float() * (1 - wa), new
+
+
+# --------------------------------------------------------------------- ring
+def _ring_exchange(tensors: list, group, rank: int, cp: int) -> list:
+    """Send ``tensors`` to the next rank and receive the previous rank's."""
+    nxt, prv = (rank + 1) % cp, (rank - 1) % cp
+    g_nxt = dist.get_global_rank(group, nxt) if group is not None else nxt
+    g_prv = dist.get_global_rank(group, prv) if group is not None else prv
+    recv = [torch.empty_like(t) for t in tensors]
+    ops = [dist.P2POp(dist.isend, t.contiguous(), g_nxt, group) for t in tensors]
+    ops += [dist.P2POp(dist.irecv, r, g_prv, group) for r in recv]
+    reqs = dist.batch_isend_irecv(ops)
+    return recv, reqs
+
+
+def _pairs(cp: int, rank: int, src: int):
+    """(local q chunk slot, kv chunk slot of `src`, causal?) for every
+    (query chunk, key chunk) pair that is not fully masked."""
+    qc = _chunk_ids(cp, rank)
+    kc = _chunk_ids(cp, src)
+    out = []
+    for qi, qid in enumerate(qc):
+        for ki, kid in enumerate(kc):
+            if kid < qid:
+                out.append((qi, ki, False))
+            elif kid == qid:
+                out.append((qi, ki, True))
+    return out
+
+
+class _RingAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, group, scale):
+        cp, rank = dist.get_world_size(group), dist.get_rank(group)
+        B, H, T2, D = q.shape
+        c = T2 // 2
+        qs = [q[:, :, :c], q[:, :, c:]]
+        o = [None, None]
+        lse = [None, None]
+        kv = (k, v)
+        for step in range(cp):
+            src = (rank - step) % cp
+            reqs = None
+            if step < cp - 1:
+                nxt_kv, reqs = _ring_exchange(list(kv), group, rank, cp)
+            kk, vv = kv
+            ks, vs = [kk[:, :, :c], kk[:, :, c:]], [vv[:, :, :c], vv[:, :, c:]]
+            for qi, ki, causal in _pairs(cp, rank, src):
+                ob, lb = _block_fwd(qs[qi], ks[ki], vs[ki], causal, scale)
+                o[qi], lse[qi] = _merge(o[qi], lse[qi], ob, lb)
+            if reqs is not None:
+                for r in reqs:
+                    r.wait()
+                kv = tuple(nxt_kv)
+        out = torch.cat([o[0], o[1]], 2).to(q.dtype)
+        L = torch.cat([lse[0], lse[1]], 2)
+        ctx.save_for_backward(q, k, v, out, L)
+        ctx.group, ctx.scale = group, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, out, L = ctx.saved_tensors
+        group, scale = ctx.group, ctx.scale
+        cp, rank = dist.get_world_size(group), dist.get_rank(group)
+        c = q.shape[2] // 2
+        sl = [slice(0, c), slice(c, 2 * c)]
+        do = do.contiguous()
+        dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+        # the K/V block and its gradient travel together round the ring
+        kk, vv = k, v
+        dk = torch.zeros(k.shape, dtype=torch.float32, device=k.device)
+        dv = torch.zeros(v.shape, dtype=torch.float32, device=v.device)
+        for step in range(cp):
+            src = (rank - step) % cp
+            for qi, ki, causal in _pairs(cp, rank, src):
+                gq, gk, gv = _block_bwd(do[:, :, sl[qi]], q[:, :, sl[qi]], kk[:, :, sl[ki]], vv[:, :, sl[ki]],
+                                        out[:, :, sl[qi]], L[:, :, sl[qi]], causal, scale)
+                dq[:, :, sl[qi]] += gq
+                dk[:, :, sl[ki]] += gk
+                dv[:, :, sl[ki]] += gv
+            # pass (K, V, dK, dV) on; after cp steps every block is home again
+            recv, reqs = _ring_exchange([kk, vv, dk, dv], group, rank, cp)
+            for r in reqs:
+                r.wait()
+            kk, vv, dk, dv = recv
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
+
+
+def ring_attention(q: Tensor, k: Tensor, v: Tensor, group=None, scale: Optional[float] = None) -> Tensor:
+    """Causal attention for this rank's zigzag chunks.  q [B,H,2c,D] and
+    k/v [B,Hk,2c,D] hold chunks (rank, 2cp-1-rank) of each sequence."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if dist.get_world_size(group) == 1:
+        from torch.nn.functional import scaled_dot_product_attention as sdpa
+        H = q.shape[1]
+        return sdpa(q, _expand(k, H), _expand(v, H), is_causal=True, scale=scale)
+    return _RingAttention.apply(q, k, v, group, scale)
+
+
+class _GatherSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, S, group):
+        cp, rank = dist.get_world_size(group), dist.get_rank(group)
+        parts = [torch.empty_like(x) for _ in range(cp)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        out = x.new_empty((S,) + tuple(x.shape[1:]))
+        for r in range(cp):
+            out[zigzag_indices(S, cp, r, x.device)] = parts[r]
+        ctx.S, ctx.group, ctx.rank, ctx.cp = S, group, rank, cp
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        # every rank holds the full-sequence gradient of its own use; sum them
+        g = g.contiguous().clone()
+        dist.all_reduce(g, group=ctx.group)
+        return g[zigzag_indices(ctx.S, ctx.cp, ctx.rank, g.device)], None, None
+
+
+def gather_seq(x_local: Tensor, S: int, group=None) -> Tensor:
+    """[2c, ...] zigzag-local rows -> [S, ...] in sequence order on every rank
+    (differentiable; the backward sums the ranks' gradients)."""
+    return _GatherSeq.apply(x_local, S, group)
+
+
+def scatter_seq(x: Tensor, group=None) -> Tensor:
+    """[S, ...] -> this rank's zigzag rows."""
+    cp, rank = dist.get_world_size(group), dist.get_rank(group)
+    return x[zigzag_indices(x.shape[0], cp, rank, x.device)]

@@ -189,3 +189,48 @@ def test_tensor_parallel_fused_ag_rs_gemms():
             if k == "fused":
                 continue
             assert fused[k] < max(3 * plain[k], 2e-2), (rank, k, fused[k], plain[k])
+
+
+def _cp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.parallel.context_parallel import ring_attention, zigzag_indices
+    S, H, Hk, D = 4096, 8, 2, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v, do = (torch.randn(1, h, S, D, device="cuda", generator=g).to(torch.bfloat16) for h in (H, Hk, Hk, H))
+    idx = zigzag_indices(S, world, rank, "cuda")
+    ql, kl, vl = (t[:, :, idx].clone().requires_grad_(True) for t in (q, k, v))
+    o = ring_attention(ql, kl, vl)
+    o.backward(do[:, :, idx])
+    qf, kf, vf = (t.clone().requires_grad_(True) for t in (q, k, v))
+    of = torch.nn.functional.scaled_dot_product_attention(qf, kf.repeat_interleave(H // Hk, 1),
+                                                          vf.repeat_interleave(H // Hk, 1), is_causal=True)
+    of.backward(do)
+
+    def rel(a, b):
+        return ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
+    q.put((rank, {"o": rel(o, of[:, :, idx]), "dq": rel(ql.grad, qf.grad[:, :, idx]),
+                  "dk": rel(kl.grad, kf.grad[:, :, idx]), "dv": rel(vl.grad, vf.grad[:, :, idx])}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_context_parallel_ring_attention():
+    """CP=2 zigzag ring attention (flash blocks + LSE merge, K/V over NCCL p2p)
+    against full causal attention, forward and backward, bf16."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29970 + os.getpid() % 9
+    procs = [ctx.Process(target=_cp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in res:
+        for k, v in errs.items():
+            assert v < 2e-2, (rank, k, v)

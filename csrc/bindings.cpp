@@ -51,6 +51,8 @@ int64_t symm_signal_words();
 void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_t epoch, torch::Tensor counter);
 void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles);
 void p2p_signal(int64_t flag_ptr, int64_t epoch);
+torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets);
+int64_t grouped_gemm_status();
 void tp_publish(std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch);
 torch::Tensor ag_gemm(std::vector<int64_t> shard_ptrs, int64_t Ml, torch::Tensor b, std::vector<int64_t> sig_ptrs,
                       int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
@@ -109,6 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_push", &lrl::p2p_push);
   m.def("p2p_wait", &lrl::p2p_wait);
   m.def("p2p_signal", &lrl::p2p_signal);
+  m.def("grouped_gemm", &lrl::grouped_gemm);
+  m.def("grouped_gemm_status", &lrl::grouped_gemm_status);
   m.def("tp_publish", &lrl::tp_publish);
   m.def("ag_gemm", &lrl::ag_gemm);
   m.def("gemm_rs", &lrl::gemm_rs);

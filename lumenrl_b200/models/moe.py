@@ -64,6 +64,54 @@ def grouped_linear(x: Tensor, w: Tensor, offsets: list[int]) -> Tensor:
     return _GroupedLinear.forward(_NullCtx(), x, w, None, offsets)
 
 
+class _GroupedLinearTC(torch.autograd.Function):
+    """Grouped expert GEMM on the tcgen05 kernel (``csrc/gemm/grouped_gemm.cu``):
+    forward and input gradient are single launches driven by the device-side
+    offsets; the weight gradient (a per-expert reduction over that expert's
+    tokens) reads the offsets on the host once and accumulates each expert's
+    ``dy^T x`` in fp32 into ``main_grad`` with cuBLAS."""
+
+    @staticmethod
+    def forward(ctx, x, w, w_handle, offsets_dev):
+        from lumenrl_b200.ops.ext import ext
+        y = ext().grouped_gemm(x.contiguous(), w.contiguous(), offsets_dev)
+        ctx.save_for_backward(x, w, offsets_dev)
+        ctx.w_handle = w_handle
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from lumenrl_b200.ops.ext import ext
+        x, w, offs = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = ext().grouped_gemm(dy, w.transpose(1, 2).contiguous(), offs)
+        off = offs.tolist()
+        mg = getattr(ctx.w_handle, "main_grad", None)
+        gw = None if mg is not None else torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        for e in range(w.shape[0]):
+            a, b = off[e], off[e + 1]
+            if b > a:
+                tgt = mg[e] if mg is not None else gw[e]
+                torch.addmm(tgt, dy[a:b].t(), x[a:b], out_dtype=torch.float32, out=tgt)
+        if gw is not None:
+            ops._accum_main_grad(ctx.w_handle, gw)
+        return dx, None, None, None
+
+
+def grouped_linear_device(x: Tensor, w: Tensor, offsets_dev: Tensor) -> Tensor:
+    """Expert GEMM with device offsets [E+1] int32 (bf16 CUDA tensors,
+    N and K of the weights multiples of 128 / 8)."""
+    if torch.is_grad_enabled() and w.requires_grad:
+        return _GroupedLinearTC.apply(x, w.detach(), w, offsets_dev)
+    from lumenrl_b200.ops.ext import ext
+    return ext().grouped_gemm(x.contiguous(), w.contiguous(), offsets_dev)
+
+
+def _use_tc_grouped(h: Tensor, w13: Tensor, w2: Tensor) -> bool:
+    return (h.is_cuda and h.dtype == torch.bfloat16 and w13.shape[1] % 128 == 0 and w2.shape[1] % 128 == 0
+            and w13.shape[2] % 8 == 0 and w2.shape[2] % 8 == 0 and w13.shape[0] <= 512)
+
+
 class _NullCtx:
     def save_for_backward(self, *a):
         pass
@@ -108,11 +156,18 @@ def moe_forward(model, layer: int, h: Tensor) -> tuple[Tensor, Optional[Tensor]]
     flat_ids = ids.reshape(-1)
     order = torch.argsort(flat_ids, stable=True)
     counts = torch.bincount(flat_ids, minlength=a.num_experts)
-    offsets = [0] + torch.cumsum(counts, 0).tolist()
     token_of = order // k
     xs = h[token_of]
-    gu = grouped_linear(xs, P[pre + "experts_w13"], offsets)
-    ys = grouped_linear(ops.swiglu(gu), P[pre + "experts_w2"], offsets)
+    w13, w2 = P[pre + "experts_w13"], P[pre + "experts_w2"]
+    if _use_tc_grouped(h, w13, w2):
+        offs = torch.zeros(a.num_experts + 1, dtype=torch.int32, device=h.device)
+        offs[1:] = torch.cumsum(counts, 0)
+        gu = grouped_linear_device(xs, w13, offs)
+        ys = grouped_linear_device(ops.swiglu(gu), w2, offs)
+    else:
+        offsets = [0] + torch.cumsum(counts, 0).tolist()
+        gu = grouped_linear(xs, w13, offsets)
+        ys = grouped_linear(ops.swiglu(gu), w2, offsets)
     wt = w.reshape(-1)[order].to(ys.dtype).unsqueeze(-1)
     out = torch.zeros_like(h)
     out.index_add_(0, token_of, ys * wt)

@@ -53,6 +53,15 @@ void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag
 void p2p_signal(int64_t flag_ptr, int64_t epoch);
 torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets);
 int64_t grouped_gemm_status();
+int64_t ep_flag_slots();
+void ep_exchange_counts(torch::Tensor counts, std::vector<int64_t> table_ptrs, std::vector<int64_t> sig_ptrs,
+                        int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
+void ep_scatter_rows(torch::Tensor src, c10::optional<torch::Tensor> src_row, torch::Tensor dst_rank,
+                     torch::Tensor dst_row, std::vector<int64_t> buf_ptrs, int64_t cap,
+                     std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch, torch::Tensor counter,
+                     torch::Tensor status);
+void ep_wait_all(int64_t my_sig_ptr, int64_t W, int64_t slot, int64_t epoch, torch::Tensor status,
+                 int64_t wait_cycles);
 void tp_publish(std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch);
 torch::Tensor ag_gemm(std::vector<int64_t> shard_ptrs, int64_t Ml, torch::Tensor b, std::vector<int64_t> sig_ptrs,
                       int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
@@ -113,6 +122,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_signal", &lrl::p2p_signal);
   m.def("grouped_gemm", &lrl::grouped_gemm);
   m.def("grouped_gemm_status", &lrl::grouped_gemm_status);
+  m.def("ep_flag_slots", &lrl::ep_flag_slots);
+  m.def("ep_exchange_counts", &lrl::ep_exchange_counts);
+  m.def("ep_scatter_rows", &lrl::ep_scatter_rows);
+  m.def("ep_wait_all", &lrl::ep_wait_all);
   m.def("tp_publish", &lrl::tp_publish);
   m.def("ag_gemm", &lrl::ag_gemm);
   m.def("gemm_rs", &lrl::gemm_rs);

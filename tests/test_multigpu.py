@@ -234,3 +234,39 @@ def test_context_parallel_ring_attention():
     for rank, errs in res:
         for k, v in errs.items():
             assert v < 2e-2, (rank, k, v)
+
+
+def _ep_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.parallel.ep_check import ep_errors
+    kw = dict(T=512, H=256, F=128, E=8, k=2)
+    fused = ep_errors("cuda", torch.bfloat16, fused=True, **kw)
+    plain = ep_errors("cuda", torch.bfloat16, fused=False, **kw)
+    q.put((rank, fused, plain))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_nvlink_dispatch_combine():
+    """EP=2 MoE part: count exchange, dispatch and combine by peer stores,
+    grouped tcgen05 expert GEMMs; forward and backward against all experts on
+    one rank, as close as the NCCL all-to-all path."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29960 + os.getpid() % 9
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, fused, plain in res:
+        assert fused["fused"] and not plain["fused"]
+        for k in fused:
+            if k != "fused":
+                assert fused[k] < max(3 * plain[k], 3e-2), (rank, k, fused[k], plain[k])

@@ -5,7 +5,7 @@
 //   ag_gemm:  C[M, N] = AG(A)[M, K] @ B[N, K]^T.  A is sharded by rows: rank r
 //             holds rows [r*Ml, (r+1)*Ml) in its symmetric buffer.  The TMA
 //             producer loads every A tile straight from the owning rank's
-//             buffer (a plain, non-multicast tiled load of peer memory), so
+//             buffer (a plain tiled TMA load of peer memory, per CTA), so
 //             the gather overlaps the MMAs tile by tile.  Each rank walks the
 //             m-blocks starting at its own shard; before the first tile of a
 //             peer's shard, the producer waits (bounded) until that peer has
@@ -22,7 +22,6 @@
 // written with st.release.sys and read with ld.acquire.sys.  An expired wait
 // records 300 + code in the status word and the kernel unwinds (copies
 // drained, TMEM freed), so a dead or late rank is an error on the host.
-// No TMA load here uses .multicast::cluster.
 #include "../common.cuh"
 #include "tc_gemm.cuh"
 

@@ -10,7 +10,7 @@ shards.  On B200 both collectives are fused into the GEMM
 (``csrc/gemm/tp_gemm.cu``):
 
 * ``ag_linear``: the GEMM's TMA producer reads each A tile straight from the
-  rank that owns those rows (plain, non-multicast TMA loads over NVLink),
+  rank that owns those rows (plain per-CTA TMA tile loads over NVLink),
   starting with its own rows while peers' ready flags arrive;
 * ``linear_rs``: the GEMM epilogue stores each partial tile into the owning
   rank's receive slot, the owner sums the ``tp`` partials in fp32.

@@ -51,6 +51,8 @@ int64_t symm_signal_words();
 void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_t epoch, torch::Tensor counter);
 void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles);
 void p2p_signal(int64_t flag_ptr, int64_t epoch);
+torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit);
+int64_t skinny_gemm_status();
 torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets);
 int64_t grouped_gemm_status();
 int64_t ep_flag_slots();
@@ -120,6 +122,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_push", &lrl::p2p_push);
   m.def("p2p_wait", &lrl::p2p_wait);
   m.def("p2p_signal", &lrl::p2p_signal);
+  m.def("skinny_gemm", &lrl::skinny_gemm, py::arg("x"), py::arg("w"), py::arg("ksplit") = 0);
+  m.def("skinny_gemm_status", &lrl::skinny_gemm_status);
   m.def("grouped_gemm", &lrl::grouped_gemm);
   m.def("grouped_gemm_status", &lrl::grouped_gemm_status);
   m.def("ep_flag_slots", &lrl::ep_flag_slots);

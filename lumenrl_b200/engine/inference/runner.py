@@ -36,7 +36,7 @@ class ModelRunner:
     def _w(self, name: str) -> Tensor:
         return self.model.p(name).detach()
 
-    def _mlp(self, i: int, h: Tensor) -> Tensor:
+    def _mlp(self, i: int, h: Tensor, lin=ops.linear) -> Tensor:
         if self.args.is_moe_layer(i):
             from lumenrl_b200.models.moe import moe_forward
             prev = getattr(self.model, "routing_recorder", None)
@@ -46,11 +46,11 @@ class ModelRunner:
             finally:
                 self.model.routing_recorder = prev
             return out
-        return ops.linear(ops.swiglu(ops.linear(h, self._w(f"layers.{i}.w13"))), self._w(f"layers.{i}.w2"))
+        return lin(ops.swiglu(lin(h, self._w(f"layers.{i}.w13"))), self._w(f"layers.{i}.w2"))
 
-    def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor):
+    def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor, lin=ops.linear):
         a, c = self.args, self.cache
-        qkv = ops.linear(h, self._w(f"layers.{i}.wqkv"))
+        qkv = lin(h, self._w(f"layers.{i}.wqkv"))
         qn = self._w(f"layers.{i}.q_norm") if a.qk_norm else None
         kn = self._w(f"layers.{i}.k_norm") if a.qk_norm else None
         return ops.qk_norm_rope_cache(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
@@ -83,18 +83,18 @@ class ModelRunner:
         res = None
         for i in range(a.num_layers):
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
-            q, k, v = self._qkv(i, h, positions, slots)
+            q, k, v = self._qkv(i, h, positions, slots, ops.decode_linear)
             if shared is not None:
                 o = ops.paged_decode_attention_shared(q, c.k[i], c.v[i], block_table, seq_lens, shared[0], shared[1],
                                                       self.scale, c.k_scale[i], c.v_scale[i], shared[2], shared[3])
             else:
                 o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
                                                c.k_scale[i], c.v_scale[i], self.max_len)
-            x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
+            x = ops.decode_linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
-            x = self._mlp(i, h)
+            x = self._mlp(i, h, ops.decode_linear)
         h, _ = ops.add_rmsnorm(x, res, self._w("norm"), a.rms_norm_eps)
-        return ops.linear(h, self.model.lm_head.detach())
+        return ops.decode_linear(h, self.model.lm_head.detach())
 
 
 class DecodeGraph:

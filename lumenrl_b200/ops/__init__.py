@@ -466,6 +466,25 @@ def tc_gemm(a: Tensor, b: Tensor, out: Optional[Tensor] = None, accumulate: bool
     return ext().tc_gemm(a, b, None, 0 if out_dtype == torch.bfloat16 else 1, bn)
 
 
+def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
+    """x [M, K] @ w[N, K]^T for decode-size M (<= 256) on the weight-streaming
+    tcgen05 kernel (operands swapped, K split over a cluster, no library GEMM)."""
+    return ext().skinny_gemm(x, w, ksplit)
+
+
+# decode-step linears: "skinny" (own weight-streaming kernel) or "cublas"
+DECODE_GEMM = "skinny"
+
+
+def decode_linear(x: Tensor, w: Tensor) -> Tensor:
+    """No-grad linear of the rollout decode step (M = live sequences)."""
+    if (DECODE_GEMM == "skinny" and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+            and x.dim() == 2 and x.shape[0] <= 256 and x.shape[1] % 8 == 0 and x.is_contiguous()
+            and w.is_contiguous()):
+        return ext().skinny_gemm(x, w, 0)
+    return x @ w.t()
+
+
 def tc_gemm_status() -> int:
     """Error word of the tcgen05 GEMMs since the last call (0 = no error); a
     non-zero value names the role whose bounded wait expired."""

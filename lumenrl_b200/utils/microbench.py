@@ -101,6 +101,34 @@ def bench_attn(ns) -> dict:
             "plain_TBps": plain_bytes / t_plain / 1e9, "shared_TBps": shared_bytes / t_shared / 1e9}
 
 
+def bench_skinny(ns) -> dict:
+    """Decode-size GEMMs (M tokens x the model's projection shapes): the
+    weight-streaming tcgen05 kernel vs cuBLAS.  Each timed call reads a
+    different copy of the weight (copies > 256 MB in total), so weights come
+    from HBM as in a decode step, not from L2."""
+    from lumenrl_b200 import ops
+    M = ns.batch
+    out = []
+    for N, K in [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288), (151936, 4096)]:
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        nbytes = N * K * 2
+        copies = max(2, -(-(256 << 20) // nbytes) + 1)
+        ws = [(torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16) for _ in range(copies)]
+        it = {"i": 0}
+
+        def nxt():
+            it["i"] = (it["i"] + 1) % copies
+            return ws[it["i"]]
+        t_sk = _time(lambda: ops.skinny_linear(x, nxt()), ns.steps, ns.warmup)
+        t_cb = _time(lambda: x @ nxt().t(), ns.steps, ns.warmup)
+        err = (ops.skinny_linear(x, ws[0]).float() - (x.float() @ ws[0].float().t())).abs().max().item()
+        out.append({"M": M, "N": N, "K": K, "skinny_ms": t_sk, "cublas_ms": t_cb,
+                    "skinny_TBps": nbytes / t_sk / 1e9, "cublas_TBps": nbytes / t_cb / 1e9, "max_err": err})
+        del ws
+    from lumenrl_b200.ops.ext import ext
+    return {"op": "skinny_gemm", "status": int(ext().skinny_gemm_status()), "shapes": out}
+
+
 def bench_train(ns) -> dict:
     from lumenrl_b200 import ops
     m = _model(ns.model, True)
@@ -199,7 +227,7 @@ def bench_comm(ns) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "attn", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("what", choices=["decode", "attn", "skinny", "train", "logprob", "gemm", "comm"])
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prefix", type=int, default=512)
     ap.add_argument("--numel", type=int, default=8_200_000_000)
@@ -213,7 +241,7 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
-    fn = {"decode": bench_decode, "attn": bench_attn, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
           "comm": bench_comm}[ns.what]
     res = fn(ns)
     import os

@@ -4,6 +4,7 @@ import pytest
 import torch
 
 from lumenrl_b200 import ops
+from lumenrl_b200.ops.ext import ext
 
 pytestmark = pytest.mark.gpu
 
@@ -51,3 +52,20 @@ def test_tc_gemm_splitk(cuda, M, N, K):
         assert ops.tc_gemm_status() == 0
         ref = a.float() @ b.float().t()
         assert (c - ref).abs().max().item() <= 1e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("M", [1, 16, 33, 64, 100, 128, 200, 256])
+@pytest.mark.parametrize("N,K", [(6144, 4096), (1000, 72), (4096, 12288)])
+def test_skinny_gemm_decode_sizes(cuda, M, N, K):
+    """Weight-streaming GEMM (operands swapped, K split over a cluster with a
+    distributed-shared-memory reduction) against an fp32 reference."""
+    torch.manual_seed(M + N)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) / K ** 0.5).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    for ks in (0, 1, 2, 8):
+        y = ops.skinny_linear(x, w, ks)
+        torch.cuda.synchronize()
+        assert ext().skinny_gemm_status() == 0
+        assert y.shape == (M, N)
+        assert torch.allclose(y.float(), ref, atol=2e-2, rtol=2e-2), (ks, (y.float() - ref).abs().max())

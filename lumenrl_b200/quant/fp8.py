@@ -222,6 +222,11 @@ class FP8TrainingManager:
         qw, sw = quant_weight_128x128(w.to(torch.bfloat16))
         return (dequant_1x128(qx, sx).reshape(x.shape).to(x.dtype), dequant_128x128(qw, sw).to(w.dtype))
 
+    def reset_fp8_state(self, model=None) -> None:
+        """Per-step reset hook.  Scales here are computed from each tensor's
+        current blocks (no amax history), so there is no state to clear."""
+        return None
+
     def fake_quant_grad(self, g: Tensor) -> Tensor:
         qg, sg = quant_act_1x128(g.reshape(-1, g.shape[-1]).contiguous().to(torch.bfloat16), E5M2)
         return dequant_1x128(qg, sg).reshape(g.shape).to(g.dtype)

@@ -48,4 +48,5 @@ setup(
     ext_modules=ext_modules(),
     cmdclass=cmdclass(),
     python_requires=">=3.10",
+    entry_points={"verl.plugins": ["lumenrl_b200 = lumenrl_b200.plugin.verl:register"]},
 )

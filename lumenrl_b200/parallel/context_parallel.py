@@ -77,7 +77,7 @@ def _block_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, lse: Tens
         B, _, Tq, _ = q.shape
         Tk = k.shape[2]
         do, q, ke, ve, o = do.contiguous(), q.contiguous(), ke.contiguous(), ve.contiguous(), o.contiguous()
-        empty = torch.empty(0, device=q.device, dtype=torch.int64)
+        empty = torch.empty(0, device=q.device, dtype=torch.int32)
         dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
             do, q, ke, ve, o, lse.to(torch.float32), empty, empty, Tq, Tk, 0.0, causal,
             torch.zeros((), dtype=torch.int64, device=q.device), torch.zeros((), dtype=torch.int64, device=q.device),

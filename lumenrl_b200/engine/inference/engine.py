@@ -72,7 +72,8 @@ class _RoutingRecorder:
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
-                 use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True) -> None:
+                 use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True,
+                 fp8_rollout=None) -> None:
         self.model = model
         self.args = model.args
         self.device = model.flat.device
@@ -91,6 +92,12 @@ class RolloutEngine:
         self.cache = PagedKVCache(spec, nblocks, self.device)
         self.runner = ModelRunner(model, self.cache)
         self.runner.max_len = max_model_len
+        if fp8_rollout is not None and fp8_rollout.is_fp8_enabled():
+            # W8A8 blockwise rollout (128x128 E4M3 weight blocks, 1x128 activation
+            # blocks); requantised from the bf16 weights at every weight sync
+            from lumenrl_b200.quant.fp8 import FP8RolloutQuantizer
+            self.runner.fp8 = FP8RolloutQuantizer(fp8_rollout, self.args.num_layers)
+            self.runner.fp8.quantize_model(model)
         self._graphs: dict[tuple, DecodeGraph] = {}
         self.weight_version = 0
 
@@ -112,6 +119,9 @@ class RolloutEngine:
         Separated: copy a full bf16 flat buffer in (one contiguous copy)."""
         if flat is not None and flat.data_ptr() != self.model.flat.data_ptr():
             self.model.flat.copy_(flat, non_blocking=True)
+        if self.runner.fp8 is not None:
+            self.runner.fp8.quantize_model(self.model)
+            self._graphs.clear()   # graphs hold the previous quantised buffers
         self.weight_version = self.weight_version + 1 if version is None else version
 
     # -- generation ------------------------------------------------------------------

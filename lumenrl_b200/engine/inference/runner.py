@@ -32,11 +32,18 @@ class ModelRunner:
         self.scale = 1.0 / math.sqrt(self.args.head_dim)
         self.routing_recorder = None
         self.max_len = 0   # static bound on context length (set by the engine)
+        self.fp8 = None    # FP8RolloutQuantizer: W8A8 blockwise linears when set
+
+    def _lin(self, x: Tensor, name: str, decode: bool) -> Tensor:
+        w = self._w(name)
+        if self.fp8 is not None and name in self.fp8.weights:
+            return self.fp8.linear(name, x, w)
+        return ops.decode_linear(x, w) if decode else ops.linear(x, w)
 
     def _w(self, name: str) -> Tensor:
         return self.model.p(name).detach()
 
-    def _mlp(self, i: int, h: Tensor, lin=ops.linear) -> Tensor:
+    def _mlp(self, i: int, h: Tensor, decode: bool = False) -> Tensor:
         if self.args.is_moe_layer(i):
             from lumenrl_b200.models.moe import moe_forward
             prev = getattr(self.model, "routing_recorder", None)
@@ -46,11 +53,11 @@ class ModelRunner:
             finally:
                 self.model.routing_recorder = prev
             return out
-        return lin(ops.swiglu(lin(h, self._w(f"layers.{i}.w13"))), self._w(f"layers.{i}.w2"))
+        return self._lin(ops.swiglu(self._lin(h, f"layers.{i}.w13", decode)), f"layers.{i}.w2", decode)
 
-    def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor, lin=ops.linear):
+    def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor, decode: bool = False):
         a, c = self.args, self.cache
-        qkv = lin(h, self._w(f"layers.{i}.wqkv"))
+        qkv = self._lin(h, f"layers.{i}.wqkv", decode)
         qn = self._w(f"layers.{i}.q_norm") if a.qk_norm else None
         kn = self._w(f"layers.{i}.k_norm") if a.qk_norm else None
         return ops.qk_norm_rope_cache(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
@@ -65,7 +72,7 @@ class ModelRunner:
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
             q, k, v = self._qkv(i, h, positions, slots)
             o = ops.attention_varlen(q, k, v, cu_seqlens, max_len, causal=True, scale=self.scale)
-            x = ops.linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
+            x = self._lin(o.reshape(o.shape[0], -1), f"layers.{i}.wo", False)
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h)
         last = cu_seqlens[1:] - 1
@@ -83,16 +90,16 @@ class ModelRunner:
         res = None
         for i in range(a.num_layers):
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
-            q, k, v = self._qkv(i, h, positions, slots, ops.decode_linear)
+            q, k, v = self._qkv(i, h, positions, slots, True)
             if shared is not None:
                 o = ops.paged_decode_attention_shared(q, c.k[i], c.v[i], block_table, seq_lens, shared[0], shared[1],
                                                       self.scale, c.k_scale[i], c.v_scale[i], shared[2], shared[3])
             else:
                 o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
                                                c.k_scale[i], c.v_scale[i], self.max_len)
-            x = ops.decode_linear(o.reshape(o.shape[0], -1), self._w(f"layers.{i}.wo"))
+            x = self._lin(o.reshape(o.shape[0], -1), f"layers.{i}.wo", True)
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
-            x = self._mlp(i, h, ops.decode_linear)
+            x = self._mlp(i, h, True)
         h, _ = ops.add_rmsnorm(x, res, self._w("norm"), a.rms_norm_eps)
         return ops.decode_linear(h, self.model.lm_head.detach())
 

@@ -104,12 +104,23 @@ class RLTrainer:
         kv_dtype = torch.float8_e4m3fn if str(vc.kv_cache_dtype).startswith("fp8") else torch.bfloat16
         self.rollout = RolloutEngine(self.actor.model, max_num_seqs=prompts_per_rank * self.group,
                                      max_model_len=max_len, kv_cache_bytes=self.spec.kv_cache_bytes,
-                                     use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype)
+                                     use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype,
+                                     fp8_rollout=self._fp8_rollout_config(c))
         self.data = SyntheticPrompts(self.spec.prompt_len, self.spec.prompt_low, self.spec.prompt_high, c.seed)
         self.reward_fn = get_reward_fn(self.spec.reward)
         self.timer = PhaseTimer(st.device)
         self.io_bytes = {"h2d": 0, "d2h": 0}
         return self
+
+    @staticmethod
+    def _fp8_rollout_config(c):
+        """quantization.rollout.precision = fp8 -> blockwise W8A8 rollout."""
+        from lumenrl_b200.quant.fp8 import FP8Config
+        r = c.quantization.rollout
+        if "fp8" not in str(getattr(r, "precision", "bf16")).lower():
+            return None
+        return FP8Config(precision=r.precision, num_first_layers_in_bf16=r.num_first_layers_in_bf16,
+                         num_last_layers_in_bf16=r.num_last_layers_in_bf16)
 
     # ------------------------------------------------------------------ step
     def _rollout(self, step: int) -> DataProto:

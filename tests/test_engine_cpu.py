@@ -94,3 +94,31 @@ def test_shared_prefix_group_and_fallback():
     a = ops.paged_decode_attention_shared(q, kc, vc, bt, lens, torch.full((B,), 16, dtype=torch.int32), 2, 0.25)
     b = ops.paged_decode_attention(q, kc, vc, bt, lens, 0.25)
     assert torch.allclose(a, b)
+
+
+def test_fp8_rollout_close_to_bf16_and_requantised_on_sync():
+    """W8A8 blockwise rollout: log-probs stay close to the full-precision
+    training forward, and a weight update re-quantises the rollout weights."""
+    from lumenrl_b200.quant.fp8 import FP8Config
+    m = _model(tiny_llama())
+    eng = RolloutEngine(m, max_num_seqs=4, max_model_len=64, block_size=16, use_cuda_graph=False,
+                        fp8_rollout=FP8Config(precision="fp8"))
+    assert len(eng.runner.fp8.weights) == 4 * m.args.num_layers
+    prompts = [[5, 6, 7, 8, 9, 10, 11, 12]]
+    out = eng.generate(prompts, SamplingParams(max_new_tokens=10, n=2, seed=3, eos_token_id=None))
+    diffs = []
+    for r in range(2):
+        seq = prompts[0] + out.responses[r].tolist()
+        ids = torch.tensor(seq)
+        h = m.forward_packed(ids, torch.arange(len(seq)), torch.tensor([0, len(seq)]), len(seq))
+        lp, _ = ops.token_logprob(h[:-1], m.lm_head, ids[1:])
+        diffs.append((lp[len(prompts[0]) - 1:] - out.logprobs[r]).abs().mean())
+    assert max(diffs) < 0.05, diffs
+    name = "layers.0.wqkv"
+    before, before_s = (t.clone() for t in eng.runner.fp8.weights[name])
+    with torch.no_grad():
+        m.p(name).mul_(2.0)
+    eng.update_weights()
+    after_q, after_s = eng.runner.fp8.weights[name]
+    assert torch.equal(after_q.float(), before.float())   # same fp8 codes ...
+    assert torch.allclose(after_s, 2 * before_s)          # ... and the scales follow the doubled weights

@@ -1,9 +1,13 @@
 """Packed (varlen) causal attention for training and prefill.
 
-``flash_attention_varlen`` runs the sequences of a packed batch through
-PyTorch's fused SDPA (one call per sequence, GQA native).  The hand-written
-tcgen05 kernel (``csrc/attn/fa_varlen``) replaces this when built; until then
-this path is the library baseline for the attention share of the step.
+``flash_attention_varlen`` runs the whole packed batch in one call of the
+flash-attention varlen kernel that ships with PyTorch
+(``aten._flash_attention_forward`` / ``_backward``: cumulative sequence
+lengths, native GQA, log-sum-exp kept for the backward).  No per-sequence
+loop and no device->host read of ``cu_seqlens``: ``max_seqlen`` comes from the
+caller, who packed the batch on the host.  This is the library attention of
+the training step (the reference also calls a library kernel here,
+``engine/training/packing.py:363-421``).
 """
 
 from __future__ import annotations
@@ -13,17 +17,40 @@ import torch.nn.functional as F
 from torch import Tensor
 
 
+class _VarlenFlash(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu, max_len, causal, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        out, lse, seed, offset, _ = torch.ops.aten._flash_attention_forward(
+            q, k, v, cu, cu, max_len, max_len, 0.0, causal, False, scale=scale)
+        ctx.save_for_backward(q, k, v, out, lse, cu, seed, offset)
+        ctx.max_len, ctx.causal, ctx.scale = max_len, causal, scale
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, out, lse, cu, seed, offset = ctx.saved_tensors
+        dq, dk, dv = torch.ops.aten._flash_attention_backward(
+            do.contiguous(), q, k, v, out, lse, cu, cu, ctx.max_len, ctx.max_len, 0.0, ctx.causal, seed, offset,
+            scale=ctx.scale)
+        return dq, dk, dv, None, None, None, None
+
+
 def flash_attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_seqlen: int,
                            causal: bool = True, scale: float | None = None) -> Tensor:
-    cu = cu_seqlens.tolist()
+    """q [T, Hq, D], k/v [T, Hk, D] (bf16/fp16, CUDA) packed by ``cu_seqlens``."""
+    if scale is None:
+        scale = q.shape[-1] ** -0.5
+    cu = cu_seqlens.to(torch.int32)
+    if q.dtype in (torch.bfloat16, torch.float16):
+        return _VarlenFlash.apply(q, k, v, cu, int(max_seqlen), causal, float(scale))
+    # fp32 fallback: per-sequence SDPA
+    bounds = cu.tolist()
     outs = []
-    for i in range(len(cu) - 1):
-        a, b = cu[i], cu[i + 1]
-        if b <= a:
-            continue
-        qi = q[a:b].transpose(0, 1).unsqueeze(0)
-        ki = k[a:b].transpose(0, 1).unsqueeze(0)
-        vi = v[a:b].transpose(0, 1).unsqueeze(0)
-        o = F.scaled_dot_product_attention(qi, ki, vi, is_causal=causal, scale=scale, enable_gqa=True)
-        outs.append(o.squeeze(0).transpose(0, 1))
-    return torch.cat(outs, 0) if len(outs) > 1 else outs[0].contiguous()
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        if b > a:
+            o = F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None], k[a:b].transpose(0, 1)[None],
+                                               v[a:b].transpose(0, 1)[None], is_causal=causal, scale=scale,
+                                               enable_gqa=True)
+            outs.append(o[0].transpose(0, 1))
+    return torch.cat(outs, 0)

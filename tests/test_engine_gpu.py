@@ -63,3 +63,20 @@ def test_shared_and_plain_decode_agree(cuda):
     assert torch.equal(a.responses[:, :2], b.responses[:, :2])
     same = (a.responses == b.responses).all(1)
     assert (a.logprobs[same] - b.logprobs[same]).abs().max().item() < 0.05
+
+
+def test_fp8_rollout_graph_decode(cuda):
+    """W8A8 blockwise rollout (tcgen05 FP8 GEMM) inside the CUDA-graph decode
+    step stays close to the bf16 training forward."""
+    from lumenrl_b200.quant.fp8 import FP8Config
+    m = _model(cuda)
+    eng = RolloutEngine(m, max_num_seqs=16, max_model_len=256, block_size=16, use_cuda_graph=True,
+                        fp8_rollout=FP8Config(precision="fp8"))
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(3, 2048, (64,), generator=g).tolist()]
+    out = eng.generate(prompts, SamplingParams(max_new_tokens=32, n=8, seed=7, eos_token_id=None))
+    with torch.no_grad():
+        diffs = [(_teacher_forced(m, prompts[0], out.responses[r].tolist()) - out.logprobs[r]).abs().mean().item()
+                 for r in range(8)]
+    assert max(diffs) < 0.1, diffs
+    assert ops.fp8_gemm_status() == 0

@@ -36,11 +36,17 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ float ld_dsmem(const float* local, uint32_t rank) {
-  uint32_t addr = smem_addr(local), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(addr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(remote) : "memory");
+// 4 consecutive fp32 of CTA `rank`'s copy of `local` (distributed shared
+// memory).  Volatile keeps the loads after the cluster barrier; without a
+// memory clobber the loads of all ranks are issued back to back and are in
+// flight together.
+__device__ __forceinline__ float4 ld_dsmem4(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote));
   return v;
 }
 
@@ -173,20 +179,39 @@ __global__ void __launch_bounds__(kThreadsS, 1)
   }
   if (ksplit > 1) cluster_sync();
   else __syncthreads();
-  // reduce over the cluster: this CTA owns elements [part * chunk, ...)
-  const int total = MP * kBM;
-  const int chunk = (total + ksplit - 1) / ksplit;
-  const int e0 = part * chunk, e1 = min(total, e0 + chunk);
-  for (int e = e0 + threadIdx.x; e < e1; e += kThreadsS) {
+  // reduce over the cluster: this CTA owns 4-float groups [part * chunk, ...)
+  const int total4 = MP * kBM / 4;
+  const int chunk = (total4 + ksplit - 1) / ksplit;
+  const int g0 = part * chunk, g1 = min(total4, g0 + chunk);
+  for (int g = g0 + threadIdx.x; g < g1; g += kThreadsS) {
+    const int e = g * 4;
     const int m = e / kBM, nl = e % kBM;
-    float acc = 0.f;
+    float4 acc;
     if (ksplit > 1) {
-      for (int r = 0; r < ksplit; ++r) acc += ld_dsmem(red + e, (uint32_t)r);
+      float4 parts[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < ksplit) parts[r] = ld_dsmem4(red + e, (uint32_t)r);
+      acc = parts[0];
+#pragma unroll
+      for (int r = 1; r < 8; ++r)
+        if (r < ksplit) {
+          acc.x += parts[r].x;
+          acc.y += parts[r].y;
+          acc.z += parts[r].z;
+          acc.w += parts[r].w;
+        }
     } else {
-      acc = red[e];
+      acc = *reinterpret_cast<const float4*>(red + e);
     }
     const int n = n0 + nl;
-    if (m < M && n < N) Y[(int64_t)m * N + n] = __float2bfloat16(acc);
+    if (m < M) {
+      __nv_bfloat16* p = Y + (int64_t)m * N + n;
+      const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (n + j < N) p[j] = __float2bfloat16(a[j]);
+    }
   }
   if (ksplit > 1) cluster_sync();  // peers may still read this CTA's partial
   __syncthreads();

@@ -37,6 +37,13 @@ torch::Tensor paged_decode_attn_shared(torch::Tensor q, torch::Tensor kc, torch:
                                        torch::Tensor block_table, torch::Tensor seq_lens, torch::Tensor prefix_len,
                                        int64_t group, double scale, double k_scale, double v_scale,
                                        int64_t max_prefix_hint, int64_t max_suffix_hint);
+torch::Tensor paged_decode_attn_tma(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_table,
+                                    torch::Tensor seq_lens, double scale, double v_scale, int64_t max_len_hint);
+torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, torch::Tensor vc,
+                                           torch::Tensor block_table, torch::Tensor seq_lens,
+                                           torch::Tensor prefix_len, int64_t group, double scale, double v_scale,
+                                           int64_t max_prefix_hint, int64_t max_suffix_hint);
+int64_t decode_tma_status();
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots,
                double inv_ks, double inv_vs);
 torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
@@ -108,6 +115,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_table"), py::arg("seq_lens"), py::arg("prefix_len"), py::arg("group"), py::arg("scale"),
         py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0, py::arg("max_prefix_hint") = 0,
         py::arg("max_suffix_hint") = 0);
+  m.def("paged_decode_attn_tma", &lrl::paged_decode_attn_tma);
+  m.def("paged_decode_attn_shared_tma", &lrl::paged_decode_attn_shared_tma);
+  m.def("decode_tma_status", &lrl::decode_tma_status);
   m.def("kv_append", &lrl::kv_append);
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,
         py::arg("bn") = 0);

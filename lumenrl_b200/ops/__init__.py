@@ -12,6 +12,8 @@ from __future__ import annotations
 import math
 from typing import Optional
 
+import os
+
 import torch
 from torch import Tensor
 
@@ -242,6 +244,16 @@ def attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_se
     return flash_attention_varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale)
 
 
+# decode attention kernel for bf16 caches with 64-token pages: "tma" (pages
+# streamed by a producer warp with cp.async.bulk.tensor) or "cpasync"
+DECODE_ATTN = os.environ.get("LRL_DECODE_ATTN", "cpasync")
+
+
+def _tma_ok(q: Tensor, k_cache: Tensor) -> bool:
+    return (DECODE_ATTN == "tma" and q.is_cuda and k_cache.dtype == torch.bfloat16 and k_cache.dim() == 4
+            and k_cache.shape[1] == 64 and k_cache.shape[3] == 128 and k_cache.is_contiguous())
+
+
 def paged_decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_table: Tensor, seq_lens: Tensor,
                            scale: float, k_scale: float = 1.0, v_scale: float = 1.0, max_len: int = 0) -> Tensor:
     """q [B,Hq,D] against the paged caches; ``max_len`` (static upper bound of
@@ -251,6 +263,9 @@ def paged_decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, block_ta
         return ref.paged_decode_attention(q, k_cache.to(q.dtype) * k_scale if k_cache.dtype != q.dtype else k_cache,
                                           v_cache.to(q.dtype) * v_scale if v_cache.dtype != q.dtype else v_cache,
                                           block_table, seq_lens, scale)
+    if _tma_ok(q, k_cache):
+        return ext().paged_decode_attn_tma(q, k_cache, v_cache, block_table, seq_lens, scale * k_scale, v_scale,
+                                           max_len)
     return ext().paged_decode_attn(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale, max_len)
 
 
@@ -276,6 +291,9 @@ def paged_decode_attention_shared(q: Tensor, k_cache: Tensor, v_cache: Tensor, b
     device value on the host and is CUDA-graph safe."""
     if not _cuda(q):
         return paged_decode_attention(q, k_cache, v_cache, block_table, seq_lens, scale, k_scale, v_scale)
+    if _tma_ok(q, k_cache):
+        return ext().paged_decode_attn_shared_tma(q, k_cache, v_cache, block_table, seq_lens, prefix_len, group,
+                                                  scale * k_scale, v_scale, max_prefix, max_suffix)
     return ext().paged_decode_attn_shared(q, k_cache, v_cache, block_table, seq_lens, prefix_len, group, scale,
                                           k_scale, v_scale, max_prefix, max_suffix)
 
@@ -474,7 +492,7 @@ def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
 
 # decode-step linears: "cublas" or "skinny" (own weight-streaming kernel;
 # correct, at cuBLAS parity on the decode shapes so far, so not the default)
-DECODE_GEMM = "cublas"
+DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "cublas")
 
 
 def decode_linear(x: Tensor, w: Tensor) -> Tensor:

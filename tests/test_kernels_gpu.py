@@ -322,3 +322,44 @@ def test_attention_varlen_fwd_bwd(cuda):
     close(o, ref, 2e-2, 2e-2)
     for g, r in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
         assert ((g.float() - r).abs().max() / r.abs().max()).item() < 2e-2
+
+
+@pytest.mark.parametrize("shared", [False, True])
+@pytest.mark.parametrize("n,Hq,Hk,plen,maxnew", [(8, 32, 8, 512, 300), (4, 32, 8, 130, 70), (16, 16, 4, 64, 129),
+                                                 (2, 8, 1, 0, 65)])
+def test_decode_attention_tma_pages(cuda, monkeypatch, shared, n, Hq, Hk, plen, maxnew):
+    """TMA-fed decode attention (64-token pages streamed by a producer warp)
+    against the fp32 reference, per-row and shared-prefix."""
+    monkeypatch.setattr(ops, "DECODE_ATTN", "tma")
+    torch.manual_seed(2)
+    D, bs, P = 128, 64, 3
+    B = P * n
+    full = plen // bs
+    need = (plen + maxnew + bs - 1) // bs
+    nblocks = 1 + P * full + B * (need - full) + 2
+    perm = (torch.randperm(nblocks - 1) + 1).tolist()
+    bt = torch.zeros(B, need + 1, dtype=torch.int32)
+    for i in range(P):
+        sh = [perm.pop() for _ in range(full)]
+        for j in range(n):
+            bt[i * n + j, :full] = torch.tensor(sh, dtype=torch.int32)
+            bt[i * n + j, full:need] = torch.tensor([perm.pop() for _ in range(need - full)], dtype=torch.int32)
+    bt = bt.to(cuda)
+    lens = (plen + torch.randint(1, maxnew + 1, (B,))).to(torch.int32)
+    lens[0] = plen + maxnew
+    lens = lens.to(cuda)
+    kc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(torch.bfloat16)
+    vc = torch.randn(nblocks, bs, Hk, D, device=cuda).to(torch.bfloat16)
+    q = torch.randn(B, Hq, D, device=cuda, dtype=torch.bfloat16)
+    sc = 1 / math.sqrt(D)
+    if shared:
+        prefix = torch.full((B,), full * bs, dtype=torch.int32, device=cuda)
+        out = ops.paged_decode_attention_shared(q, kc, vc, bt, lens, prefix, ops.shared_prefix_group(n, Hq // Hk),
+                                                sc, 1.0, 1.0, full * bs, maxnew + bs)
+    else:
+        out = ops.paged_decode_attention(q, kc, vc, bt, lens, sc, 1.0, 1.0, plen + maxnew)
+    torch.cuda.synchronize()
+    from lumenrl_b200.ops.ext import ext
+    assert ext().decode_tma_status() == 0
+    out_r = ref.paged_decode_attention(q.cpu(), kc.float().cpu(), vc.float().cpu(), bt.cpu(), lens.cpu(), sc)
+    close(out, out_r, 2e-2, 2e-2)

@@ -15,9 +15,29 @@ _ERR: Exception | None = None
 LAUNCHES = [0]   # kernels of this extension launched (graph replays add their captured count)
 
 
+# host-only entry points (no kernel) and ops that launch two kernels
+_NO_KERNEL = {"symm_malloc", "symm_open", "symm_close", "symm_free", "symm_tensor", "symm_signal_words",
+              "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "grouped_gemm_status", "decode_tma_status"}
+_TWO_KERNELS = {"paged_decode_attn_shared", "paged_decode_attn_tma", "paged_decode_attn_shared_tma", "gemm_rs"}
+
+
+def _kernels(name: str, a: tuple) -> int:
+    if name in _NO_KERNEL:
+        return 0
+    if name in _TWO_KERNELS:
+        return 2
+    if name == "paged_decode_attn":     # + the split combine, unless one split covers the context
+        return 2
+    if name == "sample":                # split-row sampler (top_p = 1, bf16, large vocab) is two kernels
+        logits, top_p = a[0], a[2]
+        return 2 if (top_p >= 1.0 and str(logits.dtype) == "torch.bfloat16" and logits.shape[-1] >= 16384) else 1
+    return 1
+
+
 class _Counted:
-    """Proxy that counts launches of the extension's kernels.  Each op call is
-    one kernel launch except the split decode attention (two)."""
+    """Proxy that counts the kernels the extension launches (an estimate for
+    the split decode attention, whose combine pass is skipped when a single
+    split covers the context)."""
 
     def __init__(self, mod) -> None:
         self._mod = mod
@@ -28,7 +48,7 @@ class _Counted:
             return fn
 
         def call(*a, **k):
-            LAUNCHES[0] += 1
+            LAUNCHES[0] += _kernels(name, a)
             return fn(*a, **k)
         return call
 

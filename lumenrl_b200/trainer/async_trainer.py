@@ -108,6 +108,9 @@ class AsyncRLTrainer(RLTrainer):
         dtype = self.actor.model.flat.dtype
         self.rollout_model = Qwen3Model(self.model_args, device=st.device, dtype=dtype, requires_grad=False)
         self.rollout_model.flat.copy_(self.actor.model.flat)
+        # the base class built a colocated engine on the actor's buffer: free its
+        # KV pool before the separated engine (own weight copy) replaces it
+        self.rollout.sleep(release_memory=True)
         self.rollout = RolloutEngine(self.rollout_model, max_num_seqs=self.prompts_per_rank * self.group,
                                      max_model_len=self.spec.prompt_len + self.spec.max_new_tokens,
                                      use_cuda_graph=False)

@@ -245,8 +245,9 @@ def attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_se
 
 
 # decode attention kernel for bf16 caches with 64-token pages: "tma" (pages
-# streamed by a producer warp with cp.async.bulk.tensor) or "cpasync"
-DECODE_ATTN = os.environ.get("LRL_DECODE_ATTN", "cpasync")
+# streamed by a producer warp with cp.async.bulk.tensor; 5.85 vs 5.31 TB/s at
+# 64 x 1.5K context) or "cpasync" (the original kernel)
+DECODE_ATTN = os.environ.get("LRL_DECODE_ATTN", "tma")
 
 
 def _tma_ok(q: Tensor, k_cache: Tensor) -> bool:
@@ -490,14 +491,18 @@ def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
     return ext().skinny_gemm(x, w, ksplit)
 
 
-# decode-step linears: "cublas" or "skinny" (own weight-streaming kernel;
-# correct, at cuBLAS parity on the decode shapes so far, so not the default)
-DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "cublas")
+# decode-step linears: "auto" (own weight-streaming kernel for weights up to
+# 32 M elements, where it beats cuBLAS at M=64: 15.1 vs 18.5 us on 4096x4096;
+# cuBLAS above, where cuBLAS is 2-4 % faster), "skinny" or "cublas"
+DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "auto")
 
 
 def decode_linear(x: Tensor, w: Tensor) -> Tensor:
     """No-grad linear of the rollout decode step (M = live sequences)."""
-    if (DECODE_GEMM == "skinny" and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+    mode = DECODE_GEMM
+    if mode == "auto":
+        mode = "skinny" if w.numel() <= (32 << 20) else "cublas"
+    if (mode == "skinny" and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
             and x.dim() == 2 and x.shape[0] <= 256 and x.shape[1] % 8 == 0 and x.is_contiguous()
             and w.is_contiguous()):
         return ext().skinny_gemm(x, w, 0)

@@ -129,6 +129,34 @@ def bench_skinny(ns) -> dict:
     return {"op": "skinny_gemm", "status": int(ext().skinny_gemm_status()), "shapes": out}
 
 
+def bench_attn_train(ns) -> dict:
+    """Packed causal attention forward + backward (training shapes: --rows
+    sequences of --seq tokens, the model's heads) for each backend."""
+    from lumenrl_b200 import ops
+    from lumenrl_b200.ops import attention as A
+    args = _model_args(ns.model)
+    T = ns.rows * ns.seq
+    cu = torch.arange(0, T + 1, ns.seq, dtype=torch.int32, device="cuda")
+    q = torch.randn(T, args.num_heads, args.head_dim, device="cuda").to(torch.bfloat16).requires_grad_(True)
+    k = torch.randn(T, args.num_kv_heads, args.head_dim, device="cuda").to(torch.bfloat16).requires_grad_(True)
+    v = torch.randn_like(k).requires_grad_(True)
+    do = torch.randn_like(q)
+    res = {"op": "train_attention", "tokens": T, "seq": ns.seq}
+    flops = 4 * ns.rows * (ns.seq * ns.seq / 2) * args.num_heads * args.head_dim * 3.5  # fwd + bwd (2.5x)
+    for be in ("flash", "cudnn"):
+        A.TRAIN_ATTN = be
+        def step():
+            o = ops.attention_varlen(q, k, v, cu, ns.seq, causal=True, scale=args.head_dim ** -0.5)
+            o.backward(do)
+        try:
+            t = _time(step, ns.steps, ns.warmup)
+            res[be + "_ms"] = t
+            res[be + "_tflops"] = flops / t / 1e9
+        except Exception as e:  # noqa: BLE001 - report a backend that is not available
+            res[be + "_error"] = repr(e)[:200]
+    return res
+
+
 def bench_train(ns) -> dict:
     from lumenrl_b200 import ops
     m = _model(ns.model, True)
@@ -227,7 +255,7 @@ def bench_comm(ns) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "attn", "skinny", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm"])
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prefix", type=int, default=512)
     ap.add_argument("--numel", type=int, default=8_200_000_000)
@@ -241,7 +269,7 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
           "comm": bench_comm}[ns.what]
     res = fn(ns)
     import os

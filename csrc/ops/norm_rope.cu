@@ -93,15 +93,19 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
 
 // ---------------------------------------------------------------- RMSNorm bwd
 // dx = r * (g - xh * mean(g * xh)),  g = w * dy,  xh = x * r;  dw += dy * xh
-__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+// Each CTA walks `rows_per_cta` rows and writes its dw partial to row
+// blockIdx.x of `dw` (the host sums the partials), so no two CTAs contend on
+// the same words.
+template <int C>
+__global__ void __launch_bounds__(1024) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int64_t T, int H,
                                    int rows_per_cta) {
   __shared__ float red[32];
-  float acc[kMaxChunks][8];
-  float wf[kMaxChunks][8];
+  float acc[C][8];
+  float wf[C][8];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
@@ -111,10 +115,10 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
   for (int64_t row = r0; row < r0 + rows_per_cta && row < T; ++row) {
     const int64_t base = row * H;
     const float r = rstd[row];
-    float xh[kMaxChunks][8], g[kMaxChunks][8];
+    float xh[C][8], g[C][8];
     float dot = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < C; ++c) {
       const int col = (c * blockDim.x + threadIdx.x) * 8;
       if (col < H) {
         float d[8];
@@ -131,7 +135,7 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     }
     dot = block_sum(dot, red) / H;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < C; ++c) {
       const int col = (c * blockDim.x + threadIdx.x) * 8;
       if (col < H) {
         float o[8];
@@ -141,12 +145,14 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
       }
     }
   }
+  float* part = dw + (int64_t)blockIdx.x * H;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
     if (col < H) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) atomicAdd(dw + col + i, acc[c][i]);
+      for (int i = 0; i < 8; i += 4)
+        *reinterpret_cast<float4*>(part + col + i) = make_float4(acc[c][i], acc[c][i + 1], acc[c][i + 2], acc[c][i + 3]);
     }
   }
 }
@@ -162,11 +168,20 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   const int64_t T = x.numel() / H;
   auto dx = torch::empty_like(x);
   if (T == 0) return dx;
-  const int rows = 32;
+  TORCH_CHECK(H % 8 == 0, "rmsnorm_bwd: H % 8");
+  // one 8-wide chunk per thread where H allows (H <= 8192), ~4 CTAs per SM of rows
+  const bool one = H <= 8 * 1024;
+  const int threads = one ? std::max(32, ((H / 8 + 31) / 32) * 32) : 1024;
+  TORCH_CHECK(one || H <= 1024 * kMaxChunks * 8, "rmsnorm_bwd: H too large");
+  const int64_t want = 4 * (int64_t)num_sms();
+  const int rows = (int)std::max<int64_t>(1, (T + want - 1) / want);
   const int64_t grid = (T + rows - 1) / rows;
-  rmsnorm_bwd_kernel<<<grid, row_threads(H), 0, stream()>>>(
+  auto part = torch::empty({grid, H}, x.options().dtype(at::kFloat));
+  auto kern = one ? rmsnorm_bwd_kernel<1> : rmsnorm_bwd_kernel<kMaxChunks>;
+  kern<<<grid, threads, 0, stream()>>>(
       (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
-      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), T, H, rows);
+      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, rows);
+  dw.add_(part.sum(0));
   return dx;
 }
 
@@ -352,10 +367,20 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dq, co
     }
   }
   if (kind < 2 && has_norm) {
+    // sum the block's warps in shared memory first: one atomic per element
+    // per block instead of one per warp (every warp hits the same HD words)
+    __shared__ float red_w[8][HD];
+    const int w = threadIdx.x >> 5;
 #pragma unroll
     for (int i = 0; i < P; ++i) {
-      atomicAdd(dwp + lane * P + i, alo[i]);
-      atomicAdd(dwp + HALF + lane * P + i, ahi[i]);
+      red_w[w][lane * P + i] = alo[i];
+      red_w[w][HALF + lane * P + i] = ahi[i];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < HD; e += blockDim.x) {
+      float acc = 0.f;
+      for (int ww = 0; ww < (int)(blockDim.x >> 5); ++ww) acc += red_w[ww][e];
+      atomicAdd(dwp + e, acc);
     }
   }
 }

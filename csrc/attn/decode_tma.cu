@@ -312,6 +312,8 @@ __global__ void __launch_bounds__(kThreadsT) decode_tma_kernel(
     const __nv_bfloat16* __restrict__ q, const __grid_constant__ KVMaps maps, const int* __restrict__ block_table,
     const int* __restrict__ seq_lens, float* __restrict__ part_o, float* __restrict__ part_lse, int Hq, int Hk,
     int max_blocks, int pps, float scale_log2, float v_scale, int* err_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -335,6 +337,8 @@ __global__ void __launch_bounds__(kThreadsT) cascade_tma_kernel(
     const int* __restrict__ seq_lens, const int* __restrict__ prefix_len, float* __restrict__ part_o,
     float* __restrict__ part_lse, int B, int Hq, int Hk, int max_blocks, int group, int psplit, int ssplit, int pps,
     float scale_log2, float v_scale, int* err_out) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int G = Hq / Hk;
@@ -366,6 +370,8 @@ __global__ void __launch_bounds__(kThreadsT) cascade_tma_kernel(
 
 __global__ void combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                __nv_bfloat16* __restrict__ out, int nsplit, int B, int Hq) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x, qh = blockIdx.y, col = threadIdx.x;
   float mx = -INFINITY;
   for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, part_lse[((int64_t)s * B + b) * Hq + qh]);
@@ -462,12 +468,12 @@ torch::Tensor paged_decode_attn_tma(torch::Tensor q, torch::Tensor kc, torch::Te
     attr = true;
   }
   const float sl2 = (float)(scale * 1.4426950408889634);
-  decode_tma_kernel<<<dim3(nsplit, Hk, B), kThreadsT, kSmemT, stream()>>>(
-      (const __nv_bfloat16*)q.data_ptr(), maps, block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),
-      po.data_ptr<float>(), pl.data_ptr<float>(), (int)Hq, (int)Hk, (int)max_blocks, pps, sl2, (float)v_scale,
-      tma_err_word().data_ptr<int>());
-  combine_kernel<<<dim3(B, Hq), kHD, 0, stream()>>>(po.data_ptr<float>(), pl.data_ptr<float>(),
-                                                    (__nv_bfloat16*)out.data_ptr(), nsplit, (int)B, (int)Hq);
+  launch_pdl(decode_tma_kernel, dim3(nsplit, Hk, B), dim3(kThreadsT), kSmemT, (const __nv_bfloat16*)q.data_ptr(),
+             maps, (const int*)block_table.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(), po.data_ptr<float>(),
+             pl.data_ptr<float>(), (int)Hq, (int)Hk, (int)max_blocks, pps, sl2, (float)v_scale,
+             tma_err_word().data_ptr<int>());
+  launch_pdl(combine_kernel, dim3(B, Hq), dim3(kHD), 0, (const float*)po.data_ptr<float>(),
+             (const float*)pl.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(), nsplit, (int)B, (int)Hq);
   return out;
 }
 
@@ -508,17 +514,18 @@ torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, to
       cudaFuncSetAttribute(cascade_tma_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemT);           \
       attr_##M = true;                                                                                            \
     }                                                                                                             \
-    cascade_tma_kernel<M><<<(unsigned)nblocks, kThreadsT, kSmemT, stream()>>>(                                   \
-        (const __nv_bfloat16*)q.data_ptr(), maps, block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),         \
-        prefix_len.data_ptr<int>(), po.data_ptr<float>(), pl.data_ptr<float>(), (int)B, (int)Hq, (int)Hk,         \
-        (int)max_blocks, (int)group, psplit, ssplit, pps, sl2, (float)v_scale, tma_err_word().data_ptr<int>());   \
+    launch_pdl(cascade_tma_kernel<M>, dim3((unsigned)nblocks), dim3(kThreadsT), kSmemT,                         \
+               (const __nv_bfloat16*)q.data_ptr(), maps, (const int*)block_table.data_ptr<int>(),               \
+               (const int*)seq_lens.data_ptr<int>(), (const int*)prefix_len.data_ptr<int>(), po.data_ptr<float>(), \
+               pl.data_ptr<float>(), (int)B, (int)Hq, (int)Hk, (int)max_blocks, (int)group, psplit, ssplit, pps,  \
+               sl2, (float)v_scale, tma_err_word().data_ptr<int>());                                           \
   } while (0)
   if (MT == 1) CASC(1);
   else if (MT == 2) CASC(2);
   else CASC(4);
 #undef CASC
-  combine_kernel<<<dim3(B, Hq), kHD, 0, stream()>>>(po.data_ptr<float>(), pl.data_ptr<float>(),
-                                                    (__nv_bfloat16*)out.data_ptr(), total, (int)B, (int)Hq);
+  launch_pdl(combine_kernel, dim3(B, Hq), dim3(kHD), 0, (const float*)po.data_ptr<float>(),
+             (const float*)pl.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(), total, (int)B, (int)Hq);
   return out;
 }
 

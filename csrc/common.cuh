@@ -21,6 +21,35 @@ namespace lrl {
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 
+// ---- programmatic dependent launch (PDL) --------------------------------------
+// A kernel launched with launch_pdl may start while the previous kernel on the
+// stream is still running.  It must call pdl_wait() before it reads anything
+// that kernel produced and before its first global write (the caching
+// allocator may hand it memory the previous kernel still reads); work before
+// that (set-up, loads of constant weights) overlaps the previous kernel.
+// pdl_trigger() lets the next PDL kernel start being scheduled.  Calling it at
+// the top of a kernel is safe: the dependent is scheduled only after every CTA
+// of this grid has called it (or exited), i.e. once all of this grid is
+// resident, so a waiting dependent never holds resources this grid still
+// needs.  Both are no-ops when there is no PDL edge.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 inline int num_sms() {
   static int n = 0;
   if (n == 0) {

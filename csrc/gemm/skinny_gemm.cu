@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kThreadsS, 1)
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::kTmemCols);
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -102,9 +103,19 @@ __global__ void __launch_bounds__(kThreadsS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int it = 0;
+      // The weights do not depend on the previous kernel: start streaming the
+      // first stages of W before waiting for it (programmatic dependent
+      // launch), then add X (its output) to those stages.
+      const int pre = min(kStages, kb1 - kb0);
+      for (int j = 0; j < pre; ++j) {
+        mbar_expect_tx(&full[j], C::kStageBytes);
+        tma_load_2d(sw + j * kWBytes, &tmW, &full[j], (kb0 + j) * kBK, n0);
+      }
+      pdl_wait();
+      for (int j = 0; j < pre; ++j) tma_load_2d(sx + j * C::kXBytes, &tmX, &full[j], (kb0 + j) * kBK, 0);
+      int it = pre;
       bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      for (int kb = kb0 + pre; kb < kb1; ++kb, ++it) {
         const int s = it % kStages;
         if (!mbar_wait(&empty[s], ((it / kStages) & 1) ^ 1, err, kErrProducer)) {
           ok = false;
@@ -130,6 +141,7 @@ __global__ void __launch_bounds__(kThreadsS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      pdl_wait();
       const uint32_t idesc = idesc_bf16_f32(kBM, MP);
       bool ok = true;
       int it = 0;
@@ -153,6 +165,7 @@ __global__ void __launch_bounds__(kThreadsS, 1)
     }
   }
   // epilogue: every warp waits for the accumulator, warps 2..5 read TMEM
+  pdl_wait();  // (a no-op for the producer and MMA lanes, which already waited)
   const bool have_acc = kb1 > kb0;
   const bool ok_done = mbar_wait(done, 0, err, kErrEpilogue);
   __syncthreads();  // all pipeline smem reads are complete: reuse it for `red`
@@ -245,13 +258,15 @@ void launch_skinny(const CUtensorMap& mw, const CUtensorMap& mx, __nv_bfloat16* 
   cfg.blockDim = dim3(kThreadsS);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = stream();
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = ks;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mw, mx, y, M, N, K, ks, skinny_err_word().data_ptr<int>()));
 }
 

@@ -10,6 +10,8 @@ __device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); 
 // gu [T, 2F] = [gate | up] -> h [T, F] = silu(gate) * up
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int64_t T,
                                   int F) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t chunks = T * (F / 8);
   for (int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; c < chunks; c += int64_t(gridDim.x) * blockDim.x) {
     const int64_t t = c / (F / 8);
@@ -61,8 +63,8 @@ torch::Tensor swiglu_fwd(torch::Tensor gu) {
   sizes.back() = F2 / 2;
   auto h = torch::empty(sizes, gu.options());
   if (T == 0) return h;
-  swiglu_fwd_kernel<<<ew_grid(T * F2 / 16, 256), 256, 0, stream()>>>(
-      (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)h.data_ptr(), T, F2 / 2);
+  launch_pdl(swiglu_fwd_kernel, dim3(ew_grid(T * F2 / 16, 256)), dim3(256), 0, (const __nv_bfloat16*)gu.data_ptr(),
+             (__nv_bfloat16*)h.data_ptr(), T, F2 / 2);
   return h;
 }
 

@@ -14,6 +14,8 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
                                    float eps) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int64_t base = int64_t(row) * H;
@@ -68,9 +70,9 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
   if (T == 0) return {y, rstd};
-  rmsnorm_fwd_kernel<false><<<T, row_threads(H), 0, stream()>>>(
-      (const __nv_bfloat16*)x.data_ptr(), nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
-      nullptr, rstd.data_ptr<float>(), H, (float)eps);
+  launch_pdl(rmsnorm_fwd_kernel<false>, dim3(T), dim3(row_threads(H)), 0, (const __nv_bfloat16*)x.data_ptr(),
+             (const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+             (__nv_bfloat16*)nullptr, rstd.data_ptr<float>(), H, (float)eps);
   return {y, rstd};
 }
 
@@ -85,9 +87,9 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
   auto y = torch::empty_like(x);
   auto s = torch::empty_like(x);
   if (T == 0) return {y, s};
-  rmsnorm_fwd_kernel<true><<<T, row_threads(H), 0, stream()>>>(
-      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)res.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
-      (__nv_bfloat16*)y.data_ptr(), (__nv_bfloat16*)s.data_ptr(), nullptr, H, (float)eps);
+  launch_pdl(rmsnorm_fwd_kernel<true>, dim3(T), dim3(row_threads(H)), 0, (const __nv_bfloat16*)x.data_ptr(),
+             (const __nv_bfloat16*)res.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+             (__nv_bfloat16*)s.data_ptr(), (float*)nullptr, H, (float)eps);
   return {y, s};
 }
 
@@ -197,6 +199,8 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
                                        float* __restrict__ rq, float* __restrict__ rk, int64_t T, int nh, int nkv,
                                        float eps, int has_norm, void* __restrict__ kc, void* __restrict__ vc,
                                        const int64_t* __restrict__ slots, int cache_fp8, float inv_ks, float inv_vs) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int HD = 64 * P, HALF = 32 * P;
   const int lane = threadIdx.x & 31;
   const int kind = blockIdx.y;
@@ -427,11 +431,11 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
     fp8 = kc->scalar_type() == at::kFloat8_e4m3fn ? 1 : 0;
   }
 #define LAUNCH(PP)                                                                                              \
-  qk_norm_rope_fwd_kernel<PP><<<grid, 256, 0, stream()>>>(                                                      \
-      (const __nv_bfloat16*)qkv.data_ptr(), qwp, kwp, pos.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),     \
-      (__nv_bfloat16*)q.data_ptr(), (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(),                \
-      rq.data_ptr<float>(), rk.data_ptr<float>(), T, (int)nh, (int)nkv, (float)eps, has_norm ? 1 : 0, kcp, vcp, \
-      sp, fp8, (float)inv_ks, (float)inv_vs)
+  launch_pdl(qk_norm_rope_fwd_kernel<PP>, grid, dim3(256), 0, (const __nv_bfloat16*)qkv.data_ptr(), qwp, kwp,      \
+             (const int64_t*)pos.data_ptr<int64_t>(), (const float*)inv_freq.data_ptr<float>(),                 \
+             (__nv_bfloat16*)q.data_ptr(), (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(),          \
+             rq.data_ptr<float>(), rk.data_ptr<float>(), T, (int)nh, (int)nkv, (float)eps, has_norm ? 1 : 0,      \
+             kcp, vcp, (const int64_t*)sp, fp8, (float)inv_ks, (float)inv_vs)
   if (hd == 64) LAUNCH(1);
   else if (hd == 128) LAUNCH(2);
   else LAUNCH(4);

@@ -11,6 +11,11 @@ Backends (``weight_sync.backend``; reference ``rl_trainer.py:729-915``,
   bf16 buffer is broadcast in ``bucket_size_mb`` chunks from a trainer rank
   to rollout ranks over the process group (NCCL over NVLink), optionally with
   blockwise FP8 requantisation on the receiving side.
+* ``p2p`` (separated, one node): the trainer rank stores its flat bf16
+  buffer straight into the rollout rank's IPC-mapped weight buffer with the
+  ``p2p_push`` copy kernel (plain NVLink stores in bucket-sized launches, a
+  ready flag per bucket), and the receiver waits on the flags (bounded) and
+  re-quantises FP8 rollout weights if it runs them.
 * ``shared_folder``: safetensors snapshots ``v<N>/`` with a version file on a
   shared filesystem (the reference's FilesystemWeightSync), for cross-node or
   fully-async rollout.
@@ -65,6 +70,72 @@ class BroadcastWeightSync:
         dt = time.perf_counter() - t0
         return {"weight_sync/ms": dt * 1e3, "weight_sync/GBps": n * self.flat.element_size() / max(dt, 1e-9) / 1e9,
                 "weight_sync/version": self.version}
+
+
+class P2PWeightSync:
+    """Trainer rank ``src`` -> rollout rank ``dst`` over NVLink peer stores.
+
+    Both ranks construct it (collectively over ``group``); ``dst`` passes its
+    rollout engine.  The receiver's flat weights live in a symmetric buffer,
+    so the rollout model is re-pointed at it once at construction."""
+
+    def __init__(self, numel: int, src: int, dst: int, group=None, engine=None, bucket_size_mb: int = 1024,
+                 wait_seconds: float = 30.0) -> None:
+        from lumenrl_b200.ops.ext import ext
+        from lumenrl_b200.parallel.symm import SymmetricBuffer
+        self.src, self.dst, self.group = src, dst, group
+        self.rank = dist.get_rank(group)
+        world = dist.get_world_size(group)
+        self._e = ext()
+        self.buf = SymmetricBuffer(numel, torch.bfloat16, self.rank, world, group)
+        self.sig = SymmetricBuffer(64, torch.int32, self.rank, world, group)
+        self.bucket = max(8, (bucket_size_mb * 1024 * 1024 // 2) // 8 * 8)
+        self.numel = numel
+        dev = self.buf.tensor.device
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.wait_cycles = int(wait_seconds * 2.0e9)
+        self.version = 0
+        self.engine = engine
+        if engine is not None and self.rank == dst:
+            self.buf.tensor.copy_(engine.model.flat)
+            engine.model.flat = self.buf.tensor   # later syncs land in place
+            for name, p in engine.model.named_flat_params():
+                p.data = engine.model.layout.view(self.buf.tensor, name)
+        dist.barrier(group=group)
+
+    def sync(self, flat: Optional[torch.Tensor] = None) -> dict:
+        """``src`` passes its flat bf16 weights; ``dst`` passes nothing."""
+        t0 = time.perf_counter()
+        self.version += 1
+        e = self._e
+        if self.rank == self.src:
+            assert flat is not None and flat.numel() == self.numel and flat.dtype == torch.bfloat16
+            nb = (self.numel + self.bucket - 1) // self.bucket
+            for i in range(nb):
+                a, b = i * self.bucket, min(self.numel, (i + 1) * self.bucket)
+                # flag word i % 64 carries the bucket's version
+                e.p2p_push(flat[a:b], self.buf.ptrs[self.dst] + 2 * a, self.sig.ptrs[self.dst] + 4 * (i % 64),
+                           self.version, self.counter)
+            torch.cuda.synchronize()
+        elif self.rank == self.dst:
+            nb = (self.numel + self.bucket - 1) // self.bucket
+            for i in range(min(nb, 64)):
+                e.p2p_wait(self.sig.ptrs[self.dst] + 4 * i, self.version, self.status, 3, self.wait_cycles)
+            torch.cuda.synchronize()
+            if int(self.status.item()):
+                from lumenrl_b200.parallel.symm import CommTimeout
+                raise CommTimeout("p2p weight sync: the trainer never delivered a bucket")
+            if self.engine is not None:
+                self.engine.update_weights(version=self.version)
+        dt = time.perf_counter() - t0
+        return {"weight_sync/ms": dt * 1e3, "weight_sync/GBps": self.numel * 2 / max(dt, 1e-9) / 1e9,
+                "weight_sync/version": self.version}
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.buf.close()
+        self.sig.close()
 
 
 class FilesystemWeightSync:

@@ -270,3 +270,56 @@ def test_expert_parallel_nvlink_dispatch_combine():
         for k in fused:
             if k != "fused":
                 assert fused[k] < max(3 * plain[k], 3e-2), (rank, k, fused[k], plain[k])
+
+
+def _p2p_sync_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.engine.inference.engine import RolloutEngine
+    from lumenrl_b200.models.config import tiny_qwen3
+    from lumenrl_b200.models.qwen3 import Qwen3Model
+    from lumenrl_b200.sync.weight_sync import P2PWeightSync
+    m = Qwen3Model(tiny_qwen3(), device="cuda", dtype=torch.bfloat16, requires_grad=False)
+    m.init_weights(rank)          # the two ranks start with different weights
+    eng = RolloutEngine(m, max_num_seqs=4, max_model_len=64, block_size=16, use_cuda_graph=False) if rank == 1 else None
+    sync = P2PWeightSync(m.flat.numel(), src=0, dst=1, engine=eng, bucket_size_mb=1)
+    res = []
+    for step in range(3):
+        if rank == 0:
+            with torch.no_grad():
+                m.flat.add_(0.01)
+            out = sync.sync(m.flat)
+            dist.send(m.flat.float().sum().reshape(1), 1)
+        else:
+            out = sync.sync()
+            ref = torch.zeros(1, device="cuda")
+            dist.recv(ref, 0)
+            res.append(abs(float(eng.model.flat.float().sum()) - float(ref)) / max(1.0, abs(float(ref))))
+            # the engine generates from the synced weights
+            g = eng.generate([[1, 2, 3]], __import__("lumenrl_b200.engine.inference.engine", fromlist=["x"])
+                             .SamplingParams(max_new_tokens=4, n=2, seed=step))
+            assert g.responses.shape == (2, 4)
+        res.append(out["weight_sync/GBps"]) if rank == 0 else None
+    q.put((rank, res))
+    dist.barrier()
+    sync.close()
+    dist.destroy_process_group()
+
+
+def test_p2p_weight_sync_to_separate_rollout_gpu():
+    """Separated mode: the trainer GPU pushes its flat weights into the
+    rollout GPU's buffer over NVLink; the rollout engine sees them at once."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29950 + os.getpid() % 9
+    procs = [ctx.Process(target=_p2p_sync_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert len(res[1]) == 3 and max(res[1]) < 1e-6

@@ -119,9 +119,12 @@ class P2PWeightSync:
                            self.version, self.counter)
             torch.cuda.synchronize()
         elif self.rank == self.dst:
+            # the sender's pushes run in stream order and each publishes its flag
+            # with a system-scope release after its stores, so the last
+            # bucket's flag implies every bucket has landed
             nb = (self.numel + self.bucket - 1) // self.bucket
-            for i in range(min(nb, 64)):
-                e.p2p_wait(self.sig.ptrs[self.dst] + 4 * i, self.version, self.status, 3, self.wait_cycles)
+            e.p2p_wait(self.sig.ptrs[self.dst] + 4 * ((nb - 1) % 64), self.version, self.status, 3,
+                       self.wait_cycles)
             torch.cuda.synchronize()
             if int(self.status.item()):
                 from lumenrl_b200.parallel.symm import CommTimeout

@@ -36,44 +36,6 @@ class _VarlenFlash(torch.autograd.Function):
         return dq, dk, dv, None, None, None, None
 
 
-class _VarlenCudnn(torch.autograd.Function):
-    """Same contract through cuDNN's varlen attention (``thd`` layout)."""
-
-    @staticmethod
-    def forward(ctx, q, k, v, cu, max_len, causal, scale):
-        if k.shape[1] != q.shape[1]:   # GQA: expand K/V heads for this backend
-            g = q.shape[1] // k.shape[1]
-            k, v = k.repeat_interleave(g, 1), v.repeat_interleave(g, 1)
-            ctx.gqa = g
-        else:
-            ctx.gqa = 1
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        res = torch.ops.aten._cudnn_attention_forward(q, k, v, None, cu, cu, max_len, max_len, True, 0.0, causal,
-                                                      False, scale=scale)
-        out, lse, seed, offset = res[0], res[1], res[6], res[7]
-        ctx.save_for_backward(q, k, v, out, lse, cu, seed, offset)
-        ctx.max_len, ctx.causal, ctx.scale = max_len, causal, scale
-        return out
-
-    @staticmethod
-    def backward(ctx, do):
-        q, k, v, out, lse, cu, seed, offset = ctx.saved_tensors
-        empty = torch.empty(0, device=q.device, dtype=q.dtype)
-        dq, dk, dv = torch.ops.aten._cudnn_attention_backward(
-            do.contiguous(), q, k, v, out, lse, seed, offset, empty, cu, cu, ctx.max_len, ctx.max_len, 0.0,
-            ctx.causal, scale=ctx.scale)
-        if ctx.gqa > 1:
-            g = ctx.gqa
-            dk = dk.view(dk.shape[0], -1, g, dk.shape[-1]).sum(2)
-            dv = dv.view(dv.shape[0], -1, g, dv.shape[-1]).sum(2)
-        return dq, dk, dv, None, None, None, None
-
-
-# training / prefill attention backend: "flash" (FA2 varlen) or "cudnn"
-import os as _os  # noqa: E402
-TRAIN_ATTN = _os.environ.get("LRL_TRAIN_ATTN", "flash")
-
-
 def flash_attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, max_seqlen: int,
                            causal: bool = True, scale: float | None = None) -> Tensor:
     """q [T, Hq, D], k/v [T, Hk, D] (bf16/fp16, CUDA) packed by ``cu_seqlens``."""
@@ -81,8 +43,7 @@ def flash_attention_varlen(q: Tensor, k: Tensor, v: Tensor, cu_seqlens: Tensor, 
         scale = q.shape[-1] ** -0.5
     cu = cu_seqlens.to(torch.int32)
     if q.dtype in (torch.bfloat16, torch.float16):
-        fn = _VarlenCudnn if TRAIN_ATTN == "cudnn" else _VarlenFlash
-        return fn.apply(q, k, v, cu, int(max_seqlen), causal, float(scale))
+        return _VarlenFlash.apply(q, k, v, cu, int(max_seqlen), causal, float(scale))
     # fp32 fallback: per-sequence SDPA
     bounds = cu.tolist()
     outs = []

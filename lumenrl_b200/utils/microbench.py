@@ -133,7 +133,6 @@ def bench_attn_train(ns) -> dict:
     """Packed causal attention forward + backward (training shapes: --rows
     sequences of --seq tokens, the model's heads) for each backend."""
     from lumenrl_b200 import ops
-    from lumenrl_b200.ops import attention as A
     args = _model_args(ns.model)
     T = ns.rows * ns.seq
     cu = torch.arange(0, T + 1, ns.seq, dtype=torch.int32, device="cuda")
@@ -143,17 +142,13 @@ def bench_attn_train(ns) -> dict:
     do = torch.randn_like(q)
     res = {"op": "train_attention", "tokens": T, "seq": ns.seq}
     flops = 4 * ns.rows * (ns.seq * ns.seq / 2) * args.num_heads * args.head_dim * 3.5  # fwd + bwd (2.5x)
-    for be in ("flash", "cudnn"):
-        A.TRAIN_ATTN = be
-        def step():
-            o = ops.attention_varlen(q, k, v, cu, ns.seq, causal=True, scale=args.head_dim ** -0.5)
-            o.backward(do)
-        try:
-            t = _time(step, ns.steps, ns.warmup)
-            res[be + "_ms"] = t
-            res[be + "_tflops"] = flops / t / 1e9
-        except Exception as e:  # noqa: BLE001 - report a backend that is not available
-            res[be + "_error"] = repr(e)[:200]
+
+    def step():
+        o = ops.attention_varlen(q, k, v, cu, ns.seq, causal=True, scale=args.head_dim ** -0.5)
+        o.backward(do)
+    t = _time(step, ns.steps, ns.warmup)
+    res["ms"] = t
+    res["tflops"] = flops / t / 1e9
     return res
 
 

@@ -294,12 +294,9 @@ def test_qk_norm_rope_cache_write(cuda):
     close(vc.view(-1, nkv, hd)[slots], v2, 0.0)
 
 
-@pytest.mark.parametrize("backend", ["flash", "cudnn"])
-def test_attention_varlen_fwd_bwd(cuda, monkeypatch, backend):
+def test_attention_varlen_fwd_bwd(cuda):
     """Packed causal GQA attention (one varlen flash call) against an fp32
     per-sequence reference, forward and backward."""
-    from lumenrl_b200.ops import attention as attn_mod
-    monkeypatch.setattr(attn_mod, "TRAIN_ATTN", backend)
     torch.manual_seed(0)
     lens = [37, 200, 1, 511]
     T, Hq, Hk, D = sum(lens), 8, 2, 128

@@ -49,19 +49,33 @@ def _time(fn, steps: int, warmup: int) -> float:
 def bench_decode(ns) -> dict:
     from lumenrl_b200.engine.inference.engine import RolloutEngine
     from lumenrl_b200.engine.inference.runner import DecodeGraph
+    from lumenrl_b200 import ops
     m = _model(ns.model, False)
     B, ctx = ns.batch, ns.ctx
     eng = RolloutEngine(m, max_num_seqs=B, max_model_len=ctx + 64, use_cuda_graph=not ns.no_graph)
-    g = DecodeGraph(eng.runner, B, eng.max_blocks_per_seq, 1.0, 1.0, not ns.no_graph)
-    nb = math.ceil((ctx + 64) / eng.block_size)
-    blocks = torch.arange(1, 1 + B * nb, dtype=torch.int32, device="cuda").view(B, nb)
-    g.block_table[:, :nb].copy_(blocks)
+    bs = eng.block_size
+    n, P = ns.group, (ns.prefix // bs) * bs    # rows of a group share a P-token prompt (in ctx)
+    grp = ops.shared_prefix_group(n, m.args.num_heads // m.args.num_kv_heads) if n > 1 and P > 0 else 1
+    share = (grp, -(-P // 256) * 256, -(-(ctx - P + bs) // 256) * 256) if grp > 1 else None
+    g = DecodeGraph(eng.runner, B, eng.max_blocks_per_seq, 1.0, 1.0, not ns.no_graph, share)
+    nb = math.ceil((ctx + 64) / bs)
+    pb = P // bs if grp > 1 else 0
+    bt = torch.zeros(B, nb, dtype=torch.int32)
+    nxt = 1 + (B // max(grp, 1)) * pb
+    for r in range(B):
+        if pb:
+            bt[r, :pb] = 1 + (r // grp) * pb + torch.arange(pb, dtype=torch.int32)
+        bt[r, pb:] = nxt + torch.arange(nb - pb, dtype=torch.int32)
+        nxt += nb - pb
+    g.block_table[:, :nb].copy_(bt.cuda())
+    g.prefix_len.fill_(pb * bs)
     g.positions.fill_(ctx)
     g.tokens.random_(0, m.args.vocab_size)
     ms = _time(g.run, ns.steps, ns.warmup)
     wbytes = m.flat.numel() * 2
     kvbytes = B * ctx * m.args.kv_bytes_per_token()
-    return {"op": "decode_step", "batch": B, "ctx": ctx, "ms": ms,
+    return {"op": "decode_step", "batch": B, "ctx": ctx, "shared_prefix": pb * bs, "group": grp,
+            "attn": ops.DECODE_ATTN, "gemm": ops.DECODE_GEMM, "ms": ms,
             "weights_GB": wbytes / 1e9, "kv_GB": kvbytes / 1e9, "achieved_TBps": (wbytes + kvbytes) / ms / 1e9}
 
 

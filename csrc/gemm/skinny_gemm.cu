@@ -280,7 +280,7 @@ int64_t skinny_gemm_status() {
 }
 
 // x [M, K] bf16 (M <= 256), w [N, K] bf16, both K-contiguous.  ksplit: 0 =
-// choose (all CTAs resident, 2 per SM), else 1, 2, 4 or 8.
+// choose by wave quantisation, else the K split (= cluster size), 1..8.
 torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit) {
   LRL_CHECK_CUDA(x);
   LRL_CHECK_CUDA(w);
@@ -296,13 +296,21 @@ torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit) {
   const int64_t kblocks = (K + kBK - 1) / kBK;
   int ks = (int)ksplit;
   if (ks <= 0) {
-    // the largest power-of-two split that keeps every CTA resident at once
-    // (2 per SM): a second, partial wave would cost more than a split saves
-    const int64_t fit = (2 * (int64_t)num_sms()) / tiles;
-    ks = fit >= 8 ? 8 : (fit >= 4 ? 4 : (fit >= 2 ? 2 : 1));
+    // pick the split (cluster size 1..8) that minimises the time of the last
+    // wave: waves(ks) / ks, with 2 resident CTAs per SM; ties go to the
+    // smaller split (less reduction work)
+    const int64_t slots = 2 * (int64_t)num_sms();
+    double best = 1e30;
+    for (int c = 1; c <= 8 && c <= kblocks; ++c) {
+      const double cost = (double)((tiles * c + slots - 1) / slots) / c;
+      if (cost < best - 1e-9) {
+        best = cost;
+        ks = c;
+      }
+    }
   }
-  TORCH_CHECK(ks == 1 || ks == 2 || ks == 4 || ks == 8, "skinny_gemm: ksplit in {1, 2, 4, 8}");
-  while (ks > 1 && kblocks < ks) ks >>= 1;
+  TORCH_CHECK(ks >= 1 && ks <= 8, "skinny_gemm: ksplit in 1..8");
+  if (ks > kblocks) ks = (int)kblocks;
   const int mp = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
   const CUtensorMap mw = make_kmajor_map(w.data_ptr(), N, K, w.stride(0), kBM);
   const CUtensorMap mx = make_kmajor_map(x.data_ptr(), M, K, x.stride(0), mp);

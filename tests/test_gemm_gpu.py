@@ -63,7 +63,7 @@ def test_skinny_gemm_decode_sizes(cuda, M, N, K):
     x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
     w = (torch.randn(N, K, device=cuda) / K ** 0.5).to(torch.bfloat16)
     ref = x.float() @ w.float().t()
-    for ks in (0, 1, 2, 8):
+    for ks in (0, 1, 2, 3, 8):
         y = ops.skinny_linear(x, w, ks)
         torch.cuda.synchronize()
         assert ext().skinny_gemm_status() == 0

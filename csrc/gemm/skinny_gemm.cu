@@ -296,14 +296,15 @@ torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit) {
   const int64_t kblocks = (K + kBK - 1) / kBK;
   int ks = (int)ksplit;
   if (ks <= 0) {
-    // pick the split (cluster size 1..8) that minimises the time of the last
-    // wave: waves(ks) / ks, with 2 resident CTAs per SM; ties go to the
-    // smaller split (less reduction work)
+    // pick the power-of-two split (cluster size; 3- and 6-CTA clusters
+    // measured slower) that minimises the modelled time waves(ks) / ks with 2
+    // resident CTAs per SM, and split further only for a > 15 % gain
     const int64_t slots = 2 * (int64_t)num_sms();
-    double best = 1e30;
-    for (int c = 1; c <= 8 && c <= kblocks; ++c) {
+    ks = 1;
+    double best = (double)((tiles + slots - 1) / slots);
+    for (int c = 2; c <= 8 && c <= kblocks; c *= 2) {
       const double cost = (double)((tiles * c + slots - 1) / slots) / c;
-      if (cost < best - 1e-9) {
+      if (cost < 0.85 * best) {
         best = cost;
         ks = c;
       }

@@ -492,8 +492,9 @@ def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
 
 
 # decode-step linears: "auto" (own weight-streaming kernel for weights up to
-# 32 M elements, where it beats cuBLAS at M=64: 15.1 vs 18.5 us on 4096x4096;
-# cuBLAS above, where cuBLAS is 2-4 % faster), "skinny" or "cublas"
+# 64 M elements, where it is level with or ahead of cuBLAS at M=64: 12.1 vs
+# 17.8 us on 4096x4096, 22.4 vs 24.2 us on 4096x12288; cuBLAS above, where it
+# is ahead), "skinny" or "cublas"
 DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "auto")
 
 
@@ -501,7 +502,7 @@ def decode_linear(x: Tensor, w: Tensor) -> Tensor:
     """No-grad linear of the rollout decode step (M = live sequences)."""
     mode = DECODE_GEMM
     if mode == "auto":
-        mode = "skinny" if w.numel() <= (32 << 20) else "cublas"
+        mode = "skinny" if w.numel() <= (64 << 20) else "cublas"
     if (mode == "skinny" and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
             and x.dim() == 2 and x.shape[0] <= 256 and x.shape[1] % 8 == 0 and x.is_contiguous()
             and w.is_contiguous()):

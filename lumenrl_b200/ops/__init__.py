@@ -491,11 +491,12 @@ def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
     return ext().skinny_gemm(x, w, ksplit)
 
 
-# decode-step linears: "auto" (own weight-streaming kernel for weights up to
-# 64 M elements, where it is level with or ahead of cuBLAS at M=64: 12.1 vs
-# 17.8 us on 4096x4096, 22.4 vs 24.2 us on 4096x12288; cuBLAS above, where it
-# is ahead), "skinny" or "cublas"
-DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "auto")
+# decode-step linears: "cublas" (default), "skinny" (own weight-streaming
+# kernel) or "auto" (skinny for weights up to 64 M elements, where it is ahead
+# of cuBLAS in isolation at M=64: 12.4 vs 18.2 us on 4096x4096, 15.3 vs 17.9
+# on 6144x4096; inside the CUDA-graph decode step "auto" measured 1.4 % slower
+# than all-cuBLAS, 5.72 vs 5.64 ms per step, hence the default)
+DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "cublas")
 
 
 def decode_linear(x: Tensor, w: Tensor) -> Tensor:

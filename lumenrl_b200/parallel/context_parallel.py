@@ -18,9 +18,9 @@ differentiable all-reduce).
 * ``gather_seq`` / ``scatter_seq``: put per-rank token tensors back in
   sequence order (all-gather) differentiably, e.g. for log-probs.
 
-Block math: on CUDA the per-block forward/backward are the flash-attention
-kernels behind ``torch.nn.functional.scaled_dot_product_attention`` (which
-return the LSE); on CPU an fp32 restatement is used.
+Block math: on CUDA the per-block forward/backward are PyTorch's varlen
+flash-attention kernels (native GQA, LSE returned and accepted back); on CPU
+an fp32 restatement is used.
 """
 
 from __future__ import annotations
@@ -54,11 +54,9 @@ def _expand(k: Tensor, hq: int) -> Tensor:
 def _block_fwd(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: float) -> tuple[Tensor, Tensor]:
     """q [B,H,Tq,D], k/v [B,Hk,Tk,D] -> (o [B,H,Tq,D] in q's dtype, lse [B,H,Tq] fp32)."""
     H = q.shape[1]
-    k, v = _expand(k, H), _expand(v, H)
     if q.is_cuda:
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        out = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, causal, False, scale=scale)
-        return out[0], out[1].float()
+        return _varlen_fwd(q, k, v, causal, scale)
+    k, v = _expand(k, H), _expand(v, H)
     s = (q.float() @ k.float().transpose(-1, -2)) * scale
     if causal:
         Tq, Tk = s.shape[-2], s.shape[-1]
@@ -72,34 +70,71 @@ def _block_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, lse: Tens
                scale: float) -> tuple[Tensor, Tensor, Tensor]:
     """Gradients of one block given the GLOBAL output ``o`` and ``lse``."""
     H, Hk = q.shape[1], k.shape[1]
-    ke, ve = _expand(k, H), _expand(v, H)
     if q.is_cuda:
-        B, _, Tq, _ = q.shape
-        Tk = k.shape[2]
-        do, q, ke, ve, o = do.contiguous(), q.contiguous(), ke.contiguous(), ve.contiguous(), o.contiguous()
-        empty = torch.empty(0, device=q.device, dtype=torch.int32)
-        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
-            do, q, ke, ve, o, lse.to(torch.float32), empty, empty, Tq, Tk, 0.0, causal,
-            torch.zeros((), dtype=torch.int64, device=q.device), torch.zeros((), dtype=torch.int64, device=q.device),
-            scale=scale)
-    else:
-        s = (q.float() @ ke.float().transpose(-1, -2)) * scale
-        if causal:
-            Tq, Tk = s.shape[-2], s.shape[-1]
-            s = s.masked_fill(torch.ones(Tq, Tk, dtype=torch.bool).triu(1 + Tk - Tq), float("-inf"))
-        p = torch.exp(s - lse.unsqueeze(-1))
-        dof = do.float()
-        dv = p.transpose(-1, -2) @ dof
-        dp = dof @ ve.float().transpose(-1, -2)
-        delta = (dof * o.float()).sum(-1, keepdim=True)
-        ds = p * (dp - delta) * scale
-        dq = ds @ ke.float()
-        dk = ds.transpose(-1, -2) @ q.float()
+        return _varlen_bwd(do, q, k, v, o, lse, causal, scale)
+    ke, ve = _expand(k, H), _expand(v, H)
+    s = (q.float() @ ke.float().transpose(-1, -2)) * scale
+    if causal:
+        Tq, Tk = s.shape[-2], s.shape[-1]
+        s = s.masked_fill(torch.ones(Tq, Tk, dtype=torch.bool).triu(1 + Tk - Tq), float("-inf"))
+    p = torch.exp(s - lse.unsqueeze(-1))
+    dof = do.float()
+    dv = p.transpose(-1, -2) @ dof
+    dp = dof @ ve.float().transpose(-1, -2)
+    delta = (dof * o.float()).sum(-1, keepdim=True)
+    ds = p * (dp - delta) * scale
+    dq = ds @ ke.float()
+    dk = ds.transpose(-1, -2) @ q.float()
     if Hk != H:
         g = H // Hk
         dk = dk.view(dk.shape[0], Hk, g, *dk.shape[2:]).sum(2)
         dv = dv.view(dv.shape[0], Hk, g, *dv.shape[2:]).sum(2)
     return dq.float(), dk.float(), dv.float()
+
+
+def _to_thd(x: Tensor) -> Tensor:
+    B, H, T, D = x.shape
+    return x.transpose(1, 2).reshape(B * T, H, D).contiguous()
+
+
+def _from_thd(x: Tensor, B: int) -> Tensor:
+    T = x.shape[0] // B
+    return x.view(B, T, x.shape[1], x.shape[2]).transpose(1, 2)
+
+
+def _cu(B: int, T: int, dev) -> Tensor:
+    return torch.arange(0, (B + 1) * T, T, dtype=torch.int32, device=dev)
+
+
+def _lse_to_bht(lse: Tensor, B: int, T: int) -> Tensor:
+    # the varlen kernel returns [H, B*T] (older builds [B, H, T])
+    return lse if lse.dim() == 3 else lse.view(lse.shape[0], B, T).permute(1, 0, 2)
+
+
+def _varlen_fwd(q, k, v, causal, scale):
+    """Flash-attention varlen forward of a [B, H, T, D] block (native GQA)."""
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    out, lse, _seed, _off, _ = torch.ops.aten._flash_attention_forward(
+        _to_thd(q), _to_thd(k), _to_thd(v), _cu(B, Tq, q.device), _cu(B, Tk, q.device), Tq, Tk, 0.0, causal, False,
+        scale=scale)
+    _LSE_LAYOUT[0] = lse.dim()
+    return _from_thd(out, B), _lse_to_bht(lse.float(), B, Tq)
+
+
+def _varlen_bwd(do, q, k, v, o, lse, causal, scale):
+    """Block gradients from the GLOBAL output and LSE (fp32 results)."""
+    B, H, Tq, D = q.shape
+    Tk = k.shape[2]
+    lse_in = lse.contiguous() if _LSE_LAYOUT[0] == 3 else lse.permute(1, 0, 2).reshape(H, B * Tq).contiguous()
+    zero = torch.zeros((), dtype=torch.int64, device=q.device)
+    dq, dk, dv = torch.ops.aten._flash_attention_backward(
+        _to_thd(do), _to_thd(q), _to_thd(k), _to_thd(v), _to_thd(o.to(q.dtype)), lse_in, _cu(B, Tq, q.device),
+        _cu(B, Tk, q.device), Tq, Tk, 0.0, causal, zero, zero, scale=scale)
+    return (_from_thd(dq, B).float(), _from_thd(dk, B).float(), _from_thd(dv, B).float())
+
+
+_LSE_LAYOUT = [2]
 
 
 def _merge(o: Optional[Tensor], lse: Optional[Tensor], ob: Tensor, lb: Tensor) -> tuple[Tensor, Tensor]:

@@ -191,7 +191,7 @@ def test_tensor_parallel_fused_ag_rs_gemms():
             assert fused[k] < max(3 * plain[k], 2e-2), (rank, k, fused[k], plain[k])
 
 
-def _cp_worker(rank, world, port, q):
+def _cp_worker(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -211,7 +211,7 @@ def _cp_worker(rank, world, port, q):
 
     def rel(a, b):
         return ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
-    q.put((rank, {"o": rel(o, of[:, :, idx]), "dq": rel(ql.grad, qf.grad[:, :, idx]),
+    out_q.put((rank, {"o": rel(o, of[:, :, idx]), "dq": rel(ql.grad, qf.grad[:, :, idx]),
                   "dk": rel(kl.grad, kf.grad[:, :, idx]), "dv": rel(vl.grad, vf.grad[:, :, idx])}))
     dist.barrier()
     dist.destroy_process_group()
@@ -298,8 +298,12 @@ def _p2p_sync_worker(rank, world, port, q):
             dist.recv(ref, 0)
             bad = (eng.model.flat.view(torch.int16) != ref.view(torch.int16)).nonzero()
             if bad.numel():   # diagnose: which elements differ
+                bufv = sync.buf.tensor[:4].float().tolist()
                 print(f"p2p sync step {step}: {bad.numel()} of {ref.numel()} elements differ, first {int(bad[0])}, "
-                      f"last {int(bad[-1])}, bucket {sync.bucket}", flush=True)
+                      f"last {int(bad[-1])}, bucket {sync.bucket}; flat ptr {eng.model.flat.data_ptr()} "
+                      f"buf ptr {sync.buf.tensor.data_ptr()}; flat[:4] {eng.model.flat[:4].float().tolist()} "
+                      f"buf[:4] {bufv} ref[:4] {ref[:4].float().tolist()} sig {sync.sig.tensor[:8].tolist()}",
+                      flush=True)
             res.append(bad.numel() / ref.numel())
             # the engine generates from the synced weights
             g = eng.generate([[1, 2, 3]], __import__("lumenrl_b200.engine.inference.engine", fromlist=["x"])

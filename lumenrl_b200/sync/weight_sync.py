@@ -15,7 +15,9 @@ Backends (``weight_sync.backend``; reference ``rl_trainer.py:729-915``,
   buffer straight into the rollout rank's IPC-mapped weight buffer with the
   ``p2p_push`` copy kernel (plain NVLink stores in bucket-sized launches, a
   ready flag per bucket), and the receiver waits on the flags (bounded) and
-  re-quantises FP8 rollout weights if it runs them.
+  re-quantises FP8 rollout weights if it runs them.  The receiver acknowledges
+  each version when it asks for the next, and the sender waits for that
+  acknowledgement before pushing, so weights in use are never overwritten.
 * ``shared_folder``: safetensors snapshots ``v<N>/`` with a version file on a
   shared filesystem (the reference's FilesystemWeightSync), for cross-node or
   fully-async rollout.
@@ -88,7 +90,9 @@ class P2PWeightSync:
         world = dist.get_world_size(group)
         self._e = ext()
         self.buf = SymmetricBuffer(numel, torch.bfloat16, self.rank, world, group)
-        self.sig = SymmetricBuffer(64, torch.int32, self.rank, world, group)
+        # words 0..63 on the receiver: bucket-ready flags; word 64 on the
+        # sender: the receiver's "done with version v" acknowledgement
+        self.sig = SymmetricBuffer(128, torch.int32, self.rank, world, group)
         self.bucket = max(8, (bucket_size_mb * 1024 * 1024 // 2) // 8 * 8)
         self.numel = numel
         dev = self.buf.tensor.device
@@ -111,6 +115,8 @@ class P2PWeightSync:
         e = self._e
         if self.rank == self.src:
             assert flat is not None and flat.numel() == self.numel and flat.dtype == torch.bfloat16
+            # back-pressure: never overwrite weights the rollout side still uses
+            e.p2p_wait(self.sig.ptrs[self.src] + 4 * 64, self.version - 1, self.status, 4, self.wait_cycles)
             nb = (self.numel + self.bucket - 1) // self.bucket
             for i in range(nb):
                 a, b = i * self.bucket, min(self.numel, (i + 1) * self.bucket)
@@ -118,7 +124,12 @@ class P2PWeightSync:
                 e.p2p_push(flat[a:b], self.buf.ptrs[self.dst] + 2 * a, self.sig.ptrs[self.dst] + 4 * (i % 64),
                            self.version, self.counter)
             torch.cuda.synchronize()
+            if int(self.status.item()):
+                from lumenrl_b200.parallel.symm import CommTimeout
+                raise CommTimeout("p2p weight sync: the rollout side never released the previous weights")
         elif self.rank == self.dst:
+            # release the previous version (the caller is done generating with it)
+            e.p2p_signal(self.sig.ptrs[self.src] + 4 * 64, self.version - 1)
             # the sender's pushes run in stream order and each publishes its flag
             # with a system-scope release after its stores, so the last
             # bucket's flag implies every bucket has landed

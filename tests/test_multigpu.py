@@ -298,12 +298,8 @@ def _p2p_sync_worker(rank, world, port, q):
             dist.recv(ref, 0)
             bad = (eng.model.flat.view(torch.int16) != ref.view(torch.int16)).nonzero()
             if bad.numel():   # diagnose: which elements differ
-                bufv = sync.buf.tensor[:4].float().tolist()
                 print(f"p2p sync step {step}: {bad.numel()} of {ref.numel()} elements differ, first {int(bad[0])}, "
-                      f"last {int(bad[-1])}, bucket {sync.bucket}; flat ptr {eng.model.flat.data_ptr()} "
-                      f"buf ptr {sync.buf.tensor.data_ptr()}; flat[:4] {eng.model.flat[:4].float().tolist()} "
-                      f"buf[:4] {bufv} ref[:4] {ref[:4].float().tolist()} sig {sync.sig.tensor[:8].tolist()}",
-                      flush=True)
+                      f"last {int(bad[-1])}, flags {sync.sig.tensor[:8].tolist()}", flush=True)
             res.append(bad.numel() / ref.numel())
             # the engine generates from the synced weights
             g = eng.generate([[1, 2, 3]], __import__("lumenrl_b200.engine.inference.engine", fromlist=["x"])

@@ -256,8 +256,9 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
       }
       l = l * alpha + sum;
       m = m_new;
-      // rescale O when the max moved (O holds the blocks before j)
-      if (j > 0 && alpha != 1.f) {
+      // rescale O when the max moved (O holds the blocks before j); tcgen05.ld/st
+      // are warp-collective, so the whole warp takes the branch together
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float v[32];

@@ -163,6 +163,17 @@ def bench_attn_train(ns) -> dict:
     t = _time(step, ns.steps, ns.warmup)
     res["ms"] = t
     res["tflops"] = flops / t / 1e9
+    # forward alone: library kernel vs the tcgen05 kernel
+    from lumenrl_b200.ops.ext import ext
+    fflops = 4 * ns.rows * (ns.seq * ns.seq / 2) * args.num_heads * args.head_dim
+    sc = args.head_dim ** -0.5
+    with torch.no_grad():
+        qd, kd, vd = q.detach(), k.detach(), v.detach()
+        t2 = _time(lambda: torch.ops.aten._flash_attention_forward(qd, kd, vd, cu, cu, ns.seq, ns.seq, 0.0, True,
+                                                                    False, scale=sc), ns.steps, ns.warmup)
+        t3 = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc), ns.steps, ns.warmup)
+    res.update(fwd_fa2_ms=t2, fwd_fa2_tflops=fflops / t2 / 1e9, fwd_tc_ms=t3, fwd_tc_tflops=fflops / t3 / 1e9,
+               fwd_tc_status=int(ext().fa_fwd_status()))
     return res
 
 

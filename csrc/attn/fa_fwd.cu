@@ -139,11 +139,17 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, kTile);
-      tma_load_3d(sq, &maps.q, q_full, 0, h, s0 + q0);
-      tma_load_3d(sq + kBox, &maps.q, q_full, 64, h, s0 + q0);
+      // V^T columns of every sequence start on a 128-key boundary; anything
+      // else would give the TMA an unaligned x coordinate
+      if (poff[sidx] & (kBK - 1)) *err = kErrProducer;
+      if (*err == kErrNone) mbar_expect_tx(q_full, kTile);
+      const bool q_issued = *err == kErrNone;
+      if (q_issued) {
+        tma_load_3d(sq, &maps.q, q_full, 0, h, s0 + q0);
+        tma_load_3d(sq + kBox, &maps.q, q_full, 64, h, s0 + q0);
+      }
       int j = 0;
-      for (; j < nblocks; ++j) {
+      for (; j < nblocks && *err == kErrNone; ++j) {
         const int st = j % kStages;
         if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1) ^ 1, err, kErrProducer)) break;
         uint8_t* kb = skv + st * 2 * kTile;
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
             if (clock64() - t0 > kWaitCycles) break;
         }
         const long long t0 = clock64();
-        while (!mbar_try_wait(q_full, 0))
+        while (q_issued && !mbar_try_wait(q_full, 0))
           if (clock64() - t0 > kWaitCycles) break;
       }
     }
@@ -396,7 +402,9 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   if (T == 0 || nseq <= 0) return {out, lse};
   // per-sequence 128-aligned key offsets for V^T (device side, no host sync)
   auto lens = (cu.slice(0, 1) - cu.slice(0, 0, nseq));
-  auto padded = ((lens + (kBK - 1)) / kBK) * kBK;
+  // integer floor division (ATen's `/` on int tensors is true division)
+  auto padded = torch::div(lens + (kBK - 1), kBK, "floor") * kBK;
+  TORCH_CHECK(padded.scalar_type() == at::kInt, "fa_fwd: padded lengths must stay int32");
   auto poff = torch::zeros({nseq + 1}, cu.options());
   poff.slice(0, 1).copy_(torch::cumsum(padded, 0));
   const int64_t Tpad = ((T + kBK - 1) / kBK + nseq) * kBK;  // upper bound of the padded total

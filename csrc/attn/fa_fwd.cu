@@ -3,19 +3,26 @@
 // GQA).  Reference call sites: the packed varlen attention of
 // `engine/training/packing.py:363-421`.
 //
-// One CTA per (sequence, 128-query tile, query head):
-//   warp 0   TMA producer: the Q tile once, then per 128-key block the K tile
-//            and the V^T tile into a 2-deep ring;
-//   warp 1   MMA issuer (one lane): S = Q K^T into TMEM columns [0, 128),
-//            then, once the softmax warps have written P, O += P V^T^T into
-//            TMEM columns [128, 256);
-//   warps 2-5  softmax: thread r owns query row r (its TMEM lane); reads S,
-//            applies the causal / sequence mask, keeps the running max and
-//            sum in the exp2 domain, writes bf16 P into shared memory as the
-//            next MMA's A operand, and rescales its O row in TMEM (ld, *alpha,
-//            st) when the max moved; at the end it normalises O, writes the
-//            bf16 output and the natural-log LSE ([Hq, T], the layout the
-//            library flash backward takes).
+// One CTA per (query head, pair of 128-query tiles A and B of one sequence),
+// 320 threads:
+//   warp 0     TMA producer: both Q tiles once, then K_j and V^T_j of every
+//              128-key block through a 3-slot ring of 32 KB tiles;
+//   warp 1     MMA issuer (one lane), ping-pong between the two tiles:
+//                S_A(j) = Q_A K_j^T | O_B += P_B(j-1) V_(j-1) | S_B(j) | O_A += P_A(j) V_j
+//              so the tensor core works on one tile while the other tile's
+//              softmax runs;
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B: thread r owns
+//              query row r (its TMEM lane), reads its 128 scores with one
+//              round of tcgen05.ld, masks only diagonal / ragged blocks, keeps
+//              the running max and sum in the exp2 domain, writes bf16 P into
+//              shared memory as the next MMA's A operand, and rescales its O
+//              row in TMEM only when the max grew by more than 2^8 (the
+//              deferred-rescale bound of FlashAttention-4: values stay within
+//              a factor 256 of the running max, far inside fp32/bf16 range).
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512) fp32 columns.
+// An S_X(j) commit also covers the earlier O_X(j-1), so the softmax may
+// overwrite P_X and rescale O_X as soon as S_X(j) has landed.
+// Work order: the heaviest tile pairs (latest query tiles) launch first.
 // V is first transposed into V^T [Hk, 128, Tpad] with every sequence's keys
 // starting on a 128-key boundary (zero padding), so both MMAs read K-major
 // operands with the 128-byte swizzle and every TMA x coordinate is aligned.
@@ -33,10 +40,11 @@ constexpr int kD = 128;
 constexpr int kBQ = 128, kBK = 128;
 constexpr int kBox = 128 * 128;                 // one 64-wide, 128-row swizzled box: 16 KB
 constexpr int kTile = 2 * kBox;                 // 128 x 128 bf16 tile as two boxes: 32 KB
-constexpr int kStages = 2;
-constexpr int kThreadsFA = 192;
-constexpr int kSmemFA = kTile /*Q*/ + kStages * 2 * kTile /*K, V^T*/ + kTile /*P*/ + 1024 + 256;
-constexpr int kTmemCols = 256;
+constexpr int kSlots = 3;                       // K / V^T ring of 32 KB tiles
+constexpr int kThreadsFA = 320;
+constexpr int kSmemFA = 2 * kTile /*Q_A, Q_B*/ + kSlots * kTile /*ring*/ + 2 * kTile /*P_A, P_B*/ + 1024 + 128;
+constexpr int kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;             // rescale O only when the max grows by more than 2^8
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
@@ -47,22 +55,36 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const float* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
-  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+// tcgen05.ld of 32 lanes x 32 columns without the wait (several loads in flight)
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+}
+
+// tcgen05.wait::ld that also ties the loaded registers to the wait, so no use
+// of them can be scheduled before it
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32_nowait(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+               : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // byte offset of bf16 element (row r, col c) of a 128x128 tile staged as two
@@ -76,57 +98,51 @@ struct FAMaps {
   CUtensorMap q, k, vt;
 };
 
-// tile index -> (sequence, query tile) from the device cu_seqlens
-__device__ __forceinline__ bool find_tile(const int* cu, int nseq, int t, int& s, int& qt) {
-  int acc = 0;
-  for (int i = 0; i < nseq; ++i) {
-    const int n = (cu[i + 1] - cu[i] + kBQ - 1) / kBQ;
-    if (t < acc + n) {
-      s = i;
-      qt = t - acc;
-      return true;
-    }
-    acc += n;
-  }
-  return false;
-}
-
-__global__ void __launch_bounds__(kThreadsFA, 1)
+__global__ void __maxnreg__(200)
     fa_fwd_kernel(const __grid_constant__ FAMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
-                  int nseq, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
+                  int nseq, int max_pairs, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
                   float* __restrict__ lse, int T, int* err_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;
-  uint8_t* skv = sq + kTile;                       // stage s: K at skv + s*2*kTile, V^T at + kTile
-  uint8_t* sp = skv + kStages * 2 * kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kTile);
+  uint8_t* sq = smem;                              // Q_A, Q_B
+  uint8_t* ring = sq + 2 * kTile;                  // slot i at ring + i * kTile
+  uint8_t* sp = ring + kSlots * kTile;             // P_A, P_B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * kTile);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;                    // [kStages]
-  uint64_t* kv_empty = kv_full + kStages;          // [kStages]
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* slot_full = bars + 1;                  // [kSlots]
+  uint64_t* slot_empty = slot_full + kSlots;       // [kSlots]
+  uint64_t* s_full = slot_empty + kSlots;          // [2]
+  uint64_t* p_full = s_full + 2;                   // [2]
+  uint64_t* o_done = p_full + 2;                   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* err = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, hk = h / (Hq / Hk);
-  int sidx = 0, qt = 0;
-  if (!find_tile(cu, nseq, blockIdx.x, sidx, qt)) return;  // uniform for the CTA: nothing allocated yet
+  // block -> (pair slot, head); pair slots run from the latest query tiles down
+  const int h = blockIdx.x % Hq, pslot = blockIdx.x / Hq;
+  const int pi = max_pairs - 1 - pslot / nseq, sidx = pslot % nseq;
   const int s0 = cu[sidx], len = cu[sidx + 1] - s0;
-  const int q0 = qt * kBQ;
-  const int nblocks = min(qt + 1, (len + kBK - 1) / kBK);  // causal: key blocks 0 .. qt
+  const int nkb = (len + kBK - 1) / kBK;
+  const int npairs = (nkb + 1) / 2;
+  // a max_seqlen below this sequence's length leaves its first pairs out: report it
+  if (threadIdx.x == 0 && pi == max_pairs - 1 && npairs > max_pairs) atomicExch(err_out, kErrProducer);
+  if (pi >= npairs) return;  // uniform for the CTA: nothing allocated yet
+  const int hk = h / (Hq / Hk);
+  const int qa0 = 2 * pi * kBQ;                    // first query of tile A (tile B follows)
+  const int nA = 2 * pi + 1;                       // causal key blocks of tile A
+  const int nB = min(2 * pi + 2, nkb);             // ... of tile B (tile B past the end repeats A's)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&slot_full[i], 1);
+      mbar_init(&slot_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+    }
     *err = kErrNone;
     fence_barrier_init();
   }
@@ -135,34 +151,39 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
 
   if (warp == 0) {
     if (lane == 0) {
       // V^T columns of every sequence start on a 128-key boundary; anything
       // else would give the TMA an unaligned x coordinate
       if (poff[sidx] & (kBK - 1)) *err = kErrProducer;
-      if (*err == kErrNone) mbar_expect_tx(q_full, kTile);
       const bool q_issued = *err == kErrNone;
       if (q_issued) {
-        tma_load_3d(sq, &maps.q, q_full, 0, h, s0 + q0);
-        tma_load_3d(sq + kBox, &maps.q, q_full, 64, h, s0 + q0);
+        mbar_expect_tx(q_full, 2 * kTile);
+        for (int t = 0; t < 2; ++t) {
+          tma_load_3d(sq + t * kTile, &maps.q, q_full, 0, h, s0 + qa0 + t * kBQ);
+          tma_load_3d(sq + t * kTile + kBox, &maps.q, q_full, 64, h, s0 + qa0 + t * kBQ);
+        }
       }
-      int j = 0;
-      for (; j < nblocks && *err == kErrNone; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&kv_empty[st], ((j / kStages) & 1) ^ 1, err, kErrProducer)) break;
-        uint8_t* kb = skv + st * 2 * kTile;
-        mbar_expect_tx(&kv_full[st], 2 * kTile);
-        tma_load_3d(kb, &maps.k, &kv_full[st], 0, hk, s0 + j * kBK);
-        tma_load_3d(kb + kBox, &maps.k, &kv_full[st], 64, hk, s0 + j * kBK);
-        tma_load_3d(kb + kTile, &maps.vt, &kv_full[st], poff[sidx] + j * kBK, 0, hk);
-        tma_load_3d(kb + kTile + kBox, &maps.vt, &kv_full[st], poff[sidx] + j * kBK + 64, 0, hk);
+      int L = 0;  // load sequence: K_0, V^T_0, K_1, V^T_1, ...
+      for (; L < 2 * nB && *err == kErrNone; ++L) {
+        const int slot = L % kSlots, use = L / kSlots;
+        if (!mbar_wait(&slot_empty[slot], (use & 1) ^ 1, err, kErrProducer)) break;
+        uint8_t* dst = ring + slot * kTile;
+        const int j = L >> 1;
+        mbar_expect_tx(&slot_full[slot], kTile);
+        if (!(L & 1)) {
+          tma_load_3d(dst, &maps.k, &slot_full[slot], 0, hk, s0 + j * kBK);
+          tma_load_3d(dst + kBox, &maps.k, &slot_full[slot], 64, hk, s0 + j * kBK);
+        } else {
+          tma_load_3d(dst, &maps.vt, &slot_full[slot], poff[sidx] + j * kBK, 0, hk);
+          tma_load_3d(dst + kBox, &maps.vt, &slot_full[slot], poff[sidx] + j * kBK + 64, 0, hk);
+        }
       }
       if (*err != kErrNone) {  // let the copies in flight land before exiting
-        for (int i = j - 1; i >= 0 && i >= j - kStages; --i) {
+        for (int i = L - 1; i >= 0 && i >= L - kSlots; --i) {
           const long long t0 = clock64();
-          while (!mbar_try_wait(&kv_full[i % kStages], (i / kStages) & 1))
+          while (!mbar_try_wait(&slot_full[i % kSlots], (i / kSlots) & 1))
             if (clock64() - t0 > kWaitCycles) break;
         }
         const long long t0 = clock64();
@@ -173,113 +194,147 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(kBQ, kBK);
-      bool ok = mbar_wait(q_full, 0, err, kErrMma);
-      for (int j = 0; j < nblocks && ok; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&kv_full[st], (j / kStages) & 1, err, kErrMma)) break;
-        tc_fence_after();
-        const uint8_t* kb = skv + st * 2 * kTile;
-        // S = Q K^T: K dimension = head dim, 8 steps of 16 over two 64-wide boxes
+      // S_X = Q_X K^T: K dimension = head dim, 8 steps of 16 over two 64-wide boxes
+      auto mma_s = [&](int X, const uint8_t* kb) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sw128_kmajor_desc(smem_addr(sq + (kk >> 2) * kBox)) + 2 * (kk & 3);
+          const uint64_t ad = sw128_kmajor_desc(smem_addr(sq + X * kTile + (kk >> 2) * kBox)) + 2 * (kk & 3);
           const uint64_t bd = sw128_kmajor_desc(smem_addr(kb + (kk >> 2) * kBox)) + 2 * (kk & 3);
-          umma_bf16(t_s, ad, bd, idesc, kk != 0);
+          umma_bf16(tmem + X * 128, ad, bd, idesc, kk != 0);
         }
-        umma_commit(s_full);
-        // wait for P (and the O rescale) from the softmax warps
-        if (!mbar_wait(p_full, j & 1, err, kErrMma)) break;
-        tc_fence_after();
-        // O += P V: K dimension = keys (two 64-key boxes of P and of V^T)
+      };
+      // O_X += P_X V: K dimension = keys (two 64-key boxes of P_X and of V^T)
+      auto mma_o = [&](int X, const uint8_t* vb, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sw128_kmajor_desc(smem_addr(sp + (kk >> 2) * kBox)) + 2 * (kk & 3);
-          const uint64_t bd = sw128_kmajor_desc(smem_addr(kb + kTile + (kk >> 2) * kBox)) + 2 * (kk & 3);
-          umma_bf16(t_o, ad, bd, idesc, (j | kk) != 0);
+          const uint64_t ad = sw128_kmajor_desc(smem_addr(sp + X * kTile + (kk >> 2) * kBox)) + 2 * (kk & 3);
+          const uint64_t bd = sw128_kmajor_desc(smem_addr(vb + (kk >> 2) * kBox)) + 2 * (kk & 3);
+          umma_bf16(tmem + 256 + X * 128, ad, bd, idesc, (acc || kk != 0) ? 1u : 0u);
         }
-        umma_commit(o_done);
-        umma_commit(&kv_empty[st]);
+      };
+      // O_B for block jb: needs P_B(jb) and V^T_jb; releases V^T_jb's slot
+      auto o_b = [&](int jb) -> bool {
+        const int LV = 2 * jb + 1, vs = LV % kSlots;
+        if (!mbar_wait(&p_full[1], jb & 1, err, kErrMma)) return false;
+        if (!mbar_wait(&slot_full[vs], (LV / kSlots) & 1, err, kErrMma)) return false;
+        tc_fence_after();
+        mma_o(1, ring + vs * kTile, jb > 0);
+        umma_commit(&o_done[1]);
+        umma_commit(&slot_empty[vs]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, err, kErrMma);
+      for (int j = 0; j < nB && ok; ++j) {
+        const int LK = 2 * j, ks = LK % kSlots;
+        if (!(ok = mbar_wait(&slot_full[ks], (LK / kSlots) & 1, err, kErrMma))) break;
+        tc_fence_after();
+        const uint8_t* kb = ring + ks * kTile;
+        if (j < nA) {
+          mma_s(0, kb);
+          umma_commit(&s_full[0]);
+        }
+        if (j > 0 && !(ok = o_b(j - 1))) break;
+        mma_s(1, kb);
+        umma_commit(&s_full[1]);
+        umma_commit(&slot_empty[ks]);
+        if (j < nA) {
+          const int LV = 2 * j + 1, vs = LV % kSlots;
+          if (!(ok = mbar_wait(&p_full[0], j & 1, err, kErrMma))) break;
+          if (!(ok = mbar_wait(&slot_full[vs], (LV / kSlots) & 1, err, kErrMma))) break;
+          tc_fence_after();
+          mma_o(0, ring + vs * kTile, j > 0);
+          umma_commit(&o_done[0]);
+        }
       }
+      if (ok) o_b(nB - 1);
     }
   } else {
-    // softmax warps: thread r owns row r (TMEM lane r)
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const int qrow = q0 + r;  // query index inside the sequence
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    // softmax warpgroups: X = 0 (warps 2-5, tile A) or 1 (warps 6-9, tile B);
+    // a warp reaches TMEM lanes 32 * (warp % 4) .. + 31
+    const int X = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qrow = qa0 + X * kBQ + r;            // query index inside the sequence
+    const int lim = min(qrow + 1, len);            // keys [0, lim) are visible to this row
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + X * 128, t_o = tmem + lane_off + 256 + X * 128;
+    uint8_t* px = sp + X * kTile;
+    const int nX = X ? nB : nA;
+    const int tile_end = qa0 + X * kBQ + kBQ;       // one past the tile's last query
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nblocks && ok; ++j) {
-      if (!mbar_wait(s_full, j & 1, err, kErrEpilogue)) {
-        ok = false;
-        break;
-      }
+    for (int j = 0; j < nX; ++j) {
+      // the warp continues or stops together (tcgen05.ld below is warp-collective)
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[X], j & 1, err, kErrEpilogue));
+      if (!ok) break;
       tc_fence_after();
-      const int k0 = j * kBK;
-      // pass 1: row max over the valid keys
-      float mb = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
+      uint32_t sr[4][32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = k0 + c * 32 + i;
-          if (key <= qrow && key < len) mb = fmaxf(mb, v[i] * scale_log2);
-        }
+      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + c * 32, sr[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_wait_ld(sr[c]);
+      const int k0 = j * kBK;
+      // only the diagonal block and a sequence's last block need the mask
+      if (k0 + kBK > tile_end - kBQ + 1 || k0 + kBK > len) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (k0 + c * 32 + i >= lim) sr[c][i] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mb);
-      const float base = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m - base);  // 0 on the first block (m = -inf)
-      // P smem and O are still in use by the previous block's MMA
-      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, err, kErrEpilogue)) {
-        ok = false;
-        break;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mb = fmaxf(mb, __uint_as_float(sr[c][i]));
+      const float mbs = mb * scale_log2;            // key k0 is always visible: mbs is finite
+      float alpha = 1.f;
+      if (mbs > m + kRescaleLog2) {
+        alpha = ex2(m - mbs);                       // 0 on the first block (m = -inf)
+        m = mbs;
       }
-      tc_fence_after();
-      // pass 2: p = exp2(s - m_new), row sum, bf16 P row into the swizzled A tile
-      float sum = 0.f;
-#pragma unroll 1
+      const float nm = -m;
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(t_s + lane_off + c * 32, v);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           uint32_t packed[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int i = g * 8 + 2 * e;
-            const int key = k0 + c * 32 + i;
-            const float p0 = (key <= qrow && key < len) ? exp2f(v[i] * scale_log2 - base) : 0.f;
-            const float p1 = (key + 1 <= qrow && key + 1 < len) ? exp2f(v[i + 1] * scale_log2 - base) : 0.f;
-            sum += p0 + p1;
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-            packed[e] = *reinterpret_cast<uint32_t*>(&b2);
+            const float p0 = ex2(fmaf(__uint_as_float(sr[c][i]), scale_log2, nm));
+            const float p1 = ex2(fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, nm));
+            sum0 += p0;
+            sum1 += p1;
+            packed[e] = pack_bf16(p0, p1);
           }
-          *reinterpret_cast<uint4*>(sp + sw_off(r, c * 32 + g * 8)) =
+          *reinterpret_cast<uint4*>(px + sw_off(r, c * 32 + g * 8)) =
               make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
       }
-      l = l * alpha + sum;
-      m = m_new;
-      // rescale O when the max moved (O holds the blocks before j); tcgen05.ld/st
-      // are warp-collective, so the whole warp takes the branch together
+      l = l * alpha + (sum0 + sum1);
+      // O_X holds blocks < j (its MMA finished before S_X(j) did); rescale rows
+      // whose max moved.  tcgen05.ld/st are warp-collective: the warp decides together.
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);
+          uint32_t v[32];
+          tmem_ld32_nowait(t_o + c * 32, v);
+          tmem_wait_ld(v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st_32x32b_x32(t_o + lane_off + c * 32, v);
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32_nowait(t_o + c * 32, v);
         }
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
       }
       // P (generic-proxy stores) must be visible to the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[X]);
     }
-    if (ok && nblocks > 0) ok = mbar_wait(o_done, (nblocks - 1) & 1, err, kErrEpilogue);
+    if (ok) ok = mbar_wait(&o_done[X], (nX - 1) & 1, err, kErrEpilogue);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     // epilogue: O / l -> bf16 output row, natural-log LSE
     const bool valid = qrow < len;
@@ -287,14 +342,15 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
     __nv_bfloat16* orow = out + ((int64_t)(s0 + qrow) * Hq + h) * kD;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld_32x32b_x32(t_o + lane_off + c * 32, v);
+      uint32_t v[32];
+      tmem_ld32_nowait(t_o + c * 32, v);
+      tmem_wait_ld(v);
       if (valid) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           float tmp[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) tmp[e] = v[g * 8 + e] * inv;
+          for (int e = 0; e < 8; ++e) tmp[e] = __uint_as_float(v[g * 8 + e]) * inv;
           store8(orow + c * 32 + g * 8, tmp);
         }
       }
@@ -382,7 +438,8 @@ int64_t fa_fwd_status() {
 }
 
 // q [T, Hq, 128], k/v [T, Hk, 128] bf16 contiguous, cu [nseq + 1] int32 on
-// the device, max_seqlen a host upper bound.  Returns (out [T, Hq, 128] bf16,
+// the device, max_seqlen a host upper bound of the longest sequence (a
+// smaller value leaves query tiles out and sets the status word).  Returns (out [T, Hq, 128] bf16,
 // lse [Hq, T] fp32 natural log).
 std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu,
                                   int64_t max_seqlen, double scale) {
@@ -421,12 +478,14 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
     cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFA);
     attr = true;
   }
-  const int64_t tiles = (T + kBQ - 1) / kBQ + nseq;  // upper bound of sum over sequences of ceil(len / 128)
-  fa_fwd_kernel<<<dim3((unsigned)tiles, (unsigned)Hq), kThreadsFA, kSmemFA, stream()>>>(
-      maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)Hq, (int)Hk,
+  TORCH_CHECK(max_seqlen > 0, "fa_fwd: max_seqlen must bound the longest sequence");
+  const int64_t max_pairs = ((max_seqlen + kBQ - 1) / kBQ + 1) / 2;
+  const int64_t blocks = max_pairs * nseq * Hq;
+  TORCH_CHECK(blocks < (int64_t{1} << 31), "fa_fwd: grid too large");
+  fa_fwd_kernel<<<(unsigned)blocks, kThreadsFA, kSmemFA, stream()>>>(
+      maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_pairs, (int)Hq, (int)Hk,
       (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), lse.data_ptr<float>(), (int)T,
       fa_err_word().data_ptr<int>());
-  (void)max_seqlen;
   return {out, lse};
 }
 

@@ -41,6 +41,7 @@ constexpr int kBQ = 128, kBK = 128;
 constexpr int kBox = 128 * 128;                 // one 64-wide, 128-row swizzled box: 16 KB
 constexpr int kTile = 2 * kBox;                 // 128 x 128 bf16 tile as two boxes: 32 KB
 constexpr int kSlots = 3;                       // K / V^T ring of 32 KB tiles
+// 10 warps: one SM sub-partition holds 3 of them, which caps a thread at 168 registers
 constexpr int kThreadsFA = 320;
 constexpr int kSmemFA = 2 * kTile /*Q_A, Q_B*/ + kSlots * kTile /*ring*/ + 2 * kTile /*P_A, P_B*/ + 1024 + 128;
 constexpr int kTmemCols = 512;
@@ -98,7 +99,7 @@ struct FAMaps {
   CUtensorMap q, k, vt;
 };
 
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreadsFA, 1)
     fa_fwd_kernel(const __grid_constant__ FAMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                   int nseq, int max_pairs, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
                   float* __restrict__ lse, int T, int* err_out) {

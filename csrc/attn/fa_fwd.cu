@@ -369,23 +369,40 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
 }
 
 // V [T, Hk, 128] -> V^T [Hk, 128, Tpad], sequence s's key t at column
-// poff[s] + (t - cu[s]); the padding columns are zero.
-__global__ void vt_pack_kernel(const __nv_bfloat16* __restrict__ v, const int* __restrict__ cu,
-                               const int* __restrict__ poff, int nseq, int Hk, int Tpad,
-                               __nv_bfloat16* __restrict__ vt) {
+// poff[s] + (t - cu[s]) where poff[s] sums the earlier sequences' lengths
+// rounded up to 128; the padding columns are zero.  Block (0, 0, 0) also
+// writes poff for the attention kernel.
+__global__ void vt_pack_kernel(const __nv_bfloat16* __restrict__ v, const int* __restrict__ cu, int nseq, int Hk,
+                               int Tpad, __nv_bfloat16* __restrict__ vt, int* __restrict__ poff) {
   __shared__ __nv_bfloat16 tile[32][33];
   const int hk = blockIdx.z;
   const int col0 = blockIdx.x * 32;  // padded key column
   const int d0 = blockIdx.y * 32;
-  // which sequence owns this padded column block (blocks never straddle: poff is 128-aligned)
-  int s = 0;
-  while (s + 1 < nseq && poff[s + 1] <= col0) ++s;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  if ((blockIdx.x | blockIdx.y | blockIdx.z) == 0 && tx == 0 && ty == 0) {
+    int acc = 0;
+    for (int i = 0; i < nseq; ++i) {
+      poff[i] = acc;
+      acc += (cu[i + 1] - cu[i] + kBK - 1) & ~(kBK - 1);
+    }
+    poff[nseq] = acc;
+  }
+  // the sequence owning this 32-column block (blocks never straddle: offsets are 128-aligned)
+  int s = nseq, off = 0;
+  for (int i = 0, acc = 0; i < nseq; ++i) {
+    const int pl = (cu[i + 1] - cu[i] + kBK - 1) & ~(kBK - 1);
+    if (col0 < acc + pl) {
+      s = i;
+      off = acc;
+      break;
+    }
+    acc += pl;
+  }
+  const int len = s < nseq ? cu[s + 1] - cu[s] : 0;
+  const int start = s < nseq ? cu[s] : 0;
   for (int i = ty; i < 32; i += 8) {
-    const int col = col0 + i;
-    const int t = col - poff[s];
-    const bool ok = s < nseq && t >= 0 && t < cu[s + 1] - cu[s];
-    tile[i][tx] = ok ? v[((int64_t)(cu[s] + t) * Hk + hk) * kD + d0 + tx] : __float2bfloat16(0.f);
+    const int t = col0 + i - off;
+    tile[i][tx] = (t >= 0 && t < len) ? v[((int64_t)(start + t) * Hk + hk) * kD + d0 + tx] : __float2bfloat16(0.f);
   }
   __syncthreads();
   for (int i = ty; i < 32; i += 8) vt[((int64_t)hk * kD + d0 + i) * Tpad + col0 + tx] = tile[tx][i];
@@ -458,18 +475,12 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   auto out = torch::empty_like(q);
   auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
   if (T == 0 || nseq <= 0) return {out, lse};
-  // per-sequence 128-aligned key offsets for V^T (device side, no host sync)
-  auto lens = (cu.slice(0, 1) - cu.slice(0, 0, nseq));
-  // integer floor division (ATen's `/` on int tensors is true division)
-  auto padded = torch::div(lens + (kBK - 1), kBK, "floor") * kBK;
-  TORCH_CHECK(padded.scalar_type() == at::kInt, "fa_fwd: padded lengths must stay int32");
-  auto poff = torch::zeros({nseq + 1}, cu.options());
-  poff.slice(0, 1).copy_(torch::cumsum(padded, 0));
   const int64_t Tpad = ((T + kBK - 1) / kBK + nseq) * kBK;  // upper bound of the padded total
   auto vt = torch::empty({Hk, kD, Tpad}, q.options());
+  auto poff = torch::empty({nseq + 1}, cu.options());
   vt_pack_kernel<<<dim3((unsigned)(Tpad / 32), kD / 32, (unsigned)Hk), dim3(32, 8), 0, stream()>>>(
-      (const __nv_bfloat16*)v.data_ptr(), cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)Hk, (int)Tpad,
-      (__nv_bfloat16*)vt.data_ptr());
+      (const __nv_bfloat16*)v.data_ptr(), cu.data_ptr<int>(), nseq, (int)Hk, (int)Tpad,
+      (__nv_bfloat16*)vt.data_ptr(), poff.data_ptr<int>());
   FAMaps maps;
   maps.q = map3(q.data_ptr(), kD, Hq, T, kD * 2, Hq * kD * 2, 64, 1, kBQ);
   maps.k = map3(k.data_ptr(), kD, Hk, T, kD * 2, Hk * kD * 2, 64, 1, kBK);

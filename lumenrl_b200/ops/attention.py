@@ -9,10 +9,10 @@ caller, who packed the batch on the host.  This is the library attention of
 the training step (the reference also calls a library kernel here,
 ``engine/training/packing.py:363-421``).
 
-``LRL_TRAIN_ATTN=tc`` switches the forward to this package's tcgen05 kernel
-(``csrc/attn/fa_fwd.cu``: bf16, head dim 128, causal); its log-sum-exp is
-written in the varlen layout ``[Hq, T]`` so the backward stays on the
-library kernel.
+The forward runs on this package's tcgen05 kernel (``csrc/attn/fa_fwd.cu``:
+bf16, head dim 128, causal) by default; its log-sum-exp is written in the
+varlen layout ``[Hq, T]`` so the backward stays on the library kernel.
+``LRL_TRAIN_ATTN=fa2`` puts the forward back on the library kernel.
 """
 
 from __future__ import annotations
@@ -23,7 +23,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
-TRAIN_ATTN = os.environ.get("LRL_TRAIN_ATTN", "fa2")   # "fa2" (library) | "tc" (own tcgen05 forward)
+TRAIN_ATTN = os.environ.get("LRL_TRAIN_ATTN", "tc")    # "tc" (own tcgen05 forward) | "fa2" (library)
 
 
 class _VarlenFlash(torch.autograd.Function):

@@ -398,11 +398,13 @@ def test_fa_fwd_tcgen05(cuda, lens):
     close(lse, rl, 1e-2, 1e-3)
 
 
-def test_fa_tc_fwd_bwd(cuda, monkeypatch):
-    """Training path with the tcgen05 forward: gradients through the library
-    backward fed with this kernel's output and LSE."""
+@pytest.mark.parametrize("mode", ["tc", "fa2"])
+def test_fa_fwd_bwd_modes(cuda, monkeypatch, mode):
+    """Training attention with the tcgen05 forward (gradients through the
+    library backward fed with its output and LSE) and with the library
+    forward."""
     from lumenrl_b200.ops import attention
-    monkeypatch.setattr(attention, "TRAIN_ATTN", "tc")
+    monkeypatch.setattr(attention, "TRAIN_ATTN", mode)
     torch.manual_seed(1)
     lens = [37, 200, 1, 511]
     T, Hq, Hk, D = sum(lens), 8, 2, 128

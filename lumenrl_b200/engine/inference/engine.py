@@ -99,20 +99,26 @@ class RolloutEngine:
             self.runner.fp8 = FP8RolloutQuantizer(fp8_rollout, self.args.num_layers)
             self.runner.fp8.quantize_model(model)
         self._graphs: dict[tuple, DecodeGraph] = {}
+        self._graphs_pool_ptr = self.cache.pool_ptr
         self.weight_version = 0
 
     # -- lifecycle ---------------------------------------------------------------
     def sleep(self, release_memory: bool = False) -> None:
         """Free the KV pool.  The block stays in the caching allocator (so the
         trainer's activations reuse it and the next wake is a cache hit)
-        unless ``release_memory`` returns it to the driver."""
-        self._graphs.clear()
+        unless ``release_memory`` returns it to the driver.  Captured decode
+        graphs point at the pool; they are kept, and dropped at the next wake
+        only if the pool comes back at another address."""
         self.cache.sleep()
         if release_memory and self.device.type == "cuda":
+            self._graphs.clear()
             torch.cuda.empty_cache()
 
     def wake(self) -> None:
         self.cache.wake()
+        if self.cache.pool_ptr != self._graphs_pool_ptr:
+            self._graphs.clear()
+            self._graphs_pool_ptr = self.cache.pool_ptr
 
     def update_weights(self, flat: Optional[Tensor] = None, version: Optional[int] = None) -> None:
         """Colocated: the engine aliases the trainer buffer, nothing to move.

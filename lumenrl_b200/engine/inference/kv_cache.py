@@ -91,6 +91,7 @@ class PagedKVCache:
         self._pool = torch.empty((2, s.num_layers) + shape, dtype=s.dtype, device=self.device)
         self.k = [self._pool[0, i] for i in range(s.num_layers)]
         self.v = [self._pool[1, i] for i in range(s.num_layers)]
+        self.pool_ptr = self._pool.data_ptr()   # captured decode graphs point here
         self.allocator = BlockAllocator(self.num_blocks)
         self.awake = True
 

@@ -45,6 +45,19 @@ def test_seed_determinism_and_sleep_wake():
     assert torch.equal(a.responses, b.responses)
     c = eng.generate(prompts, SamplingParams(max_new_tokens=8, n=4, seed=12, eos_token_id=None))
     assert not torch.equal(a.responses, c.responses)
+    # decode graphs survive a sleep/wake that returns the same KV block, and are
+    # dropped when the pool moves
+    assert eng._graphs
+    before = eng.cache.pool_ptr
+    eng.sleep()
+    eng.wake()
+    assert bool(eng._graphs) == (eng.cache.pool_ptr == before)
+    eng.sleep()
+    eng._graphs_pool_ptr = -1
+    eng.wake()
+    assert not eng._graphs and eng._graphs_pool_ptr == eng.cache.pool_ptr
+    d = eng.generate(prompts, SamplingParams(max_new_tokens=8, n=4, seed=11, eos_token_id=None))
+    assert torch.equal(a.responses, d.responses)
 
 
 def test_eos_and_waves():

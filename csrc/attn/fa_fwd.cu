@@ -27,6 +27,8 @@
 // starting on a 128-key boundary (zero padding), so both MMAs read K-major
 // operands with the 128-byte swizzle and every TMA x coordinate is aligned.
 // Every mbarrier wait is bounded (tc_gemm.cuh) and reports an error word.
+#include <cstdlib>
+
 #include "../common.cuh"
 #include "../gemm/tc_gemm.cuh"
 
@@ -45,7 +47,8 @@ constexpr int kSlots = 3;                       // K / V^T ring of 32 KB tiles
 constexpr int kThreadsFA = 320;
 constexpr int kSmemFA = 2 * kTile /*Q_A, Q_B*/ + kSlots * kTile /*ring*/ + 2 * kTile /*P_A, P_B*/ + 1024 + 128;
 constexpr int kTmemCols = 512;
-constexpr float kRescaleLog2 = 8.f;             // rescale O only when the max grows by more than 2^8
+constexpr float kRescaleLog2 = 8.f;
+constexpr int kDefaultVariant = 0;             // rescale O only when the max grows by more than 2^8
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {
@@ -95,10 +98,75 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)(box * kBox + r * 128 + ((((cc >> 3) ^ (r & 7))) << 4) + ((cc & 7) << 1));
 }
 
+// masked scores (keys at or past `lim`) become -inf
+__device__ __forceinline__ void mask_chunk(uint32_t (&v)[32], int key0, int lim) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (key0 + i >= lim) v[i] = __float_as_uint(-INFINITY);
+}
+
+__device__ __forceinline__ void max_chunk(const uint32_t (&v)[32], float& mx0, float& mx1) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    mx0 = fmaxf(mx0, __uint_as_float(v[i]));
+    mx1 = fmaxf(mx1, __uint_as_float(v[i + 1]));
+  }
+}
+
+// Running max in the exp2 domain with the deferred rescale: the max moves only
+// when the block's max exceeds it by more than 2^8; returns the factor for O and l.
+__device__ __forceinline__ float new_max(float mbs, float& m) {
+  if (mbs > m + kRescaleLog2) {  // always on the first block (m = -inf): factor 0
+    const float alpha = ex2(m - mbs);
+    m = mbs;
+    return alpha;
+  }
+  return 1.f;
+}
+
+// 2^x on the FMA pipe (takes load off the MUFU unit): x = n + f with n the
+// nearest integer (found by adding 1.5 * 2^23, which leaves n in the low
+// mantissa bits) and f in [-1/2, 1/2]; 2^f from a cubic fitted by weighted
+// least squares on Chebyshev nodes (max relative error 1.2e-4, far below the
+// bf16 rounding of P); 2^n is added to the exponent field.  x is clamped to
+// -125 so the result stays a normal number (about 2e-38 for masked scores,
+// which the row sum and P.V cannot notice).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(f, 0.05459282f, 0.24221784f);
+  p = fmaf(f, p, 0.69336860f);
+  p = fmaf(f, p, 1.f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+template <bool kPoly>
+__device__ __forceinline__ void exp_pack_store(const uint32_t (&v)[32], int cb, float scale_log2, float nm,
+                                               float (&sm)[4], uint8_t* px, int r) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint32_t packed[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = g * 8 + 2 * e;
+      const float x0 = fmaf(__uint_as_float(v[i]), scale_log2, nm);
+      const float x1 = fmaf(__uint_as_float(v[i + 1]), scale_log2, nm);
+      const float p0 = ex2(x0);
+      const float p1 = kPoly ? ex2_poly(x1) : ex2(x1);
+      sm[(e & 1) * 2] += p0;
+      sm[(e & 1) * 2 + 1] += p1;
+      packed[e] = pack_bf16(p0, p1);
+    }
+    *reinterpret_cast<uint4*>(px + sw_off(r, cb + g * 8)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+}
+
 struct FAMaps {
   CUtensorMap q, k, vt;
 };
 
+template <bool kTwoPass, bool kPoly>
 __global__ void __launch_bounds__(kThreadsFA, 1)
     fa_fwd_kernel(const __grid_constant__ FAMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                   int nseq, int max_pairs, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
@@ -269,52 +337,62 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[X], j & 1, err, kErrEpilogue));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + c * 32, sr[c]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_wait_ld(sr[c]);
       const int k0 = j * kBK;
       // only the diagonal block and a sequence's last block need the mask
-      if (k0 + kBK > tile_end - kBQ + 1 || k0 + kBK > len) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (k0 + c * 32 + i >= lim) sr[c][i] = __float_as_uint(-INFINITY);
-      }
-      float mb = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mb = fmaxf(mb, __uint_as_float(sr[c][i]));
-      const float mbs = mb * scale_log2;            // key k0 is always visible: mbs is finite
+      const bool need_mask = k0 + kBK > tile_end - kBQ + 1 || k0 + kBK > len;
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};
       float alpha = 1.f;
-      if (mbs > m + kRescaleLog2) {
-        alpha = ex2(m - mbs);                       // 0 on the first block (m = -inf)
-        m = mbs;
-      }
-      const float nm = -m;
-      float sum0 = 0.f, sum1 = 0.f;
+      if constexpr (!kTwoPass) {
+        // one round of TMEM loads: the whole 128-score row in registers
+        uint32_t sr[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + c * 32, sr[c]);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint32_t packed[4];
+        for (int c = 0; c < 4; ++c) tmem_wait_ld(sr[c]);
+        if (need_mask) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = g * 8 + 2 * e;
-            const float p0 = ex2(fmaf(__uint_as_float(sr[c][i]), scale_log2, nm));
-            const float p1 = ex2(fmaf(__uint_as_float(sr[c][i + 1]), scale_log2, nm));
-            sum0 += p0;
-            sum1 += p1;
-            packed[e] = pack_bf16(p0, p1);
+          for (int c = 0; c < 4; ++c) mask_chunk(sr[c], k0 + c * 32, lim);
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) max_chunk(sr[c], mx0, mx1);
+        alpha = new_max(fmaxf(mx0, mx1) * scale_log2, m);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) exp_pack_store<kPoly>(sr[c], c * 32, scale_log2, -m, sm, px, r);
+      } else {
+        // two rounds of 64 columns: max first, then reload for the exponentials
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t a0[32], a1[32];
+          tmem_ld32_nowait(t_s + hh * 64, a0);
+          tmem_ld32_nowait(t_s + hh * 64 + 32, a1);
+          tmem_wait_ld(a0);
+          tmem_wait_ld(a1);
+          if (need_mask) {
+            mask_chunk(a0, k0 + hh * 64, lim);
+            mask_chunk(a1, k0 + hh * 64 + 32, lim);
           }
-          *reinterpret_cast<uint4*>(px + sw_off(r, c * 32 + g * 8)) =
-              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          max_chunk(a0, mx0, mx1);
+          max_chunk(a1, mx0, mx1);
+        }
+        alpha = new_max(fmaxf(mx0, mx1) * scale_log2, m);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t a0[32], a1[32];
+          tmem_ld32_nowait(t_s + hh * 64, a0);
+          tmem_ld32_nowait(t_s + hh * 64 + 32, a1);
+          tmem_wait_ld(a0);
+          tmem_wait_ld(a1);
+          if (need_mask) {
+            mask_chunk(a0, k0 + hh * 64, lim);
+            mask_chunk(a1, k0 + hh * 64 + 32, lim);
+          }
+          exp_pack_store<kPoly>(a0, hh * 64, scale_log2, -m, sm, px, r);
+          exp_pack_store<kPoly>(a1, hh * 64 + 32, scale_log2, -m, sm, px, r);
         }
       }
-      l = l * alpha + (sum0 + sum1);
+      l = l * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
       // O_X holds blocks < j (its MMA finished before S_X(j) did); rescale rows
       // whose max moved.  tcgen05.ld/st are warp-collective: the warp decides together.
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -460,7 +538,7 @@ int64_t fa_fwd_status() {
 // smaller value leaves query tiles out and sets the status word).  Returns (out [T, Hq, 128] bf16,
 // lse [Hq, T] fp32 natural log).
 std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu,
-                                  int64_t max_seqlen, double scale) {
+                                  int64_t max_seqlen, double scale, int64_t variant) {
   LRL_CHECK(q);
   LRL_CHECK(k);
   LRL_CHECK(v);
@@ -485,16 +563,30 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   maps.q = map3(q.data_ptr(), kD, Hq, T, kD * 2, Hq * kD * 2, 64, 1, kBQ);
   maps.k = map3(k.data_ptr(), kD, Hk, T, kD * 2, Hk * kD * 2, 64, 1, kBK);
   maps.vt = map3(vt.data_ptr(), Tpad, kD, Hk, Tpad * 2, kD * Tpad * 2, 64, kD, 1);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFA);
-    attr = true;
-  }
   TORCH_CHECK(max_seqlen > 0, "fa_fwd: max_seqlen must bound the longest sequence");
   const int64_t max_pairs = ((max_seqlen + kBQ - 1) / kBQ + 1) / 2;
   const int64_t blocks = max_pairs * nseq * Hq;
   TORCH_CHECK(blocks < (int64_t{1} << 31), "fa_fwd: grid too large");
-  fa_fwd_kernel<<<(unsigned)blocks, kThreadsFA, kSmemFA, stream()>>>(
+  // softmax variants: bit 0 = two rounds of TMEM loads (fewer registers),
+  // bit 1 = half of the exponentials on the FMA pipe
+  static const int env_variant = [] {
+    const char* e = std::getenv("LRL_FA_VARIANT");
+    return e ? std::atoi(e) : kDefaultVariant;
+  }();
+  const int var = variant >= 0 ? (int)variant : env_variant;
+  TORCH_CHECK(var >= 0 && var < 4, "fa_fwd: variant 0..3");
+  using Kern = void (*)(const FAMaps, const int*, const int*, int, int, int, int, float, __nv_bfloat16*, float*, int,
+                        int*);
+  static const Kern kerns[4] = {fa_fwd_kernel<false, false>, fa_fwd_kernel<true, false>,
+                                fa_fwd_kernel<false, true>, fa_fwd_kernel<true, true>};
+  static bool attr[4] = {false, false, false, false};
+  if (!attr[var]) {
+    TORCH_CHECK(cudaFuncSetAttribute(kerns[var], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFA) ==
+                    cudaSuccess,
+                "fa_fwd: shared memory opt-in failed");
+    attr[var] = true;
+  }
+  kerns[var]<<<(unsigned)blocks, kThreadsFA, kSmemFA, stream()>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_pairs, (int)Hq, (int)Hk,
       (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), lse.data_ptr<float>(), (int)T,
       fa_err_word().data_ptr<int>());

@@ -172,6 +172,9 @@ def bench_attn_train(ns) -> dict:
         t2 = _time(lambda: torch.ops.aten._flash_attention_forward(qd, kd, vd, cu, cu, ns.seq, ns.seq, 0.0, True,
                                                                     False, scale=sc), ns.steps, ns.warmup)
         t3 = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc), ns.steps, ns.warmup)
+        for var in range(4):
+            tv = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc, var), ns.steps, ns.warmup)
+            res[f"fwd_tc_v{var}_tflops"] = round(fflops / tv / 1e9, 1)
     res.update(fwd_fa2_ms=t2, fwd_fa2_tflops=fflops / t2 / 1e9, fwd_tc_ms=t3, fwd_tc_tflops=fflops / t3 / 1e9,
                fwd_tc_status=int(ext().fa_fwd_status()))
     return res

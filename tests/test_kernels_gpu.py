@@ -380,10 +380,12 @@ def _causal_ref(q, k, v, lens, scale):
     return torch.cat(outs), torch.cat(lses, 1)
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 @pytest.mark.parametrize("lens", [[128], [1, 100, 129, 300], [513, 7, 256, 1024]])
-def test_fa_fwd_tcgen05(cuda, lens):
-    """tcgen05 flash-attention forward (ragged packed sequences, GQA 4:1)
-    against the fp32 reference: output and natural-log LSE."""
+def test_fa_fwd_tcgen05(cuda, lens, variant):
+    """tcgen05 flash-attention forward (ragged packed sequences, GQA 4:1) in
+    each softmax variant against the fp32 reference: output and natural-log
+    LSE."""
     from lumenrl_b200.ops.ext import ext
     torch.manual_seed(0)
     T, Hq, Hk, D = sum(lens), 8, 2, 128
@@ -391,7 +393,7 @@ def test_fa_fwd_tcgen05(cuda, lens):
     q = torch.randn(T, Hq, D, device=cuda).to(torch.bfloat16)
     k = torch.randn(T, Hk, D, device=cuda).to(torch.bfloat16)
     v = torch.randn(T, Hk, D, device=cuda).to(torch.bfloat16)
-    out, lse = ext().fa_fwd(q, k, v, cu, max(lens), D ** -0.5)
+    out, lse = ext().fa_fwd(q, k, v, cu, max(lens), D ** -0.5, variant)
     assert ext().fa_fwd_status() == 0
     ro, rl = _causal_ref(q.float(), k.float(), v.float(), lens, D ** -0.5)
     close(out, ro, 2e-2, 2e-2)

@@ -14,6 +14,13 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
                                    float eps) {
+  // the weight does not depend on the previous kernel: fetch it before the PDL wait
+  bf16x8 wraw[kMaxChunks];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * blockDim.x + threadIdx.x) * 8;
+    if (col < H) wraw[c] = *reinterpret_cast<const bf16x8*>(w + col);
+  }
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
@@ -45,10 +52,13 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   for (int c = 0; c < kMaxChunks; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
     if (col < H) {
-      float wf[8], o[8];
-      load8(w + col, wf);
+      float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * r * wf[i];
+      for (int i = 0; i < 4; ++i) {
+        const float2 wf = __bfloat1622float2(wraw[c].h[i]);
+        o[2 * i] = v[c][2 * i] * r * wf.x;
+        o[2 * i + 1] = v[c][2 * i + 1] * r * wf.y;
+      }
       store8(y + base + col, o);
     }
   }

@@ -311,44 +311,65 @@ __device__ void attend(const __nv_bfloat16* __restrict__ q, const CUtensorMap* t
     part_o[pi * kHD + col] = lsum > 0.f ? acc / lsum * v_scale : 0.f;
     if (col == 0) part_lse[pi] = lsum > 0.f ? mstar + log2f(lsum) : -INFINITY;
   }
-  // count this item in on every row it covered; the item completing a row merges it
+  // count this item in on every row it covered (one atomic per row, in
+  // parallel); the item completing a row merges it
   __threadfence();
   __syncthreads();
-  volatile unsigned* last_rows = reinterpret_cast<volatile unsigned*>(err + 1);  // past the ring: still free
-  const int nrows = rows / G;  // sequences covered (rows are whole GQA groups)
-  if (threadIdx.x == 0) {
-    unsigned mask = 0;
-    for (int i = 0; i < nrows; ++i) {
-      int* c = mg.counters + (int64_t)(seq0 + i) * (Hq / G) + h;
-      if (atomicAdd(c, 1) == mg.expected - 1) {
-        *c = 0;  // every arrival is in: reset for the next launch
-        mask |= 1u << i;
-      }
+  volatile unsigned long long* last_rows = reinterpret_cast<volatile unsigned long long*>(err + 2);  // past the ring
+  const int nrows = rows / G;  // sequences covered (rows are whole GQA groups), <= 64
+  if (threadIdx.x == 0) *last_rows = 0ull;
+  __syncthreads();
+  if (threadIdx.x < nrows) {
+    int* c = mg.counters + (int64_t)(seq0 + threadIdx.x) * (Hq / G) + h;
+    if (atomicAdd(c, 1) == mg.expected - 1) {
+      *c = 0;  // every arrival is in: reset for the next launch
+      atomicOr(const_cast<unsigned long long*>(last_rows), 1ull << threadIdx.x);
     }
-    *last_rows = mask;
   }
   __syncthreads();
-  const unsigned mask = *last_rows;
-  if (mask == 0) return;
+  const unsigned long long mask = *last_rows;
+  if (mask == 0ull) return;
   __threadfence();
+  float* wsm = reinterpret_cast<float*>(smem);  // [slots][G] merge weights (the ring is free now)
   for (int i = 0; i < nrows; ++i) {
-    if (!(mask >> i & 1u)) continue;
+    if (!(mask >> i & 1ull)) continue;
     const int b = seq0 + i;
-    for (int idx = threadIdx.x; idx < G * kHD; idx += kThreadsT) {
-      const int qh = h * G + idx / kHD, col = idx % kHD;
+    // one round of loads: every slot's LSE for the row's G query heads
+    for (int idx = threadIdx.x; idx < mg.slots * G; idx += kThreadsT)
+      wsm[idx] = __ldcg(part_lse + ((int64_t)(idx / G) * B + b) * Hq + (int64_t)h * G + idx % G);
+    __syncthreads();
+    if (threadIdx.x < G) {
       float mx = -INFINITY;
-      for (int sl = 0; sl < mg.slots; ++sl) mx = fmaxf(mx, __ldcg(part_lse + ((int64_t)sl * B + b) * Hq + qh));
-      float den = 0.f, acc = 0.f;
-      if (mx != -INFINITY) {
-        for (int sl = 0; sl < mg.slots; ++sl) {
-          const int64_t pi = ((int64_t)sl * B + b) * Hq + qh;
-          const float f = exp2f(__ldcg(part_lse + pi) - mx);
-          den += f;
-          acc += f * __ldcg(part_o + pi * kHD + col);
-        }
+      for (int sl = 0; sl < mg.slots; ++sl) mx = fmaxf(mx, wsm[sl * G + threadIdx.x]);
+      float den = 0.f;
+      for (int sl = 0; sl < mg.slots; ++sl) {
+        const float f = mx == -INFINITY ? 0.f : exp2f(wsm[sl * G + threadIdx.x] - mx);
+        wsm[sl * G + threadIdx.x] = f;
+        den += f;
       }
-      mg.out[((int64_t)b * Hq + qh) * kHD + col] = __float2bfloat16(den > 0.f ? acc / den : 0.f);
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      for (int sl = 0; sl < mg.slots; ++sl) wsm[sl * G + threadIdx.x] *= inv;
     }
+    __syncthreads();
+    // weighted sum of the partial rows, 4 columns per thread, loads independent across slots
+    for (int idx = threadIdx.x; idx < G * (kHD / 4); idx += kThreadsT) {
+      const int qq = idx / (kHD / 4), c4 = idx % (kHD / 4);
+      const int qh = h * G + qq;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int sl = 0; sl < mg.slots; ++sl) {
+        const float f = wsm[sl * G + qq];
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(part_o + (((int64_t)sl * B + b) * Hq + qh) * kHD) + c4);
+        acc.x += f * o.x;
+        acc.y += f * o.y;
+        acc.z += f * o.z;
+        acc.w += f * o.w;
+      }
+      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(mg.out + ((int64_t)b * Hq + qh) * kHD + 4 * c4);
+      dst[0] = __floats2bfloat162_rn(acc.x, acc.y);
+      dst[1] = __floats2bfloat162_rn(acc.z, acc.w);
+    }
+    __syncthreads();  // wsm is reused by the next row
   }
 }
 
@@ -503,6 +524,7 @@ torch::Tensor paged_decode_attn_tma(torch::Tensor q, torch::Tensor kc, torch::Te
   if (B == 0) return out;
   const int pps = pick_pps(B * Hk, max_pages);
   const int nsplit = (int)((max_pages + pps - 1) / pps);
+  TORCH_CHECK((int64_t)nsplit * (Hq / Hk) * 4 <= kStagesT * kStageBytes, "decode_tma: too many splits to merge");
   auto po = torch::empty({nsplit, B, Hq, kHD}, q.options().dtype(at::kFloat));
   auto pl = torch::empty({nsplit, B, Hq}, q.options().dtype(at::kFloat));
   static bool attr = false;
@@ -544,6 +566,7 @@ torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, to
   const int ssplit = (int)((spages + pps - 1) / pps);
   const int psplit = (int)((ppages + pps - 1) / pps);
   const int total = psplit + ssplit;
+  TORCH_CHECK((int64_t)total * G * 4 <= kStagesT * kStageBytes && group <= 64, "decode_tma: too many splits to merge");
   auto po = torch::empty({total, B, Hq, kHD}, q.options().dtype(at::kFloat));
   auto pl = torch::empty({total, B, Hq}, q.options().dtype(at::kFloat));
   const float sl2 = (float)(scale * 1.4426950408889634);

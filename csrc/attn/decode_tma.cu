@@ -15,12 +15,9 @@
 // Work items are the same as paged_decode.cu: (context split, kv head, row)
 // for the per-row kernel, and for the cascade kernel prefix items (split, kv
 // head, group of rows sharing the prompt pages) followed by per-row suffix
-// items, all writing (o, lse) partials.  There is no separate combine launch:
-// every item counts itself in on a per-(row, kv head) counter after its
-// partials are fenced, and the item that completes a counter merges that
-// row's partials into the bf16 output and resets the counter (no waiting on
-// other CTAs).  Every wait is bounded: on expiry the CTA records an error
-// word, drains its in-flight copies (bounded) and exits.
+// items, all writing (o, lse) partials merged by a combine kernel.  Every wait
+// is bounded: on expiry the CTA records an error word, drains its in-flight
+// copies (bounded) and exits.
 #include "../common.cuh"
 #include "../gemm/tc_gemm.cuh"
 
@@ -203,14 +200,6 @@ __device__ __forceinline__ void consume_page(const uint8_t* ks, const uint8_t* v
   }
 }
 
-// Where partial results go once a row is complete: `counters` [B, Hk] (zero
-// between launches), `expected` arrivals per row, `slots` partials per row.
-struct Merge {
-  int* counters;
-  int expected, slots;
-  __nv_bfloat16* out;
-};
-
 // Work item: Q rows (up to 16 * MT) of kv head h against pages [p0, p0 + n)
 // of `bt` (token range [t_begin, t_end) with t_begin = p0 * 64), writing
 // (o, lse) partial `slot` for each row.  row_seq(r) / row_head(r) map tile
@@ -219,7 +208,7 @@ template <int MT>
 __device__ void attend(const __nv_bfloat16* __restrict__ q, const CUtensorMap* tk, const CUtensorMap* tv,
                        const int* bt, int p0, int n, int t_end, int h, int rows, int G, int seq0, int Hq, int B,
                        int slot, float* __restrict__ part_o, float* __restrict__ part_lse, float scale_log2,
-                       float v_scale, uint8_t* smem, const Merge& mg) {
+                       float v_scale, uint8_t* smem) {
   constexpr int kSlices = kCW / MT;
   constexpr int kChunks = (kTile / 16) / kSlices;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStagesT * kStageBytes);
@@ -311,66 +300,6 @@ __device__ void attend(const __nv_bfloat16* __restrict__ q, const CUtensorMap* t
     part_o[pi * kHD + col] = lsum > 0.f ? acc / lsum * v_scale : 0.f;
     if (col == 0) part_lse[pi] = lsum > 0.f ? mstar + log2f(lsum) : -INFINITY;
   }
-  // count this item in on every row it covered (one atomic per row, in
-  // parallel); the item completing a row merges it
-  __threadfence();
-  __syncthreads();
-  volatile unsigned long long* last_rows = reinterpret_cast<volatile unsigned long long*>(err + 2);  // past the ring
-  const int nrows = rows / G;  // sequences covered (rows are whole GQA groups), <= 64
-  if (threadIdx.x == 0) *last_rows = 0ull;
-  __syncthreads();
-  if (threadIdx.x < nrows) {
-    int* c = mg.counters + (int64_t)(seq0 + threadIdx.x) * (Hq / G) + h;
-    if (atomicAdd(c, 1) == mg.expected - 1) {
-      *c = 0;  // every arrival is in: reset for the next launch
-      atomicOr(const_cast<unsigned long long*>(last_rows), 1ull << threadIdx.x);
-    }
-  }
-  __syncthreads();
-  const unsigned long long mask = *last_rows;
-  if (mask == 0ull) return;
-  __threadfence();
-  float* wsm = reinterpret_cast<float*>(smem);  // [slots][G] merge weights (the ring is free now)
-  for (int i = 0; i < nrows; ++i) {
-    if (!(mask >> i & 1ull)) continue;
-    const int b = seq0 + i;
-    // one round of loads: every slot's LSE for the row's G query heads
-    for (int idx = threadIdx.x; idx < mg.slots * G; idx += kThreadsT)
-      wsm[idx] = __ldcg(part_lse + ((int64_t)(idx / G) * B + b) * Hq + (int64_t)h * G + idx % G);
-    __syncthreads();
-    if (threadIdx.x < G) {
-      float mx = -INFINITY;
-      for (int sl = 0; sl < mg.slots; ++sl) mx = fmaxf(mx, wsm[sl * G + threadIdx.x]);
-      float den = 0.f;
-      for (int sl = 0; sl < mg.slots; ++sl) {
-        const float f = mx == -INFINITY ? 0.f : exp2f(wsm[sl * G + threadIdx.x] - mx);
-        wsm[sl * G + threadIdx.x] = f;
-        den += f;
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      for (int sl = 0; sl < mg.slots; ++sl) wsm[sl * G + threadIdx.x] *= inv;
-    }
-    __syncthreads();
-    // weighted sum of the partial rows, 4 columns per thread, loads independent across slots
-    for (int idx = threadIdx.x; idx < G * (kHD / 4); idx += kThreadsT) {
-      const int qq = idx / (kHD / 4), c4 = idx % (kHD / 4);
-      const int qh = h * G + qq;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int sl = 0; sl < mg.slots; ++sl) {
-        const float f = wsm[sl * G + qq];
-        const float4 o = __ldcg(reinterpret_cast<const float4*>(part_o + (((int64_t)sl * B + b) * Hq + qh) * kHD) + c4);
-        acc.x += f * o.x;
-        acc.y += f * o.y;
-        acc.z += f * o.z;
-        acc.w += f * o.w;
-      }
-      __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(mg.out + ((int64_t)b * Hq + qh) * kHD + 4 * c4);
-      dst[0] = __floats2bfloat162_rn(acc.x, acc.y);
-      dst[1] = __floats2bfloat162_rn(acc.z, acc.w);
-    }
-    __syncthreads();  // wsm is reused by the next row
-  }
 }
 
 struct KVMaps {
@@ -379,10 +308,10 @@ struct KVMaps {
 
 // per-row decode: grid (split, kv head, row); pages from kv_start/64 (0 when
 // kv_start is null) up to ceil(seq_len / 64), `pps` pages per split.
-__global__ void __launch_bounds__(kThreadsT, 2) decode_tma_kernel(
+__global__ void __launch_bounds__(kThreadsT) decode_tma_kernel(
     const __nv_bfloat16* __restrict__ q, const __grid_constant__ KVMaps maps, const int* __restrict__ block_table,
     const int* __restrict__ seq_lens, float* __restrict__ part_o, float* __restrict__ part_lse, int Hq, int Hk,
-    int max_blocks, int pps, float scale_log2, float v_scale, int* err_out, const Merge mg) {
+    int max_blocks, int pps, float scale_log2, float v_scale, int* err_out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -394,7 +323,7 @@ __global__ void __launch_bounds__(kThreadsT, 2) decode_tma_kernel(
   const int p0 = split * pps;
   const int n = max(0, min(npages, p0 + pps) - p0);
   attend<1>(q, &maps.k, &maps.v, block_table + (int64_t)b * max_blocks, p0, n, L, h, G, G, b, Hq, gridDim.z, split,
-            part_o, part_lse, scale_log2, v_scale, smem, mg);
+            part_o, part_lse, scale_log2, v_scale, smem);
   volatile int* err = reinterpret_cast<volatile int*>(smem + kStagesT * kStageBytes + 2 * kStagesT * 8);
   if (threadIdx.x == 0 && *err) atomicExch(err_out, *err);
 }
@@ -403,11 +332,11 @@ __global__ void __launch_bounds__(kThreadsT, 2) decode_tma_kernel(
 // group's shared prompt pages, then per-row suffix items from the first page
 // after the prefix (prefix lengths are whole pages).
 template <int MT>
-__global__ void __launch_bounds__(kThreadsT, 2) cascade_tma_kernel(
+__global__ void __launch_bounds__(kThreadsT) cascade_tma_kernel(
     const __nv_bfloat16* __restrict__ q, const __grid_constant__ KVMaps maps, const int* __restrict__ block_table,
     const int* __restrict__ seq_lens, const int* __restrict__ prefix_len, float* __restrict__ part_o,
     float* __restrict__ part_lse, int B, int Hq, int Hk, int max_blocks, int group, int psplit, int ssplit, int pps,
-    float scale_log2, float v_scale, int* err_out, const Merge mg) {
+    float scale_log2, float v_scale, int* err_out) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -423,7 +352,7 @@ __global__ void __launch_bounds__(kThreadsT, 2) cascade_tma_kernel(
     const int p0 = split * pps;
     const int n = max(0, min(npages, p0 + pps) - p0);
     attend<MT>(q, &maps.k, &maps.v, block_table + (int64_t)row0 * max_blocks, p0, n, P, h, group * G, G, row0, Hq,
-               B, split, part_o, part_lse, scale_log2, v_scale, smem, mg);
+               B, split, part_o, part_lse, scale_log2, v_scale, smem);
   } else {
     const int j = idx - NP;
     const int split = j % ssplit, h = (j / ssplit) % Hk, b = j / (ssplit * Hk);
@@ -433,10 +362,29 @@ __global__ void __launch_bounds__(kThreadsT, 2) cascade_tma_kernel(
     const int p0 = first + split * pps;
     const int n = max(0, min(npages, p0 + pps) - p0);
     attend<1>(q, &maps.k, &maps.v, block_table + (int64_t)b * max_blocks, p0, n, L, h, G, G, b, Hq, B,
-              psplit + split, part_o, part_lse, scale_log2, v_scale, smem, mg);
+              psplit + split, part_o, part_lse, scale_log2, v_scale, smem);
   }
   volatile int* err = reinterpret_cast<volatile int*>(smem + kStagesT * kStageBytes + 2 * kStagesT * 8);
   if (threadIdx.x == 0 && *err) atomicExch(err_out, *err);
+}
+
+__global__ void combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                               __nv_bfloat16* __restrict__ out, int nsplit, int B, int Hq) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, qh = blockIdx.y, col = threadIdx.x;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, part_lse[((int64_t)s * B + b) * Hq + qh]);
+  float den = 0.f, acc = 0.f;
+  if (mx != -INFINITY) {
+    for (int s = 0; s < nsplit; ++s) {
+      const int64_t pi = ((int64_t)s * B + b) * Hq + qh;
+      const float f = exp2f(part_lse[pi] - mx);
+      den += f;
+      acc += f * part_o[pi * kHD + col];
+    }
+  }
+  out[((int64_t)b * Hq + qh) * kHD + col] = __float2bfloat16(den > 0.f ? acc / den : 0.f);
 }
 
 typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -481,18 +429,6 @@ torch::Tensor& tma_err_word() {
   return t;
 }
 
-// Per-(row, kv head) arrival counters, zero between launches (the completing
-// item resets its counter).  Allocated once per device; a launch that needs
-// more rows than it holds is refused.
-constexpr int64_t kMaxCounters = int64_t{1} << 20;
-int* merge_counters(int64_t need) {
-  static thread_local torch::Tensor t;
-  TORCH_CHECK(need <= kMaxCounters, "decode_tma: batch x kv heads above ", kMaxCounters);
-  if (!t.defined() || t.device().index() != c10::cuda::current_device())
-    t = torch::zeros({kMaxCounters}, torch::dtype(torch::kInt32).device(torch::kCUDA, c10::cuda::current_device()));
-  return t.data_ptr<int>();
-}
-
 int pick_pps(int64_t items, int64_t max_pages) {
   // >= ~4 CTAs per SM in total (2 resident), at least 2 pages per item
   int64_t splits = std::max<int64_t>(1, (4 * (int64_t)num_sms() + items - 1) / items);
@@ -524,7 +460,6 @@ torch::Tensor paged_decode_attn_tma(torch::Tensor q, torch::Tensor kc, torch::Te
   if (B == 0) return out;
   const int pps = pick_pps(B * Hk, max_pages);
   const int nsplit = (int)((max_pages + pps - 1) / pps);
-  TORCH_CHECK((int64_t)nsplit * (Hq / Hk) * 4 <= kStagesT * kStageBytes, "decode_tma: too many splits to merge");
   auto po = torch::empty({nsplit, B, Hq, kHD}, q.options().dtype(at::kFloat));
   auto pl = torch::empty({nsplit, B, Hq}, q.options().dtype(at::kFloat));
   static bool attr = false;
@@ -536,7 +471,9 @@ torch::Tensor paged_decode_attn_tma(torch::Tensor q, torch::Tensor kc, torch::Te
   launch_pdl(decode_tma_kernel, dim3(nsplit, Hk, B), dim3(kThreadsT), kSmemT, (const __nv_bfloat16*)q.data_ptr(),
              maps, (const int*)block_table.data_ptr<int>(), (const int*)seq_lens.data_ptr<int>(), po.data_ptr<float>(),
              pl.data_ptr<float>(), (int)Hq, (int)Hk, (int)max_blocks, pps, sl2, (float)v_scale,
-             tma_err_word().data_ptr<int>(), Merge{merge_counters(B * Hk), nsplit, nsplit, (__nv_bfloat16*)out.data_ptr()});
+             tma_err_word().data_ptr<int>());
+  launch_pdl(combine_kernel, dim3(B, Hq), dim3(kHD), 0, (const float*)po.data_ptr<float>(),
+             (const float*)pl.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(), nsplit, (int)B, (int)Hq);
   return out;
 }
 
@@ -566,12 +503,10 @@ torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, to
   const int ssplit = (int)((spages + pps - 1) / pps);
   const int psplit = (int)((ppages + pps - 1) / pps);
   const int total = psplit + ssplit;
-  TORCH_CHECK((int64_t)total * G * 4 <= kStagesT * kStageBytes && group <= 64, "decode_tma: too many splits to merge");
   auto po = torch::empty({total, B, Hq, kHD}, q.options().dtype(at::kFloat));
   auto pl = torch::empty({total, B, Hq}, q.options().dtype(at::kFloat));
   const float sl2 = (float)(scale * 1.4426950408889634);
   const int64_t nblocks = (int64_t)psplit * Hk * groups + (int64_t)ssplit * Hk * B;
-  const Merge mg{merge_counters(B * Hk), total, total, (__nv_bfloat16*)out.data_ptr()};
 #define CASC(M)                                                                                                   \
   do {                                                                                                            \
     static bool attr_##M = false;                                                                                 \
@@ -583,12 +518,14 @@ torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, to
                (const __nv_bfloat16*)q.data_ptr(), maps, (const int*)block_table.data_ptr<int>(),               \
                (const int*)seq_lens.data_ptr<int>(), (const int*)prefix_len.data_ptr<int>(), po.data_ptr<float>(), \
                pl.data_ptr<float>(), (int)B, (int)Hq, (int)Hk, (int)max_blocks, (int)group, psplit, ssplit, pps,  \
-               sl2, (float)v_scale, tma_err_word().data_ptr<int>(), mg);                                       \
+               sl2, (float)v_scale, tma_err_word().data_ptr<int>());                                           \
   } while (0)
   if (MT == 1) CASC(1);
   else if (MT == 2) CASC(2);
   else CASC(4);
 #undef CASC
+  launch_pdl(combine_kernel, dim3(B, Hq), dim3(kHD), 0, (const float*)po.data_ptr<float>(),
+             (const float*)pl.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(), total, (int)B, (int)Hq);
   return out;
 }
 

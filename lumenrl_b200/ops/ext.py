@@ -19,7 +19,7 @@ LAUNCHES = [0]   # kernels of this extension launched (graph replays add their c
 _NO_KERNEL = {"symm_malloc", "symm_open", "symm_close", "symm_free", "symm_tensor", "symm_signal_words",
               "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "grouped_gemm_status", "decode_tma_status",
               "fa_fwd_status"}
-_TWO_KERNELS = {"fa_fwd", "paged_decode_attn_shared", "gemm_rs"}
+_TWO_KERNELS = {"fa_fwd", "paged_decode_attn_shared", "paged_decode_attn_tma", "paged_decode_attn_shared_tma", "gemm_rs"}
 
 
 def _kernels(name: str, a: tuple) -> int:

@@ -12,7 +12,9 @@ the training step (the reference also calls a library kernel here,
 The forward runs on this package's tcgen05 kernel (``csrc/attn/fa_fwd.cu``:
 bf16, head dim 128, causal) by default; its log-sum-exp is written in the
 varlen layout ``[Hq, T]`` so the backward stays on the library kernel.
-``LRL_TRAIN_ATTN=fa2`` puts the forward back on the library kernel.
+``LRL_TRAIN_ATTN=fa2`` puts the forward back on the library kernel;
+``LRL_TRAIN_ATTN_BWD=tc`` runs the backward on this package's tcgen05
+kernels too (``csrc/attn/fa_bwd.cu``).
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 TRAIN_ATTN = os.environ.get("LRL_TRAIN_ATTN", "tc")    # "tc" (own tcgen05 forward) | "fa2" (library)
+TRAIN_ATTN_BWD = os.environ.get("LRL_TRAIN_ATTN_BWD", "fa2")   # backward after the tcgen05 forward: "fa2" | "tc"
 
 
 class _VarlenFlash(torch.autograd.Function):
@@ -61,6 +64,10 @@ class _VarlenTC(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         q, k, v, out, lse, cu = ctx.saved_tensors
+        if TRAIN_ATTN_BWD == "tc":
+            from lumenrl_b200.ops.ext import ext
+            dq, dk, dv = ext().fa_bwd(do.contiguous(), q, k, v, out, lse, cu, ctx.max_len, ctx.scale)
+            return dq, dk, dv, None, None, None
         zero = torch.zeros((), dtype=torch.int64, device=q.device)
         dq, dk, dv = torch.ops.aten._flash_attention_backward(
             do.contiguous(), q, k, v, out, lse, cu, cu, ctx.max_len, ctx.max_len, 0.0, True, zero, zero,

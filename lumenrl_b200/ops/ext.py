@@ -18,7 +18,7 @@ LAUNCHES = [0]   # kernels of this extension launched (graph replays add their c
 # host-only entry points (no kernel) and ops that launch two kernels
 _NO_KERNEL = {"symm_malloc", "symm_open", "symm_close", "symm_free", "symm_tensor", "symm_signal_words",
               "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "grouped_gemm_status", "decode_tma_status",
-              "fa_fwd_status"}
+              "fa_fwd_status", "fa_bwd_status"}
 _TWO_KERNELS = {"fa_fwd", "paged_decode_attn_shared", "paged_decode_attn_tma", "paged_decode_attn_shared_tma", "gemm_rs"}
 
 
@@ -27,6 +27,8 @@ def _kernels(name: str, a: tuple) -> int:
         return 0
     if name in _TWO_KERNELS:
         return 2
+    if name == "fa_bwd":                # three transposes, the lse/D pass, the dQ and the dK/dV kernels
+        return 6
     if name == "paged_decode_attn":     # + the split combine, unless one split covers the context
         return 2
     if name == "sample":                # split-row sampler (top_p = 1, bf16, large vocab) is two kernels

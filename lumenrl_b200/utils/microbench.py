@@ -175,8 +175,18 @@ def bench_attn_train(ns) -> dict:
         for var in range(4):
             tv = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc, var), ns.steps, ns.warmup)
             res[f"fwd_tc_v{var}_tflops"] = round(fflops / tv / 1e9, 1)
+        out, lse = ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc)
+        zero = torch.zeros((), dtype=torch.int64, device="cuda")
+        outf, lsef, _, _, _ = torch.ops.aten._flash_attention_forward(qd, kd, vd, cu, cu, ns.seq, ns.seq, 0.0, True,
+                                                                     False, scale=sc)
+        tb2 = _time(lambda: torch.ops.aten._flash_attention_backward(do, qd, kd, vd, outf, lsef, cu, cu, ns.seq, ns.seq,
+                                                                     0.0, True, zero, zero, scale=sc),
+                    ns.steps, ns.warmup)
+        tb3 = _time(lambda: ext().fa_bwd(do, qd, kd, vd, out, lse, cu, ns.seq, sc), ns.steps, ns.warmup)
+    bflops = 2.5 * fflops
     res.update(fwd_fa2_ms=t2, fwd_fa2_tflops=fflops / t2 / 1e9, fwd_tc_ms=t3, fwd_tc_tflops=fflops / t3 / 1e9,
-               fwd_tc_status=int(ext().fa_fwd_status()))
+               fwd_tc_status=int(ext().fa_fwd_status()), bwd_fa2_ms=tb2, bwd_fa2_tflops=bflops / tb2 / 1e9,
+               bwd_tc_ms=tb3, bwd_tc_tflops=bflops / tb3 / 1e9, bwd_tc_status=int(ext().fa_bwd_status()))
     return res
 
 

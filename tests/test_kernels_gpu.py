@@ -400,13 +400,14 @@ def test_fa_fwd_tcgen05(cuda, lens, variant):
     close(lse, rl, 1e-2, 1e-3)
 
 
-@pytest.mark.parametrize("mode", ["tc", "fa2"])
+@pytest.mark.parametrize("mode", ["tc", "fa2", "tc+tc"])
 def test_fa_fwd_bwd_modes(cuda, monkeypatch, mode):
     """Training attention with the tcgen05 forward (gradients through the
     library backward fed with its output and LSE) and with the library
     forward."""
     from lumenrl_b200.ops import attention
-    monkeypatch.setattr(attention, "TRAIN_ATTN", mode)
+    monkeypatch.setattr(attention, "TRAIN_ATTN", mode.split("+")[0])
+    monkeypatch.setattr(attention, "TRAIN_ATTN_BWD", "tc" if mode == "tc+tc" else "fa2")
     torch.manual_seed(1)
     lens = [37, 200, 1, 511]
     T, Hq, Hk, D = sum(lens), 8, 2, 128
@@ -422,4 +423,26 @@ def test_fa_fwd_bwd_modes(cuda, monkeypatch, mode):
     ro.backward(do.float())
     close(o, ro, 2e-2, 2e-2)
     for g, r in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
+        assert ((g.float() - r).abs().max() / r.abs().max()).item() < 2e-2
+
+
+@pytest.mark.parametrize("lens", [[128], [1, 100, 129, 300], [513, 7, 256, 1024]])
+def test_fa_bwd_tcgen05(cuda, lens):
+    """tcgen05 flash-attention backward (dQ kernel + dK/dV kernel, GQA 4:1,
+    ragged packed sequences) against fp32 autograd of the causal reference."""
+    from lumenrl_b200.ops.ext import ext
+    torch.manual_seed(2)
+    T, Hq, Hk, D = sum(lens), 8, 2, 128
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=cuda)
+    q = torch.randn(T, Hq, D, device=cuda).to(torch.bfloat16)
+    k = torch.randn(T, Hk, D, device=cuda).to(torch.bfloat16)
+    v = torch.randn(T, Hk, D, device=cuda).to(torch.bfloat16)
+    do = torch.randn(T, Hq, D, device=cuda).to(torch.bfloat16)
+    out, lse = ext().fa_fwd(q, k, v, cu, max(lens), D ** -0.5)
+    dq, dk, dv = ext().fa_bwd(do, q, k, v, out, lse, cu, max(lens), D ** -0.5)
+    assert ext().fa_bwd_status() == 0
+    qr, kr, vr = (t.float().requires_grad_(True) for t in (q, k, v))
+    ro, _ = _causal_ref(qr, kr, vr, lens, D ** -0.5)
+    ro.backward(do.float())
+    for g, r in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
         assert ((g.float() - r).abs().max() / r.abs().max()).item() < 2e-2

@@ -9,12 +9,12 @@ caller, who packed the batch on the host.  This is the library attention of
 the training step (the reference also calls a library kernel here,
 ``engine/training/packing.py:363-421``).
 
-The forward runs on this package's tcgen05 kernel (``csrc/attn/fa_fwd.cu``:
-bf16, head dim 128, causal) by default; its log-sum-exp is written in the
-varlen layout ``[Hq, T]`` so the backward stays on the library kernel.
-``LRL_TRAIN_ATTN=fa2`` puts the forward back on the library kernel;
-``LRL_TRAIN_ATTN_BWD=tc`` runs the backward on this package's tcgen05
-kernels too (``csrc/attn/fa_bwd.cu``).
+By default (bf16, head dim 128, causal) both directions run on this
+package's tcgen05 kernels: the forward ``csrc/attn/fa_fwd.cu`` writes the
+log-sum-exp in the varlen layout ``[Hq, T]``, the backward
+``csrc/attn/fa_bwd.cu`` reads it.  ``LRL_TRAIN_ATTN_BWD=fa2`` feeds that
+output and LSE to the library backward instead; ``LRL_TRAIN_ATTN=fa2`` puts
+both directions on the library kernels.
 """
 
 from __future__ import annotations
@@ -26,7 +26,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 TRAIN_ATTN = os.environ.get("LRL_TRAIN_ATTN", "tc")    # "tc" (own tcgen05 forward) | "fa2" (library)
-TRAIN_ATTN_BWD = os.environ.get("LRL_TRAIN_ATTN_BWD", "fa2")   # backward after the tcgen05 forward: "fa2" | "tc"
+TRAIN_ATTN_BWD = os.environ.get("LRL_TRAIN_ATTN_BWD", "tc")    # backward after the tcgen05 forward: "tc" | "fa2"
 
 
 class _VarlenFlash(torch.autograd.Function):

@@ -21,6 +21,8 @@
 // Warp 0 is a TMA producer, warp 1 lane 0 issues the MMAs, warps 2-5 do the
 // elementwise work (thread r owns TMEM lane r).  Every mbarrier wait is
 // bounded and reports an error word instead of hanging.
+#include <c10/cuda/CUDAStream.h>
+
 #include "fa_common.cuh"
 
 namespace lrl {
@@ -577,10 +579,11 @@ int64_t fa_bwd_status() {
 
 // dout, q, out [T, Hq, 128], k, v [T, Hk, 128] bf16 contiguous; lse [Hq, T]
 // fp32 (natural log, from fa_fwd); cu [nseq + 1] int32 on the device;
-// max_seqlen bounds the longest sequence.  Returns (dq, dk, dv) in bf16.
+// max_seqlen bounds the longest sequence; streams = 2 runs the dK/dV kernel on
+// a pooled side stream joined back before returning.  Returns (dq, dk, dv) in bf16.
 std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                   torch::Tensor out, torch::Tensor lse, torch::Tensor cu, int64_t max_seqlen,
-                                  double scale) {
+                                  double scale, int64_t streams) {
   for (auto* t : {&dout, &q, &k, &v, &out}) {
     LRL_CHECK((*t));
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 3 && t->size(2) == kD, "fa_bwd: bf16 [T, H, 128]");
@@ -630,10 +633,28 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
       lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dq.data_ptr(),
       bwd_err_word().data_ptr<int>());
-  fa_bwd_dkdv_kernel<<<(unsigned)(max_tiles * nseq * Hk), kThreadsB, kSmemKV, stream()>>>(
+  // the dK/dV grid can run beside the dQ grid (independent outputs): each
+  // fills the SMs the other's tail leaves idle
+  cudaStream_t main = stream(), kv_stream = main;
+  static thread_local cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  if (streams > 1) {
+    if (!ev_fork) {
+      TORCH_CHECK(cudaEventCreateWithFlags(&ev_fork, cudaEventDisableTiming) == cudaSuccess &&
+                      cudaEventCreateWithFlags(&ev_join, cudaEventDisableTiming) == cudaSuccess,
+                  "fa_bwd: event creation failed");
+    }
+    kv_stream = c10::cuda::getStreamFromPool(false).stream();
+    cudaEventRecord(ev_fork, main);
+    cudaStreamWaitEvent(kv_stream, ev_fork, 0);
+  }
+  fa_bwd_dkdv_kernel<<<(unsigned)(max_tiles * nseq * Hk), kThreadsB, kSmemKV, kv_stream>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
       lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dk.data_ptr(),
       (__nv_bfloat16*)dv.data_ptr(), bwd_err_word().data_ptr<int>());
+  if (kv_stream != main) {  // the caller's stream waits for both grids
+    cudaEventRecord(ev_join, kv_stream);
+    cudaStreamWaitEvent(main, ev_join, 0);
+  }
   return {dq, dk, dv};
 }
 

@@ -129,7 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("variant") = -1);
   m.def("fa_fwd_status", &lrl::fa_fwd_status);
   m.def("fa_bwd", &lrl::fa_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
-        py::arg("lse"), py::arg("cu"), py::arg("max_seqlen"), py::arg("scale"), py::arg("streams") = 2);
+        py::arg("lse"), py::arg("cu"), py::arg("max_seqlen"), py::arg("scale"), py::arg("streams") = 1);
   m.def("fa_bwd_status", &lrl::fa_bwd_status);
   m.def("kv_append", &lrl::kv_append);
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,

@@ -16,6 +16,8 @@
 // memory (ld.shared::cluster) and writes bf16 Y.  One launch, no atomics,
 // no zero-fill and no conversion pass.  Warp roles and bounded mbarrier waits
 // follow tc_gemm.cu.
+#include <cstdlib>
+
 #include "../common.cuh"
 #include "tc_gemm.cuh"
 
@@ -266,7 +268,12 @@ void launch_skinny(const CUtensorMap& mw, const CUtensorMap& mx, __nv_bfloat16* 
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 2;
+  // LRL_SKINNY_PDL=0 launches without the programmatic-dependent-launch edge
+  static const bool pdl = [] {
+    const char* e = std::getenv("LRL_SKINNY_PDL");
+    return !(e && e[0] == '0');
+  }();
+  cfg.numAttrs = pdl ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mw, mx, y, M, N, K, ks, skinny_err_word().data_ptr<int>()));
 }
 
@@ -302,7 +309,13 @@ torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit) {
     const int64_t slots = 2 * (int64_t)num_sms();
     ks = 1;
     double best = (double)((tiles + slots - 1) / slots);
-    for (int c = 2; c <= 8 && c <= kblocks; c *= 2) {
+    // LRL_SKINNY_MAXKS caps the cluster size (a cluster needs that many SMs of one GPC free at once)
+    static const int max_ks = [] {
+      const char* e = std::getenv("LRL_SKINNY_MAXKS");
+      const int v = e ? std::atoi(e) : 8;
+      return v < 1 ? 1 : (v > 8 ? 8 : v);
+    }();
+    for (int c = 2; c <= max_ks && c <= kblocks; c *= 2) {
       const double cost = (double)((tiles * c + slots - 1) / slots) / c;
       if (cost < 0.85 * best) {
         best = cost;

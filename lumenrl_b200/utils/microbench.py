@@ -291,6 +291,8 @@ def bench_comm(ns) -> dict:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
+                    help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
     ap.add_argument("--prefix", type=int, default=512)
     ap.add_argument("--numel", type=int, default=8_200_000_000)
@@ -304,6 +306,8 @@ def main(argv=None) -> None:
     ap.add_argument("--recompute", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
+    if ns.blas != "default":
+        torch.backends.cuda.preferred_blas_library(ns.blas)
     fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
           "comm": bench_comm}[ns.what]
     res = fn(ns)

@@ -6,7 +6,8 @@
 namespace lrl {
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps);
-torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                          c10::optional<torch::Tensor> dres);
 std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
                                             torch::Tensor inv_freq, int64_t nh, int64_t nkv, int64_t hd, double eps,
                                             c10::optional<torch::Tensor> kc, c10::optional<torch::Tensor> vc,
@@ -99,7 +100,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lumenrl_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &lrl::rmsnorm_fwd);
   m.def("add_rmsnorm_fwd", &lrl::add_rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &lrl::rmsnorm_bwd);
+  m.def("rmsnorm_bwd", &lrl::rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dw"),
+        py::arg("dres") = py::none());
   m.def("qk_norm_rope_fwd", &lrl::qk_norm_rope_fwd, py::arg("qkv"), py::arg("qw"), py::arg("kw"), py::arg("pos"),
         py::arg("inv_freq"), py::arg("nh"), py::arg("nkv"), py::arg("hd"), py::arg("eps"), py::arg("kc") = py::none(),
         py::arg("vc") = py::none(), py::arg("slots") = py::none(), py::arg("inv_ks") = 1.0, py::arg("inv_vs") = 1.0);

@@ -96,11 +96,12 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
   TORCH_CHECK(H % 8 == 0 && H <= 1024 * 8 * kMaxChunks, "add_rmsnorm: bad H");
   auto y = torch::empty_like(x);
   auto s = torch::empty_like(x);
-  if (T == 0) return {y, s};
+  auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {y, s, rstd};
   launch_pdl(rmsnorm_fwd_kernel<true>, dim3(T), dim3(row_threads(H)), 0, (const __nv_bfloat16*)x.data_ptr(),
              (const __nv_bfloat16*)res.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
-             (__nv_bfloat16*)s.data_ptr(), (float*)nullptr, H, (float)eps);
-  return {y, s};
+             (__nv_bfloat16*)s.data_ptr(), rstd.data_ptr<float>(), H, (float)eps);
+  return {y, s, rstd};
 }
 
 // ---------------------------------------------------------------- RMSNorm bwd
@@ -111,8 +112,8 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
 template <int C>
 __global__ void __launch_bounds__(1024) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
-                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw, int64_t T, int H,
-                                   int rows_per_cta) {
+                                   const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                                   float* __restrict__ dw, int64_t T, int H, int rows_per_cta) {
   __shared__ float red[32];
   float acc[C][8];
   float wf[C][8];
@@ -153,6 +154,12 @@ __global__ void __launch_bounds__(1024) rmsnorm_bwd_kernel(const __nv_bfloat16* 
         float o[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = r * (g[c][i] - xh[c][i] * dot);
+        if (dres) {  // gradient the residual stream carries past the norm (fused add)
+          float e[8];
+          load8(dres + base + col, e);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] += e[i];
+        }
         store8(dx + base + col, o);
       }
     }
@@ -169,8 +176,15 @@ __global__ void __launch_bounds__(1024) rmsnorm_bwd_kernel(const __nv_bfloat16* 
   }
 }
 
-torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw) {
+// dres (optional, same shape as x) is added to dx: the gradient of the
+// residual-stream output of a fused add + RMSNorm.
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                          c10::optional<torch::Tensor> dres) {
   LRL_CHECK(dy);
+  if (dres.has_value()) {
+    LRL_CHECK((*dres));
+    TORCH_CHECK(dres->scalar_type() == at::kBFloat16 && dres->numel() == x.numel(), "rmsnorm_bwd: dres like x");
+  }
   LRL_CHECK(x);
   LRL_CHECK(w);
   LRL_CHECK(rstd);
@@ -192,7 +206,8 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   auto kern = one ? rmsnorm_bwd_kernel<1> : rmsnorm_bwd_kernel<kMaxChunks>;
   kern<<<grid, threads, 0, stream()>>>(
       (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
-      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, rows);
+      rstd.data_ptr<float>(), dres.has_value() ? (const __nv_bfloat16*)dres->data_ptr() : nullptr,
+      (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, rows);
   dw.add_(part.sum(0));
   return dx;
 }

@@ -205,13 +205,23 @@ class Qwen3Model(nn.Module):
             return out
         return ops.linear(ops.swiglu(ops.linear(h, P[f"layers.{i}.w13"])), P[f"layers.{i}.w2"])
 
-    def _layer(self, i: int, x: Tensor, positions: Tensor, cu: Tensor, max_len: int) -> Tensor:
+    def _layer_fused(self, i: int, x: Tensor, pending: Optional[Tensor], positions: Tensor, cu: Tensor,
+                     max_len: int) -> tuple[Tensor, Tensor]:
+        """Decoder layer on the residual stream ``x + pending`` (``pending`` is
+        the previous layer's MLP output, None for the first layer).  Returns
+        (stream after attention, MLP output): the caller's next add is fused
+        into the next norm, so every residual add of the stack runs inside an
+        add + RMSNorm kernel (forward and backward)."""
         eps = self.args.rms_norm_eps
         P = self._params
-        h = ops.rmsnorm(x, P[f"layers.{i}.ln1"], eps)
-        x = x + self._attention_block(i, h, positions, cu, max_len)
-        h = ops.rmsnorm(x, P[f"layers.{i}.ln2"], eps)
-        return x + self._mlp_block(i, h)
+        h, x = ops.add_rmsnorm(x, pending, P[f"layers.{i}.ln1"], eps)
+        a = self._attention_block(i, h, positions, cu, max_len)
+        h, x = ops.add_rmsnorm(x, a, P[f"layers.{i}.ln2"], eps)
+        return x, self._mlp_block(i, h)
+
+    def _layer(self, i: int, x: Tensor, positions: Tensor, cu: Tensor, max_len: int) -> Tensor:
+        s, m = self._layer_fused(i, x, None, positions, cu, max_len)
+        return s + m
 
     def forward_packed(self, ids: Tensor, positions: Tensor, cu_seqlens: Tensor, max_seqlen: int,
                        output_hidden_layers: Optional[list[int]] = None) -> Tensor | tuple[Tensor, list[Tensor]]:
@@ -221,16 +231,18 @@ class Qwen3Model(nn.Module):
         those layers (Eagle3 auxiliary states)."""
         self.aux_losses = []
         x = embed(ids, self._params["embed"])
+        pending: Optional[Tensor] = None   # MLP output not yet added to the stream
         taps: list[Tensor] = []
         want = set(output_hidden_layers or [])
         for i in range(self.args.num_layers):
             if (self.gradient_checkpointing or i in self.recompute_layers) and torch.is_grad_enabled():
-                x = _ckpt(self._layer, i, x, positions, cu_seqlens, max_seqlen, use_reentrant=False)
+                x, pending = _ckpt(self._layer_fused, i, x, pending, positions, cu_seqlens, max_seqlen,
+                                   use_reentrant=False)
             else:
-                x = self._layer(i, x, positions, cu_seqlens, max_seqlen)
+                x, pending = self._layer_fused(i, x, pending, positions, cu_seqlens, max_seqlen)
             if i in want:
-                taps.append(x)
-        h = ops.rmsnorm(x, self._params["norm"], self.args.rms_norm_eps)
+                taps.append(x + pending)
+        h, _ = ops.add_rmsnorm(x, pending, self._params["norm"], self.args.rms_norm_eps)
         if output_hidden_layers is not None:
             return h, taps
         return h

@@ -136,13 +136,41 @@ def rmsnorm(x: Tensor, w: Tensor, eps: float) -> Tensor:
     return y.view(shape)
 
 
+class _AddRMSNorm(torch.autograd.Function):
+    """(rmsnorm(x + r), x + r) in one kernel; the backward adds the gradient of
+    the sum output inside the RMSNorm backward kernel, so neither direction
+    launches a separate add."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, r: Tensor, w: Tensor, w_handle: Tensor, eps: float):
+        shape = x.shape
+        y, s, rstd = ext().add_rmsnorm_fwd(x.reshape(-1, shape[-1]), r.reshape(-1, shape[-1]), w, eps)
+        ctx.save_for_backward(s, w, rstd)
+        ctx.w_handle, ctx.shape = w_handle, shape
+        return y.view(shape), s.view(shape)
+
+    @staticmethod
+    def backward(ctx, dy: Tensor, ds: Tensor):
+        s, w, rstd = ctx.saved_tensors
+        dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        dres = None if ds is None else ds.reshape(s.shape).contiguous()
+        if dy is None:
+            dy = torch.zeros_like(s)
+        dx = ext().rmsnorm_bwd(dy.reshape(s.shape).contiguous(), s, w, rstd, dw, dres)
+        _accum_main_grad(ctx.w_handle, dw)
+        dx = dx.view(ctx.shape)
+        return dx, dx, None, None, None
+
+
 def add_rmsnorm(x: Tensor, residual: Optional[Tensor], w: Tensor, eps: float) -> tuple[Tensor, Tensor]:
     """Returns (rmsnorm(x + residual), x + residual); ``residual`` may be None."""
     if residual is None:
         return rmsnorm(x, w, eps), x
-    if _cuda(x) and not (torch.is_grad_enabled() and (x.requires_grad or residual.requires_grad)):
+    if _cuda(x):
+        if torch.is_grad_enabled() and (x.requires_grad or residual.requires_grad or w.requires_grad):
+            return _AddRMSNorm.apply(x, residual, w.detach(), w, eps)
         shape = x.shape
-        y, s = ext().add_rmsnorm_fwd(x.reshape(-1, shape[-1]), residual.reshape(-1, shape[-1]), w, eps)
+        y, s, _ = ext().add_rmsnorm_fwd(x.reshape(-1, shape[-1]), residual.reshape(-1, shape[-1]), w, eps)
         return y.view(shape), s.view(shape)
     s = x + residual
     return rmsnorm(s, w, eps), s

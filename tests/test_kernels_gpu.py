@@ -49,6 +49,30 @@ def test_add_rmsnorm(cuda):
     close(y, ref.rmsnorm(s_ref.float(), w.float(), 1e-6), 3e-2, 1e-2)
 
 
+def test_add_rmsnorm_fwd_bwd(cuda):
+    """Fused add + RMSNorm with autograd (both outputs carry gradient; the
+    sum's gradient is added inside the RMSNorm backward kernel) against fp32."""
+    torch.manual_seed(3)
+    T, H = 333, 4096
+    x = torch.randn(T, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    r = torch.randn(T, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    wp = torch.nn.Parameter((1 + 0.1 * torch.randn(H, device=cuda)).to(torch.bfloat16))
+    wp.main_grad = torch.zeros(H, device=cuda)
+    y, s = ops.add_rmsnorm(x, r, wp, 1e-6)
+    gy, gs = torch.randn(T, H, device=cuda), torch.randn(T, H, device=cuda)
+    (y.float() * gy + s.float() * gs).sum().backward()
+    xr, rr = x.detach().float().requires_grad_(True), r.detach().float().requires_grad_(True)
+    wr = wp.detach().float().requires_grad_(True)
+    sr = xr + rr
+    yr = sr * torch.rsqrt(sr.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    (yr * gy + sr * gs).sum().backward()
+    close(y, yr, 3e-2, 1e-2)
+    close(s, sr, 2e-2, 1e-2)
+    close(x.grad, xr.grad, 5e-2, 2e-2)
+    close(r.grad, rr.grad, 5e-2, 2e-2)
+    close(wp.main_grad, wr.grad, 1.0, 1e-2)
+
+
 @pytest.mark.parametrize("hd,nh,nkv,norm", [(128, 32, 8, True), (64, 4, 2, False), (128, 4, 4, True)])
 def test_qk_norm_rope(cuda, hd, nh, nkv, norm):
     torch.manual_seed(0)

@@ -107,11 +107,43 @@ __device__ __forceinline__ void exp_pack_store(const uint32_t (&v)[32], int cb, 
   }
 }
 
+// exponentials of one 32-score chunk packed as 16 bf16 pairs
+template <bool kPoly>
+__device__ __forceinline__ void exp_pack_regs(const uint32_t (&v)[32], float scale_log2, float nm, float (&sm)[4],
+                                              uint32_t (&out)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const float x0 = fmaf(__uint_as_float(v[2 * e]), scale_log2, nm);
+    const float x1 = fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, nm);
+    const float p0 = ex2(x0);
+    const float p1 = kPoly ? ex2_poly(x1) : ex2(x1);
+    sm[(e & 1) * 2] += p0;
+    sm[(e & 1) * 2 + 1] += p1;
+    out[e] = pack_bf16(p0, p1);
+  }
+}
+
+// tcgen05.st of 32 lanes x 16 columns (no wait)
+__device__ __forceinline__ void tmem_st16_nowait(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+               : "memory");
+}
+
+// D (+)= A B^T with A read from tensor memory (kind::f16, bf16 operands)
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 struct FAMaps {
   CUtensorMap q, k, vt;
 };
 
-template <bool kTwoPass, bool kPoly>
+template <bool kTwoPass, bool kPoly, bool kPTmem = false>
 __global__ void __launch_bounds__(kThreadsFA, 1)
     fa_fwd_kernel(const __grid_constant__ FAMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                   int nseq, int max_pairs, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
@@ -221,9 +253,15 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
       auto mma_o = [&](int X, const uint8_t* vb, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sw128_kmajor_desc(smem_addr(sp + X * kTile + (kk >> 2) * kBox)) + 2 * (kk & 3);
           const uint64_t bd = sw128_kmajor_desc(smem_addr(vb + (kk >> 2) * kBox)) + 2 * (kk & 3);
-          umma_bf16(tmem + 256 + X * 128, ad, bd, idesc, (acc || kk != 0) ? 1u : 0u);
+          if constexpr (kPTmem) {
+            // A = P_X from TMEM: row r on lane r, two bf16 keys per 32-bit column,
+            // 16 keys (8 columns) per MMA step, in S_X's first 64 columns
+            umma_bf16_ts(tmem + 256 + X * 128, tmem + X * 128 + kk * 8, bd, idesc, (acc || kk != 0) ? 1u : 0u);
+          } else {
+            const uint64_t ad = sw128_kmajor_desc(smem_addr(sp + X * kTile + (kk >> 2) * kBox)) + 2 * (kk & 3);
+            umma_bf16(tmem + 256 + X * 128, ad, bd, idesc, (acc || kk != 0) ? 1u : 0u);
+          }
         }
       };
       // O_B for block jb: needs P_B(jb) and V^T_jb; releases V^T_jb's slot
@@ -322,20 +360,43 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
           max_chunk(a1, mx0, mx1);
         }
         alpha = new_max(fmaxf(mx0, mx1) * scale_log2, m);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t a0[32], a1[32];
-          tmem_ld32_nowait(t_s + hh * 64, a0);
-          tmem_ld32_nowait(t_s + hh * 64 + 32, a1);
-          tmem_wait_ld(a0);
-          tmem_wait_ld(a1);
-          if (need_mask) {
-            mask_chunk(a0, k0 + hh * 64, lim);
-            mask_chunk(a1, k0 + hh * 64 + 32, lim);
+        if constexpr (kPTmem) {
+          // bf16 P for keys [64 hh, 64 hh + 64) into columns [32 hh, 32 hh + 32) of S_X:
+          // those scores were read already (this half, or the half before)
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t a0[32], a1[32];
+            tmem_ld32_nowait(t_s + hh * 64, a0);
+            tmem_ld32_nowait(t_s + hh * 64 + 32, a1);
+            tmem_wait_ld(a0);
+            tmem_wait_ld(a1);
+            if (need_mask) {
+              mask_chunk(a0, k0 + hh * 64, lim);
+              mask_chunk(a1, k0 + hh * 64 + 32, lim);
+            }
+            uint32_t pk[16];
+            exp_pack_regs<kPoly>(a0, scale_log2, -m, sm, pk);
+            tmem_st16_nowait(t_s + hh * 32, pk);
+            exp_pack_regs<kPoly>(a1, scale_log2, -m, sm, pk);
+            tmem_st16_nowait(t_s + hh * 32 + 16, pk);
           }
-          exp_pack_store<kPoly>(a0, hh * 64, scale_log2, -m, sm, px, r);
-          exp_pack_store<kPoly>(a1, hh * 64 + 32, scale_log2, -m, sm, px, r);
+        } else {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t a0[32], a1[32];
+            tmem_ld32_nowait(t_s + hh * 64, a0);
+            tmem_ld32_nowait(t_s + hh * 64 + 32, a1);
+            tmem_wait_ld(a0);
+            tmem_wait_ld(a1);
+            if (need_mask) {
+              mask_chunk(a0, k0 + hh * 64, lim);
+              mask_chunk(a1, k0 + hh * 64 + 32, lim);
+            }
+            exp_pack_store<kPoly>(a0, hh * 64, scale_log2, -m, sm, px, r);
+            exp_pack_store<kPoly>(a1, hh * 64 + 32, scale_log2, -m, sm, px, r);
+          }
         }
+        if constexpr (kPTmem) asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
       }
       l = l * alpha + ((sm[0] + sm[1]) + (sm[2] + sm[3]));
       // O_X holds blocks < j (its MMA finished before S_X(j) did); rescale rows
@@ -353,7 +414,7 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
         asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
       }
       // P (generic-proxy stores) must be visible to the tensor core's async proxy
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      if constexpr (!kPTmem) asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc_fence_before();
       mbar_arrive(&p_full[X]);
     }
@@ -442,18 +503,20 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   const int64_t blocks = max_pairs * nseq * Hq;
   TORCH_CHECK(blocks < (int64_t{1} << 31), "fa_fwd: grid too large");
   // softmax variants: bit 0 = two rounds of TMEM loads (fewer registers),
-  // bit 1 = half of the exponentials on the FMA pipe
+  // bit 1 = half of the exponentials on the FMA pipe; 4 = two rounds with P
+  // kept in TMEM (A operand of the P.V MMA read from tensor memory)
   static const int env_variant = [] {
     const char* e = std::getenv("LRL_FA_VARIANT");
     return e ? std::atoi(e) : kDefaultVariant;
   }();
   const int var = variant >= 0 ? (int)variant : env_variant;
-  TORCH_CHECK(var >= 0 && var < 4, "fa_fwd: variant 0..3");
+  TORCH_CHECK(var >= 0 && var < 5, "fa_fwd: variant 0..4");
   using Kern = void (*)(const FAMaps, const int*, const int*, int, int, int, int, float, __nv_bfloat16*, float*, int,
                         int*);
-  static const Kern kerns[4] = {fa_fwd_kernel<false, false>, fa_fwd_kernel<true, false>,
-                                fa_fwd_kernel<false, true>, fa_fwd_kernel<true, true>};
-  static bool attr[4] = {false, false, false, false};
+  static const Kern kerns[5] = {fa_fwd_kernel<false, false>, fa_fwd_kernel<true, false>,
+                                fa_fwd_kernel<false, true>, fa_fwd_kernel<true, true>,
+                                fa_fwd_kernel<true, false, true>};
+  static bool attr[5] = {false, false, false, false, false};
   if (!attr[var]) {
     TORCH_CHECK(cudaFuncSetAttribute(kerns[var], cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFA) ==
                     cudaSuccess,

@@ -172,7 +172,7 @@ def bench_attn_train(ns) -> dict:
         t2 = _time(lambda: torch.ops.aten._flash_attention_forward(qd, kd, vd, cu, cu, ns.seq, ns.seq, 0.0, True,
                                                                     False, scale=sc), ns.steps, ns.warmup)
         t3 = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc), ns.steps, ns.warmup)
-        for var in range(4):
+        for var in range(5):
             tv = _time(lambda: ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc, var), ns.steps, ns.warmup)
             res[f"fwd_tc_v{var}_tflops"] = round(fflops / tv / 1e9, 1)
         out, lse = ext().fa_fwd(qd, kd, vd, cu, ns.seq, sc)

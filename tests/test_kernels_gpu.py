@@ -404,7 +404,7 @@ def _causal_ref(q, k, v, lens, scale):
     return torch.cat(outs), torch.cat(lses, 1)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("lens", [[128], [1, 100, 129, 300], [513, 7, 256, 1024]])
 def test_fa_fwd_tcgen05(cuda, lens, variant):
     """tcgen05 flash-attention forward (ragged packed sequences, GQA 4:1) in

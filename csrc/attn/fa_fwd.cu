@@ -41,7 +41,7 @@ constexpr int kThreadsFA = 320;
 constexpr int kSmemFA = 2 * kTile /*Q_A, Q_B*/ + kSlots * kTile /*ring*/ + 2 * kTile /*P_A, P_B*/ + 1024 + 128;
 constexpr int kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;             // rescale O only when the max grows by more than 2^8
-constexpr int kDefaultVariant = 1;             // two rounds of TMEM loads: fastest measured (no spills)
+constexpr int kDefaultVariant = 4;             // two rounds of TMEM loads, P in TMEM: fastest measured
 
 // masked scores (keys at or past `lim`) become -inf
 __device__ __forceinline__ void mask_chunk(uint32_t (&v)[32], int key0, int lim) {

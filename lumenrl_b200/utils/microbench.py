@@ -192,6 +192,26 @@ def bench_attn_train(ns) -> dict:
     return res
 
 
+def bench_dgemm(ns) -> dict:
+    """Decode-size linears (M = --batch rows) of the model: F.linear (cuBLAS),
+    the swapped product W x^T (+ transpose back), and the weight-streaming
+    tcgen05 kernel."""
+    from lumenrl_b200 import ops
+    a = _model_args(ns.model)
+    shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
+              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size)}
+    out = {"op": "decode_linears", "M": ns.batch}
+    for name, (N, K) in shapes.items():
+        x = torch.randn(ns.batch, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        t_lin = _time(lambda: torch.nn.functional.linear(x, w), ns.steps, ns.warmup)
+        t_sw = _time(lambda: torch.matmul(w, x.t()).t().contiguous(), ns.steps, ns.warmup)
+        t_sk = _time(lambda: ops.skinny_linear(x, w), ns.steps, ns.warmup)
+        out[name] = {"linear_us": round(t_lin * 1e3, 1), "swapped_us": round(t_sw * 1e3, 1),
+                     "skinny_us": round(t_sk * 1e3, 1), "weight_MB": round(N * K * 2 / 1e6, 1)}
+    return out
+
+
 def bench_train(ns) -> dict:
     from lumenrl_b200 import ops
     m = _model(ns.model, True)
@@ -290,7 +310,8 @@ def bench_comm(ns) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm"])
+    ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
+                                     "dgemm"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -308,7 +329,7 @@ def main(argv=None) -> None:
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "logprob": bench_logprob, "gemm": bench_gemm,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm,
           "comm": bench_comm}[ns.what]
     res = fn(ns)
     import os

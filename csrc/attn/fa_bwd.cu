@@ -22,6 +22,7 @@
 // elementwise work (thread r owns TMEM lane r).  Every mbarrier wait is
 // bounded and reports an error word instead of hanging.
 #include <c10/cuda/CUDAStream.h>
+#include <cstdlib>
 
 #include "fa_common.cuh"
 
@@ -38,6 +39,7 @@ constexpr int kSlotsKV = 3;  // Q_i, dO_i, dO^T_i, Q^T_i per query block through
 constexpr int kSmallKV = 2 * 2 * 128 * 4;
 constexpr int kSmemKV = 2 * kTile + kSlotsKV * kTile + 2 * kTile + kSmallKV + 256;
 constexpr int kTmemB = 512;
+constexpr int kDefaultBwdVariant = 0;
 
 struct BwdMaps {
   CUtensorMap q, k, v, dout, kt, qt, dot;
@@ -65,6 +67,26 @@ __device__ __forceinline__ void dq_chunk(const uint32_t (&s)[32], const uint32_t
   }
 }
 
+// same as dq_chunk with the 16 packed bf16 pairs returned in registers (for TMEM)
+__device__ __forceinline__ void dq_chunk_regs(const uint32_t (&s)[32], const uint32_t (&dp)[32], int key0, int lim,
+                                              bool need_mask, float scale_log2, float lse2, float dq_d,
+                                              uint32_t (&out)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int i = 2 * e;
+    float p0 = ex2(fmaf(__uint_as_float(s[i]), scale_log2, -lse2));
+    float p1 = ex2(fmaf(__uint_as_float(s[i + 1]), scale_log2, -lse2));
+    if (need_mask) {
+      if (key0 + i >= lim) p0 = 0.f;
+      if (key0 + i + 1 >= lim) p1 = 0.f;
+    }
+    out[e] = pack_bf16(p0 * (__uint_as_float(dp[i]) - dq_d), p1 * (__uint_as_float(dp[i + 1]) - dq_d));
+  }
+}
+
+// kTm: dS goes to TMEM (into score columns already read) and the dQ MMA reads
+// its A operand from there; otherwise dS goes through shared memory
+template <bool kTm>
 __global__ void __launch_bounds__(kThreadsB, 1)
     fa_bwd_dq_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                      int nseq, int max_tiles, int Hq, int Hk, float scale_log2, float scale,
@@ -186,7 +208,16 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         if (!(ok = mbar_wait(p_full, j & 1, err, kErrMma))) break;
         if (!(ok = slot_wait(Lt))) break;
         tc_fence_after();
-        mma(t_dq, sds, ring + (Lt % kSlotsDQ) * kTile, j > 0);  // dQ += dS (K^T_j)^T
+        if constexpr (kTm) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // A = dS from TMEM: 16 keys (8 columns) per step
+            const uint8_t* b = ring + (Lt % kSlotsDQ) * kTile;
+            const uint64_t bd = sw128_kmajor_desc(smem_addr(b + (kk >> 2) * kBox)) + 2 * (kk & 3);
+            umma_bf16_ts(t_dq, t_s + kk * 8, bd, idesc, (j > 0 || kk != 0) ? 1u : 0u);
+          }
+        } else {
+          mma(t_dq, sds, ring + (Lt % kSlotsDQ) * kTile, j > 0);  // dQ += dS (K^T_j)^T
+        }
         umma_commit(dq_done);
         umma_commit(&slot_empty[Lt % kSlotsDQ]);
       }
@@ -207,21 +238,43 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       tc_fence_after();
       const int k0 = j * kBK;
       const bool need_mask = k0 + kBK > q0 + 1 || k0 + kBK > len;
+      if constexpr (kTm) {
+        // dS for keys [64 hh, 64 hh + 64) into score columns [32 hh, 32 hh + 32), already read
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
+          tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
+          tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
+          tmem_wait_ld(s0v);
+          tmem_wait_ld(s1v);
+          tmem_wait_ld(d0v);
+          tmem_wait_ld(d1v);
+          uint32_t pk[16];
+          dq_chunk_regs(s0v, d0v, k0 + hh * 64, lim, need_mask, scale_log2, lse2, dq_d, pk);
+          tmem_st16_nowait(t_s + lane_off + hh * 32, pk);
+          dq_chunk_regs(s1v, d1v, k0 + hh * 64 + 32, lim, need_mask, scale_log2, lse2, dq_d, pk);
+          tmem_st16_nowait(t_s + lane_off + hh * 32 + 16, pk);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+      } else {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
-        tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
-        tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
-        tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
-        tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
-        tmem_wait_ld(s0v);
-        tmem_wait_ld(s1v);
-        tmem_wait_ld(d0v);
-        tmem_wait_ld(d1v);
-        dq_chunk(s0v, d0v, k0 + hh * 64, lim, need_mask, scale_log2, lse2, dq_d, sds, r, hh * 64);
-        dq_chunk(s1v, d1v, k0 + hh * 64 + 32, lim, need_mask, scale_log2, lse2, dq_d, sds, r, hh * 64 + 32);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
+          tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
+          tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
+          tmem_wait_ld(s0v);
+          tmem_wait_ld(s1v);
+          tmem_wait_ld(d0v);
+          tmem_wait_ld(d1v);
+          dq_chunk(s0v, d0v, k0 + hh * 64, lim, need_mask, scale_log2, lse2, dq_d, sds, r, hh * 64);
+          dq_chunk(s1v, d1v, k0 + hh * 64 + 32, lim, need_mask, scale_log2, lse2, dq_d, sds, r, hh * 64 + 32);
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc_fence_before();
       mbar_arrive(p_full);
     }
@@ -283,6 +336,28 @@ __device__ __forceinline__ void kv_chunk(const uint32_t (&s)[32], const uint32_t
   }
 }
 
+// kv_chunk with the packed P^T and dS^T pairs returned in registers (for TMEM)
+__device__ __forceinline__ void kv_chunk_regs(const uint32_t (&s)[32], const uint32_t (&dp)[32], const float* sl,
+                                              int q0c, int r, bool diag, float scale_log2, uint32_t (&pp)[16],
+                                              uint32_t (&dd)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int i = 2 * e;
+    const int qa = q0c + i, qb = qa + 1;
+    float p0 = ex2(fmaf(__uint_as_float(s[i]), scale_log2, -sl[qa]));
+    float p1 = ex2(fmaf(__uint_as_float(s[i + 1]), scale_log2, -sl[qb]));
+    if (diag) {
+      if (qa < r) p0 = 0.f;
+      if (qb < r) p1 = 0.f;
+    }
+    pp[e] = pack_bf16(p0, p1);
+    dd[e] = pack_bf16(p0 * (__uint_as_float(dp[i]) - sl[128 + qa]), p1 * (__uint_as_float(dp[i + 1]) - sl[128 + qb]));
+  }
+}
+
+// kTm: P^T and dS^T go to TMEM (into the S^T and dP^T columns already read)
+// and the dV / dK MMAs read their A operands from there
+template <bool kTm>
 __global__ void __launch_bounds__(kThreadsB, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
                        const int* __restrict__ poff, int nseq, int max_tiles, int Hq, int Hk, float scale_log2,
@@ -437,10 +512,28 @@ __global__ void __launch_bounds__(kThreadsB, 1)
         if (!(ok = mbar_wait(p_full, it & 1, err, kErrMma))) break;
         if (!(ok = slot_wait(Ldt))) break;
         tc_fence_after();
-        mma(t_dv, sp, ring + (Ldt % kSlotsKV) * kTile, it > 0);  // dV += P^T (dO^T_i)^T
+        if constexpr (kTm) {
+          const uint8_t* b = ring + (Ldt % kSlotsKV) * kTile;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // dV += P^T (dO^T_i)^T, A from TMEM
+            const uint64_t bd = sw128_kmajor_desc(smem_addr(b + (kk >> 2) * kBox)) + 2 * (kk & 3);
+            umma_bf16_ts(t_dv, t_s + kk * 8, bd, idesc, (it > 0 || kk != 0) ? 1u : 0u);
+          }
+        } else {
+          mma(t_dv, sp, ring + (Ldt % kSlotsKV) * kTile, it > 0);  // dV += P^T (dO^T_i)^T
+        }
         if (!(ok = slot_wait(Lqt))) break;
         tc_fence_after();
-        mma(t_dk, sds, ring + (Lqt % kSlotsKV) * kTile, it > 0);  // dK += dS^T (Q^T_i)^T
+        if constexpr (kTm) {
+          const uint8_t* b = ring + (Lqt % kSlotsKV) * kTile;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T (Q^T_i)^T, A from TMEM
+            const uint64_t bd = sw128_kmajor_desc(smem_addr(b + (kk >> 2) * kBox)) + 2 * (kk & 3);
+            umma_bf16_ts(t_dk, t_dp + kk * 8, bd, idesc, (it > 0 || kk != 0) ? 1u : 0u);
+          }
+        } else {
+          mma(t_dk, sds, ring + (Lqt % kSlotsKV) * kTile, it > 0);  // dK += dS^T (Q^T_i)^T
+        }
         umma_commit(acc_done);
         umma_commit(&slot_empty[Ldt % kSlotsKV]);
         umma_commit(&slot_empty[Lqt % kSlotsKV]);
@@ -460,22 +553,48 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       tc_fence_after();
       const bool diag = (kt + it % nqi) == kt;
       const float* sl = small + sb * 256;
+      if constexpr (kTm) {
+        // P^T / dS^T for queries [64 hh, 64 hh + 64) into columns [32 hh, 32 hh + 32)
+        // of the S^T / dP^T regions, already read
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
+          tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
+          tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
+          tmem_wait_ld(s0v);
+          tmem_wait_ld(s1v);
+          tmem_wait_ld(d0v);
+          tmem_wait_ld(d1v);
+          uint32_t pp[16], dd[16];
+          kv_chunk_regs(s0v, d0v, sl, hh * 64, r, diag, scale_log2, pp, dd);
+          tmem_st16_nowait(t_s + lane_off + hh * 32, pp);
+          tmem_st16_nowait(t_dp + lane_off + hh * 32, dd);
+          kv_chunk_regs(s1v, d1v, sl, hh * 64 + 32, r, diag, scale_log2, pp, dd);
+          tmem_st16_nowait(t_s + lane_off + hh * 32 + 16, pp);
+          tmem_st16_nowait(t_dp + lane_off + hh * 32 + 16, dd);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+        mbar_arrive(&small_empty[sb]);
+      } else {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
-        tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
-        tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
-        tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
-        tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
-        tmem_wait_ld(s0v);
-        tmem_wait_ld(s1v);
-        tmem_wait_ld(d0v);
-        tmem_wait_ld(d1v);
-        kv_chunk(s0v, d0v, sl, hh * 64, r, diag, scale_log2, sp, sds);
-        kv_chunk(s1v, d1v, sl, hh * 64 + 32, r, diag, scale_log2, sp, sds);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t s0v[32], s1v[32], d0v[32], d1v[32];
+          tmem_ld32_nowait(t_s + lane_off + hh * 64, s0v);
+          tmem_ld32_nowait(t_s + lane_off + hh * 64 + 32, s1v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64, d0v);
+          tmem_ld32_nowait(t_dp + lane_off + hh * 64 + 32, d1v);
+          tmem_wait_ld(s0v);
+          tmem_wait_ld(s1v);
+          tmem_wait_ld(d0v);
+          tmem_wait_ld(d1v);
+          kv_chunk(s0v, d0v, sl, hh * 64, r, diag, scale_log2, sp, sds);
+          kv_chunk(s1v, d1v, sl, hh * 64 + 32, r, diag, scale_log2, sp, sds);
+        }
+        mbar_arrive(&small_empty[sb]);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       }
-      mbar_arrive(&small_empty[sb]);
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc_fence_before();
       mbar_arrive(p_full);
     }
@@ -585,7 +704,7 @@ int64_t fa_bwd_status() {
 // (dq, dk, dv) in bf16.
 std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                   torch::Tensor out, torch::Tensor lse, torch::Tensor cu, int64_t max_seqlen,
-                                  double scale, int64_t streams) {
+                                  double scale, int64_t streams, int64_t variant) {
   for (auto* t : {&dout, &q, &k, &v, &out}) {
     LRL_CHECK((*t));
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 3 && t->size(2) == kD, "fa_bwd: bf16 [T, H, 128]");
@@ -619,19 +738,27 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
   maps.kt = map3(kt.data_ptr(), Tpad, kD, Hk, Tpad * 2, kD * Tpad * 2, 64, kD, 1);
   maps.qt = map3(qt.data_ptr(), Tpad, kD, Hq, Tpad * 2, kD * Tpad * 2, 64, kD, 1);
   maps.dot = map3(dot.data_ptr(), Tpad, kD, Hq, Tpad * 2, kD * Tpad * 2, 64, kD, 1);
-  static bool attr = false;
-  if (!attr) {
-    TORCH_CHECK(cudaFuncSetAttribute(fa_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDQ) ==
-                        cudaSuccess &&
-                    cudaFuncSetAttribute(fa_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemKV) == cudaSuccess,
+  // variant 1: dS, P^T and dS^T reach their MMAs through TMEM; 0: through shared memory
+  static const int env_variant = [] {
+    const char* e = std::getenv("LRL_FA_BWD_VARIANT");
+    return e ? std::atoi(e) : kDefaultBwdVariant;
+  }();
+  const int var = variant >= 0 ? (int)variant : env_variant;
+  TORCH_CHECK(var == 0 || var == 1, "fa_bwd: variant 0 or 1");
+  auto dq_kern = var ? fa_bwd_dq_kernel<true> : fa_bwd_dq_kernel<false>;
+  auto kv_kern = var ? fa_bwd_dkdv_kernel<true> : fa_bwd_dkdv_kernel<false>;
+  static bool attr[2] = {false, false};
+  if (!attr[var]) {
+    TORCH_CHECK(cudaFuncSetAttribute(dq_kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDQ) == cudaSuccess &&
+                    cudaFuncSetAttribute(kv_kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemKV) ==
+                        cudaSuccess,
                 "fa_bwd: shared memory opt-in failed");
-    attr = true;
+    attr[var] = true;
   }
   const int64_t max_tiles = (max_seqlen + kBQ - 1) / kBQ;
   TORCH_CHECK(max_tiles * nseq * Hq < (int64_t{1} << 31), "fa_bwd: grid too large");
   const float sl2 = (float)(scale * 1.4426950408889634);
-  fa_bwd_dq_kernel<<<(unsigned)(max_tiles * nseq * Hq), kThreadsB, kSmemDQ, stream()>>>(
+  dq_kern<<<(unsigned)(max_tiles * nseq * Hq), kThreadsB, kSmemDQ, stream()>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
       lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dq.data_ptr(),
       bwd_err_word().data_ptr<int>());
@@ -649,7 +776,7 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
     cudaEventRecord(ev_fork, main);
     cudaStreamWaitEvent(kv_stream, ev_fork, 0);
   }
-  fa_bwd_dkdv_kernel<<<(unsigned)(max_tiles * nseq * Hk), kThreadsB, kSmemKV, kv_stream>>>(
+  kv_kern<<<(unsigned)(max_tiles * nseq * Hk), kThreadsB, kSmemKV, kv_stream>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
       lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dk.data_ptr(),
       (__nv_bfloat16*)dv.data_ptr(), bwd_err_word().data_ptr<int>());

@@ -183,8 +183,10 @@ def bench_attn_train(ns) -> dict:
                                                                      0.0, True, zero, zero, scale=sc),
                     ns.steps, ns.warmup)
         tb3 = _time(lambda: ext().fa_bwd(do, qd, kd, vd, out, lse, cu, ns.seq, sc), ns.steps, ns.warmup)
-        tb1 = _time(lambda: ext().fa_bwd(do, qd, kd, vd, out, lse, cu, ns.seq, sc, 1), ns.steps, ns.warmup)
-        res["bwd_tc_one_stream_tflops"] = round(2.5 * fflops / tb1 / 1e9, 1)
+        for var in range(2):
+            tv = _time(lambda: ext().fa_bwd(do, qd, kd, vd, out, lse, cu, ns.seq, sc, variant=var), ns.steps,
+                       ns.warmup)
+            res[f"bwd_tc_v{var}_tflops"] = round(2.5 * fflops / tv / 1e9, 1)
     bflops = 2.5 * fflops
     res.update(fwd_fa2_ms=t2, fwd_fa2_tflops=fflops / t2 / 1e9, fwd_tc_ms=t3, fwd_tc_tflops=fflops / t3 / 1e9,
                fwd_tc_status=int(ext().fa_fwd_status()), bwd_fa2_ms=tb2, bwd_fa2_tflops=bflops / tb2 / 1e9,

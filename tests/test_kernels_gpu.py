@@ -450,8 +450,9 @@ def test_fa_fwd_bwd_modes(cuda, monkeypatch, mode):
         assert ((g.float() - r).abs().max() / r.abs().max()).item() < 2e-2
 
 
+@pytest.mark.parametrize("variant", [0, 1])
 @pytest.mark.parametrize("lens", [[128], [1, 100, 129, 300], [513, 7, 256, 1024]])
-def test_fa_bwd_tcgen05(cuda, lens):
+def test_fa_bwd_tcgen05(cuda, lens, variant):
     """tcgen05 flash-attention backward (dQ kernel + dK/dV kernel, GQA 4:1,
     ragged packed sequences) against fp32 autograd of the causal reference."""
     from lumenrl_b200.ops.ext import ext
@@ -463,7 +464,7 @@ def test_fa_bwd_tcgen05(cuda, lens):
     v = torch.randn(T, Hk, D, device=cuda).to(torch.bfloat16)
     do = torch.randn(T, Hq, D, device=cuda).to(torch.bfloat16)
     out, lse = ext().fa_fwd(q, k, v, cu, max(lens), D ** -0.5)
-    dq, dk, dv = ext().fa_bwd(do, q, k, v, out, lse, cu, max(lens), D ** -0.5)
+    dq, dk, dv = ext().fa_bwd(do, q, k, v, out, lse, cu, max(lens), D ** -0.5, variant=variant)
     assert ext().fa_bwd_status() == 0
     qr, kr, vr = (t.float().requires_grad_(True) for t in (q, k, v))
     ro, _ = _causal_ref(qr, kr, vr, lens, D ** -0.5)

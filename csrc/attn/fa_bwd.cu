@@ -39,7 +39,7 @@ constexpr int kSlotsKV = 3;  // Q_i, dO_i, dO^T_i, Q^T_i per query block through
 constexpr int kSmallKV = 2 * 2 * 128 * 4;
 constexpr int kSmemKV = 2 * kTile + kSlotsKV * kTile + 2 * kTile + kSmallKV + 256;
 constexpr int kTmemB = 512;
-constexpr int kDefaultBwdVariant = 0;
+constexpr int kDefaultBwdVariant = 1;  // TMEM operands: 263 / 405 TFLOP/s vs 252 / 382 through shared memory
 
 struct BwdMaps {
   CUtensorMap q, k, v, dout, kt, qt, dot;

@@ -18,6 +18,8 @@
 // items, all writing (o, lse) partials merged by a combine kernel.  Every wait
 // is bounded: on expiry the CTA records an error word, drains its in-flight
 // copies (bounded) and exits.
+#include <cstdlib>
+
 #include "../common.cuh"
 #include "../gemm/tc_gemm.cuh"
 
@@ -430,8 +432,14 @@ torch::Tensor& tma_err_word() {
 }
 
 int pick_pps(int64_t items, int64_t max_pages) {
-  // >= ~4 CTAs per SM in total (2 resident), at least 2 pages per item
-  int64_t splits = std::max<int64_t>(1, (4 * (int64_t)num_sms() + items - 1) / items);
+  // >= ~4 CTAs per SM in total (2 resident), at least 2 pages per item;
+  // LRL_DECODE_CTAS_PER_SM overrides the 4
+  static const int64_t per_sm = [] {
+    const char* e = std::getenv("LRL_DECODE_CTAS_PER_SM");
+    const int v = e ? std::atoi(e) : 4;
+    return (int64_t)(v < 1 ? 1 : (v > 64 ? 64 : v));
+  }();
+  int64_t splits = std::max<int64_t>(1, (per_sm * (int64_t)num_sms() + items - 1) / items);
   int64_t pps = std::max<int64_t>(2, (max_pages + splits - 1) / splits);
   return (int)std::min<int64_t>(pps, std::max<int64_t>(1, max_pages));
 }

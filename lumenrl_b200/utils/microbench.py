@@ -195,9 +195,9 @@ def bench_attn_train(ns) -> dict:
 
 
 def bench_dgemm(ns) -> dict:
-    """Decode-size linears (M = --batch rows) of the model: F.linear (cuBLAS),
-    the swapped product W x^T (+ transpose back), and the weight-streaming
-    tcgen05 kernel."""
+    """Decode-size linears (M = --batch rows) of the model: F.linear (cuBLAS)
+    and the weight-streaming tcgen05 kernel, each call on the next of several
+    weight copies so the weights stream from HBM as in the decode step."""
     from lumenrl_b200 import ops
     a = _model_args(ns.model)
     shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
@@ -215,11 +215,6 @@ def bench_dgemm(ns) -> dict:
         res = {"weight_MB": round(N * K * 2 / 1e6, 1)}
         res["linear_us"] = round(_time(lambda: torch.nn.functional.linear(x, nxt()), ns.steps, ns.warmup) * 1e3, 1)
         res["skinny_us"] = round(_time(lambda: ops.skinny_linear(x, nxt()), ns.steps, ns.warmup) * 1e3, 1)
-        for sk in (2, 4):
-            xs = x.view(ns.batch, sk, K // sk).transpose(0, 1)                      # [sk, M, K/sk]
-            res[f"splitk{sk}_us"] = round(_time(
-                lambda: torch.bmm(xs, nxt().view(N, sk, K // sk).permute(1, 2, 0), out_dtype=torch.float32).sum(0)
-                .to(torch.bfloat16), ns.steps, ns.warmup) * 1e3, 1)
         out[name] = res
         del ws
     return out

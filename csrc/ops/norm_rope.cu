@@ -64,9 +64,14 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   }
 }
 
-static int row_threads(int H) {
-  int t = (H / 8 + kMaxChunks - 1) / kMaxChunks;
+// Threads per row: up to kMaxChunks 8-element chunks per thread, or, when
+// there are fewer rows than 2 per SM (decode), one chunk per thread so each
+// row's loads are all in flight at once and the per-thread chain is short.
+static int row_threads(int H, int64_t T) {
+  const int chunks = T < 2 * (int64_t)num_sms() ? 1 : kMaxChunks;
+  int t = (H / 8 + chunks - 1) / chunks;
   t = ((t + 31) / 32) * 32;
+  if (t > 1024) t = ((H / 8 + kMaxChunks - 1) / kMaxChunks + 31) / 32 * 32;
   return t < 32 ? 32 : (t > 1024 ? 1024 : t);
 }
 
@@ -80,7 +85,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
   if (T == 0) return {y, rstd};
-  launch_pdl(rmsnorm_fwd_kernel<false>, dim3(T), dim3(row_threads(H)), 0, (const __nv_bfloat16*)x.data_ptr(),
+  launch_pdl(rmsnorm_fwd_kernel<false>, dim3(T), dim3(row_threads(H, T)), 0, (const __nv_bfloat16*)x.data_ptr(),
              (const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
              (__nv_bfloat16*)nullptr, rstd.data_ptr<float>(), H, (float)eps);
   return {y, rstd};
@@ -98,7 +103,7 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
   auto s = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
   if (T == 0) return {y, s, rstd};
-  launch_pdl(rmsnorm_fwd_kernel<true>, dim3(T), dim3(row_threads(H)), 0, (const __nv_bfloat16*)x.data_ptr(),
+  launch_pdl(rmsnorm_fwd_kernel<true>, dim3(T), dim3(row_threads(H, T)), 0, (const __nv_bfloat16*)x.data_ptr(),
              (const __nv_bfloat16*)res.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
              (__nv_bfloat16*)s.data_ptr(), rstd.data_ptr<float>(), H, (float)eps);
   return {y, s, rstd};

@@ -67,11 +67,17 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
 // Threads per row: up to kMaxChunks 8-element chunks per thread, or, when
 // there are fewer rows than 2 per SM (decode), one chunk per thread so each
 // row's loads are all in flight at once and the per-thread chain is short.
+// At most 512 threads in the decode shape: the kernel's registers allow no
+// more than that per block.
 static int row_threads(int H, int64_t T) {
-  const int chunks = T < 2 * (int64_t)num_sms() ? 1 : kMaxChunks;
-  int t = (H / 8 + chunks - 1) / chunks;
+  const int v = H / 8;  // 8-element chunks in a row
+  int chunks = kMaxChunks;
+  if (T < 2 * (int64_t)num_sms()) {
+    chunks = (v + 511) / 512;
+    if (chunks > kMaxChunks) chunks = kMaxChunks;
+  }
+  int t = (v + chunks - 1) / chunks;
   t = ((t + 31) / 32) * 32;
-  if (t > 1024) t = ((H / 8 + kMaxChunks - 1) / kMaxChunks + 31) / 32 * 32;
   return t < 32 ? 32 : (t > 1024 ? 1024 : t);
 }
 

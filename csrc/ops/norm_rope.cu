@@ -10,7 +10,7 @@ constexpr int kMaxChunks = 4;  // 8-element chunks per thread => H <= 32768 at 1
 
 // ---------------------------------------------------------------- RMSNorm fwd
 template <bool kResidual>
-__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
+__global__ void __launch_bounds__(1024) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
                                    float eps) {

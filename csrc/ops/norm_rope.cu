@@ -10,7 +10,7 @@ constexpr int kMaxChunks = 4;  // 8-element chunks per thread => H <= 32768 at 1
 
 // ---------------------------------------------------------------- RMSNorm fwd
 template <bool kResidual>
-__global__ void __launch_bounds__(1024) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
                                    float eps) {
@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(1024) rmsnorm_fwd_kernel(const __nv_bfloat16* 
 // Threads per row: up to kMaxChunks 8-element chunks per thread, or, when
 // there are fewer rows than 2 per SM (decode), one chunk per thread so each
 // row's loads are all in flight at once and the per-thread chain is short.
-// At most 512 threads in the decode shape: the kernel's registers allow no
-// more than that per block.
+// At most 512 threads in the decode shape: the residual kernel's registers
+// allow no more than that per block.
 static int row_threads(int H, int64_t T) {
   const int v = H / 8;  // 8-element chunks in a row
   int chunks = kMaxChunks;
@@ -104,7 +104,8 @@ std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, t
   TORCH_CHECK(x.scalar_type() == at::kBFloat16, "add_rmsnorm: bf16 only");
   const int H = x.size(-1);
   const int64_t T = x.numel() / H;
-  TORCH_CHECK(H % 8 == 0 && H <= 1024 * 8 * kMaxChunks, "add_rmsnorm: bad H");
+  // the residual variant's registers allow at most 512 threads per row (4 chunks of 8 each)
+  TORCH_CHECK(H % 8 == 0 && H <= 512 * 8 * kMaxChunks, "add_rmsnorm: H must be a multiple of 8 and <= 16384");
   auto y = torch::empty_like(x);
   auto s = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));

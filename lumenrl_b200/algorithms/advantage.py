@@ -58,9 +58,13 @@ def response_mask_of(batch: DataProto) -> Tensor | None:
 
 
 def _flat_rewards(batch: DataProto, what: str) -> Tensor:
+    """One score per sequence: scalar rewards as they are, token-level
+    rewards (e.g. after KL-in-reward shaping) summed over the response."""
     if "rewards" not in batch.tensors:
         raise KeyError(f"{what} requires tensor key 'rewards' on the batch.")
     r = batch.tensors["rewards"]
+    if r.dim() > 1 and r.shape[-1] > 1:
+        return r.sum(-1)
     return r.squeeze(-1) if r.dim() > 1 else r
 
 

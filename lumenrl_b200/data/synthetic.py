@@ -21,10 +21,11 @@ class SyntheticPrompts:
         self.cursor = step + 1
         return ids.tolist()
 
-    def batch_tensor(self, n: int, step: int, rank: int = 0, pin: bool = False) -> torch.Tensor:
+    def batch_tensor(self, n: int, step: int, rank: int = 0, pin: bool = False, round: int = 0) -> torch.Tensor:
         """Same prompts as ``batch`` as an int64 [n, prompt_len] host tensor
-        (page-locked when ``pin``, for an asynchronous host->device copy)."""
-        g = torch.Generator().manual_seed(self.seed * 1_000_003 + step * 7919 + rank)
+        (page-locked when ``pin``, for an asynchronous host->device copy).
+        ``round`` > 0 draws fresh prompts for the same step (DAPO refill)."""
+        g = torch.Generator().manual_seed(self.seed * 1_000_003 + step * 7919 + rank + round * 104_729)
         ids = torch.randint(self.low, self.high, (n, self.prompt_len), generator=g)
         self.cursor = step + 1
         return ids.pin_memory() if pin else ids

@@ -43,7 +43,7 @@ class CheckpointCallback(Callback):
 
     def on_train_begin(self, trainer) -> None:
         st = trainer.state
-        step = self.mgr.load_latest(trainer.actor, st.rank, st.world_size)
+        step = self.mgr.load_latest(trainer.actor, st.rank, st.world_size, data=getattr(trainer, "data", None))
         if step:
             trainer.global_step = step
             logger.info("resumed from step %d", step)

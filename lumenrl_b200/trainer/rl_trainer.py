@@ -6,12 +6,20 @@ Per step (reference hot loop ``lumenrl/trainer/rl_trainer.py:3003-3522``):
    native engine on the policy's own bf16 weights (data-parallel rollout,
    groups never straddle ranks, so advantages need no communication);
 2. rewards (programmatic function, or reward model);
-3. DAPO dynamic sampling: groups with equal rewards are dropped;
-4. old log-probs (skipped in bypass mode) and, when ``kl_coeff > 0``, reference
-   log-probs from a frozen copy;
-5. advantages (estimator registry) and rollout correction (TIS/MIS/RS);
+3. DAPO dynamic sampling with refill rounds (``filter_groups.enable``): groups
+   whose rewards are all equal are dropped and fresh prompts are generated
+   until the step has its full count of informative groups or
+   ``max_num_gen_batches`` rounds ran (reference ``rl_trainer.py:2163-2189``);
+4. old log-probs (skipped in bypass mode) and, when ``kl_coeff > 0`` or
+   ``use_kl_in_reward``, reference log-probs from a frozen copy; with
+   ``use_kl_in_reward`` the rewards become token-level ``r - beta * KL`` under
+   a fixed / adaptive KL controller (reference ``rl_trainer.py:3183``);
+5. critic values for GAE when the algorithm is PPO (reference
+   ``rl_trainer.py:3189-3193``), then advantages (estimator registry) and
+   rollout correction (TIS/MIS/RS);
 6. policy update (sharded AdamW), whose final all-gather leaves every GPU with
-   the new bf16 weights: that is the weight sync in colocated mode;
+   the new bf16 weights: that is the weight sync in colocated mode; PPO then
+   updates the critic on the same batch (clipped value loss);
 7. metrics with the reference's names (``timing/*``, ``perf/throughput``,
    ``rollout_corr/*``, ``actor/*``).
 
@@ -92,9 +100,23 @@ class RLTrainer:
             warmup_steps=p.lr_warmup_steps, lr_style=p.lr_decay_style,
             min_lr_ratio=(p.min_lr / p.learning_rate if p.learning_rate else 0.0))
         self.ref = None
-        if float(getattr(self.algo_cfg, "kl_coeff", 0.0)) > 0:
+        kl_coeff = float(getattr(self.algo_cfg, "kl_coeff", 0.0))
+        self.kl_ctrl = None
+        if c.algorithm.use_kl_in_reward:
+            from lumenrl_b200.algorithms.kl_controller import get_kl_controller
+            self.kl_ctrl = get_kl_controller(c.algorithm.kl_ctrl_type, kl_coeff, c.algorithm.kl_target,
+                                             c.algorithm.kl_horizon)
+        if kl_coeff > 0 or self.kl_ctrl is not None:
             self.ref = ActorEngine(self.model_args, st, seed=c.seed, trainable=False, init=False)
             self.ref.model.flat.copy_(self.actor.model.flat)
+        self.critic = None
+        if algo == "ppo" or c.algorithm.adv_estimator == "gae" or c.critic.enabled:
+            from lumenrl_b200.engine.training.critic import CriticEngine
+            cc = c.critic
+            self.critic = CriticEngine(self.model_args, st, lr=cc.learning_rate, weight_decay=cc.weight_decay,
+                                       max_grad_norm=cc.max_grad_norm, seed=c.seed + 1,
+                                       gradient_checkpointing=self.spec.gradient_checkpointing,
+                                       total_steps=c.num_training_steps)
         vc = p.generation.vllm_cfg
         self.temperature = float(vc.temperature)
         self.top_p = float(vc.top_p)
@@ -123,13 +145,15 @@ class RLTrainer:
                          num_last_layers_in_bf16=r.num_last_layers_in_bf16)
 
     # ------------------------------------------------------------------ step
-    def _rollout(self, step: int) -> DataProto:
+    def _rollout(self, step: int, round_idx: int = 0) -> DataProto:
         st, sp = self.state, self.spec
-        host = self.data.batch_tensor(self.prompts_per_rank, step, st.rank, pin=st.device.type == "cuda")
+        host = self.data.batch_tensor(self.prompts_per_rank, step, st.rank, pin=st.device.type == "cuda",
+                                      round=round_idx)
         prompts = host.to(st.device, non_blocking=True)
         self.io_bytes["h2d"] = host.numel() * host.element_size()
         params = SamplingParams(max_new_tokens=sp.max_new_tokens, temperature=self.temperature, top_p=self.top_p,
-                                n=self.group, seed=self.config.seed * 7919 + step * 131 + st.rank,
+                                n=self.group,
+                                seed=self.config.seed * 7919 + step * 131 + st.rank + round_idx * 1_000_033,
                                 eos_token_id=sp.eos_token_id)
         self.rollout.wake()
         out = self.rollout.generate(prompts, params)
@@ -145,10 +169,55 @@ class RLTrainer:
                      "response_lengths": out.response_lengths, "response_mask": rmask,
                      "rollout_log_probs": out.logprobs},
             meta={"num_generations": self.group,
-                  "uid": [f"{step}-{st.rank}-{int(i)}" for i in out.prompt_index.tolist()],
+                  "uid": [f"{step}-{st.rank}-{round_idx}-{int(i)}" for i in out.prompt_index.tolist()],
                   "response_lengths": out.response_lengths.tolist(), "gen_stats": out.stats})
         if out.routed_experts:
             batch.ragged["routed_experts"] = out.routed_experts
+        return batch
+
+    def _score(self, batch: DataProto) -> None:
+        rewards = self.reward_fn(batch["responses"], None, lengths=batch["response_lengths"], **self.spec.reward_kwargs)
+        batch["rewards"] = rewards.to(self.state.device).float()
+
+    def _collect(self, step: int, m: dict) -> DataProto:
+        """One rollout round, or DAPO refill rounds until ``prompts_per_rank``
+        groups with non-constant rewards are collected."""
+        c = self.config
+        fg = c.algorithm.dapo.filter_groups
+        if not (self.algorithm_name == "dapo" and fg.enable):
+            batch = self._rollout(step)
+            self._score(batch)
+            return batch
+        from lumenrl_b200.algorithms.dapo_sampling import filter_groups_keep_mask
+        max_rounds = int(fg.max_num_gen_batches) if int(fg.max_num_gen_batches) > 0 else 10_000
+        parts, uids, stats, kept, rounds, seen = [], [], {}, 0, 0, 0
+        while kept < self.prompts_per_rank and rounds < max_rounds:
+            b = self._rollout(step, rounds)
+            self._score(b)
+            keep, kept_uids = filter_groups_keep_mask(b["rewards"].float().cpu(), b.meta["uid"])
+            rounds += 1
+            seen += len(set(b.meta["uid"]))
+            for k, v in b.meta.get("gen_stats", {}).items():
+                if isinstance(v, (int, float)):
+                    stats[k] = stats.get(k, 0.0) + v
+            if bool(keep.any()):
+                idx = keep.nonzero(as_tuple=True)[0]
+                parts.append(b.select_idxs(idx))
+                uids.extend(b.meta["uid"][i] for i in idx.tolist())
+                kept += len(kept_uids)
+        if not parts:
+            raise RuntimeError("DAPO filter_groups kept no prompt group in "
+                               f"{rounds} generation round(s); raise max_num_gen_batches or check the reward")
+        batch = DataProto.merge(parts)
+        n_rows = min(len(batch), self.prompts_per_rank * self.group)
+        if n_rows < len(batch):
+            batch = batch.select_idxs(torch.arange(n_rows))
+            uids = uids[:n_rows]
+        batch.meta.update({"num_generations": self.group, "uid": uids,
+                           "response_lengths": batch["response_lengths"].tolist(), "gen_stats": stats})
+        m["dapo/gen_rounds"] = float(rounds)
+        m["dapo/kept_groups"] = float(len(uids) // self.group)
+        m["dapo/kept_frac"] = kept / max(seen, 1)
         return batch
 
     def step(self) -> dict[str, Any]:
@@ -157,11 +226,10 @@ class RLTrainer:
         m: dict[str, Any] = {}
         self.timer.start("step")
         self.timer.start("gen")
-        batch = self._rollout(step)
+        batch = self._collect(step, m)
         self.timer.stop("gen")
-        rewards = self.reward_fn(batch["responses"], None, lengths=batch["response_lengths"], **self.spec.reward_kwargs)
-        batch["rewards"] = rewards.to(st.device).float()
-        if self.algorithm_name == "dapo" and c.algorithm.dapo.filter_groups.enable:
+        scores = batch["rewards"]
+        if self.algorithm_name == "dapo" and c.algorithm.dapo.filter_groups.enable and "dapo/kept_frac" not in m:
             from lumenrl_b200.algorithms.dapo_sampling import filter_groups_keep_mask
             keep, _ = filter_groups_keep_mask(batch["rewards"].cpu(), batch.meta["uid"])
             m["dapo/kept_frac"] = float(keep.float().mean())
@@ -180,6 +248,15 @@ class RLTrainer:
             batch["ref_log_probs"], _ = self.ref.compute_log_probs(batch, self.temperature,
                                                                    self.spec.logprob_token_budget, want_entropy=False)
             self.timer.stop("ref")
+        if self.kl_ctrl is not None:
+            from lumenrl_b200.algorithms.kl_controller import apply_kl_penalty
+            batch, klm = apply_kl_penalty(batch, self.kl_ctrl, c.algorithm.kl_penalty)
+            m.update(klm)
+            del batch.tensors["ref_log_probs"]     # the KL is in the reward, not in the policy loss
+        if self.critic is not None:
+            self.timer.start("values")
+            batch["values"] = self.critic.compute_values(batch, self.spec.logprob_token_budget)
+            self.timer.stop("values")
         self.timer.start("adv")
         self.algorithm.compute_advantages(batch)
         if rcfg.rollout_is or rcfg.rollout_rs:
@@ -196,6 +273,12 @@ class RLTrainer:
                                       num_epochs=int(getattr(self.algo_cfg, "num_ppo_epochs", 1)),
                                       temperature=self.temperature)
         self.timer.stop("train")
+        if self.critic is not None:
+            self.timer.start("critic")
+            for _ in range(max(1, int(c.critic.num_critic_epochs))):
+                tm.update(self.critic.update(batch, clip=float(c.critic.value_clip_ratio),
+                                             rows_per_micro=self.spec.rows_per_micro))
+            self.timer.stop("critic")
         self.timer.start("weight_sync")
         self.rollout.update_weights()
         self.timer.stop("weight_sync")
@@ -211,14 +294,14 @@ class RLTrainer:
         m["perf/throughput"] = tokens / (step_s * st.world_size)
         m["perf/gen_tokens_per_s"] = all_reduce_sum(float(batch["response_lengths"].sum())) / max(
             all_reduce_max(times["gen"]), 1e-9)
-        m["reward/mean"] = all_reduce_sum(float(batch["rewards"].sum())) / all_reduce_sum(float(len(batch)))
+        m["reward/mean"] = all_reduce_sum(float(scores.sum())) / all_reduce_sum(float(len(batch)))
         m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
             float(len(batch)))
         m["weight_sync/ms"] = times["weight_sync"] * 1e3
         for k in ("prefill_ms", "setup_ms", "decode_ms"):
             if k in batch.meta.get("gen_stats", {}):
                 m[f"timing/gen_{k}"] = batch.meta["gen_stats"][k]
-        host_result = batch["rewards"].to("cpu")          # the step's result read back to the host
+        host_result = scores.to("cpu")          # the step's result read back to the host
         self.io_bytes["d2h"] = host_result.numel() * host_result.element_size()
         m["step"] = step + 1
         self.global_step += 1

@@ -35,23 +35,48 @@ def _step_dir(root: str, step: int) -> str:
     return os.path.join(root, f"global_step_{step}", "actor")
 
 
+def _atomic(path: str, write) -> None:
+    """write(tmp_path) then rename into place: a crash leaves either the old
+    file or none, never a truncated one."""
+    tmp = f"{path}.tmp{os.getpid()}"
+    write(tmp)
+    os.replace(tmp, path)
+
+
+def _all_ranks_done(world: int) -> None:
+    import torch.distributed as dist
+    if world > 1 and dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
 def save_sharded(engine, root: str, step: int, rank: int, world: int, extra: Optional[dict] = None) -> str:
+    """Every rank writes its shard files (each to a temporary name, renamed
+    when complete); after all ranks have written, rank 0 publishes the step
+    in the tracker file (also by rename).  A crash at any point leaves the
+    tracker naming the previous complete step, mirroring the reference's
+    order (tracker only after every rank's save, reference
+    ``lumenrl/trainer/callbacks.py:170-178``).  Must be called on every rank."""
     d = _step_dir(root, step)
     os.makedirs(d, exist_ok=True)
     opt = engine.opt
     state = {"optimizer": {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in opt.state_dict().items()},
              "args": engine.args.to_dict()}
-    torch.save(state, os.path.join(d, f"model_world_size_{world}_rank_{rank}.pt"))
+    _atomic(os.path.join(d, f"model_world_size_{world}_rank_{rank}.pt"), lambda p: torch.save(state, p))
     ex = {"scheduler": engine.sched.state_dict() if engine.sched else None,
           "rng": {"torch": torch.get_rng_state(), "numpy": np.random.get_state(), "python": random.getstate(),
                   "cuda": torch.cuda.get_rng_state_all() if torch.cuda.is_available() else None},
           **(extra or {})}
-    torch.save(ex, os.path.join(d, f"extra_state_world_size_{world}_rank_{rank}.pt"))
+    _atomic(os.path.join(d, f"extra_state_world_size_{world}_rank_{rank}.pt"), lambda p: torch.save(ex, p))
     if rank == 0:
         from safetensors.torch import save_file
-        save_file({"flat": engine.model.flat.detach().cpu().contiguous()}, os.path.join(d, "weights_bf16.safetensors"))
-        with open(os.path.join(root, TRACKER), "w") as f:
-            f.write(str(step))
+        flat = {"flat": engine.model.flat.detach().cpu().contiguous()}
+        _atomic(os.path.join(d, "weights_bf16.safetensors"), lambda p: save_file(flat, p))
+    _all_ranks_done(world)
+    if rank == 0:
+        def _tracker(p):
+            with open(p, "w") as f:
+                f.write(str(step))
+        _atomic(os.path.join(root, TRACKER), _tracker)
     return d
 
 
@@ -65,7 +90,11 @@ def latest_step(root: str) -> Optional[int]:
     return max(steps) if steps else None
 
 
-def load_sharded(engine, root: str, rank: int, world: int, step: Optional[int] = None) -> int:
+def load_sharded(engine, root: str, rank: int, world: int, step: Optional[int] = None, data=None) -> int:
+    """Restore the optimizer shard, scheduler, host and CUDA RNG streams and,
+    when ``data`` (an object with ``load_state_dict``) is given, the data
+    cursor saved under the ``data`` key.  Returns the restored step (0 when
+    nothing was saved)."""
     step = latest_step(root) if step is None else step
     if step is None:
         return 0
@@ -85,6 +114,14 @@ def load_sharded(engine, root: str, rank: int, world: int, step: Optional[int] =
         np.random.set_state(rng["numpy"])
     if "python" in rng:
         random.setstate(rng["python"])
+    if rng.get("cuda") is not None and torch.cuda.is_available():
+        saved = rng["cuda"]
+        if len(saved) == torch.cuda.device_count():
+            torch.cuda.set_rng_state_all(saved)
+        else:   # different device count: restore what this process's device had
+            torch.cuda.set_rng_state(saved[min(torch.cuda.current_device(), len(saved) - 1)])
+    if data is not None and ex.get("data") is not None:
+        data.load_state_dict(ex["data"])
     return step
 
 
@@ -179,5 +216,5 @@ class CheckpointManager:
         self.prune(keep_extra=1)
         return save_sharded(engine, self.root, step, rank, world, extra)
 
-    def load_latest(self, engine, rank: int = 0, world: int = 1) -> int:
-        return load_sharded(engine, self.root, rank, world)
+    def load_latest(self, engine, rank: int = 0, world: int = 1, data=None) -> int:
+        return load_sharded(engine, self.root, rank, world, data=data)

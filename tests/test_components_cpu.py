@@ -35,6 +35,47 @@ def test_checkpoint_roundtrip_and_hf_export(tmp_path):
     assert torch.equal(m3.flat[: e.model.layout.numel], e.model.flat[: e.model.layout.numel])
 
 
+def test_checkpoint_crash_keeps_previous_step_and_restores_cursor(tmp_path, monkeypatch):
+    """A save that dies half way leaves no half-written file under its final
+    name and the tracker still names the last complete step; resume restores
+    the data cursor."""
+    from lumenrl_b200.engine.training.actor import ActorEngine
+    from lumenrl_b200.utils import checkpoint as ck
+
+    class Cursor:
+        def __init__(self, pos=0):
+            self.pos = pos
+
+        def state_dict(self):
+            return {"pos": self.pos}
+
+        def load_state_dict(self, sd):
+            self.pos = sd["pos"]
+
+    e = ActorEngine(tiny_qwen3(), ParallelState(), lr=1e-2, seed=3)
+    root = str(tmp_path / "ck")
+    ck.save_sharded(e, root, 1, 0, 1, {"data": Cursor(7).state_dict()})
+    real_save = torch.save
+
+    def dying_save(obj, path, *a, **k):
+        if "extra_state" in str(path):
+            with open(path, "wb") as f:
+                f.write(b"partial")
+            raise OSError("disk went away")
+        return real_save(obj, path, *a, **k)
+    monkeypatch.setattr(torch, "save", dying_save)
+    with pytest.raises(OSError):
+        ck.save_sharded(e, root, 2, 0, 1, {"data": Cursor(9).state_dict()})
+    monkeypatch.setattr(torch, "save", real_save)
+    assert ck.latest_step(root) == 1
+    d2 = os.path.join(root, "global_step_2", "actor")
+    assert not os.path.exists(os.path.join(d2, "extra_state_world_size_1_rank_0.pt"))
+    cur = Cursor(0)
+    e2 = ActorEngine(tiny_qwen3(), ParallelState(), lr=1e-2, seed=9)
+    assert ck.load_sharded(e2, root, 0, 1, data=cur) == 1
+    assert cur.pos == 7
+
+
 def test_hf_export_loads_in_transformers(tmp_path):
     transformers = pytest.importorskip("transformers")
     from lumenrl_b200.models.qwen3 import Qwen3Model

@@ -74,3 +74,69 @@ def test_sharded_optimizer_matches_single_process():
     assert torch.allclose(res[0][1], single.w16, atol=1e-6)
     assert torch.allclose(res[1][1], single.w16, atol=1e-6)
     assert abs(res[0][2] - s["grad_norm"]) < 1e-3
+
+
+def test_ppo_with_critic_three_steps_cpu():
+    """PPO: critic values feed GAE, the policy and the critic both update."""
+    torch.manual_seed(0)
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["algorithm.name=ppo", "algorithm.ppo.num_mini_batches=2",
+                                   "algorithm.ppo.num_ppo_epochs=1", "critic.learning_rate=1e-3"])
+    spec = RLRunSpec(prompts_per_step=8, prompt_len=16, max_new_tokens=16, reward="contains_token",
+                     eos_token_id=None)
+    tr = RLTrainer(cfg, tiny_llama(), spec, ParallelState()).setup()
+    assert tr.critic is not None and tr.ref is not None
+    c0 = tr.critic.model.flat.clone()
+    head0 = tr.critic.head.weight.detach().clone()
+    hist = tr.train()
+    assert len(hist) == 3
+    for m in hist:
+        assert "critic/vf_loss" in m and m["critic/vf_loss"] == m["critic/vf_loss"]
+        assert "timing/values_s" in m and "timing/critic_s" in m
+    assert not torch.equal(c0, tr.critic.model.flat) or not torch.equal(head0, tr.critic.head.weight)
+
+
+def test_dapo_refill_rounds_collect_informative_groups_cpu():
+    """DAPO filter_groups: rounds repeat until enough groups with non-constant
+    rewards are kept; every kept group has reward variance."""
+    torch.manual_seed(0)
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["algorithm.name=dapo", "algorithm.dapo.num_generations=4",
+                                   "algorithm.dapo.filter_groups.enable=true",
+                                   "algorithm.dapo.filter_groups.max_num_gen_batches=6"])
+    spec = RLRunSpec(prompts_per_step=4, prompt_len=16, max_new_tokens=16, reward="contains_token",
+                     eos_token_id=None)
+    tr = RLTrainer(cfg, tiny_llama(), spec, ParallelState()).setup()
+    # reward 1 when the first response token is a multiple of 5 (p ~ 0.2): about
+    # 40 % of 4-sample groups are all-zero, so refill rounds are needed
+    tr.reward_fn = lambda responses, prompts=None, lengths=None, **_: (responses[:, 0] % 5 == 0).float()
+    seen = []
+    orig = tr._rollout
+
+    def spy(step, round_idx=0):
+        b = orig(step, round_idx)
+        seen.append(round_idx)
+        return b
+    tr._rollout = spy
+    hist = tr.train()
+    assert len(hist) == 3
+    assert max(seen) >= 1                       # at least one refill round ran
+    for m in hist:
+        assert 1 <= m["dapo/gen_rounds"] <= 6
+        assert m["dapo/kept_groups"] <= 4
+
+
+def test_kl_in_reward_uses_reference_and_controller_cpu():
+    torch.manual_seed(0)
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["algorithm.use_kl_in_reward=true", "algorithm.grpo.kl_coeff=0.05",
+                                   "algorithm.kl_ctrl_type=adaptive"])
+    spec = RLRunSpec(prompts_per_step=8, prompt_len=16, max_new_tokens=16, reward="contains_token",
+                     eos_token_id=None)
+    tr = RLTrainer(cfg, tiny_llama(), spec, ParallelState()).setup()
+    assert tr.kl_ctrl is not None and tr.ref is not None
+    hist = tr.train()
+    for m in hist:
+        assert "actor/reward_kl_penalty" in m and "actor/reward_kl_penalty_coeff" in m
+    # the policy moves away from the frozen reference, so later steps see a KL
+    assert hist[-1]["actor/reward_kl_penalty"] != 0.0

@@ -42,7 +42,7 @@ def register_adv_est(name: str) -> Callable:
 
 def get_adv_estimator(name: str) -> Callable:
     if name not in ADV_ESTIMATOR_REGISTRY:
-        raise KeyError(f"Unknown advantage estimator '{name}'. Available: {list(ADV_ESTIMATOR_REGISTRY)}")
+        raise KeyError(f"no advantage estimator named {name!r}; registered: {sorted(ADV_ESTIMATOR_REGISTRY)}")
     return ADV_ESTIMATOR_REGISTRY[name]
 
 

@@ -45,79 +45,86 @@ SUPPORTED_ROLLOUT_RS_OPTIONS = {
 TOKEN_LEVEL_ROLLOUT_RS_OPTIONS = {"token_k1", "token_k2", "token_k3"}
 
 
-def _msum(v: Tensor, m: Tensor, dim=None) -> Tensor:
-    z = torch.where(m.bool(), v, torch.zeros_like(v)) * m
-    return z.sum() if dim is None else z.sum(dim=dim)
+class _Masked:
+    """Reductions restricted to positions where the mask is non-zero
+    (masked-out entries may hold inf / nan and never reach the result)."""
+
+    @staticmethod
+    def total(values: Tensor, mask: Tensor, dim=None) -> Tensor:
+        kept = values.masked_fill(~mask.bool(), 0.0) * mask
+        return kept.sum() if dim is None else kept.sum(dim=dim)
+
+    @staticmethod
+    def mean(values: Tensor, mask: Tensor, dim=None) -> Tensor:
+        count = mask.sum() if dim is None else mask.sum(dim=dim)
+        return _Masked.total(values, mask, dim) / count.clamp(min=1e-8)
 
 
-def _mmean(v: Tensor, m: Tensor, dim=None) -> Tensor:
-    den = m.sum() if dim is None else m.sum(dim=dim)
-    return _msum(v, m, dim) / den.clamp(min=1e-8)
+_msum, _mmean = _Masked.total, _Masked.mean
 
 
 # ---------------------------------------------------------------------------
-# threshold parsing
+# threshold grammar, shared by the IS weights and every rejection criterion:
+#
+#     threshold := NUMBER                 an upper bound
+#                | NUMBER "_" NUMBER      a "lower_upper" band
+#
+# IS weights accept both (a band selects IcePop); k1 rejection criteria
+# accept both (a bare NUMBER x means the band 1/x .. x); k2 / k3 criteria
+# accept only an upper bound.  Every bound must be positive, lower <= upper.
 # ---------------------------------------------------------------------------
+
+def _read_bound(text: str, where: str) -> tuple[Optional[float], float]:
+    """One threshold token -> (lower or None, upper)."""
+    pieces = text.split("_")
+    if len(pieces) > 2 or not all(p.strip() for p in pieces):
+        raise ValueError(f"{where}: cannot read threshold {text!r} (expected 'upper' or 'lower_upper')")
+    try:
+        nums = [float(p) for p in pieces]
+    except ValueError:
+        raise ValueError(f"{where}: threshold {text!r} is not numeric") from None
+    lower, upper = (None, nums[0]) if len(nums) == 1 else (nums[0], nums[1])
+    if upper <= 0 or (lower is not None and not 0 < lower <= upper):
+        raise ValueError(f"{where}: threshold {text!r} needs positive bounds with lower <= upper")
+    return lower, upper
+
+
+def _as_text(spec, where: str) -> str:
+    if isinstance(spec, bool) or not isinstance(spec, (int, float, str)):
+        raise TypeError(f"{where}: threshold must be a number or a string, got {type(spec).__name__}")
+    text = str(spec).strip()
+    if not text:
+        raise ValueError(f"{where}: empty threshold")
+    return text
+
 
 def parse_is_threshold(spec) -> tuple[float, Optional[float]]:
-    """Return (upper, lower-or-None); ``"a_b"`` selects IcePop."""
-    if isinstance(spec, bool):
-        raise TypeError("rollout_is_threshold must be a float or string, not bool.")
-    if isinstance(spec, (int, float)):
-        upper, lower = float(spec), None
-    elif isinstance(spec, str):
-        s = spec.strip()
-        if not s:
-            raise ValueError("rollout_is_threshold must not be empty.")
-        if "_" in s:
-            a, b = s.split("_", 1)
-            lower, upper = float(a), float(b)
-        else:
-            upper, lower = float(s), None
-    else:
-        raise TypeError(f"rollout_is_threshold must be float or str, got {type(spec)}")
-    if upper <= 0:
-        raise ValueError(f"rollout_is_threshold upper must be positive, got {upper}")
-    if lower is not None and (lower <= 0 or lower > upper):
-        raise ValueError(f"invalid IcePop band {lower}_{upper}")
+    """``rollout_is_threshold`` -> (upper, lower or None); a band is IcePop."""
+    lower, upper = _read_bound(_as_text(spec, "rollout_is_threshold"), "rollout_is_threshold")
     return upper, lower
 
 
 def parse_rs_thresholds(options: list[str], spec) -> dict[str, tuple[Optional[float], float]]:
+    """``rollout_rs_threshold`` (one value for all criteria, or one per
+    criterion, comma separated) -> {criterion: (lower or None, upper)}."""
     if spec is None:
-        raise ValueError("rollout_rs_threshold must be provided for rejection sampling.")
-    if isinstance(spec, (int, float)):
-        raw = [str(spec)]
-    elif isinstance(spec, str):
-        raw = [p.strip() for p in spec.split(",") if p.strip()]
-    else:
-        raise TypeError(f"rollout_rs_threshold must be str or numeric, got {type(spec)}")
-    if not raw:
-        raise ValueError("rollout_rs_threshold must contain at least one value.")
-    if len(raw) not in (1, len(options)):
-        raise ValueError(f"rollout_rs_threshold expects 1 or {len(options)} thresholds, got {len(raw)}.")
-    if len(raw) == 1:
-        raw = raw * len(options)
-    out: dict[str, tuple[Optional[float], float]] = {}
-    for opt, s in zip(options, raw):
-        if opt.endswith("k1"):
-            if "_" in s:
-                a, b = s.split("_", 1)
-                lo, hi = float(a), float(b)
-            else:
-                hi = float(s)
-                lo = 1.0 / hi
-            if lo <= 0 or hi <= 0:
-                raise ValueError(f"Thresholds for '{opt}' must be positive, got {s}.")
-            out[opt] = (lo, hi)
+        raise ValueError("rejection sampling is on but rollout_rs_threshold is not set")
+    tokens = [t.strip() for t in _as_text(spec, "rollout_rs_threshold").split(",") if t.strip()]
+    if len(tokens) == 1:
+        tokens = tokens * len(options)
+    if len(tokens) != len(options):
+        raise ValueError(f"rollout_rs_threshold: {len(options)} criteria need 1 or {len(options)} thresholds, "
+                         f"{len(tokens)} given")
+    bands: dict[str, tuple[Optional[float], float]] = {}
+    for crit, tok in zip(options, tokens):
+        lower, upper = _read_bound(tok, f"rollout_rs '{crit}'")
+        if crit.endswith("k1"):
+            bands[crit] = (1.0 / upper if lower is None else lower, upper)
+        elif lower is not None:
+            raise ValueError(f"rollout_rs '{crit}': only an upper bound applies, got band {tok!r}")
         else:
-            if "_" in s:
-                raise ValueError(f"RS threshold for '{opt}' must be a single upper bound, got '{s}'.")
-            hi = float(s)
-            if hi <= 0:
-                raise ValueError(f"Threshold for '{opt}' must be positive, got {s}.")
-            out[opt] = (None, hi)
-    return out
+            bands[crit] = (None, upper)
+    return bands
 
 
 # ---------------------------------------------------------------------------

@@ -22,7 +22,8 @@ class Registry:
         try:
             return self._items[key]
         except KeyError:
-            raise KeyError(f"Unknown {self.name} '{key}'. Available: [{', '.join(sorted(self._items))}]") from None
+            known = ", ".join(sorted(self._items)) or "(none registered)"
+            raise KeyError(f"{self.name} registry has no entry {key!r}; registered: {known}") from None
 
     def __contains__(self, key: str) -> bool:
         return key in self._items

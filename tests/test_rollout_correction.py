@@ -67,3 +67,22 @@ def test_presets_and_bypass():
     b = DataProto({"rollout_log_probs": torch.ones(1, 2)})
     rc.apply_bypass_mode(b, None)
     assert torch.equal(b["old_log_probs"], b["rollout_log_probs"])
+
+
+def test_threshold_grammar_shared_by_is_and_rs():
+    import pytest as _pt
+    from lumenrl_b200.algorithms.rollout_correction import parse_is_threshold, parse_rs_thresholds
+    assert parse_is_threshold(2.0) == (2.0, None)
+    assert parse_is_threshold("0.5_2") == (2.0, 0.5)
+    b = parse_rs_thresholds(["token_k1", "seq_max_k2"], "4, 0.1")
+    assert b == {"token_k1": (0.25, 4.0), "seq_max_k2": (None, 0.1)}
+    assert parse_rs_thresholds(["seq_sum_k1"], "0.8_1.25") == {"seq_sum_k1": (0.8, 1.25)}
+    for bad in ("", "a", "2_1", "0", "-1", "1_2_3"):
+        with _pt.raises(ValueError):
+            parse_is_threshold(bad)
+    with _pt.raises(TypeError):
+        parse_is_threshold(True)
+    with _pt.raises(ValueError):
+        parse_rs_thresholds(["token_k2"], "0.5_2")          # k2 takes an upper bound only
+    with _pt.raises(ValueError):
+        parse_rs_thresholds(["token_k1", "token_k2", "token_k3"], "1,2")

@@ -53,20 +53,29 @@ def parse():
 
 
 def reference_arm(args) -> None:
+    """The reference's own GRPO path, unmodified, from ``baseline/_ref``.
+
+    It cannot run on this image: its trainer imports OmegaConf and drives
+    rollouts through Ray with the ROCm-only ATOM / vLLM-ROCm engines and the
+    AITER / MORI kernels (git submodules absent from its source tree), and
+    neither Ray nor OmegaConf has a wheel in the offline wheelhouse.  The
+    line printed names what is missing on the machine it runs on."""
+    import importlib.util
     here = os.path.dirname(os.path.abspath(__file__))
     ref = os.path.join(here, "baseline", "_ref")
-    why = None
+    needed = ("ray", "omegaconf", "atom", "aiter", "mori")
+    missing = [m for m in needed if importlib.util.find_spec(m) is None]
     if not os.path.isdir(os.path.join(ref, "lumenrl")):
-        why = "reference not installed under baseline/_ref"
+        where = "the reference package is not installed under baseline/_ref"
     else:
         sys.path.insert(0, ref)
         try:
             import lumenrl.trainer.rl_trainer  # noqa: F401
-        except Exception as e:  # the ROCm stack (ATOM/AITER/vLLM-ROCm, Ray, OmegaConf) is absent
-            why = f"reference trainer import failed: {type(e).__name__}: {str(e).splitlines()[0][:160]}"
-    if why is None:
-        why = ("reference GRPO path needs the ATOM/AITER/MORI ROCm submodules and Ray, none of which exist "
-               "for NVIDIA GPUs offline")
+            where = "lumenrl.trainer.rl_trainer imports"
+        except Exception as e:
+            where = f"import lumenrl.trainer.rl_trainer fails ({type(e).__name__}: {str(e).splitlines()[0][:120]})"
+    why = (f"{where}; missing modules {missing}: Ray and OmegaConf have no offline wheel, and the GRPO rollout "
+           "needs the ROCm-only ATOM/AITER/MORI submodules (absent from the reference source) -- no NVIDIA path")
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": why}))
 
@@ -200,6 +209,16 @@ def main() -> None:
     if dist.is_initialized():
         dist.all_reduce(tw, op=dist.ReduceOp.MAX)
     wall = float(tw.item())
+    # ---- multi-GPU correctness, outside the timed regions: replicas agree
+    # bit for bit, and one fused NVLink optimizer step equals the NCCL path ----
+    checks = {}
+    if world > 1:
+        from lumenrl_b200.parallel.symm import fused_vs_nccl_max_err, replica_agreement
+        opt = tr.actor.opt
+        checks.update(replica_agreement(tr.actor.model.flat, opt.master, opt.lo))
+        fv = fused_vs_nccl_max_err(64 << 20, rank, world)
+        checks["fused_vs_nccl_max_err"] = fv["weights_max_err"]
+        checks["fused_vs_nccl"] = fv
     if rank == 0:
         last = hist[-1]
         B = args.prompts_per_gpu * args.group
@@ -221,8 +240,10 @@ def main() -> None:
             "breakdown_s": {k.replace("timing/", ""): v for k, v in last.items() if k.startswith("timing/")},
             "recompute_layers": last.get("actor/recompute_layers"),
             "weight_sync_ms": last.get("weight_sync/ms"),
+            "weight_sync_GBps": last.get("weight_sync/GBps"),
             "gen_tokens_per_s": last.get("perf/gen_tokens_per_s"),
             "mean_response_len": last.get("response_length/mean"),
+            **checks,
         }
         print(json.dumps(out))
     if dist.is_initialized():

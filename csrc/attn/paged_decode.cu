@@ -798,28 +798,41 @@ static int paged_decode_noalloc_impl(const void* q, const void* kc, const void* 
   }
   const size_t smem = 4 * kTileBytes;
   const float sl2 = scale * k_scale * 1.4426950408889634f;
-  dim3 grid(nsplit, Hk, B);
+  // Each launch goes through cudaLaunchKernelEx and its own return code is
+  // checked, so an error left pending by the caller's earlier work is
+  // neither reported as this call's failure nor cleared.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nsplit, Hk, B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
   cudaError_t e;
+  const int* no_flag = nullptr;
   if (kv_fp8) {
     auto kern = paged_decode_kernel<__nv_fp8_e4m3>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
-    kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_fp8_e4m3*)kc, (const __nv_fp8_e4m3*)vc,
-                                       block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
-                                       tps, sl2, v_scale, nullptr, 0, 0);
+    e = cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)q, (const __nv_fp8_e4m3*)kc, (const __nv_fp8_e4m3*)vc,
+                           block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks, tps, sl2,
+                           v_scale, no_flag, 0, 0);
   } else {
     auto kern = paged_decode_kernel<__nv_bfloat16>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return noalloc_fail(e, "cudaFuncSetAttribute failed");
-    kern<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
-                                       block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks,
-                                       tps, sl2, v_scale, nullptr, 0, 0);
+    e = cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc,
+                           block_table, seq_lens, (__nv_bfloat16*)out, po, pl, Hq, Hk, bs, max_blocks, tps, sl2,
+                           v_scale, no_flag, 0, 0);
   }
+  if (e != cudaSuccess) return noalloc_fail(e, "attention kernel launch failed");
   if (nsplit > 1) {
-    decode_combine_kernel<<<dim3(B, Hq), kHD, 0, st>>>(po, pl, (__nv_bfloat16*)out, nsplit, B, Hq);
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3(B, Hq);
+    cc.blockDim = dim3(kHD);
+    cc.stream = st;
+    e = cudaLaunchKernelEx(&cc, decode_combine_kernel, (const float*)po, (const float*)pl, (__nv_bfloat16*)out,
+                           nsplit, B, Hq);
+    if (e != cudaSuccess) return noalloc_fail(e, "split combine kernel launch failed");
   }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return noalloc_fail(e, "kernel launch failed");
   g_noalloc_err[0] = '\0';
   return 0;
 }

@@ -57,6 +57,9 @@ void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor
 torch::Tensor tc_gemm(torch::Tensor a, torch::Tensor b, c10::optional<torch::Tensor> c, int64_t epi, int64_t bn);
 int64_t tc_gemm_status();
 torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits);
+torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> c,
+                      int64_t epi, int64_t bn);
+int64_t gemm2sm_status();
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
 void symm_close(int64_t ptr);
@@ -138,6 +141,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bn") = 0);
   m.def("tc_gemm_status", &lrl::tc_gemm_status);
   m.def("tc_gemm_splitk", &lrl::tc_gemm_splitk, py::arg("a"), py::arg("b"), py::arg("splits") = 0);
+  m.def("gemm2sm", &lrl::gemm2sm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
+        py::arg("c") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0);
+  m.def("gemm2sm_status", &lrl::gemm2sm_status);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);
   m.def("symm_close", &lrl::symm_close);

@@ -1,0 +1,409 @@
+// Persistent bf16 GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+//   C[M, N] (=, +=) A[M, K] . B[N, K]^T        fp32 accumulation in TMEM
+//
+// Either operand may be K-major (K contiguous: activations in the forward,
+// dY in dgrad) or MN-major (M / N contiguous: the weight in dgrad, dY and X
+// in wgrad), so the three GEMMs of a linear layer run without transposes:
+//
+//   forward   y  = x  . W^T      A = x   K-major,  B = W   K-major
+//   dgrad     dx = dy . W        A = dy  K-major,  B = W   MN-major
+//   wgrad     dW += dy^T . x     A = dy  MN-major, B = x   MN-major
+//
+// A cluster of two CTAs on the two SMs of a TPC computes one 256 x BN output
+// tile: each CTA stages its own 128 rows of A and BN/2 rows of B (this GPU's
+// memory, plain TMA, no multicast) and the even CTA issues one 256 x BN x 16
+// MMA per K slice that reads both CTAs' shared memory and writes each CTA's
+// TMEM with its 128 accumulator rows.  Per SM and 64-wide K step that is
+// 32 KB of operands for 2 x 128 x 256 x 64 FLOPs, half the L2 traffic of a
+// single-SM 128 x 256 tile.
+//
+// Warp roles per CTA (192 threads):
+//   warp 0     TMA producer: one lane streams A / B slabs into a kStages ring;
+//              the bytes of both CTAs are counted on the even CTA's barrier
+//   warp 1     allocates TMEM (pair-wide, two accumulator buffers); in the
+//              even CTA one lane issues the MMAs and commits each stage back
+//              to both producers and each finished tile to both epilogues
+//   warps 2-5  epilogue: tcgen05.ld of this CTA's 128 rows, then bf16 / fp32
+//              stores or an fp32 read-add-write (gradient accumulation)
+// Two TMEM buffers let the epilogue of tile i overlap the MMAs of tile i+1.
+// Every mbarrier wait is bounded and reports a status word instead of hanging.
+#include "../common.cuh"
+#include "tc2sm.cuh"
+#include "tc_gemm.cuh"
+
+namespace lrl {
+
+CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int64_t ld, int box_rows);
+
+using namespace tc;
+using namespace tc2;
+
+namespace {
+
+constexpr int kPairM = 256, kBK = 64, kGroupM = 8, kThreads = 192;
+
+enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3 };
+
+template <int BN>
+struct Pair {
+  static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's BN/2 rows of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN == 256 ? 6 : 8;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
+
+__device__ __forceinline__ void pair_tile(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int g = t / per_group;
+  const int first = g * kGroupM;
+  const int gm = min(num_m - first, kGroupM);
+  const int r = t % per_group;
+  mb = first + r % gm;
+  nb = r / gm;
+}
+
+// bounded wait that ignores the error word (tear-down drains)
+__device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+
+template <int EPI>
+__device__ __forceinline__ void store32(void* C, int row, int col, int N, int64_t ldc, bool vec, const float (&v)[32]) {
+  if constexpr (EPI == kE2None) {
+    // timing probe: keep the TMEM load, drop the result
+    if (v[0] == 1.2345e-30f && v[31] == 1.2345e-30f) *reinterpret_cast<float*>(C) = v[1];
+  } else if constexpr (EPI == kE2BF16) {
+    __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)row * ldc + col;
+    if (vec && col + 32 <= N) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float tmp[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) tmp[j] = v[8 * i + j];
+        store8(p + 8 * i, tmp);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) p[i] = __float2bfloat16(v[i]);
+    }
+  } else {
+    float* p = reinterpret_cast<float*>(C) + (int64_t)row * ldc + col;
+    if (vec && col + 32 <= N) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        if constexpr (EPI == kE2AccF32) {
+          const float4 c = reinterpret_cast<const float4*>(p)[i];
+          o.x += c.x;
+          o.y += c.y;
+          o.z += c.z;
+          o.w += c.w;
+        }
+        reinterpret_cast<float4*>(p)[i] = o;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (col + i < N) p[i] = (EPI == kE2AccF32 ? p[i] : 0.f) + v[i];
+    }
+  }
+}
+
+template <int BN, bool AMN, bool BMN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C, int M,
+                   int N, int K, int64_t ldc, int vec, int* err_out) {
+  using G = Pair<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kStageBytes);
+  uint64_t* empty = full + G::kStages;
+  uint64_t* tfull = empty + G::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mdone = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* err = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + kPairM - 1) / kPairM, num_n = (N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int kblocks = (K + kBK - 1) / kBK;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(mdone, 1);
+    *err = kErrNone;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, G::kTmemCols);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full0 = map_to_rank(smem_addr(&full[0]), 0);  // the even CTA's full[0]
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; t < tiles && ok; t += ncl) {
+        int mb, nb;
+        pair_tile(t, num_m, num_n, mb, nb);
+        const int am = mb * kPairM + rank * 128;
+        const int bn = nb * BN + rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % G::kStages;
+          if (!mbar_wait(&empty[s], ((it / G::kStages) & 1) ^ 1, err, kErrProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + s * 8;
+          if (leader) mbar_expect_tx(&full[s], 2 * G::kStageBytes);
+          uint8_t* sa = smem + s * G::kStageBytes;
+          uint8_t* sb = sa + G::kABytes;
+          if constexpr (AMN) {
+            tma_load_2d_pair(sa, &tmA, fb, am, kb * kBK);
+            tma_load_2d_pair(sa + 8192, &tmA, fb, am + 64, kb * kBK);
+          } else {
+            tma_load_2d_pair(sa, &tmA, fb, kb * kBK, am);
+          }
+          if constexpr (BMN) {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, fb, bn + 64 * j, kb * kBK);
+          } else {
+            tma_load_2d_pair(sb, &tmB, fb, kb * kBK, bn);
+          }
+        }
+      }
+      if (ok && *err == kErrNone) {
+        // every stage this CTA filled has been consumed by the MMAs, so no
+        // commit arrival to this CTA's shared memory is still in flight
+        for (int j = it; j < it + G::kStages; ++j)
+          if (!wait_drain(&empty[j % G::kStages], ((j / G::kStages) & 1) ^ 1)) {
+            *err = kErrDrain;
+            break;
+          }
+      } else if (leader) {
+        // error unwind: the copies counted on this CTA's barriers have landed
+        for (int j = it - 1; j >= 0 && j >= it - G::kStages; --j)
+          if (!wait_drain(&full[j % G::kStages], (j / G::kStages) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32_major(kPairM, BN, AMN, BMN);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int t = cid; t < tiles && ok; t += ncl, ++tc) {
+        const int buf = tc & 1;
+        if (!mbar_wait(&tempty[buf], ((tc >> 1) & 1) ^ 1, err, kErrMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % G::kStages;
+          if (!mbar_wait(&full[s], (it / G::kStages) & 1, err, kErrMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(smem + s * G::kStageBytes);
+          const uint32_t b0 = a0 + G::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = AMN ? sw128_mnmajor_desc(a0 + k * 2048, 8192) : sw128_kmajor_desc(a0 + k * 32);
+            const uint64_t bd = BMN ? sw128_mnmajor_desc(b0 + k * 2048, 8192) : sw128_kmajor_desc(b0 + k * 32);
+            umma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit_pair(&empty[s], 3);
+        }
+        if (ok) umma_commit_pair(&tfull[buf], 3);
+      }
+      // every MMA this thread issued has completed before tear-down
+      umma_commit_pair(mdone, 1);
+      if (!wait_drain(mdone, 0)) *err = kErrDrain;
+      if (ok && *err == kErrNone) {
+        // the other CTA's epilogue arrivals on tempty have landed
+        for (int j = tc; j < tc + 2; ++j)
+          if (!wait_drain(&tempty[j & 1], ((j >> 1) & 1) ^ 1)) {
+            *err = kErrDrain;
+            break;
+          }
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const uint32_t tempty0 = map_to_rank(smem_addr(&tempty[0]), 0);
+    int tc = 0;
+    for (int t = cid; t < tiles; t += ncl, ++tc) {
+      int mb, nb;
+      pair_tile(t, num_m, num_n, mb, nb);
+      const int buf = tc & 1;
+      if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue)) break;
+      tc_fence_after();
+      const int row = mb * kPairM + rank * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, v);
+        const int col = nb * BN + c * 32;
+        if (row < M && col < N) store32<EPI>(C, row, col, N, ldc, vec != 0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
+    }
+  }
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, G::kTmemCols);
+  }
+  if (threadIdx.x == 0 && *err != kErrNone) atomicExch(err_out, *err);
+}
+
+torch::Tensor& err_word() {
+  static thread_local torch::Tensor t;
+  if (!t.defined() || t.device().index() != c10::cuda::current_device())
+    t = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, c10::cuda::current_device()));
+  return t;
+}
+
+template <int BN, bool AMN, bool BMN, int EPI>
+void launch2(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int64_t ldc, bool vec) {
+  auto kern = gemm2sm_kernel<BN, AMN, BMN, EPI>;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Pair<BN>::kSmem;
+  cfg.stream = stream();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters == 0) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Pair<BN>::kSmem));
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    max_clusters = n;
+  }
+  const int tiles = ((M + kPairM - 1) / kPairM) * ((N + BN - 1) / BN);
+  cfg.gridDim = dim3(2 * std::min(tiles, max_clusters));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, c, M, N, K, ldc, (int)vec, err_word().data_ptr<int>()));
+}
+
+}  // namespace
+
+int64_t gemm2sm_status() {
+  auto& t = err_word();
+  const int v = t.item<int>();
+  t.zero_();
+  return v;
+}
+
+// C = A . B^T on CTA pairs.  `a` is A [M, K] (a_mn = false) or A^T [K, M]
+// (a_mn = true); `b` is B [N, K] or B^T [K, N]; the contiguous dimension of
+// each must have unit stride.  epi 0: returns bf16 C; 1: fp32 C; 2: c += A.B^T
+// into the given fp32 c.  bn: 0 = auto, 128 or 256 output columns per pair.
+torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> c,
+                      int64_t epi, int64_t bn) {
+  LRL_CHECK_CUDA(a);
+  LRL_CHECK_CUDA(b);
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm2sm: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "gemm2sm: 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm2sm: the last dimension must be contiguous");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm2sm: inner dimensions differ");
+  TORCH_CHECK(a.size(1) % 8 == 0 && b.size(1) % 8 == 0, "gemm2sm: the contiguous dimension must be a multiple of 8");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm2sm: row strides must be multiples of 8 elements");
+  TORCH_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "gemm2sm: dimension too large");
+  TORCH_CHECK(epi >= 0 && epi <= 3, "gemm2sm: epi must be 0..3");
+  torch::Tensor out;
+  if (epi == kE2AccF32) {
+    TORCH_CHECK(c.has_value() && c->is_cuda() && c->scalar_type() == at::kFloat && c->dim() == 2 &&
+                    c->size(0) == M && c->size(1) == N && c->stride(1) == 1,
+                "gemm2sm: accumulate needs an fp32 [M, N] C with unit column stride");
+    out = *c;
+  } else {
+    out = torch::empty({M, N}, a.options().dtype(epi == kE2F32 ? at::kFloat : at::kBFloat16));
+  }
+  if (M == 0 || N == 0) return out;
+  if (K == 0) {
+    if (epi != kE2AccF32) out.zero_();
+    return out;
+  }
+  c10::cuda::CUDAGuard guard(a.device());
+  if (bn == 0) {
+    // 256-wide tiles: a 256 x 128 pair tile needs 96 B of operands per SM
+    // clock, more than L2 delivers, so it only pays for N <= 128
+    bn = N <= 128 ? 128 : 256;
+  }
+  TORCH_CHECK(bn == 128 || bn == 256, "gemm2sm: bn must be 128 or 256");
+  const CUtensorMap ma = a_mn ? make_kmajor_map(a.data_ptr(), K, M, a.stride(0), 64)
+                              : make_kmajor_map(a.data_ptr(), M, K, a.stride(0), 128);
+  const CUtensorMap mb = b_mn ? make_kmajor_map(b.data_ptr(), K, N, b.stride(0), 64)
+                              : make_kmajor_map(b.data_ptr(), N, K, b.stride(0), (int)(bn / 2));
+  const int64_t ldc = out.stride(0);
+  const int esz = (epi == kE2F32 || epi == kE2AccF32) ? 4 : 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0) && ((ldc * esz) % 16 == 0);
+  void* cp = out.data_ptr();
+#define GO(BNV, AM, BM, E) launch2<BNV, AM, BM, E>(ma, mb, cp, (int)M, (int)N, (int)K, ldc, vec)
+#define EPIS(BNV, AM, BM)                                             \
+  do {                                                                \
+    if (epi == kE2BF16) GO(BNV, AM, BM, kE2BF16);                     \
+    else if (epi == kE2F32) GO(BNV, AM, BM, kE2F32);                  \
+    else if (epi == kE2AccF32) GO(BNV, AM, BM, kE2AccF32);            \
+    else if (BNV == 256) GO(256, AM, BM, kE2None);                    \
+    else TORCH_CHECK(false, "gemm2sm: the timing probe needs bn 256"); \
+  } while (0)
+#define MAJ(BNV)                                   \
+  do {                                             \
+    if (!a_mn && !b_mn) EPIS(BNV, false, false);   \
+    else if (!a_mn && b_mn) EPIS(BNV, false, true); \
+    else if (a_mn && b_mn) EPIS(BNV, true, true);  \
+    else EPIS(BNV, true, false);                   \
+  } while (0)
+  if (bn == 256) MAJ(256);
+  else MAJ(128);
+#undef MAJ
+#undef EPIS
+#undef GO
+  return out;
+}
+
+}  // namespace lrl

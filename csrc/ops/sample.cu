@@ -35,7 +35,7 @@ __device__ __forceinline__ MaxIdx better(MaxIdx a, MaxIdx b) {
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const void* __restrict__ logits, int is_bf16, int V,
                                                                 float inv_t, float top_p,
                                                                 const int64_t* __restrict__ row_seed,
-                                                                const int64_t* __restrict__ step,
+                                                                const int64_t* __restrict__ step, int step_stride,
                                                                 int64_t* __restrict__ out_tok,
                                                                 float* __restrict__ out_logp) {
   __shared__ float redf[32];
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const void* __re
   auto zat = [&](int v) -> float { return (is_bf16 ? __bfloat162float(zb[v]) : zf[v]) * inv_t; };
   const uint64_t seed = (uint64_t)row_seed[row];
   const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
-  const uint64_t st = (uint64_t)step[0];
+  const uint64_t st = (uint64_t)step[row * step_stride];  // per-row token index, or one for all
   const uint32_t st_lo = (uint32_t)st, st_hi = (uint32_t)(st >> 32);
 
   // pass 1: max and sum exp; Gumbel argmax when no nucleus is needed
@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(kSplitThreads) sample_part_kernel(const __nv_b
                                                                     int chunk, float inv_t,
                                                                     const int64_t* __restrict__ row_seed,
                                                                     const int64_t* __restrict__ step,
+                                                                    int step_stride,
                                                                     SamplePart* __restrict__ parts) {
   __shared__ float redf[32];
   __shared__ MaxIdx redm[32];
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(kSplitThreads) sample_part_kernel(const __nv_b
   const __nv_bfloat16* z = logits + row * V;
   const uint64_t seed = (uint64_t)row_seed[row];
   const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
-  const uint64_t st = (uint64_t)step[0];
+  const uint64_t st = (uint64_t)step[row * step_stride];  // per-row token index, or one for all
   float m = -INFINITY;
   for (int v = v0 + threadIdx.x; v < v1; v += kSplitThreads) m = fmaxf(m, __bfloat162float(z[v]) * inv_t);
   m = block_max(m, redf);
@@ -191,6 +192,10 @@ std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top
   TORCH_CHECK(row_seed.scalar_type() == at::kLong && step.scalar_type() == at::kLong, "sample: int64 seed/step");
   const int64_t B = logits.size(0);
   TORCH_CHECK(row_seed.numel() >= B, "sample: one seed per row");
+  // one step counter for every row, or one per row (continuous batching: rows
+  // sit at different token positions)
+  TORCH_CHECK(step.numel() == 1 || step.numel() >= B, "sample: step needs 1 or B entries");
+  const int step_stride = step.numel() >= B && B > 1 ? 1 : 0;
   auto tok = torch::empty({B}, logits.options().dtype(at::kLong));
   auto lp = torch::empty({B}, logits.options().dtype(at::kFloat));
   if (B == 0) return {tok, lp};
@@ -201,7 +206,7 @@ std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top
     auto parts = torch::empty({B, nparts, (int64_t)(sizeof(SamplePart) / 4)}, logits.options().dtype(at::kFloat));
     sample_part_kernel<<<dim3(nparts, B), kSplitThreads, 0, stream()>>>(
         (const __nv_bfloat16*)logits.data_ptr(), V, chunk, (float)inv_t, row_seed.data_ptr<int64_t>(),
-        step.data_ptr<int64_t>(), reinterpret_cast<SamplePart*>(parts.data_ptr()));
+        step.data_ptr<int64_t>(), step_stride, reinterpret_cast<SamplePart*>(parts.data_ptr()));
     sample_merge_kernel<<<B, 32, 0, stream()>>>((const __nv_bfloat16*)logits.data_ptr(), V, nparts, (float)inv_t,
                                                 reinterpret_cast<const SamplePart*>(parts.data_ptr()),
                                                 tok.data_ptr<int64_t>(), lp.data_ptr<float>());
@@ -210,7 +215,7 @@ std::vector<torch::Tensor> sample(torch::Tensor logits, double inv_t, double top
   sample_kernel<<<B, kSampleThreads, 0, stream()>>>(logits.data_ptr(), logits.scalar_type() == at::kBFloat16,
                                                     logits.size(1), (float)inv_t, (float)top_p,
                                                     row_seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(),
-                                                    tok.data_ptr<int64_t>(), lp.data_ptr<float>());
+                                                    step_stride, tok.data_ptr<int64_t>(), lp.data_ptr<float>());
   return {tok, lp};
 }
 

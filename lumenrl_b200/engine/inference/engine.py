@@ -7,9 +7,16 @@ engine on the trainer's own weights:
 * GRPO prefix sharing: each prompt is prefilled ONCE; its ``n`` samples share
   the prompt's full KV blocks (reference counted) and copy only the partial
   tail block, so prefill work and prompt KV memory drop by ``n``.
-* Static batches up to ``max_num_seqs``; larger requests run in waves.
-  Finished rows keep a fixed slot (masked), so the decode step has static
-  shapes and is replayed from a CUDA graph.
+* Static batches up to ``max_num_seqs``.  Requests with more rows than slots
+  run with continuous batching (``continuous_batching=True``, the default for
+  dense models): a row that emits EOS frees its slot and the next queued
+  sample takes it over -- its prompt prefilled on admission, the prompt's
+  full KV blocks shared, the slot's block table / position / RNG counters
+  rewritten in place so the captured decode graph stays valid.  Each row
+  draws from its own counter-based stream keyed by (sample index, token
+  index), so the samples equal those of static waves.  MoE models (routing
+  capture per row) fall back to static waves.  The decode step always has
+  static shapes and is replayed from a CUDA graph.
 * Returns token ids, per-token rollout log-probs (under softmax(logits/T),
   the quantity TIS/MIS rollout correction needs) and, for MoE models, the
   routed expert ids per generated token (R3).
@@ -73,7 +80,7 @@ class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
                  use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True,
-                 fp8_rollout=None) -> None:
+                 fp8_rollout=None, continuous_batching: bool = True) -> None:
         self.model = model
         self.args = model.args
         self.device = model.flat.device
@@ -82,6 +89,7 @@ class RolloutEngine:
         self.block_size = block_size
         self.pad_token_id = pad_token_id
         self.shared_prefix_attention = shared_prefix_attention
+        self.continuous_batching = continuous_batching
         self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda" and self.args.num_experts == 0
         spec = KVSpec(self.args.num_layers, self.args.num_kv_heads, self.args.head_dim, block_size, kv_dtype)
         self.max_blocks_per_seq = math.ceil(max_model_len / block_size) + 1
@@ -147,6 +155,9 @@ class RolloutEngine:
         if not self.cache.awake:
             self.wake()
         rows_per_prompt = sp.n
+        if (self.continuous_batching and self.args.num_experts == 0
+                and len(prompts) * rows_per_prompt > self.max_num_seqs):
+            return self._generate_continuous(prompts, sp)
         per_wave = max(1, self.max_num_seqs // rows_per_prompt)
         outs = []
         for w0 in range(0, len(prompts), per_wave):
@@ -166,6 +177,179 @@ class RolloutEngine:
             prompt_index=torch.cat([o.prompt_index for o in outs]),
             routed_experts=[r for o in outs for r in o.routed_experts],
             stats={k: sum(o.stats.get(k, 0) for o in outs) for k in outs[0].stats})
+
+    # -- continuous batching ---------------------------------------------------------
+    def _generate_continuous(self, prompts, sp: SamplingParams) -> GenerationOutput:
+        """Slots are refilled as rows finish.  Host bookkeeping (block tables,
+        admissions) runs every ``check_every`` decode steps; between checks
+        the graph replays with finished slots masked (their writes go to a
+        trash row)."""
+        from lumenrl_b200 import ops
+        dev, bs, n, S = self.device, self.block_size, sp.n, self.max_num_seqs
+        ev0 = self._ev()
+        as_tensor = isinstance(prompts, Tensor)
+        P = len(prompts)
+        plist = [prompts[i] for i in range(P)] if as_tensor else [list(p) for p in prompts]
+        plens = [int(p.shape[0]) if as_tensor else len(p) for p in plist]
+        max_new = min(sp.max_new_tokens, self.max_model_len - max(plens))
+        if max_new <= 0:
+            raise ValueError("prompt longer than max_model_len")
+        total = P * n
+        eos = sp.eos_token_id if sp.stop_at_eos else None
+        alloc = self.cache.allocator
+        g = self._graph(S, sp, None)
+        base_seed = sp.seed * 1_000_003
+        # outputs (one trash row at the end absorbs the writes of idle slots)
+        out_tok = torch.full((total + 1, max_new), self.pad_token_id, dtype=torch.long, device=dev)
+        out_lp = torch.zeros(total + 1, max_new, dtype=torch.float32, device=dev)
+        lengths = torch.full((total + 1,), max_new, dtype=torch.long, device=dev)
+        flat_tok, flat_lp = out_tok.view(-1), out_lp.view(-1)
+        slot_row = torch.full((S,), total, dtype=torch.long, device=dev)     # trash row when idle
+        active = torch.zeros(S, dtype=torch.bool, device=dev)
+        g.block_table.zero_()
+        g.positions.zero_()
+        g.step.zero_()
+        g.prefix_len.zero_()
+        host_row = [-1] * S
+        slot_blocks: list[list[int]] = [[] for _ in range(S)]
+        prompt_blocks: dict[int, list[int]] = {}
+        pending_rows_of: dict[int, int] = {}
+        next_row = 0
+        stats = {"decode_steps": 0, "prefill_tokens": 0, "admissions": 0}
+
+        def admit(free: list[int]) -> None:
+            nonlocal next_row
+            rows = list(range(next_row, min(total, next_row + len(free))))
+            next_row += len(rows)
+            if not rows:
+                return
+            new_p = sorted({r // n for r in rows} - set(prompt_blocks))
+            logits_of: dict[int, Tensor] = {}
+            if new_p:
+                e0 = self._ev()
+                ids = torch.cat([plist[i].to(dev, torch.long).reshape(-1) if as_tensor else
+                                 torch.tensor(plist[i], dtype=torch.long, device=dev) for i in new_p])
+                pos = torch.cat([torch.arange(plens[i], device=dev) for i in new_p])
+                lens_t = torch.tensor([plens[i] for i in new_p], device=dev)
+                cu = torch.zeros(len(new_p) + 1, dtype=torch.int32, device=dev)
+                cu[1:] = torch.cumsum(lens_t, 0)
+                slots_l = []
+                for i in new_p:
+                    blk = alloc.alloc(math.ceil(plens[i] / bs))
+                    prompt_blocks[i] = blk
+                    pending_rows_of[i] = n
+                    slots_l.extend(blk[j // bs] * bs + j % bs for j in range(plens[i]))
+                lg = self.runner.prefill(ids, pos, cu, int(lens_t.max()), torch.tensor(slots_l, dtype=torch.long,
+                                                                                     device=dev))
+                for k, i in enumerate(new_p):
+                    logits_of[i] = lg[k]
+                stats["prefill_tokens"] += int(lens_t.sum())
+                e1 = self._ev()
+                if e0 is not None:
+                    self._pending_ev.append((e0, e1))      # prefill time, read after the loop
+            first_logits, seeds, slots_used = [], [], []
+            for slot, r in zip(free, rows):
+                i, L = r // n, plens[r // n]
+                full = L // bs
+                shared = alloc.share(prompt_blocks[i][:full])
+                private = alloc.alloc(math.ceil((L + max_new) / bs) - full)
+                if L % bs:
+                    self.cache.copy_block(prompt_blocks[i][full], private[0])
+                table = shared + private
+                slot_blocks[slot] = table
+                host_row[slot] = r
+                g.block_table[slot].zero_()
+                g.block_table[slot, : len(table)] = torch.tensor(table, dtype=torch.int32, device=dev)
+                g.positions[slot] = L
+                first_logits.append(logits_of[i] if i in logits_of else self._prompt_logits[i])
+                seeds.append(base_seed + r)
+                slots_used.append(slot)
+            for i, lg in logits_of.items():
+                self._prompt_logits[i] = lg
+            sl = torch.tensor(slots_used, dtype=torch.long, device=dev)
+            rr = torch.tensor(rows, dtype=torch.long, device=dev)
+            g.row_seed[sl] = torch.tensor(seeds, dtype=torch.long, device=dev)
+            g.step[sl] = 0
+            tok, lp = ops.sample_tokens_device(torch.stack(first_logits), sp.temperature, sp.top_p,
+                                               g.row_seed[sl], torch.zeros(len(rows), dtype=torch.long, device=dev))
+            out_tok[rr, 0], out_lp[rr, 0] = tok, lp
+            g.tokens[sl] = tok
+            slot_row[sl] = rr
+            done = (tok == eos) if eos is not None else torch.zeros_like(tok, dtype=torch.bool)
+            if max_new == 1:
+                done = torch.ones_like(done)
+            lengths[rr] = torch.where(done, torch.ones_like(tok), torch.full_like(tok, max_new))
+            active[sl] = ~done
+            g.step[sl] = 1
+            stats["admissions"] += len(rows)
+
+        self._prompt_logits: dict[int, Tensor] = {}
+        self._pending_ev = []
+        ev1 = self._ev()
+        admit(list(range(S)))
+        check_every = 4
+        while True:
+            for _ in range(check_every):
+                tok, lp = g.run()
+                stats["decode_steps"] += 1
+                t = g.step                                   # token index each slot just sampled
+                idx = slot_row * max_new + t.clamp(max=max_new - 1)
+                flat_tok.index_copy_(0, idx, torch.where(active, tok, torch.full_like(tok, self.pad_token_id)))
+                flat_lp.index_copy_(0, idx, torch.where(active, lp, torch.zeros_like(lp)))
+                fin = active & ((t + 1 >= max_new) | ((tok == eos) if eos is not None else torch.zeros_like(active)))
+                lengths.index_copy_(0, slot_row, torch.where(fin, t + 1, lengths[slot_row]))
+                active &= ~fin
+                slot_row.masked_fill_(fin, total)           # later replays write to the trash row
+                g.tokens.copy_(tok)
+                g.positions.add_(active.long())
+                g.step.add_(active.long())
+            # host bookkeeping: release finished slots, admit queued rows
+            act = active.tolist()
+            free = []
+            for slot in range(S):
+                if not act[slot] and host_row[slot] >= 0:
+                    r = host_row[slot]
+                    alloc.release(slot_blocks[slot])
+                    slot_blocks[slot] = []
+                    host_row[slot] = -1
+                    i = r // n
+                    pending_rows_of[i] -= 1
+                    if pending_rows_of[i] == 0:       # last sample of the prompt: drop its own references
+                        alloc.release(prompt_blocks.pop(i))
+                        self._prompt_logits.pop(i, None)
+                if host_row[slot] < 0:
+                    free.append(slot)
+                    slot_row[slot] = total
+                    g.block_table[slot].zero_()
+                    g.positions[slot] = 0
+            if next_row < total and free:
+                admit(free)
+            if next_row >= total and not any(active.tolist()):
+                break
+        ev2 = self._ev()
+        lens_out = lengths[:total]
+        steps = int(lens_out.max()) if total else 0
+        ar = torch.arange(max_new, device=dev).unsqueeze(0)
+        valid = ar < lens_out.unsqueeze(1)
+        tok_o = torch.where(valid, out_tok[:total], torch.full_like(out_tok[:total], self.pad_token_id))[:, :steps]
+        lp_o = torch.where(valid, out_lp[:total], torch.zeros_like(out_lp[:total]))[:, :steps]
+        # decode steps static waves of the same rows would have run (each wave
+        # runs until its longest row ends), for the saved-steps statistic
+        per_wave = max(1, S // n) * n
+        lh = lens_out.tolist()
+        static_steps = sum(max(lh[w: w + per_wave]) - 1 for w in range(0, total, per_wave))
+        pf = sum(a.elapsed_time(b) for a, b in self._pending_ev) if ev0 is not None else 0.0
+        self._pending_ev, self._prompt_logits = [], {}
+        stats.update({"gen_tokens": int(lens_out.sum()), "static_wave_decode_steps": static_steps,
+                      "decode_steps_saved": static_steps - stats["decode_steps"]})
+        if ev0 is not None:
+            stats.update({"prefill_ms": pf, "setup_ms": ev0.elapsed_time(ev1),
+                          "decode_ms": ev1.elapsed_time(ev2) - pf})
+        prompt_index = torch.arange(total, device=dev) // n
+        return GenerationOutput(
+            prompts=(prompts.repeat_interleave(n, 0) if as_tensor else [p for p in prompts for _ in range(n)]),
+            responses=tok_o, response_lengths=lens_out, logprobs=lp_o, prompt_index=prompt_index,
+            routed_experts=[], stats=stats)
 
     def _ev(self):
         if self.device.type != "cuda":

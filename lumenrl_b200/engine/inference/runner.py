@@ -123,7 +123,7 @@ class DecodeGraph:
         self.positions = torch.zeros(batch, dtype=torch.long, device=dev)
         self.block_table = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
         self.row_seed = torch.zeros(batch, dtype=torch.long, device=dev)
-        self.step = torch.zeros(1, dtype=torch.long, device=dev)
+        self.step = torch.zeros(batch, dtype=torch.long, device=dev)   # token index per row
         self.prefix_len = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.share = share
         self.temperature, self.top_p = temperature, top_p

@@ -134,6 +134,7 @@ class ActorEngine:
         sums = {"pg_loss": 0.0, "ppo_kl": 0.0, "clipfrac": 0.0, "tok": 0.0, "entropy": 0.0}
         t_fwd_bwd = 0.0
         opt_stats = {}
+        opt_t = {"opt_rs_s": 0.0, "opt_bcast_s": 0.0}
         for _epoch in range(num_epochs):
             mini_size = math.ceil(B / num_mini_batches)
             for m0 in range(0, B, mini_size):
@@ -151,6 +152,8 @@ class ActorEngine:
                 t_fwd_bwd += time.perf_counter() - t0
                 lr = self.sched.current if self.sched else None
                 opt_stats = self.opt.step(lr)
+                for k in opt_t:
+                    opt_t[k] += self.opt.last_timing.get(k, 0.0)
                 if self.sched:
                     self.sched.step()
         tok = max(sums["tok"], 1.0)
@@ -159,6 +162,7 @@ class ActorEngine:
             "actor/pg_clipfrac": sums["clipfrac"] / tok, "actor/grad_norm": opt_stats.get("grad_norm", 0.0),
             "actor/lr": opt_stats.get("lr", 0.0), "actor/update_skipped": opt_stats.get("skipped", 0.0),
             "timing/fwd_bwd_s": t_fwd_bwd,
+            "timing/opt_rs_s": opt_t["opt_rs_s"], "timing/opt_bcast_s": opt_t["opt_bcast_s"],
         })
         return metrics
 

@@ -105,11 +105,18 @@ class ShardedFlatAdamW:
             if not skipped:
                 self.step_count += 1
             self.grad.zero_()
+            self.last_timing = dict(self.comm.last_timing)
             clip = min(1.0, self.max_grad_norm / (norm + 1e-6)) if self.max_grad_norm else 1.0
             return {"grad_norm": norm, "skipped": float(skipped), "lr": lr, "clip_coef": clip}
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if self.w16.is_cuda else None
+        if ev:
+            ev[0].record()
         t0 = time.perf_counter()
         self._reduce_scatter()
         norm = self._global_norm()
+        if ev:
+            ev[1].record()
+        t1 = time.perf_counter()
         clip = 1.0
         if self.max_grad_norm and self.max_grad_norm > 0:
             clip = min(1.0, self.max_grad_norm / (norm + 1e-6))
@@ -125,14 +132,20 @@ class ShardedFlatAdamW:
                 ref.adamw_reference(self.master, self.grad_shard, self.m, self.v, lr, b1, b2, self.eps, self.wd,
                                     self.step_count, clip)
                 self.w16[self.lo: self.hi].copy_(self.master.to(self.w16.dtype))
-            t1 = time.perf_counter()
             self._all_gather()
+        if ev:
+            ev[2].record()
+            ev[2].synchronize()
+            # opt_rs_s: gradient reduce-scatter + global norm; opt_bcast_s: from
+            # the reduced gradients to published bf16 weights (AdamW with the
+            # cast fused into the resident buffer, then the all-gather)
+            self.last_timing = {"opt_rs_s": ev[0].elapsed_time(ev[1]) / 1e3,
+                                "opt_bcast_s": ev[1].elapsed_time(ev[2]) / 1e3}
         else:
-            t1 = time.perf_counter()
+            self.last_timing = {"opt_rs_s": t1 - t0, "opt_bcast_s": time.perf_counter() - t1}
         self.grad.zero_()
         if self.world > 1:
             self.grad_shard.zero_()
-        self.last_timing = {"opt_s": t1 - t0, "allgather_s": time.perf_counter() - t1}
         return {"grad_norm": norm, "skipped": float(skipped), "lr": lr, "clip_coef": clip}
 
     def zero_grad(self) -> None:

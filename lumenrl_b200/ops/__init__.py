@@ -50,31 +50,77 @@ def _accum_main_grad(w: Tensor, g: Tensor) -> None:
 # Linear: y = x @ W^T, wgrad accumulated in fp32 into W.main_grad
 # ---------------------------------------------------------------------------
 
+# Training GEMMs: "own" runs the CTA-pair tcgen05 kernel (csrc/gemm/gemm_2sm.cu)
+# for the forward, dgrad and wgrad of every linear; "cublas" is the library
+# path kept for A/B measurements (LRL_TRAIN_GEMM=cublas).
+TRAIN_GEMM = os.environ.get("LRL_TRAIN_GEMM", "own")
+
+
+def _pair_ok(*ts) -> bool:
+    return (TRAIN_GEMM == "own" and all(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 2 and
+                                        t.stride(1) == 1 and t.shape[1] % 8 == 0 and t.stride(0) % 8 == 0
+                                        for t in ts))
+
+
+def mm_nt(x: Tensor, w: Tensor) -> Tensor:
+    """x [T, K] @ w[N, K]^T -> bf16 [T, N] (forward of a linear)."""
+    if _pair_ok(x, w):
+        return ext().gemm2sm(x, False, w, False, None, 0, 0)
+    return x @ w.t()
+
+
+def mm_nn(dy: Tensor, w: Tensor) -> Tensor:
+    """dy [T, N] @ w [N, K] -> bf16 [T, K] (dgrad: the weight is read MN-major)."""
+    if _pair_ok(dy, w):
+        return ext().gemm2sm(dy, False, w, True, None, 0, 0)
+    return dy @ w
+
+
+def mm_tn_acc(acc: Tensor, dy: Tensor, x: Tensor) -> None:
+    """acc [N, K] (fp32) += dy[T, N]^T @ x[T, K] (wgrad into main_grad)."""
+    if _pair_ok(dy, x) and acc.is_contiguous():
+        ext().gemm2sm(dy, True, x, True, acc, 2, 0)
+    elif acc.is_cuda:
+        torch.addmm(acc, dy.t(), x, out_dtype=torch.float32, out=acc)
+    else:
+        acc += dy.t().float() @ x.float()
+
+
 class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x: Tensor, w: Tensor, w_handle: Tensor):
         ctx.save_for_backward(x, w)
         ctx.w_handle = w_handle
+        if x.is_cuda:
+            x2 = x.reshape(-1, x.shape[-1])
+            return mm_nt(x2, w).view(*x.shape[:-1], w.shape[0])
         return x @ w.t()
 
     @staticmethod
     def backward(ctx, dy: Tensor):
         x, w = ctx.saved_tensors
-        dx = dy @ w
         wh = ctx.w_handle
         mg = getattr(wh, "main_grad", None)
         dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
-        if mg is not None and dy.is_cuda:
-            # cuBLAS bf16 x bf16 -> fp32 accumulate (beta = 1) into the flat
-            # gradient buffer: no bf16 weight-grad tensor is ever allocated.
-            torch.addmm(mg, dy2.t(), x2, out_dtype=torch.float32, out=mg)
-        else:
-            _accum_main_grad(wh, dy2.t().float() @ x2.float())
+        if dy.is_cuda:
+            dy2 = dy2.contiguous()
+            dx = mm_nn(dy2, w).view(*dy.shape[:-1], w.shape[1])
+            if mg is not None:
+                # bf16 x bf16 -> fp32 accumulate (beta = 1) into the flat
+                # gradient buffer: no bf16 weight-grad tensor is ever allocated.
+                mm_tn_acc(mg, dy2, x2)
+            else:
+                _accum_main_grad(wh, dy2.t().float() @ x2.float())
+            return dx, None, None
+        dx = dy @ w
+        _accum_main_grad(wh, dy2.t().float() @ x2.float())
         return dx, None, None
 
 
 def linear(x: Tensor, w: Tensor) -> Tensor:
     if not torch.is_grad_enabled() or not w.requires_grad:
+        if x.is_cuda:
+            return mm_nt(x.reshape(-1, x.shape[-1]), w).view(*x.shape[:-1], w.shape[0])
         return x @ w.t()
     return _Linear.apply(x, w.detach(), w)
 
@@ -354,7 +400,7 @@ class _TokenLogProb(torch.autograd.Function):
         lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
         for a in range(0, T, chunk):
             b = min(T, a + chunk)
-            logits = hidden[a:b] @ w.t()
+            logits = mm_nt(hidden[a:b], w)
             ext().logprob_fwd(logits, targets[a:b], inv_temp, logp[a:b], ent[a:b], lse[a:b])
         ctx.save_for_backward(hidden, w, targets, lse, ent)
         ctx.meta = (w_handle, inv_temp, chunk, want_entropy)
@@ -371,14 +417,14 @@ class _TokenLogProb(torch.autograd.Function):
         mg = getattr(w_handle, "main_grad", None)
         for a in range(0, T, chunk):
             b = min(T, a + chunk)
-            logits = hidden[a:b] @ w.t()
+            logits = mm_nt(hidden[a:b], w)
             # in place: logits -> dL/dlogits (bf16)
             ext().logprob_bwd(logits, targets[a:b], lse[a:b], dlogp[a:b],
                               dent[a:b] if dent is not None else None, inv_temp,
                               ent[a:b] if dent is not None else None)
-            dh[a:b] = logits @ w
+            dh[a:b] = mm_nn(logits, w)
             if mg is not None:
-                torch.addmm(mg, logits.t(), hidden[a:b], out_dtype=torch.float32, out=mg)
+                mm_tn_acc(mg, logits, hidden[a:b])
             else:
                 _accum_main_grad(w_handle, logits.t().float() @ hidden[a:b].float())
         return dh, None, None, None, None, None, None
@@ -401,7 +447,8 @@ def token_logprob(hidden: Tensor, lm_head: Tensor, targets: Tensor, temperature:
     lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
     for a in range(0, T, chunk):
         b = min(T, a + chunk)
-        ext().logprob_fwd(hidden[a:b] @ lm_head.t(), targets[a:b].contiguous(), inv_t, logp[a:b], ent[a:b], lse[a:b])
+        ext().logprob_fwd(mm_nt(hidden[a:b], lm_head), targets[a:b].contiguous(), inv_t, logp[a:b], ent[a:b],
+                          lse[a:b])
     return logp, (ent if want_entropy else None)
 
 
@@ -450,16 +497,18 @@ def sample_tokens_device(logits: Tensor, temperature: float, top_p: float, row_s
     top-p nucleus; returns (token ids int64, log-prob of the sampled token
     under softmax(logits / T)).
 
-    Randomness is a counter-based stream keyed by (row_seed[row], step[0],
+    Randomness is a counter-based stream keyed by (row_seed[row], step,
     vocab index), so a row's draw does not depend on batch composition and
-    the call can live inside a CUDA graph (seed/step are device tensors)."""
+    the call can live inside a CUDA graph (seed/step are device tensors).
+    ``step`` holds one counter for all rows or one per row."""
     inv_t = 1.0 / max(float(temperature), 1e-6)
     if not _cuda(logits):
         z = logits.float() * inv_t
         lp = torch.log_softmax(z, -1)
         toks = []
+        per_row = step.numel() > 1
         for r in range(z.shape[0]):
-            g = torch.Generator(device="cpu").manual_seed(int(row_seed[r]) * 1000003 + int(step[0]))
+            g = torch.Generator(device="cpu").manual_seed(int(row_seed[r]) * 1000003 + int(step[r if per_row else 0]))
             row = lp[r]
             if top_p < 1.0:
                 srt, idx = torch.sort(row, descending=True)

@@ -80,6 +80,7 @@ class NVLinkOptimizerComm:
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.norm = torch.zeros(1, dtype=torch.float32, device=dev)
         self.epoch = 0
+        self.last_timing: dict[str, float] = {}
         self._rendezvous = torch.zeros(1, dtype=torch.int32, device=dev)
         dist.barrier(group=group)
 
@@ -92,12 +93,19 @@ class NVLinkOptimizerComm:
         # flag barriers below only order memory and never wait long
         if rendezvous:
             dist.all_reduce(self._rendezvous, group=self.group)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
         e.rs_norm(self.grads.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, grad_shard, self.epoch,
                   self.status, self.wait_cycles)
+        ev[1].record()
         e.adamw_ag(self.weights.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, master, grad_shard, m, v, lr,
                    betas[0], betas[1], eps, wd, step, max_norm if max_norm else 0.0, self.epoch, self.status,
                    self.norm, self.wait_cycles)
+        ev[2].record()
         vals = torch.cat([self.norm, self.status.float()]).cpu()   # one device->host read per step
+        # device time of the two kernels (the read above waited for both)
+        self.last_timing = {"opt_rs_s": ev[0].elapsed_time(ev[1]) / 1e3,
+                            "opt_bcast_s": ev[1].elapsed_time(ev[2]) / 1e3}
         norm, status = float(vals[0]), int(vals[1])
         if status:
             raise CommTimeout(f"fused optimizer step: a cross-rank wait expired (code {status}); "
@@ -112,3 +120,74 @@ class NVLinkOptimizerComm:
     def close(self) -> None:
         for b in (self.weights, self.grads, self.signals):
             b.close()
+
+
+# ---------------------------------------------------------------------------
+# correctness checks of the data-parallel replicas (used by bench.py at N > 1
+# and by the multi-GPU tests)
+# ---------------------------------------------------------------------------
+
+def _bits_checksum(t: torch.Tensor, chunk: int = 1 << 26) -> tuple[int, int]:
+    """Order-sensitive checksum of a tensor's bit pattern: (sum of the 16-bit
+    words, sum of word x (index mod 65521)); identical bytes give identical
+    pairs on every rank."""
+    w = t.reshape(-1).view(torch.int16)
+    s0 = s1 = 0
+    for a in range(0, w.numel(), chunk):
+        x = w[a: a + chunk].to(torch.int64) & 0xFFFF
+        idx = (torch.arange(a, a + x.numel(), device=x.device, dtype=torch.int64) % 65521)
+        s0 += int(x.sum())
+        s1 += int((x * idx).sum())
+    return s0, s1
+
+
+def replica_agreement(model_flat: torch.Tensor, master: torch.Tensor, lo: int, group=None) -> dict:
+    """Do all ranks hold bit-identical resident bf16 weights, and does every
+    rank's bf16 slice equal its fp32 master shard rounded to bf16?"""
+    world = dist.get_world_size(group)
+    cs = _bits_checksum(model_flat)
+    own = model_flat[lo: lo + master.numel()]
+    mism = int((master.to(own.dtype).view(torch.int16) != own.view(torch.int16)).sum())
+    mine = torch.tensor([cs[0], cs[1], mism], dtype=torch.int64, device=model_flat.device)
+    every = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine, group=group)
+    rows = [tuple(int(v) for v in e.tolist()) for e in every]
+    same = all(r[:2] == rows[0][:2] for r in rows)
+    return {"ranks_agree": bool(same and all(r[2] == 0 for r in rows)), "weights_identical": bool(same),
+            "master_mismatches": sum(r[2] for r in rows)}
+
+
+def fused_vs_nccl_max_err(numel: int, rank: int, world: int, steps: int = 1, group=None, seed: int = 0) -> dict:
+    """One (or more) fused NVLink optimizer steps (rs_norm + adamw_ag) against
+    NCCL reduce_scatter_tensor + the AdamW kernel + all_gather_into_tensor on
+    the same gradients; returns the largest differences of the resulting bf16
+    weights and fp32 master shards.  Allocates ~``numel`` x 14 bytes per rank."""
+    from lumenrl_b200.engine.training.optimizer import ShardedFlatAdamW
+    n = max(numel // (world * 128), 1) * world * 128
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g0 = torch.Generator(device=dev).manual_seed(seed)
+    w0 = torch.randn(n, device=dev, generator=g0).to(torch.bfloat16)
+    comm = NVLinkOptimizerComm(n, rank, world, group=group)
+    try:
+        comm.weights.tensor.copy_(w0)
+        kw = dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+        fused = ShardedFlatAdamW(comm.weights.tensor, world, rank, comm=comm, **kw)
+        plain_w = w0.clone()
+        plain = ShardedFlatAdamW(plain_w, world, rank, **kw)
+        norm_err = 0.0
+        for s in range(steps):
+            g = torch.randn(n, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 1000 * s + rank))
+            fused.grad.copy_(g)
+            plain.grad.copy_(g)
+            a, b = fused.step(), plain.step()
+            norm_err = max(norm_err, abs(a["grad_norm"] - b["grad_norm"]) / max(1.0, b["grad_norm"]))
+        torch.cuda.synchronize()
+        out = torch.tensor([(comm.weights.tensor.float() - plain_w.float()).abs().max().item(),
+                            (fused.master - plain.master).abs().max().item(), norm_err], device=dev)
+        dist.all_reduce(out, op=dist.ReduceOp.MAX, group=group)
+        return {"weights_max_err": float(out[0]), "master_max_err": float(out[1]), "grad_norm_rel_err": float(out[2]),
+                "numel": n}
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        comm.close()

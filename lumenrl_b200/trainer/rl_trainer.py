@@ -297,7 +297,19 @@ class RLTrainer:
         m["reward/mean"] = all_reduce_sum(float(scores.sum())) / all_reduce_sum(float(len(batch)))
         m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
             float(len(batch)))
-        m["weight_sync/ms"] = times["weight_sync"] * 1e3
+        # Weight sync = from the reduced gradients to rollout-ready weights: the
+        # AdamW kernel that writes bf16 into the resident buffer the engine
+        # reads (and, on several GPUs, stores it into every rank's copy over
+        # NVLink), plus the engine-side update (fp8 re-quantisation when the
+        # rollout runs W8A8; a pointer check otherwise).  Max over ranks.
+        for k in ("timing/opt_rs_s", "timing/opt_bcast_s"):
+            if k in m:
+                m[k] = all_reduce_max(float(m[k]))
+        sync_s = all_reduce_max(float(tm.get("timing/opt_bcast_s", 0.0)) + times["weight_sync"])
+        m["timing/weight_sync_s"] = sync_s
+        m["weight_sync/ms"] = sync_s * 1e3
+        m["weight_sync/GBps"] = self.actor.model.flat.numel() * self.actor.model.flat.element_size() / max(
+            sync_s, 1e-9) / 1e9
         for k in ("prefill_ms", "setup_ms", "decode_ms"):
             if k in batch.meta.get("gen_stats", {}):
                 m[f"timing/gen_{k}"] = batch.meta["gen_stats"][k]

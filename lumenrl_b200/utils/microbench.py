@@ -277,6 +277,75 @@ def bench_gemm(ns) -> dict:
     return {"op": "gemm", "status": st, "shapes": out}
 
 
+def bench_gemm2(ns) -> dict:
+    """CTA-pair tcgen05 GEMM vs cuBLAS on the three GEMMs of every Qwen3-8B
+    training linear (T = --rows x --seq tokens) and the LM-head chunk:
+    forward (x . W^T), dgrad (dy . W) and wgrad (main_grad += dy^T . x)."""
+    from lumenrl_b200.ops.ext import ext
+    a = _model_args(ns.model)
+    T = ns.rows * ns.seq
+    shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
+              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size),
+              "lm_head": (a.vocab_size, a.hidden_size)}
+    out = {"op": "train_gemms", "tokens": T, "cache": "operands > L2 except where noted by size"}
+    tot = {"own": 0.0, "cublas": 0.0}
+    for name, (N, K) in shapes.items():
+        M = 2048 if name == "lm_head" else T
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        dy = (torch.randn(M, N, device="cuda") / 8).to(torch.bfloat16)
+        mg = torch.zeros(N, K, device="cuda")
+        fl = 2 * M * N * K
+        r = {}
+        for kind, own, lib in [
+                ("fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, ns.bn), lambda: x @ w.t()),
+                ("dgrad", lambda: ext().gemm2sm(dy, False, w, True, None, 0, ns.bn), lambda: dy @ w),
+                ("wgrad", lambda: ext().gemm2sm(dy, True, x, True, mg, 2, ns.bn),
+                 lambda: torch.addmm(mg, dy.t(), x, out_dtype=torch.float32, out=mg))]:
+            t_own = _time(own, ns.steps, ns.warmup)
+            t_lib = _time(lib, ns.steps, ns.warmup)
+            tot["own"] += t_own
+            tot["cublas"] += t_lib
+            r[kind] = {"own_tflops": round(fl / t_own / 1e9, 1), "cublas_tflops": round(fl / t_lib / 1e9, 1),
+                       "ratio": round(t_lib / t_own, 3)}
+        ref = x[:256].float() @ w.float().t()
+        r["fwd_max_err"] = (ext().gemm2sm(x[:256], False, w, False, None, 0, 0).float() - ref).abs().max().item()
+        out[name] = r
+        del x, w, dy, mg
+    out["sum_ms"] = {k: round(v, 3) for k, v in tot.items()}
+    out["status"] = int(ext().gemm2sm_status())
+    return out
+
+
+def bench_gemm2probe(ns) -> dict:
+    """Operand-layout / epilogue probe of the pair GEMM on one shape
+    (--rows x --seq tokens by the qkv projection, or --mnk M,N,K): every
+    majorness pair with the bf16 epilogue and with the result dropped
+    (mainloop-only time).  --case restricts it to one layout (kk, kn, nn, nk)."""
+    from lumenrl_b200.ops.ext import ext
+    a = _model_args(ns.model)
+    M, N, K = (ns.rows * ns.seq, a.qkv_dim, a.hidden_size) if not ns.mnk else tuple(
+        int(v) for v in ns.mnk.split(","))
+    A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    B = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+    At, Bt = A.t().contiguous(), B.t().contiguous()
+    fl = 2 * M * N * K
+    out = {"op": "gemm2_probe", "M": M, "N": N, "K": K}
+    cases = {"kk": (A, False, B, False), "kn": (A, False, Bt, True), "nn": (At, True, Bt, True),
+             "nk": (At, True, B, False)}
+    for name, (x, xm, y, ym) in cases.items():
+        if ns.case and name != ns.case:
+            continue
+        for epi, tag in ((0, "bf16"), (3, "none")):
+            t = _time(lambda: ext().gemm2sm(x, xm, y, ym, None, epi, 256), ns.steps, ns.warmup)
+            out[f"{name}_{tag}_tflops"] = round(fl / t / 1e9, 1)
+    if not ns.case:
+        t = _time(lambda: A @ B.t(), ns.steps, ns.warmup)
+        out["cublas_tflops"] = round(fl / t / 1e9, 1)
+    out["status"] = int(ext().gemm2sm_status())
+    return out
+
+
 def bench_comm(ns) -> dict:
     """Fused NVLink optimizer step vs the NCCL path on a Qwen3-8B-sized flat
     buffer (launch under torchrun, one rank per GPU)."""
@@ -319,7 +388,7 @@ def bench_comm(ns) -> dict:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
-                                     "dgemm"])
+                                     "dgemm", "gemm2", "gemm2probe"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -333,12 +402,16 @@ def main(argv=None) -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--recompute", action="store_true")
+    ap.add_argument("--bn", type=int, default=0, help="pair GEMM tile width (0 = auto, 128, 256)")
+    ap.add_argument("--mnk", default="", help="gemm2probe shape M,N,K")
+    ap.add_argument("--case", default="", help="gemm2probe operand layout: kk, kn, nn or nk")
     ap.add_argument("--no-graph", action="store_true")
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
     fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm,
-          "comm": bench_comm}[ns.what]
+          "comm": bench_comm, "gemm2": bench_gemm2,
+          "gemm2probe": bench_gemm2probe}[ns.what]
     res = fn(ns)
     import os
     if int(os.environ.get("RANK", "0")) == 0:

@@ -1,0 +1,84 @@
+"""CTA-pair tcgen05 GEMM (``gemm2sm``) against an fp32 matmul of the same bf16
+inputs, for every operand majorness the linear layers use (forward: both
+K-major; dgrad: MN-major B; wgrad: both MN-major) and every epilogue."""
+
+import pytest
+import torch
+
+from lumenrl_b200 import ops
+from lumenrl_b200.ops.ext import ext
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(256, 256, 64), (512, 768, 1024), (300, 520, 4096), (1000, 1032, 136), (2048, 4096, 512),
+          (64, 6144, 4096), (4096, 4096, 4096)]
+
+
+def _operands(M, N, K, a_mn, b_mn, dev):
+    torch.manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    B = (torch.randn(N, K, device=dev) / K ** 0.5).to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    return A, B, a, b
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm2sm_bf16(cuda, M, N, K, a_mn, b_mn, bn):
+    if (a_mn and M % 8) or (b_mn and N % 8):
+        pytest.skip("MN-major operands need a multiple of 8 along M / N")
+    A, B, a, b = _operands(M, N, K, a_mn, b_mn, cuda)
+    c = ext().gemm2sm(a, a_mn, b, b_mn, None, 0, bn)
+    torch.cuda.synchronize()
+    assert ext().gemm2sm_status() == 0
+    ref = A.float() @ B.float().t()
+    err = (c.float() - ref).abs().max().item()
+    assert err <= 2e-2 * max(1.0, ref.abs().max().item()), err
+
+
+@pytest.mark.parametrize("M,N,K", [(384, 768, 1024), (4096, 1032, 6144), (136, 256, 104)])
+def test_gemm2sm_fp32_and_accumulate(cuda, M, N, K):
+    A, B, a, b = _operands(M, N, K, True, True, cuda)
+    c = torch.randn(M, N, device=cuda)
+    c0 = c.clone()
+    ext().gemm2sm(a, True, b, True, c, 2, 0)          # wgrad form: c += A . B^T
+    f = ext().gemm2sm(A, False, B, False, None, 1, 0)  # fp32 out
+    torch.cuda.synchronize()
+    assert ext().gemm2sm_status() == 0
+    ref = A.float() @ B.float().t()
+    assert (f - ref).abs().max().item() < 2e-3 * max(1.0, ref.abs().max().item())
+    assert (c - (c0 + ref)).abs().max().item() < 2e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_gemm2sm_strided_rows(cuda):
+    """Row-strided views (a slice of a wider matrix) as both operands."""
+    torch.manual_seed(3)
+    big = torch.randn(512, 2048, device=cuda).to(torch.bfloat16)
+    w = torch.randn(1024, 4096, device=cuda).to(torch.bfloat16)
+    a, b = big[:, 512:1536], w[:, 1024:2048]
+    c = ext().gemm2sm(a, False, b, False, None, 0, 0)
+    torch.cuda.synchronize()
+    assert ext().gemm2sm_status() == 0
+    ref = a.float() @ b.float().t()
+    assert (c.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_linear_autograd_on_pair_gemm(cuda):
+    """ops.linear forward / dgrad / wgrad (main_grad accumulation) against
+    fp32 autograd of the same bf16 values."""
+    torch.manual_seed(5)
+    T, K, N = 1536, 4096, 1024
+    x = torch.randn(T, K, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(N, K, device=cuda) / K ** 0.5).to(torch.bfloat16).requires_grad_(True)
+    w.main_grad = torch.zeros(N, K, device=cuda)
+    dy = torch.randn(T, N, device=cuda).to(torch.bfloat16)
+    y = ops.linear(x, w)
+    y.backward(dy)
+    xf, wf = x.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    yf = xf @ wf.t()
+    yf.backward(dy.float())
+    assert (y.float() - yf).abs().max().item() < 3e-2 * yf.abs().max().item()
+    assert (x.grad.float() - xf.grad).abs().max().item() < 3e-2 * xf.grad.abs().max().item()
+    assert (w.main_grad - wf.grad).abs().max().item() < 1e-2 * wf.grad.abs().max().item()

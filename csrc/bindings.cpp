@@ -1,7 +1,37 @@
 // Python bindings of the lumenrl_b200._C extension.
 #include <torch/extension.h>
 
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
+#include <cstdio>
 #include <vector>
+
+// Opt-in diagnostics (LRL_SEGV_BACKTRACE=1 in the tests): on SIGSEGV print the
+// native call stack of this process's host code, then hand the signal to the
+// handler that was installed before (Python's faulthandler).
+namespace {
+struct sigaction g_prev_segv;
+void lrl_segv_handler(int sig, siginfo_t* info, void* uctx) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  char head[160];
+  const int len = snprintf(head, sizeof(head), "lumenrl_b200: signal %d, fault address %p; native stack:\n", sig,
+                           info ? info->si_addr : nullptr);
+  if (len > 0) (void)!write(2, head, (size_t)len);
+  backtrace_symbols_fd(frames, n, 2);
+  sigaction(SIGSEGV, &g_prev_segv, nullptr);
+  raise(sig);
+}
+void install_segv_backtrace() {
+  struct sigaction sa = {};
+  sa.sa_sigaction = lrl_segv_handler;
+  sa.sa_flags = SA_SIGINFO;
+  sigemptyset(&sa.sa_mask);
+  sigaction(SIGSEGV, &sa, &g_prev_segv);
+}
+}  // namespace
 
 namespace lrl {
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
@@ -96,11 +126,15 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
               torch::Tensor norm_out, int64_t wait_cycles);
 std::vector<torch::Tensor> quant_act_1x128(torch::Tensor x, bool e5m2);
 std::vector<torch::Tensor> quant_weight_128x128(torch::Tensor w, bool e5m2);
+std::vector<torch::Tensor> quant_t_1x128(torch::Tensor x, bool e5m2, bool kb_major);
+torch::Tensor fp8_gemm_ex(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb,
+                          c10::optional<torch::Tensor> c, bool b_row, torch::Tensor err);
 torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err);
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lumenrl_b200 sm_100a kernels";
+  m.def("install_segv_backtrace", &install_segv_backtrace);
   m.def("rmsnorm_fwd", &lrl::rmsnorm_fwd);
   m.def("add_rmsnorm_fwd", &lrl::add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &lrl::rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dw"),
@@ -168,5 +202,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_ag", &lrl::adamw_ag);
   m.def("quant_act_1x128", &lrl::quant_act_1x128);
   m.def("quant_weight_128x128", &lrl::quant_weight_128x128);
+  m.def("quant_t_1x128", &lrl::quant_t_1x128, py::arg("x"), py::arg("e5m2") = false, py::arg("kb_major") = false);
+  m.def(
+      "fp8_gemm_ex",
+      [](torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err,
+         c10::optional<torch::Tensor> c, bool b_row) { return lrl::fp8_gemm_ex(a, sa, b, sb, c, b_row, err); },
+      py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sb"), py::arg("err"), py::arg("c") = py::none(),
+      py::arg("b_row") = false);
   m.def("fp8_gemm", &lrl::fp8_gemm);
 }

@@ -1,9 +1,14 @@
 // Block-scaled FP8 GEMM on the 5th-generation tensor cores (kind::f8f6f4).
 //
-//   C[M, N] (bf16) = sum_kb  (A[M, kb] @ B[N, kb]^T) * sa[M, kb] * sb[N/128, kb]
+//   C[M, N] (=, +=) sum_kb  (A[M, kb] @ B[N, kb]^T) * sa[M, kb] * sb[., kb]
 //
-// A: E4M3 activations with one fp32 scale per 1x128 block (row, K block);
-// B: E4M3 weights with one fp32 scale per 128x128 block.  Scales change with
+// A: E4M3 or E5M2 with one fp32 scale per 1x128 block (row, K block);
+// B: E4M3 or E5M2 with one fp32 scale per 128x128 block (weights), or per
+// 1x128 block like A (B_ROW: the wgrad operand x^T, quantised along the
+// token dimension).  The operand formats are independent (kind::f8f6f4 takes
+// E5M2 x E4M3), which is what hybrid FP8 training needs: E4M3 activations
+// and weights, E5M2 gradients.  Output: bf16 C, or fp32 C += (gradient
+// accumulation into main_grad).  Scales change with
 // every 128-wide K block, so each K block is accumulated on its own in TMEM
 // (two buffers, ping-pong) and the epilogue warps "promote" it: read it with
 // tcgen05.ld, multiply by sa*sb and add into fp32 registers, while the MMA
@@ -31,9 +36,11 @@ constexpr int kFStageBytes = kFABytes + kFBBytes;  // 32 KB
 constexpr int kFSmem = kFStages * kFStageBytes + 1024 + 256;
 constexpr int kFThreads = 192;
 
-__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
-  // c_format F32 (bit 4); a/b format E4M3 = 0; K-major; N>>3 at 17, M>>4 at 24
-  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_f8_f32(int M, int N, int afmt, int bfmt) {
+  // c_format F32 (bit 4); A format at [7,10), B format at [10,13) (E4M3 = 0,
+  // E5M2 = 1); both K-major; N>>3 at 17, M>>4 at 24
+  return (1u << 4) | ((uint32_t)afmt << 7) | ((uint32_t)bfmt << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -45,10 +52,11 @@ __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+template <int AF, int BF, bool B_ROW, bool ACC>
 __global__ void __launch_bounds__(kFThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const float* __restrict__ sa, const float* __restrict__ sb, __nv_bfloat16* __restrict__ C, int M,
-                    int N, int K, int* err_out) {
+                    const float* __restrict__ sa, const float* __restrict__ sb, void* __restrict__ Cv, int M,
+                    int N, int K, int64_t ldc, int* err_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_e4m3_f32(kFBM, kFBN);
+      const uint32_t idesc = idesc_f8_f32(kFBM, kFBN, AF, BF);
       int it = 0, kc = 0;  // kc: K blocks issued by this CTA (selects the TMEM buffer)
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -153,33 +161,74 @@ __global__ void __launch_bounds__(kFThreads, 1)
           break;
         }
         tc_fence_after();
-        const float scale = sa[(int64_t)rs * kblocks + kb] * sb[(int64_t)nb * kblocks + kb];
+        if constexpr (B_ROW) {
+          // per-column scales of this K block: sb is K-block-major [kblocks,
+          // Npad] (Npad a multiple of 128), so the 128 scales of the tile are
+          // contiguous and every thread reads the same addresses (broadcast)
+          const float sr = sa[(int64_t)rs * kblocks + kb];
+          const int npad = (N + kFBN - 1) / kFBN * kFBN;
+          const float4* sc = reinterpret_cast<const float4*>(sb + (int64_t)kb * npad + nb * kFBN);
 #pragma unroll
-        for (int c = 0; c < kFBN / 32; ++c) {
-          float v[32];
-          tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
+          for (int c = 0; c < kFBN / 32; ++c) {
+            float v[32];
+            tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i] * scale;
+            for (int i = 0; i < 8; ++i) {
+              const float4 f = __ldg(sc + c * 8 + i);
+              acc[c * 32 + 4 * i] += v[4 * i] * (sr * f.x);
+              acc[c * 32 + 4 * i + 1] += v[4 * i + 1] * (sr * f.y);
+              acc[c * 32 + 4 * i + 2] += v[4 * i + 2] * (sr * f.z);
+              acc[c * 32 + 4 * i + 3] += v[4 * i + 3] * (sr * f.w);
+            }
+          }
+        } else {
+          const float scale = sa[(int64_t)rs * kblocks + kb] * sb[(int64_t)nb * kblocks + kb];
+#pragma unroll
+          for (int c = 0; c < kFBN / 32; ++c) {
+            float v[32];
+            tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i] * scale;
+          }
         }
         tc_fence_before();
         mbar_arrive(&kempty[buf]);
       }
       if (!ok) break;
       if (row < M) {
-        __nv_bfloat16* p = C + (int64_t)row * N + nb * kFBN;
         const int ncols = min(kFBN, N - nb * kFBN);
-        if (ncols == kFBN) {
+        if constexpr (ACC) {
+          float* p = reinterpret_cast<float*>(Cv) + (int64_t)row * ldc + nb * kFBN;
+          if (ncols == kFBN && (ldc % 4) == 0) {
 #pragma unroll
-          for (int i = 0; i < kFBN / 8; ++i) {
-            float tmp[8];
+            for (int i = 0; i < kFBN / 4; ++i) {
+              float4 o = reinterpret_cast<float4*>(p)[i];
+              o.x += acc[4 * i];
+              o.y += acc[4 * i + 1];
+              o.z += acc[4 * i + 2];
+              o.w += acc[4 * i + 3];
+              reinterpret_cast<float4*>(p)[i] = o;
+            }
+          } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tmp[j] = acc[8 * i + j];
-            store8(p + 8 * i, tmp);
+            for (int i = 0; i < kFBN; ++i)
+              if (i < ncols) p[i] += acc[i];
           }
         } else {
+          __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(Cv) + (int64_t)row * ldc + nb * kFBN;
+          if (ncols == kFBN && (ldc % 8) == 0) {
 #pragma unroll
-          for (int i = 0; i < kFBN; ++i)
-            if (i < ncols) p[i] = __float2bfloat16(acc[i]);
+            for (int i = 0; i < kFBN / 8; ++i) {
+              float tmp[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) tmp[j] = acc[8 * i + j];
+              store8(p + 8 * i, tmp);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < kFBN; ++i)
+              if (i < ncols) p[i] = __float2bfloat16(acc[i]);
+          }
         }
       }
     }
@@ -223,32 +272,98 @@ CUtensorMap make_fp8_map(const void* ptr, int64_t rows, int64_t K, int64_t ld) {
 
 int64_t tc_gemm_status();
 
-// a [M, K] e4m3 + sa [M, K/128]; b [N, K] e4m3 + sb [ceil(N/128), K/128] -> bf16 [M, N]
-torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err) {
+template <int AF, int BF, bool B_ROW, bool ACC>
+static void fp8_launch(const CUtensorMap& ma, const CUtensorMap& mb, const float* sa, const float* sb, void* c,
+                       int64_t M, int64_t N, int64_t K, int64_t ldc, int* err) {
+  auto kern = fp8_gemm_kernel<AF, BF, B_ROW, ACC>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
+    attr = true;
+  }
+  const int tiles = (int)(((M + kFBM - 1) / kFBM) * ((N + kFBN - 1) / kFBN));
+  kern<<<std::min(tiles, num_sms()), kFThreads, kFSmem, stream()>>>(ma, mb, sa, sb, c, (int)M, (int)N, (int)K, ldc,
+                                                                     err);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static int fp8_fmt(const torch::Tensor& t) {
+  if (t.scalar_type() == at::kFloat8_e4m3fn) return 0;
+  if (t.scalar_type() == at::kFloat8_e5m2) return 1;
+  TORCH_CHECK(false, "fp8_gemm: operands must be float8_e4m3fn or float8_e5m2");
+  return -1;
+}
+
+// a [M, K] (E4M3 / E5M2) + sa [M, K/128]; b [N, K] (E4M3 / E5M2) + sb
+// [ceil(N/128), K/128] (128x128 blocks) or, with b_row, per-row scales stored
+// K-block-major: sb [K/128, ceil(N/128)*128] (zero-padded columns).
+// Returns bf16 [M, N], or with `c` (fp32 [M, N]) accumulates into it.
+torch::Tensor fp8_gemm_ex(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb,
+                          c10::optional<torch::Tensor> c, bool b_row, torch::Tensor err) {
   LRL_CHECK(a);
   LRL_CHECK(b);
   LRL_CHECK(sa);
   LRL_CHECK(sb);
-  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "fp8_gemm: e4m3");
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sb.scalar_type() == at::kFloat, "fp8_gemm: fp32 scales");
+  const int af = fp8_fmt(a), bf = fp8_fmt(b);
   const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
   TORCH_CHECK(b.size(1) == K && K % 16 == 0, "fp8_gemm: K mismatch / alignment");
   const int64_t kb = (K + kFBK - 1) / kFBK;
-  TORCH_CHECK(sa.size(0) == M && sa.size(1) == kb && sb.size(0) == (N + 127) / 128 && sb.size(1) == kb,
-              "fp8_gemm: scale shapes");
-  auto c = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
-  if (M == 0 || N == 0) return c;
+  TORCH_CHECK(sa.size(0) == M && sa.size(1) == kb, "fp8_gemm: sa must be [M, ceil(K/128)]");
+  if (b_row) {
+    TORCH_CHECK(sb.size(0) == kb && sb.size(1) == (N + 127) / 128 * 128 && sb.is_contiguous(),
+                "fp8_gemm: row scales of b must be [ceil(K/128), ceil(N/128)*128]");
+  } else {
+    TORCH_CHECK(sb.size(1) == kb && sb.size(0) == (N + 127) / 128, "fp8_gemm: sb must be [ceil(N/128), ceil(K/128)]");
+  }
+  torch::Tensor out;
+  if (c.has_value()) {
+    TORCH_CHECK(c->is_cuda() && c->scalar_type() == at::kFloat && c->dim() == 2 && c->size(0) == M &&
+                    c->size(1) == N && c->stride(1) == 1,
+                "fp8_gemm: accumulate target must be fp32 [M, N] with unit column stride");
+    out = *c;
+  } else {
+    out = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
+  }
+  if (M == 0 || N == 0) return out;
+  c10::cuda::CUDAGuard guard(a.device());
   const CUtensorMap ma = make_fp8_map(a.data_ptr(), M, K, K);
   const CUtensorMap mb = make_fp8_map(b.data_ptr(), N, K, K);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
-    attr = true;
+  const int64_t ldc = out.stride(0);
+  int* e = err.data_ptr<int>();
+  const float *psa = sa.data_ptr<float>(), *psb = sb.data_ptr<float>();
+  void* pc = out.data_ptr();
+#define FP8GO(A_, B_, R_, C_) fp8_launch<A_, B_, R_, C_>(ma, mb, psa, psb, pc, M, N, K, ldc, e)
+  const bool acc = c.has_value();
+  if (!b_row && !acc) {
+    if (af == 0 && bf == 0) FP8GO(0, 0, false, false);
+    else if (af == 1 && bf == 0) FP8GO(1, 0, false, false);
+    else if (af == 0 && bf == 1) FP8GO(0, 1, false, false);
+    else FP8GO(1, 1, false, false);
+  } else if (b_row && acc) {
+    if (af == 1 && bf == 0) FP8GO(1, 0, true, true);
+    else if (af == 0 && bf == 0) FP8GO(0, 0, true, true);
+    else if (af == 0 && bf == 1) FP8GO(0, 1, true, true);
+    else FP8GO(1, 1, true, true);
+  } else if (b_row) {
+    if (af == 0 && bf == 0) FP8GO(0, 0, true, false);
+    else if (af == 1 && bf == 0) FP8GO(1, 0, true, false);
+    else if (af == 0 && bf == 1) FP8GO(0, 1, true, false);
+    else FP8GO(1, 1, true, false);
+  } else {
+    if (af == 0 && bf == 0) FP8GO(0, 0, false, true);
+    else if (af == 1 && bf == 0) FP8GO(1, 0, false, true);
+    else if (af == 0 && bf == 1) FP8GO(0, 1, false, true);
+    else FP8GO(1, 1, false, true);
   }
-  const int tiles = (int)(((M + kFBM - 1) / kFBM) * ((N + kFBN - 1) / kFBN));
-  fp8_gemm_kernel<<<std::min(tiles, num_sms()), kFThreads, kFSmem, stream()>>>(
-      ma, mb, sa.data_ptr<float>(), sb.data_ptr<float>(), (__nv_bfloat16*)c.data_ptr(), (int)M, (int)N, (int)K,
-      err.data_ptr<int>());
-  return c;
+#undef FP8GO
+  return out;
+}
+
+// W8A8 rollout entry point: E4M3 activations (1x128) x E4M3 weights (128x128) -> bf16
+torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch::Tensor sb, torch::Tensor err) {
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && b.scalar_type() == at::kFloat8_e4m3fn, "fp8_gemm: e4m3");
+  return fp8_gemm_ex(a, sa, b, sb, c10::nullopt, false, err);
 }
 
 }  // namespace lrl

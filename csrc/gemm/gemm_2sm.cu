@@ -12,7 +12,7 @@
 //
 // A cluster of two CTAs on the two SMs of a TPC computes one 256 x BN output
 // tile: each CTA stages its own 128 rows of A and BN/2 rows of B (this GPU's
-// memory, plain TMA, no multicast) and the even CTA issues one 256 x BN x 16
+// memory, plain single-destination TMA) and the even CTA issues one 256 x BN x 16
 // MMA per K slice that reads both CTAs' shared memory and writes each CTA's
 // TMEM with its 128 accumulator rows.  Per SM and 64-wide K step that is
 // 32 KB of operands for 2 x 128 x 256 x 64 FLOPs, half the L2 traffic of a
@@ -24,10 +24,19 @@
 //   warp 1     allocates TMEM (pair-wide, two accumulator buffers); in the
 //              even CTA one lane issues the MMAs and commits each stage back
 //              to both producers and each finished tile to both epilogues
-//   warps 2-5  epilogue: tcgen05.ld of this CTA's 128 rows, then bf16 / fp32
-//              stores or an fp32 read-add-write (gradient accumulation)
+//   warps 2-5  epilogue: tcgen05.ld of this CTA's 128 rows (32 per warp),
+//              staged per 32 x 128-byte chunk in 128-byte-swizzled shared
+//              memory and written by a TMA bulk store -- or, for gradient
+//              accumulation, a TMA bulk reduce-add of fp32 into C performed
+//              in L2 (no read-modify-write by the SM).  Each warp double-
+//              buffers its staging chunk; TMEM is released as soon as the
+//              tile's last columns are in registers.
 // Two TMEM buffers let the epilogue of tile i overlap the MMAs of tile i+1.
+// Rows / columns of C whose stride is not 16-byte aligned fall back to
+// per-thread stores.
 // Every mbarrier wait is bounded and reports a status word instead of hanging.
+#include <mutex>
+
 #include "../common.cuh"
 #include "tc2sm.cuh"
 #include "tc_gemm.cuh"
@@ -45,6 +54,9 @@ constexpr int kPairM = 256, kBK = 64, kGroupM = 8, kThreads = 192;
 
 enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3 };
 
+constexpr int kStageChunk = 32 * 128;               // one warp's 32 rows x 128 bytes of C
+constexpr int kStagingBytes = 4 * 2 * kStageChunk;  // 4 epilogue warps, double-buffered
+
 template <int BN>
 struct Pair {
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 rows of A
@@ -52,7 +64,7 @@ struct Pair {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = BN == 256 ? 6 : 8;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmem = kStages * kStageBytes + kStagingBytes + 1024 + 256;
 };
 
 __device__ __forceinline__ void pair_tile(int t, int num_m, int num_n, int& mb, int& nb) {
@@ -118,12 +130,14 @@ __device__ __forceinline__ void store32(void* C, int row, int col, int N, int64_
 
 template <int BN, bool AMN, bool BMN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* C, int M,
-                   int N, int K, int64_t ldc, int vec, int* err_out) {
+    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, void* C, int M, int N, int K, int64_t ldc, int vec,
+                   int tma_c, int* err_out) {
   using G = Pair<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kStages * G::kStageBytes);
+  uint8_t* staging = smem + G::kStages * G::kStageBytes;   // 1024-aligned (stage sizes are multiples of 1 KB)
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes);
   uint64_t* empty = full + G::kStages;
   uint64_t* tfull = empty + G::kStages;
   uint64_t* tempty = tfull + 2;
@@ -156,6 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (tma_c) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -258,25 +273,82 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     const uint32_t tempty0 = map_to_rank(smem_addr(&tempty[0]), 0);
-    int tc = 0;
+    // bf16: 64 columns (128 B) per staged chunk; fp32: 32 columns
+    constexpr int kCols = (EPI == kE2BF16 || EPI == kE2None) ? 64 : 32;
+    constexpr int kChunks = BN / kCols;
+    uint8_t* mybuf = staging + (warp - 2) * 2 * kStageChunk;
+    int tc = 0, nst = 0;
     for (int t = cid; t < tiles; t += ncl, ++tc) {
       int mb, nb;
       pair_tile(t, num_m, num_n, mb, nb);
       const int buf = tc & 1;
       if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue)) break;
       tc_fence_after();
-      const int row = mb * kPairM + rank * 128 + q * 32 + lane;
+      const int row0 = mb * kPairM + rank * 128 + q * 32;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, v);
-        const int col = nb * BN + c * 32;
-        if (row < M && col < N) store32<EPI>(C, row, col, N, ldc, vec != 0, v);
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32_nowait(tbase + c * kCols, r0);
+        if constexpr (kCols == 64) tmem_ld32_nowait(tbase + c * kCols + 32, r1);
+        tmem_ld_wait();
+        if (c == kChunks - 1) {
+          // every accumulator column of this tile is in registers: give the
+          // TMEM buffer back to the MMA warp before the stores
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
+        }
+        const int col0 = nb * BN + c * kCols;
+        if constexpr (EPI == kE2None) {
+          if (__uint_as_float(r0[0]) == 1.2345e-30f && __uint_as_float(r1[31]) == 1.2345e-30f)
+            *reinterpret_cast<float*>(C) = 0.f;
+        } else if (tma_c) {
+          // stage 32 rows x 128 B in this warp's buffer (128-byte swizzle:
+          // 16-byte unit j of row r sits at unit j ^ (r & 7)), then one bulk store
+          uint8_t* sb = mybuf + (nst & 1) * kStageChunk;
+          if (lane == 0) bulk_wait_read<1>();   // the store that used this buffer has read it
+          __syncwarp();
+          uint4* rowp = reinterpret_cast<uint4*>(sb + lane * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 u;
+            if constexpr (kCols == 64) {
+              const uint32_t* src = (j < 4) ? &r0[8 * j] : &r1[8 * (j - 4)];
+              __nv_bfloat162 h0 = __floats2bfloat162_rn(__uint_as_float(src[0]), __uint_as_float(src[1]));
+              __nv_bfloat162 h1 = __floats2bfloat162_rn(__uint_as_float(src[2]), __uint_as_float(src[3]));
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(__uint_as_float(src[4]), __uint_as_float(src[5]));
+              __nv_bfloat162 h3 = __floats2bfloat162_rn(__uint_as_float(src[6]), __uint_as_float(src[7]));
+              u = make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                             *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+            } else {
+              u = make_uint4(r0[4 * j], r0[4 * j + 1], r0[4 * j + 2], r0[4 * j + 3]);
+            }
+            rowp[j ^ (lane & 7)] = u;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < M && col0 < N) {
+            if constexpr (EPI == kE2AccF32) tma_reduce_add_2d(&tmC, sb, col0, row0);
+            else tma_store_2d(&tmC, sb, col0, row0);
+            bulk_commit();
+          }
+          ++nst;
+        } else {
+          const int row = row0 + lane;
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r0[i]);
+          if (row < M && col0 < N) store32<EPI>(C, row, col0, N, ldc, vec != 0, v);
+          if constexpr (kCols == 64) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r1[i]);
+            if (row < M && col0 + 32 < N) store32<EPI>(C, row, col0 + 32, N, ldc, vec != 0, v);
+          }
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
     }
+    if (lane == 0) bulk_wait_all();   // stores complete before the CTA exits
   }
   __syncthreads();
   cluster_sync();
@@ -288,15 +360,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *err != kErrNone) atomicExch(err_out, *err);
 }
 
-torch::Tensor& err_word() {
-  static thread_local torch::Tensor t;
-  if (!t.defined() || t.device().index() != c10::cuda::current_device())
-    t = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, c10::cuda::current_device()));
-  return t;
+// One status word per device, shared by every host thread (the autograd
+// engine runs backward GEMMs on its own thread).
+int* err_word() {
+  static int* words[64] = {};
+  static std::mutex mu;
+  const int dev = c10::cuda::current_device();
+  TORCH_CHECK(dev >= 0 && dev < 64, "gemm2sm: device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!words[dev]) {
+    C10_CUDA_CHECK(cudaMalloc(&words[dev], sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(words[dev], 0, sizeof(int)));
+  }
+  return words[dev];
 }
 
 template <int BN, bool AMN, bool BMN, int EPI>
-void launch2(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N, int K, int64_t ldc, bool vec) {
+void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, void* c, int M, int N, int K,
+             int64_t ldc, bool vec, bool tma_c) {
   auto kern = gemm2sm_kernel<BN, AMN, BMN, EPI>;
   static int max_clusters = 0;
   cudaLaunchConfig_t cfg = {};
@@ -322,16 +403,42 @@ void launch2(const CUtensorMap& ma, const CUtensorMap& mb, void* c, int M, int N
   }
   const int tiles = ((M + kPairM - 1) / kPairM) * ((N + BN - 1) / BN);
   cfg.gridDim = dim3(2 * std::min(tiles, max_clusters));
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, c, M, N, K, ldc, (int)vec, err_word().data_ptr<int>()));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, err_word()));
 }
 
 }  // namespace
 
 int64_t gemm2sm_status() {
-  auto& t = err_word();
-  const int v = t.item<int>();
-  t.zero_();
+  int* w = err_word();
+  int v = 0;
+  C10_CUDA_CHECK(cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, stream()));
+  C10_CUDA_CHECK(cudaStreamSynchronize(stream()));
+  C10_CUDA_CHECK(cudaMemsetAsync(w, 0, sizeof(int), stream()));
   return v;
+}
+
+// TMA map of the output C [M, N] (row stride ldc elements): 32-row boxes of
+// 128 bytes with the 128-byte swizzle the epilogue stages with.
+static bool make_c_map(CUtensorMap* m, void* ptr, int64_t M, int64_t N, int64_t ldc, int esz) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ldc * esz) % 16 || (N * esz) % 16) return false;
+  typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && p,
+                "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ldc * esz)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides,
+            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // C = A . B^T on CTA pairs.  `a` is A [M, K] (a_mn = false) or A^T [K, M]
@@ -382,7 +489,10 @@ torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c1
   const int esz = (epi == kE2F32 || epi == kE2AccF32) ? 4 : 2;
   const bool vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0) && ((ldc * esz) % 16 == 0);
   void* cp = out.data_ptr();
-#define GO(BNV, AM, BM, E) launch2<BNV, AM, BM, E>(ma, mb, cp, (int)M, (int)N, (int)K, ldc, vec)
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  const bool tma_c = epi != kE2None && make_c_map(&mc, cp, M, N, ldc, esz);
+#define GO(BNV, AM, BM, E) launch2<BNV, AM, BM, E>(ma, mb, mc, cp, (int)M, (int)N, (int)K, ldc, vec, tma_c)
 #define EPIS(BNV, AM, BM)                                             \
   do {                                                                \
     if (epi == kE2BF16) GO(BNV, AM, BM, kE2BF16);                     \

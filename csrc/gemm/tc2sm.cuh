@@ -3,8 +3,8 @@
 // arrivals, pair-wide TMEM allocation, the 2-SM MMA and its commit, and the
 // TMA tile load whose completion is counted on the pair leader's mbarrier.
 // Written from the PTX ISA chapters on tcgen05, cp.async.bulk.tensor,
-// mbarrier and clusters.  No load here uses cluster multicast: each CTA
-// loads its own half of every operand tile from this GPU's memory.
+// mbarrier and clusters.  Every CTA fetches its own half of each operand
+// tile from this GPU's memory with a plain (single-destination) TMA copy.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -87,8 +87,9 @@ __device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
-// Arrive on the mbarrier at the same shared offset in every CTA of `mask`
-// once all tcgen05 ops issued so far by this thread have completed.
+// MMA completion signal: arrive on the mbarrier at the same shared offset in
+// every CTA of `mask` once all tcgen05 ops issued so far by this thread have
+// completed (a tcgen05.commit, which moves no data).
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t mask) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
@@ -128,6 +129,54 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_major(int M, int N, bool a
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
+
+
+// ---- epilogue: TMA bulk stores from shared memory --------------------------------
+// tcgen05.ld without the wait (issue several, then one tcgen05.wait::ld)
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// generic-proxy shared-memory writes -> visible to the TMA (async proxy)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// 2-D tile store shared -> global (rows / columns outside the tensor are
+// clipped by the TMA unit)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(map),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// 2-D tile element-wise add into global memory (fp32), performed in L2
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"(
+                   map),
+               "r"(smem_addr(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+
+// at most N of this thread's bulk groups still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+
+// all of this thread's bulk groups complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
 
 }  // namespace tc2
 }  // namespace lrl

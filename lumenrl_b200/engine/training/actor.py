@@ -152,6 +152,8 @@ class ActorEngine:
                 t_fwd_bwd += time.perf_counter() - t0
                 lr = self.sched.current if self.sched else None
                 opt_stats = self.opt.step(lr)
+                if self.model.fp8_training is not None:
+                    self.model.fp8_training.weights_updated()   # quantised weights are stale now
                 for k in opt_t:
                     opt_t[k] += self.opt.last_timing.get(k, 0.0)
                 if self.sched:

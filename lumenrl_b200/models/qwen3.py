@@ -150,6 +150,7 @@ class Qwen3Model(nn.Module):
         self.recompute_layers: set[int] = set()   # per-layer activation recomputation (memory budget)
         self.routing_replay = None   # set by moe.r3 for rollout routing replay
         self.aux_losses: list[Tensor] = []
+        self.fp8_training = None     # quant.fp8.FP8TrainingManager: FP8 decoder linears when set
 
     # -- parameter access ------------------------------------------------------
     def p(self, name: str) -> nn.Parameter:
@@ -184,16 +185,23 @@ class Qwen3Model(nn.Module):
                 p.fill_(1.0)
 
     # -- forward ---------------------------------------------------------------
+    def _linear(self, name: str, x: Tensor) -> Tensor:
+        w = self._params[name]
+        f8 = self.fp8_training
+        if f8 is not None and f8.applies_to(name):
+            return f8.linear(name, x, w)
+        return ops.linear(x, w)
+
     def _attention_block(self, i: int, x: Tensor, positions: Tensor, cu: Tensor, max_len: int) -> Tensor:
         a = self.args
         P = self._params
-        qkv = ops.linear(x, P[f"layers.{i}.wqkv"])
+        qkv = self._linear(f"layers.{i}.wqkv", x)
         qn = P.get(f"layers.{i}.q_norm")
         kn = P.get(f"layers.{i}.k_norm")
         q, k, v = ops.qk_norm_rope(qkv, qn, kn, positions, self.inv_freq, a.num_heads, a.num_kv_heads, a.head_dim,
                                    a.rms_norm_eps)
         o = ops.attention_varlen(q, k, v, cu, max_len, causal=True, scale=1.0 / math.sqrt(a.head_dim))
-        return ops.linear(o.reshape(o.shape[0], -1), P[f"layers.{i}.wo"])
+        return self._linear(f"layers.{i}.wo", o.reshape(o.shape[0], -1))
 
     def _mlp_block(self, i: int, h: Tensor) -> Tensor:
         P = self._params
@@ -203,7 +211,7 @@ class Qwen3Model(nn.Module):
             if aux is not None:
                 self.aux_losses.append(aux)
             return out
-        return ops.linear(ops.swiglu(ops.linear(h, P[f"layers.{i}.w13"])), P[f"layers.{i}.w2"])
+        return self._linear(f"layers.{i}.w2", ops.swiglu(self._linear(f"layers.{i}.w13", h)))
 
     def _layer_fused(self, i: int, x: Tensor, pending: Optional[Tensor], positions: Tensor, cu: Tensor,
                      max_len: int) -> tuple[Tensor, Tensor]:
@@ -232,7 +240,7 @@ class Qwen3Model(nn.Module):
         self.aux_losses = []
         x = embed(ids, self._params["embed"])
         pending: Optional[Tensor] = None   # MLP output not yet added to the stream
-        taps: list[Tensor] = []
+        tapped: dict[int, Tensor] = {}
         want = set(output_hidden_layers or [])
         for i in range(self.args.num_layers):
             if (self.gradient_checkpointing or i in self.recompute_layers) and torch.is_grad_enabled():
@@ -241,10 +249,10 @@ class Qwen3Model(nn.Module):
             else:
                 x, pending = self._layer_fused(i, x, pending, positions, cu_seqlens, max_seqlen)
             if i in want:
-                taps.append(x + pending)
+                tapped[i] = x + pending
         h, _ = ops.add_rmsnorm(x, pending, self._params["norm"], self.args.rms_norm_eps)
         if output_hidden_layers is not None:
-            return h, taps
+            return h, [tapped[i] for i in output_hidden_layers]   # requested order, repeats allowed
         return h
 
     def activation_bytes_per_token_layer(self) -> int:

@@ -53,7 +53,7 @@ def _accum_main_grad(w: Tensor, g: Tensor) -> None:
 # Training GEMMs: "own" runs the CTA-pair tcgen05 kernel (csrc/gemm/gemm_2sm.cu)
 # for the forward, dgrad and wgrad of every linear; "cublas" is the library
 # path kept for A/B measurements (LRL_TRAIN_GEMM=cublas).
-TRAIN_GEMM = os.environ.get("LRL_TRAIN_GEMM", "own")
+TRAIN_GEMM = os.environ.get("LRL_TRAIN_GEMM", "cublas")
 
 
 def _pair_ok(*ts) -> bool:

@@ -208,25 +208,158 @@ class FP8KVCacheQuantizer:
         cache.k_scale, cache.v_scale = self.scales()
 
 
+def quant_t_1x128(x: Tensor, dtype=E4M3, kb_major: bool = False) -> tuple[Tensor, Tensor]:
+    """x [R, C] -> (x^T quantised 1x128 along R: [C, Rpad] with Rpad = R
+    rounded up to 128 (zero rows), scales [C, Rpad/128] or, ``kb_major``,
+    [Rpad/128, Cpad] with Cpad = C rounded up to 128)."""
+    if x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2:
+        from lumenrl_b200.ops.ext import ext
+        return tuple(ext().quant_t_1x128(x.contiguous(), dtype == E5M2, kb_major))
+    R, C = x.shape
+    Rpad = (R + 127) // 128 * 128
+    xt = torch.nn.functional.pad(x.float().t(), (0, Rpad - R))
+    q, s = quant_1x128_ref(xt, dtype)
+    if kb_major:
+        Cpad = (C + 127) // 128 * 128
+        s = torch.nn.functional.pad(s.t(), (0, Cpad - C)).contiguous()
+    return q, s
+
+
+_FP8_ERR: dict = {}
+
+
+def _err_word(dev) -> Tensor:
+    if dev not in _FP8_ERR:
+        _FP8_ERR[dev] = torch.zeros(1, dtype=torch.int32, device=dev)
+    return _FP8_ERR[dev]
+
+
+def fp8_matmul(qa: Tensor, sa: Tensor, qb: Tensor, sb: Tensor, out: Optional[Tensor] = None,
+               b_row: bool = False) -> Tensor:
+    """sum_kb (qa[:, kb] . qb[:, kb]^T) * sa[:, kb] * sb(kb): block-scaled
+    FP8 GEMM (E4M3 / E5M2 in any combination).  ``b_row``: ``sb`` holds one
+    scale per row of ``qb`` and K block, K-block-major ([K/128, Npad]); else
+    128x128 blocks ([N/128, K/128]).  Returns bf16, or accumulates into the
+    fp32 ``out``."""
+    if qa.is_cuda:
+        from lumenrl_b200.ops.ext import ext
+        return ext().fp8_gemm_ex(qa, sa.contiguous(), qb, sb.contiguous(), _err_word(qa.device), out, b_row)
+    a = dequant_1x128(qa, sa)
+    if b_row:
+        N = qb.shape[0]
+        b = dequant_1x128(qb, sb[:, :N].t())
+    else:
+        b = dequant_128x128(qb, sb)
+    r = a @ b.t()
+    if out is not None:
+        out += r
+        return out
+    return r.to(torch.bfloat16)
+
+
+def fp8_gemm_status() -> int:
+    v = 0
+    for t in _FP8_ERR.values():
+        v = max(v, int(t.item()))
+        t.zero_()
+    return v
+
+
+class _FP8Linear(torch.autograd.Function):
+    """y = x W^T with E4M3 forward operands; E5M2 gradients in dgrad and
+    wgrad; the weight gradient accumulates in fp32 into W.main_grad."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, w: Tensor, w_handle: Tensor, mgr: "FP8TrainingManager", name: str):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        qx, sx = quant_act_1x128(x2, E4M3)
+        qw, sw = mgr.forward_weight(name, w)
+        y = fp8_matmul(qx, sx, qw, sw)
+        ctx.save_for_backward(x2, w)
+        ctx.meta = (w_handle, mgr, name, x.shape)
+        return y.to(x.dtype).view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):
+        x2, w = ctx.saved_tensors
+        w_handle, mgr, name, xshape = ctx.meta
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        if dy2.dtype != torch.bfloat16 and dy2.is_cuda:
+            dy2 = dy2.to(torch.bfloat16)
+        # dgrad: dx = dy . W   (E5M2 gradient x E4M3 transposed weight)
+        qdy, sdy = quant_act_1x128(dy2, E5M2)
+        qwt, swt = mgr.backward_weight(name, w)
+        dx = fp8_matmul(qdy, sdy, qwt, swt).to(x2.dtype).view(xshape)
+        # wgrad: dW += dy^T . x, contraction over tokens: both operands
+        # quantised 1x128 along the token dimension
+        qdt, sdt = quant_t_1x128(dy2, E5M2)
+        qxt, sxt = quant_t_1x128(x2.to(dy2.dtype) if not x2.is_cuda else x2, E4M3, kb_major=True)
+        mg = getattr(w_handle, "main_grad", None)
+        if mg is not None:
+            fp8_matmul(qdt, sdt, qxt, sxt, out=mg, b_row=True)
+        else:
+            g = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+            fp8_matmul(qdt, sdt, qxt, sxt, out=g, b_row=True)
+            w_handle.grad = g.to(w_handle.dtype) if w_handle.grad is None else w_handle.grad + g.to(w_handle.dtype)
+        return dx, None, None, None, None
+
+
 class FP8TrainingManager:
-    """Hybrid FP8 training: forward GEMM operands in E4M3 (1x128 activations,
-    128x128 weights), gradients in E5M2, bf16 master weights.  Enabled by
-    ``quantization.training.fp8``; the lm_head stays bf16 as in the reference."""
+    """Hybrid FP8 training (reference ``lumenrl/quantization/fp8_training.py:41-134``
+    and the Lumen recipe of ``engine/training/fsdp_backend.py:251-366``).
+
+    Every decoder linear (qkv, o, gate/up, down) runs three block-scaled FP8
+    GEMMs on the tcgen05 tensor cores (``csrc/gemm/fp8_gemm.cu``):
+
+    * forward: E4M3 activations (1x128 scales) x E4M3 weights (128x128);
+    * dgrad: E5M2 output gradient (1x128) x E4M3 transposed weight (128x128);
+    * wgrad: E5M2 gradient^T x E4M3 activations^T, both quantised 1x128 along
+      the token dimension, accumulated in fp32 into ``main_grad``.
+
+    Master weights and the optimizer stay fp32 / bf16 as before; the LM head,
+    embeddings and norms stay bf16.  Quantised weights (and their transposes)
+    are computed once per optimizer step and reused by every micro-batch;
+    ``weights_updated()`` drops them after the step."""
+
+    TARGETS = ("wqkv", "wo", "w13", "w2")
 
     def __init__(self, config: FP8Config) -> None:
         self.config = config
         self.enabled = config.is_fp8_enabled()
+        self._fwd: dict[str, tuple[Tensor, Tensor]] = {}
+        self._bwd: dict[str, tuple[Tensor, Tensor]] = {}
 
-    def fake_quant_forward(self, x: Tensor, w: Tensor) -> tuple[Tensor, Tensor]:
-        qx, sx = quant_act_1x128(x.reshape(-1, x.shape[-1]).contiguous().to(torch.bfloat16))
-        qw, sw = quant_weight_128x128(w.to(torch.bfloat16))
-        return (dequant_1x128(qx, sx).reshape(x.shape).to(x.dtype), dequant_128x128(qw, sw).to(w.dtype))
+    def applies_to(self, name: str) -> bool:
+        return self.enabled and name.rsplit(".", 1)[-1] in self.TARGETS
+
+    def attach(self, model) -> None:
+        model.fp8_training = self if self.enabled else None
+
+    def weights_updated(self) -> None:
+        self._fwd.clear()
+        self._bwd.clear()
+
+    def forward_weight(self, name: str, w: Tensor) -> tuple[Tensor, Tensor]:
+        if name not in self._fwd:
+            self._fwd[name] = quant_weight_128x128(w, E4M3)
+        return self._fwd[name]
+
+    def backward_weight(self, name: str, w: Tensor) -> tuple[Tensor, Tensor]:
+        if name not in self._bwd:
+            qw, sw = self.forward_weight(name, w)
+            # the 128x128 blocks of W^T are those of W transposed: same bytes, same scales
+            self._bwd[name] = (qw.t().contiguous(), sw.t().contiguous())
+        return self._bwd[name]
+
+    def linear(self, name: str, x: Tensor, w: Tensor) -> Tensor:
+        if torch.is_grad_enabled() and w.requires_grad:
+            return _FP8Linear.apply(x, w.detach(), w, self, name)
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        qx, sx = quant_act_1x128(x2, E4M3)
+        qw, sw = self.forward_weight(name, w.detach())
+        return fp8_matmul(qx, sx, qw, sw).to(x.dtype).view(*x.shape[:-1], w.shape[0])
 
     def reset_fp8_state(self, model=None) -> None:
-        """Per-step reset hook.  Scales here are computed from each tensor's
-        current blocks (no amax history), so there is no state to clear."""
-        return None
-
-    def fake_quant_grad(self, g: Tensor) -> Tensor:
-        qg, sg = quant_act_1x128(g.reshape(-1, g.shape[-1]).contiguous().to(torch.bfloat16), E5M2)
-        return dequant_1x128(qg, sg).reshape(g.shape).to(g.dtype)
+        """Per-step hook of the reference API: quantised weights are dropped;
+        scales come from each tensor's current blocks (no amax history)."""
+        self.weights_updated()

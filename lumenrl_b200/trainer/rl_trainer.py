@@ -99,6 +99,12 @@ class RLTrainer:
             gradient_checkpointing=self.spec.gradient_checkpointing, total_steps=c.num_training_steps,
             warmup_steps=p.lr_warmup_steps, lr_style=p.lr_decay_style,
             min_lr_ratio=(p.min_lr / p.learning_rate if p.learning_rate else 0.0))
+        self.fp8_training = None
+        if c.quantization.training.fp8:
+            # hybrid FP8 training: E4M3 forward, E5M2 gradients, bf16/fp32 master
+            from lumenrl_b200.quant.fp8 import FP8Config, FP8TrainingManager
+            self.fp8_training = FP8TrainingManager(FP8Config.from_config(c.quantization))
+            self.fp8_training.attach(self.actor.model)
         self.ref = None
         kl_coeff = float(getattr(self.algo_cfg, "kl_coeff", 0.0))
         self.kl_ctrl = None

@@ -21,4 +21,6 @@ def cuda():
         pytest.skip("no CUDA device")
     from lumenrl_b200.ops.ext import ext
     ext()  # fail loudly if the extension is missing on a GPU box
+    if os.environ.get("LRL_SEGV_BACKTRACE"):
+        ext().install_segv_backtrace()
     return torch.device("cuda", 0)

@@ -11,7 +11,7 @@ from lumenrl_b200.ops.ext import ext
 pytestmark = pytest.mark.gpu
 
 SHAPES = [(256, 256, 64), (512, 768, 1024), (300, 520, 4096), (1000, 1032, 136), (2048, 4096, 512),
-          (64, 6144, 4096), (4096, 4096, 4096)]
+          (64, 6144, 4096), (4096, 4096, 4096), (77, 1001, 128)]   # the last: C rows not 16-byte aligned
 
 
 def _operands(M, N, K, a_mn, b_mn, dev):
@@ -63,6 +63,24 @@ def test_gemm2sm_strided_rows(cuda):
     assert ext().gemm2sm_status() == 0
     ref = a.float() @ b.float().t()
     assert (c.float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_pair_gemm_from_another_thread(cuda):
+    """The autograd engine runs backward GEMMs on its own thread."""
+    import threading
+    A, B, a, b = _operands(512, 1024, 1024, False, True, cuda)
+    res = {}
+
+    def work():
+        torch.cuda.set_device(cuda)
+        res["c"] = ext().gemm2sm(a, False, b, True, None, 0, 0)
+        torch.cuda.synchronize()
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert ext().gemm2sm_status() == 0
+    ref = A.float() @ B.float().t()
+    assert (res["c"].float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
 
 
 def test_linear_autograd_on_pair_gemm(cuda):

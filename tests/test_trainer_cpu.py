@@ -140,3 +140,30 @@ def test_kl_in_reward_uses_reference_and_controller_cpu():
         assert "actor/reward_kl_penalty" in m and "actor/reward_kl_penalty_coeff" in m
     # the policy moves away from the frozen reference, so later steps see a KL
     assert hist[-1]["actor/reward_kl_penalty"] != 0.0
+
+
+def test_dapo_fp8_recipe_runs_cpu():
+    """Config 2 plumbing: W8A8 FP8 rollout + hybrid FP8 training linears."""
+    torch.manual_seed(0)
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["algorithm.name=dapo", "algorithm.dapo.num_generations=4",
+                                   "quantization.training.fp8=hybrid", "quantization.rollout.precision=fp8",
+                                   "quantization.rollout_correction.rollout_is=token",
+                                   "quantization.rollout_correction.rollout_is_threshold=2.0", "num_training_steps=1"])
+    spec = RLRunSpec(prompts_per_step=4, prompt_len=16, max_new_tokens=16, reward="contains_token",
+                     eos_token_id=None)
+    tr = RLTrainer(cfg, tiny_llama(), spec, ParallelState()).setup()
+    assert tr.actor.model.fp8_training is tr.fp8_training and tr.fp8_training.enabled
+    assert tr.rollout.runner.fp8 is not None
+    calls = {"n": 0}
+    orig = tr.fp8_training.linear
+
+    def spy(*a, **k):
+        calls["n"] += 1
+        return orig(*a, **k)
+    tr.fp8_training.linear = spy
+    hist = tr.train()
+    assert calls["n"] > 0
+    for m in hist:
+        assert m["actor/grad_norm"] == m["actor/grad_norm"]
+        assert "rollout_corr/kl" in m

@@ -59,7 +59,7 @@ class ActorEngine:
         numel = padded_numel(args, state.world_size if trainable else 1)
         if comm is None and trainable and state.world_size > 1 and self.device.type == "cuda" and fused_comm:
             from lumenrl_b200.parallel.symm import NVLinkOptimizerComm
-            comm = NVLinkOptimizerComm(numel, state.rank, state.world_size, dtype)
+            comm = NVLinkOptimizerComm(numel, state.rank, state.world_size, dtype, group=state.dp_group)
         if comm is not None and hasattr(comm, "weights"):
             flat = comm.weights.tensor      # resident weights live in NVLink-mapped memory
         else:
@@ -75,7 +75,8 @@ class ActorEngine:
         self.sched: Optional[LRSchedule] = None
         if trainable:
             self.opt = ShardedFlatAdamW(flat, state.world_size, state.rank, lr=lr, betas=betas, eps=eps,
-                                        weight_decay=weight_decay, max_grad_norm=max_grad_norm, comm=comm)
+                                        weight_decay=weight_decay, max_grad_norm=max_grad_norm, comm=comm,
+                                        group=state.dp_group)
             self.model.attach_main_grad(self.opt.grad)
             self.sched = LRSchedule(lr, total_steps, warmup_steps, lr_style, min_lr_ratio)
 

@@ -36,7 +36,7 @@ from lumenrl_b200.ops import reference as ref
 class ShardedFlatAdamW:
     def __init__(self, w16: Tensor, world: int = 1, rank: int = 0, lr: float = 1e-6, betas=(0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 0.01, max_grad_norm: float = 1.0,
-                 comm=None, grad_dtype: torch.dtype = torch.float32) -> None:
+                 comm=None, grad_dtype: torch.dtype = torch.float32, group=None) -> None:
         n = w16.numel()
         if n % (world * 128):
             raise ValueError("flat buffer must be padded to a multiple of world * 128 elements")
@@ -56,6 +56,7 @@ class ShardedFlatAdamW:
         self.max_grad_norm = max_grad_norm
         self.step_count = 0
         self.comm = comm
+        self.group = group          # process group of the data-parallel replicas (None = world)
         self.last_timing: dict[str, float] = {}
 
     # -- collectives --------------------------------------------------------------
@@ -65,9 +66,9 @@ class ShardedFlatAdamW:
         if self.comm is not None and hasattr(self.comm, "reduce_scatter_sum"):
             self.comm.reduce_scatter_sum(self.grad, self.grad_shard)
         elif self.grad.is_cuda:
-            dist.reduce_scatter_tensor(self.grad_shard, self.grad)
+            dist.reduce_scatter_tensor(self.grad_shard, self.grad, group=self.group)
         else:  # gloo has no reduce-scatter
-            dist.all_reduce(self.grad)
+            dist.all_reduce(self.grad, group=self.group)
             self.grad_shard.copy_(self.grad[self.lo: self.hi])
 
     def _all_gather(self) -> None:
@@ -76,10 +77,10 @@ class ShardedFlatAdamW:
         if self.comm is not None and hasattr(self.comm, "all_gather"):
             self.comm.all_gather(self.w16, self.lo, self.hi)
         elif self.w16.is_cuda:
-            dist.all_gather_into_tensor(self.w16, self.w16[self.lo: self.hi].clone())
+            dist.all_gather_into_tensor(self.w16, self.w16[self.lo: self.hi].clone(), group=self.group)
         else:
             parts = list(self.w16.view(self.world, -1).unbind(0))
-            dist.all_gather(parts, self.w16[self.lo: self.hi].clone())
+            dist.all_gather(parts, self.w16[self.lo: self.hi].clone(), group=self.group)
 
     def _global_norm(self) -> float:
         g = self.grad_shard
@@ -89,7 +90,7 @@ class ShardedFlatAdamW:
         else:
             sq = (g.double() ** 2).sum().float().reshape(1)
         if self.world > 1:
-            dist.all_reduce(sq)
+            dist.all_reduce(sq, group=self.group)
         return float(sq.sqrt().item())
 
     # -- update -------------------------------------------------------------------

@@ -66,16 +66,33 @@ def init_distributed(backend: Optional[str] = None, timeout_s: float = 600.0, de
     return _STATE
 
 
+def set_state(st: ParallelState) -> ParallelState:
+    """Make ``st`` the process's state: the scalar collectives below then run
+    on ``st.dp_group`` (a sub-group, e.g. the trainer ranks of a separated
+    trainer / rollout layout)."""
+    global _STATE
+    _STATE = st
+    return st
+
+
+def sub_state(ranks: list[int], group) -> ParallelState:
+    """State of this process inside ``group`` (built over global ``ranks``):
+    group-local rank and size, same device."""
+    me = dist.get_rank()
+    return ParallelState(world_size=len(ranks), rank=ranks.index(me), local_rank=_STATE.local_rank,
+                         device=_STATE.device, dp_group=group)
+
+
 def barrier() -> None:
     if dist.is_initialized():
-        dist.barrier()
+        dist.barrier(group=_STATE.dp_group)
 
 
 def all_reduce_max(x: float) -> float:
     if not dist.is_initialized():
         return x
     t = torch.tensor([x], dtype=torch.float64, device=_STATE.device if _STATE.device.type == "cuda" else "cpu")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_STATE.dp_group)
     return float(t.item())
 
 
@@ -83,7 +100,7 @@ def all_reduce_sum(x: float) -> float:
     if not dist.is_initialized():
         return x
     t = torch.tensor([x], dtype=torch.float64, device=_STATE.device if _STATE.device.type == "cuda" else "cpu")
-    dist.all_reduce(t)
+    dist.all_reduce(t, group=_STATE.dp_group)
     return float(t.item())
 
 

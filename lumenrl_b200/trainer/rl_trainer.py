@@ -86,6 +86,14 @@ class RLTrainer:
         if self.state is None:
             self.state = get_state() if get_state().world_size > 1 or get_state().device.type == "cuda" \
                 else init_distributed()
+        self._setup_training()
+        self._setup_rollout(self.actor.model, self.state.world_size)
+        return self
+
+    def _setup_training(self) -> None:
+        """Algorithm, actor (+ FP8 training, reference, critic), data and
+        rewards on ``self.state`` (the trainer's data-parallel group)."""
+        c = self.config
         st = self.state
         algo = c.algorithm.name.lower()
         self.algorithm_name = algo
@@ -123,22 +131,35 @@ class RLTrainer:
                                        max_grad_norm=cc.max_grad_norm, seed=c.seed + 1,
                                        gradient_checkpointing=self.spec.gradient_checkpointing,
                                        total_steps=c.num_training_steps)
-        vc = p.generation.vllm_cfg
+        self._setup_common()
+
+    def _setup_common(self) -> None:
+        c, st = self.config, self.state
+        if not hasattr(self, "algorithm_name"):
+            self.algorithm_name = c.algorithm.name.lower()
+            self.algo_cfg = getattr(c.algorithm, self.algorithm_name)
+            self.group = int(getattr(self.algo_cfg, "num_generations", 1) or 1)
+        vc = c.policy.generation.vllm_cfg
         self.temperature = float(vc.temperature)
         self.top_p = float(vc.top_p)
-        max_len = self.spec.prompt_len + self.spec.max_new_tokens
-        prompts_per_rank = max(1, self.spec.prompts_per_step // st.world_size)
-        self.prompts_per_rank = prompts_per_rank
-        kv_dtype = torch.float8_e4m3fn if str(vc.kv_cache_dtype).startswith("fp8") else torch.bfloat16
-        self.rollout = RolloutEngine(self.actor.model, max_num_seqs=prompts_per_rank * self.group,
-                                     max_model_len=max_len, kv_cache_bytes=self.spec.kv_cache_bytes,
-                                     use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype,
-                                     fp8_rollout=self._fp8_rollout_config(c))
         self.data = SyntheticPrompts(self.spec.prompt_len, self.spec.prompt_low, self.spec.prompt_high, c.seed)
         self.reward_fn = get_reward_fn(self.spec.reward)
         self.timer = PhaseTimer(st.device)
         self.io_bytes = {"h2d": 0, "d2h": 0}
-        return self
+
+    def _setup_rollout(self, model, rollout_ranks: int) -> None:
+        """Rollout engine over ``model`` (the trainer's own weights when
+        colocated); ``rollout_ranks`` split the step's prompts."""
+        c = self.config
+        vc = c.policy.generation.vllm_cfg
+        max_len = self.spec.prompt_len + self.spec.max_new_tokens
+        prompts_per_rank = max(1, self.spec.prompts_per_step // rollout_ranks)
+        self.prompts_per_rank = prompts_per_rank
+        kv_dtype = torch.float8_e4m3fn if str(vc.kv_cache_dtype).startswith("fp8") else torch.bfloat16
+        self.rollout = RolloutEngine(model, max_num_seqs=prompts_per_rank * self.group,
+                                     max_model_len=max_len, kv_cache_bytes=self.spec.kv_cache_bytes,
+                                     use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype,
+                                     fp8_rollout=self._fp8_rollout_config(c))
 
     @staticmethod
     def _fp8_rollout_config(c):
@@ -286,7 +307,7 @@ class RLTrainer:
                                              rows_per_micro=self.spec.rows_per_micro))
             self.timer.stop("critic")
         self.timer.start("weight_sync")
-        self.rollout.update_weights()
+        m.update(self._sync_weights())
         self.timer.stop("weight_sync")
         self.timer.stop("step")
         times = self.timer.collect()
@@ -327,6 +348,13 @@ class RLTrainer:
         for cb in self.callbacks:
             cb.on_step_end(self, m)
         return m
+
+    def _sync_weights(self) -> dict:
+        """Colocated: the engine reads the trainer's resident buffer (the
+        optimizer kernel already wrote the new weights there); only the FP8
+        rollout re-quantises.  Overridden by the separated trainer."""
+        self.rollout.update_weights()
+        return {}
 
     def train(self) -> list[dict]:
         for cb in self.callbacks:

@@ -83,9 +83,10 @@ def test_pair_gemm_from_another_thread(cuda):
     assert (res["c"].float() - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
 
 
-def test_linear_autograd_on_pair_gemm(cuda):
-    """ops.linear forward / dgrad / wgrad (main_grad accumulation) against
-    fp32 autograd of the same bf16 values."""
+def test_linear_autograd_on_pair_gemm(cuda, monkeypatch):
+    """ops.linear forward / dgrad / wgrad (main_grad accumulation) on the pair
+    GEMM against fp32 autograd of the same bf16 values."""
+    monkeypatch.setattr(ops, "TRAIN_GEMM", "own")
     torch.manual_seed(5)
     T, K, N = 1536, 4096, 1024
     x = torch.randn(T, K, device=cuda).to(torch.bfloat16).requires_grad_(True)

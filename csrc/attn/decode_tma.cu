@@ -413,6 +413,7 @@ CUtensorMap cache_map(const torch::Tensor& c) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0, "decode_tma: 16-byte aligned cache");
   const int64_t Hk = c.size(2), pages = c.size(0);
   CUtensorMap m;
+  bind_current_context();
   cuuint64_t dims[4] = {(cuuint64_t)kHD, (cuuint64_t)Hk, (cuuint64_t)kTile, (cuuint64_t)pages};
   cuuint64_t strides[3] = {(cuuint64_t)(kHD * 2), (cuuint64_t)(Hk * kHD * 2), (cuuint64_t)(kTile * Hk * kHD * 2)};
   cuuint32_t box[4] = {64, 1, (cuuint32_t)kTile, 1};
@@ -420,7 +421,7 @@ CUtensorMap cache_map(const torch::Tensor& c) {
   CUresult r = encode4()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, c.data_ptr(), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (kv cache) failed: ", (int)r);
+  LRL_CHECK_FMT(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (kv cache) failed (%d)", (int)r);
   return m;
 }
 

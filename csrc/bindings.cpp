@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 
 #include <execinfo.h>
+#include <fcntl.h>
 #include <signal.h>
 #include <unistd.h>
 
@@ -13,18 +14,24 @@
 // handler that was installed before (Python's faulthandler).
 namespace {
 struct sigaction g_prev_segv;
+int g_segv_fd = 2;
 void lrl_segv_handler(int sig, siginfo_t* info, void* uctx) {
   void* frames[64];
   const int n = backtrace(frames, 64);
   char head[160];
   const int len = snprintf(head, sizeof(head), "lumenrl_b200: signal %d, fault address %p; native stack:\n", sig,
                            info ? info->si_addr : nullptr);
-  if (len > 0) (void)!write(2, head, (size_t)len);
-  backtrace_symbols_fd(frames, n, 2);
+  if (len > 0) (void)!write(g_segv_fd, head, (size_t)len);
+  backtrace_symbols_fd(frames, n, g_segv_fd);
   sigaction(SIGSEGV, &g_prev_segv, nullptr);
   raise(sig);
 }
-void install_segv_backtrace() {
+// `path`: file the stack is appended to (test runners capture fd 2), "" = stderr
+void install_segv_backtrace(const std::string& path) {
+  if (!path.empty()) {
+    const int fd = open(path.c_str(), O_WRONLY | O_CREAT | O_APPEND, 0644);
+    if (fd >= 0) g_segv_fd = fd;
+  }
   struct sigaction sa = {};
   sa.sa_sigaction = lrl_segv_handler;
   sa.sa_flags = SA_SIGINFO;
@@ -90,6 +97,7 @@ torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits);
 torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> c,
                       int64_t epi, int64_t bn);
 int64_t gemm2sm_status();
+std::vector<torch::Tensor> gemm2sm_logprob(torch::Tensor h, torch::Tensor w, torch::Tensor targets, double inv_t);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
 void symm_close(int64_t ptr);
@@ -134,7 +142,7 @@ torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lumenrl_b200 sm_100a kernels";
-  m.def("install_segv_backtrace", &install_segv_backtrace);
+  m.def("install_segv_backtrace", &install_segv_backtrace, py::arg("path") = "");
   m.def("rmsnorm_fwd", &lrl::rmsnorm_fwd);
   m.def("add_rmsnorm_fwd", &lrl::add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &lrl::rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dw"),
@@ -178,6 +186,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2sm", &lrl::gemm2sm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0);
   m.def("gemm2sm_status", &lrl::gemm2sm_status);
+  m.def("gemm2sm_logprob", &lrl::gemm2sm_logprob);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);
   m.def("symm_close", &lrl::symm_close);

@@ -50,6 +50,26 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
+// Driver-API calls (cuTensorMapEncodeTiled) need a current context on the
+// calling thread.  Runtime calls bind the device's primary context lazily, but
+// a thread that has made none yet -- PyTorch's autograd worker thread, which
+// skips cudaSetDevice when the index already matches -- has none, and the
+// driver call fails.  cudaSetDevice makes the primary context current.
+inline void bind_current_context() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) (void)cudaSetDevice(dev);
+}
+
+// TORCH_CHECK without iostream formatting (snprintf into a fixed buffer)
+#define LRL_CHECK_FMT(cond, ...)                       \
+  do {                                                 \
+    if (!(cond)) {                                     \
+      char lrl_msg_[256];                              \
+      snprintf(lrl_msg_, sizeof(lrl_msg_), __VA_ARGS__); \
+      TORCH_CHECK(false, (const char*)lrl_msg_);       \
+    }                                                  \
+  } while (0)
+
 inline int num_sms() {
   static int n = 0;
   if (n == 0) {

@@ -256,6 +256,7 @@ CUtensorMap make_fp8_map(const void* ptr, int64_t rows, int64_t K, int64_t ld) {
     fn = reinterpret_cast<EncodeFn>(p);
   }
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 16 == 0, "fp8 TMA: 16-byte alignment");
+  bind_current_context();
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld};
@@ -264,7 +265,7 @@ CUtensorMap make_fp8_map(const void* ptr, int64_t rows, int64_t K, int64_t ld) {
   CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp8) failed: ", (int)r);
+  LRL_CHECK_FMT(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp8) failed (%d)", (int)r);
   return m;
 }
 

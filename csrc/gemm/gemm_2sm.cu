@@ -52,7 +52,19 @@ namespace {
 
 constexpr int kPairM = 256, kBK = 64, kGroupM = 8, kThreads = 192;
 
-enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3 };
+enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3, kE2LogProb = 4 };
+
+// Log-prob epilogue (the LM head of scoring and training): instead of writing
+// logits, each row of a 256-column tile is reduced to (max, sum exp(z - max),
+// sum exp(z - max) * z, target logit or -inf) with z = bf16(logit) * inv_t --
+// the bf16 rounding matches logits that were materialised in bf16 -- and the
+// four floats go to part[row * ntiles_n + tile_n]; a combine kernel merges
+// the tiles of a row.
+struct LogProbArgs {
+  const int64_t* targets;
+  float4* part;
+  float inv_t;
+};
 
 constexpr int kStageChunk = 32 * 128;               // one warp's 32 rows x 128 bytes of C
 constexpr int kStagingBytes = 4 * 2 * kStageChunk;  // 4 epilogue warps, double-buffered
@@ -132,7 +144,7 @@ template <int BN, bool AMN, bool BMN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, void* C, int M, int N, int K, int64_t ldc, int vec,
-                   int tma_c, int* err_out) {
+                   int tma_c, LogProbArgs lp, int* err_out) {
   using G = Pair<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -286,6 +298,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row0 = mb * kPairM + rank * 128 + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+      if constexpr (EPI == kE2LogProb) {
+        const int row = row0 + lane;
+        const int64_t tg = row < M ? lp.targets[row] : -1;
+        float m = -INFINITY, se = 0.f, sz = 0.f, zt = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r0[32];
+          tmem_ld32_nowait(tbase + c * 32, r0);
+          tmem_ld_wait();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + buf * 8);
+          }
+          const int col0 = nb * BN + c * 32;
+          float z[32];
+          float cm = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float zi = __bfloat162float(__float2bfloat16(__uint_as_float(r0[i]))) * lp.inv_t;
+            z[i] = (col0 + i < N) ? zi : -INFINITY;
+            cm = fmaxf(cm, z[i]);
+            if (col0 + i == tg) zt = zi;
+          }
+          if (cm > m) {
+            const float e = __expf(m - cm);   // 0 when m is -inf
+            se *= e;
+            sz *= e;
+            m = cm;
+          }
+          if (m != -INFINITY) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float e = __expf(z[i] - m);
+              se += e;
+              sz += (z[i] == -INFINITY) ? 0.f : e * z[i];
+            }
+          }
+        }
+        if (row < M) lp.part[(int64_t)row * num_n + nb] = make_float4(m, se, sz, zt);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c) {
         uint32_t r0[32], r1[32];
@@ -377,7 +431,7 @@ int* err_word() {
 
 template <int BN, bool AMN, bool BMN, int EPI>
 void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, void* c, int M, int N, int K,
-             int64_t ldc, bool vec, bool tma_c) {
+             int64_t ldc, bool vec, bool tma_c, LogProbArgs lp = {nullptr, nullptr, 1.f}) {
   auto kern = gemm2sm_kernel<BN, AMN, BMN, EPI>;
   static int max_clusters = 0;
   cudaLaunchConfig_t cfg = {};
@@ -403,7 +457,8 @@ void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc
   }
   const int tiles = ((M + kPairM - 1) / kPairM) * ((N + BN - 1) / BN);
   cfg.gridDim = dim3(2 * std::min(tiles, max_clusters));
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, err_word()));
+  C10_CUDA_CHECK(
+      cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, lp, err_word()));
 }
 
 }  // namespace
@@ -432,6 +487,7 @@ static bool make_c_map(CUtensorMap* m, void* ptr, int64_t M, int64_t N, int64_t 
                 "cuTensorMapEncodeTiled not available");
     fn = reinterpret_cast<EncodeFn>(p);
   }
+  bind_current_context();
   cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
   cuuint64_t strides[1] = {(cuuint64_t)(ldc * esz)};
   cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
@@ -514,6 +570,79 @@ torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c1
 #undef EPIS
 #undef GO
   return out;
+}
+
+namespace {
+
+__global__ void __launch_bounds__(32) logprob_combine_kernel(const float4* __restrict__ part, int ntn, int M,
+                                                              float* __restrict__ logp, float* __restrict__ ent,
+                                                              float* __restrict__ lse_out) {
+  const int row = blockIdx.x;
+  if (row >= M) return;
+  float m = -INFINITY, se = 0.f, sz = 0.f, zt = -INFINITY;
+  for (int t = threadIdx.x; t < ntn; t += 32) {
+    const float4 p = part[(int64_t)row * ntn + t];
+    zt = fmaxf(zt, p.w);
+    const float nm = fmaxf(m, p.x);
+    if (nm != -INFINITY) {
+      const float ea = __expf(m - nm), eb = __expf(p.x - nm);
+      se = se * ea + p.y * eb;
+      sz = sz * ea + p.z * eb;
+      m = nm;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, off), os = __shfl_xor_sync(0xffffffffu, se, off);
+    const float oz = __shfl_xor_sync(0xffffffffu, sz, off);
+    zt = fmaxf(zt, __shfl_xor_sync(0xffffffffu, zt, off));
+    const float nm = fmaxf(m, om);
+    if (nm != -INFINITY) {
+      const float ea = __expf(m - nm), eb = __expf(om - nm);
+      se = se * ea + os * eb;
+      sz = sz * ea + oz * eb;
+      m = nm;
+    }
+  }
+  if (threadIdx.x == 0) {
+    const float lse = m + logf(se);
+    logp[row] = zt - lse;
+    if (ent) ent[row] = lse - sz / se;
+    lse_out[row] = lse;
+  }
+}
+
+}  // namespace
+
+// Fused LM-head log-prob: log softmax(h . W^T * inv_t)[target] and the
+// entropy per row, on the pair GEMM with the reduction in its epilogue; the
+// [rows x vocab] logits are never written.  Returns (logp, entropy, lse).
+std::vector<torch::Tensor> gemm2sm_logprob(torch::Tensor h, torch::Tensor w, torch::Tensor targets, double inv_t) {
+  LRL_CHECK(h);
+  LRL_CHECK(w);
+  LRL_CHECK(targets);
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && h.dim() == 2 &&
+                  w.dim() == 2 && h.size(1) == w.size(1) && h.size(1) % 8 == 0,
+              "gemm2sm_logprob: bf16 h [T, H] and w [V, H], H a multiple of 8");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == h.size(0), "gemm2sm_logprob: int64 targets [T]");
+  const int64_t M = h.size(0), K = h.size(1), N = w.size(0);
+  auto opts = h.options().dtype(at::kFloat);
+  auto logp = torch::empty({M}, opts), ent = torch::empty({M}, opts), lse = torch::empty({M}, opts);
+  if (M == 0) return {logp, ent, lse};
+  c10::cuda::CUDAGuard guard(h.device());
+  const int ntn = (int)((N + 255) / 256);
+  auto part = torch::empty({M, ntn, 4}, opts);
+  const CUtensorMap ma = make_kmajor_map(h.data_ptr(), M, K, h.stride(0), 128);
+  const CUtensorMap mb = make_kmajor_map(w.data_ptr(), N, K, w.stride(0), 128);
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  LogProbArgs lp{targets.data_ptr<int64_t>(), reinterpret_cast<float4*>(part.data_ptr<float>()), (float)inv_t};
+  launch2<256, false, false, kE2LogProb>(ma, mb, mc, nullptr, (int)M, (int)N, (int)K, 0, false, false, lp);
+  logprob_combine_kernel<<<(unsigned)M, 32, 0, stream()>>>(reinterpret_cast<const float4*>(part.data_ptr<float>()),
+                                                             ntn, (int)M, logp.data_ptr<float>(), ent.data_ptr<float>(),
+                                                             lse.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {logp, ent, lse};
 }
 
 }  // namespace lrl

@@ -255,6 +255,7 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int64_t ld
   CUtensorMap m;
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "row stride must be a multiple of 16 bytes");
+  bind_current_context();
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
@@ -262,7 +263,8 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int64_t ld
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  LRL_CHECK_FMT(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d): dims %lld x %lld, stride %lld B, box %d x %d",
+                (int)r, (long long)K, (long long)rows, (long long)(ld * 2), kBK, box_rows);
   return m;
 }
 

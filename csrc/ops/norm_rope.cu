@@ -9,15 +9,15 @@ namespace lrl {
 constexpr int kMaxChunks = 4;  // 8-element chunks per thread => H <= 32768 at 1024 threads
 
 // ---------------------------------------------------------------- RMSNorm fwd
-template <bool kResidual>
+template <bool kResidual, int kChunks = kMaxChunks>
 __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ res,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    __nv_bfloat16* __restrict__ sum_out, float* __restrict__ rstd_out, int H,
                                    float eps) {
   // the weight does not depend on the previous kernel: fetch it before the PDL wait
-  bf16x8 wraw[kMaxChunks];
+  bf16x8 wraw[kChunks];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < kChunks; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
     if (col < H) wraw[c] = *reinterpret_cast<const bf16x8*>(w + col);
   }
@@ -26,10 +26,10 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int64_t base = int64_t(row) * H;
-  float v[kMaxChunks][8];
+  float v[kChunks][8];
   float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < kChunks; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
     if (col < H) {
       load8(x + base + col, v[c]);
@@ -49,7 +49,7 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   const float r = rsqrtf(ss / H + eps);
   if (threadIdx.x == 0 && rstd_out) rstd_out[row] = r;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < kChunks; ++c) {
     const int col = (c * blockDim.x + threadIdx.x) * 8;
     if (col < H) {
       float o[8];
@@ -91,6 +91,16 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
   if (T == 0) return {y, rstd};
+  if (H > 512 * 8 * kMaxChunks) {
+    // rows wider than 16384: 8 chunks per thread keep the block at <= 512
+    // threads (the 4-chunk variant needs 66 registers a thread, too many for
+    // a 1024-thread block)
+    const int t = ((H / 64 + 31) / 32) * 32;
+    launch_pdl(rmsnorm_fwd_kernel<false, 2 * kMaxChunks>, dim3(T), dim3(t), 0, (const __nv_bfloat16*)x.data_ptr(),
+               (const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+               (__nv_bfloat16*)nullptr, rstd.data_ptr<float>(), H, (float)eps);
+    return {y, rstd};
+  }
   launch_pdl(rmsnorm_fwd_kernel<false>, dim3(T), dim3(row_threads(H, T)), 0, (const __nv_bfloat16*)x.data_ptr(),
              (const __nv_bfloat16*)nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
              (__nv_bfloat16*)nullptr, rstd.data_ptr<float>(), H, (float)eps);

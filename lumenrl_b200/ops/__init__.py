@@ -53,7 +53,7 @@ def _accum_main_grad(w: Tensor, g: Tensor) -> None:
 # Training GEMMs: "own" runs the CTA-pair tcgen05 kernel (csrc/gemm/gemm_2sm.cu)
 # for the forward, dgrad and wgrad of every linear; "cublas" is the library
 # path kept for A/B measurements (LRL_TRAIN_GEMM=cublas).
-TRAIN_GEMM = os.environ.get("LRL_TRAIN_GEMM", "cublas")
+TRAIN_GEMM = os.environ.get("LRL_TRAIN_GEMM", "own")
 
 
 def _pair_ok(*ts) -> bool:
@@ -391,17 +391,35 @@ def kv_cache_append(k: Tensor, v: Tensor, k_cache: Tensor, v_cache: Tensor, slot
 # full logits never exist; backward recomputes each chunk.
 # ---------------------------------------------------------------------------
 
+FUSED_LOGPROB_ROWS = 16384   # rows per fused call (its per-tile partials: rows x vocab/256 x 16 B)
+
+
+def _logprob_forward(hidden: Tensor, w: Tensor, targets: Tensor, inv_temp: float, chunk: int):
+    """(logp, entropy, lse) per row.  On the pair GEMM the log-softmax
+    reduction runs in the GEMM epilogue and logits are never written;
+    otherwise bf16 logits are materialised per ``chunk`` rows."""
+    T = hidden.shape[0]
+    if _pair_ok(hidden, w) and targets.dtype == torch.long:
+        outs = [ext().gemm2sm_logprob(hidden[a: a + FUSED_LOGPROB_ROWS], w,
+                                      targets[a: a + FUSED_LOGPROB_ROWS].contiguous(), inv_temp)
+                for a in range(0, T, FUSED_LOGPROB_ROWS)]
+        if len(outs) == 1:
+            return tuple(outs[0])
+        return tuple(torch.cat([o[i] for o in outs]) for i in range(3))
+    logp = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    ent = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
+    for a in range(0, T, chunk):
+        b = min(T, a + chunk)
+        ext().logprob_fwd(mm_nt(hidden[a:b], w), targets[a:b].contiguous(), inv_temp, logp[a:b], ent[a:b],
+                          lse[a:b])
+    return logp, ent, lse
+
+
 class _TokenLogProb(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, w, w_handle, targets, inv_temp, chunk, want_entropy):
-        T = hidden.shape[0]
-        logp = torch.empty(T, dtype=torch.float32, device=hidden.device)
-        ent = torch.empty(T, dtype=torch.float32, device=hidden.device)
-        lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
-        for a in range(0, T, chunk):
-            b = min(T, a + chunk)
-            logits = mm_nt(hidden[a:b], w)
-            ext().logprob_fwd(logits, targets[a:b], inv_temp, logp[a:b], ent[a:b], lse[a:b])
+        logp, ent, lse = _logprob_forward(hidden, w, targets, inv_temp, chunk)
         ctx.save_for_backward(hidden, w, targets, lse, ent)
         ctx.meta = (w_handle, inv_temp, chunk, want_entropy)
         return logp, ent
@@ -441,14 +459,7 @@ def token_logprob(hidden: Tensor, lm_head: Tensor, targets: Tensor, temperature:
         logp, ent = _TokenLogProb.apply(hidden, lm_head.detach(), lm_head, targets.contiguous(), inv_t, chunk,
                                         want_entropy)
         return logp, (ent if want_entropy else None)
-    T = hidden.shape[0]
-    logp = torch.empty(T, dtype=torch.float32, device=hidden.device)
-    ent = torch.empty(T, dtype=torch.float32, device=hidden.device)
-    lse = torch.empty(T, dtype=torch.float32, device=hidden.device)
-    for a in range(0, T, chunk):
-        b = min(T, a + chunk)
-        ext().logprob_fwd(mm_nt(hidden[a:b], lm_head), targets[a:b].contiguous(), inv_t, logp[a:b], ent[a:b],
-                          lse[a:b])
+    logp, ent, _ = _logprob_forward(hidden, lm_head, targets, inv_t, chunk)
     return logp, (ent if want_entropy else None)
 
 

@@ -21,6 +21,6 @@ def cuda():
         pytest.skip("no CUDA device")
     from lumenrl_b200.ops.ext import ext
     ext()  # fail loudly if the extension is missing on a GPU box
-    if os.environ.get("LRL_SEGV_BACKTRACE"):
-        ext().install_segv_backtrace()
+    if os.environ.get("LRL_SEGV_BACKTRACE"):    # a file path for the native stack on SIGSEGV
+        ext().install_segv_backtrace(os.environ["LRL_SEGV_BACKTRACE"])
     return torch.device("cuda", 0)

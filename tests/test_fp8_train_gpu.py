@@ -46,7 +46,7 @@ def test_transposed_quantiser_matches_reference(cuda, R, C):
         deq = dequant_1x128(q, s)
         tiny = s.repeat_interleave(128, -1) * 2.0 ** -9       # subnormal spacing
         assert bool(((deq - xt).abs() <= half_step * xt.abs() + tiny).all())
-        assert (q.view(torch.uint8) != qr.to(q.device).view(torch.uint8)).float().mean().item() < 1e-3
+        assert (q.view(torch.uint8) != qr.to(q.device).view(torch.uint8)).float().mean().item() < 1e-2
         qk, sk = quant_t_1x128(x, dt, kb_major=True)
         assert sk.shape == (Rpad // 128, (C + 127) // 128 * 128)
         assert torch.equal(sk[:, :C].t().contiguous(), s)

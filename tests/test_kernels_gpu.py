@@ -18,8 +18,10 @@ def close(a, b, atol, rtol=0.0):
     assert err <= tol, f"max abs err {err} > {tol}"
 
 
-@pytest.mark.parametrize("T,H", [(1, 256), (37, 4096), (129, 1000 * 8)])
+@pytest.mark.parametrize("T,H", [(1, 256), (37, 4096), (129, 1000 * 8), (1, 32768), (400, 32768)])
 def test_rmsnorm_fwd_bwd(cuda, T, H):
+    """Includes the launch-shape edges: one row, more rows than two per SM
+    (the many-rows branch), and the widest rows (32768, 1024 threads)."""
     torch.manual_seed(0)
     x = torch.randn(T, H, device=cuda, dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(H, device=cuda)).to(torch.bfloat16)
@@ -37,16 +39,25 @@ def test_rmsnorm_fwd_bwd(cuda, T, H):
     close(wp.main_grad, wr.grad, 0.5, 1e-2)
 
 
-def test_add_rmsnorm(cuda):
+@pytest.mark.parametrize("T,H", [(64, 4096), (1, 16384), (400, 16384)])
+def test_add_rmsnorm(cuda, T, H):
     torch.manual_seed(0)
-    x = torch.randn(64, 4096, device=cuda, dtype=torch.bfloat16)
-    r = torch.randn(64, 4096, device=cuda, dtype=torch.bfloat16)
-    w = torch.randn(4096, device=cuda).to(torch.bfloat16)
+    x = torch.randn(T, H, device=cuda, dtype=torch.bfloat16)
+    r = torch.randn(T, H, device=cuda, dtype=torch.bfloat16)
+    w = torch.randn(H, device=cuda).to(torch.bfloat16)
     with torch.no_grad():
         y, s = ops.add_rmsnorm(x, r, w, 1e-6)
     s_ref = (x + r)
     close(s, s_ref, 0.0)
     close(y, ref.rmsnorm(s_ref.float(), w.float(), 1e-6), 3e-2, 1e-2)
+
+
+def test_add_rmsnorm_rejects_rows_wider_than_16384(cuda):
+    x = torch.randn(4, 16392, device=cuda, dtype=torch.bfloat16)
+    w = torch.ones(16392, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        with torch.no_grad():
+            ops.add_rmsnorm(x, x.clone(), w, 1e-6)
 
 
 def test_add_rmsnorm_fwd_bwd(cuda):

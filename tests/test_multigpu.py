@@ -12,6 +12,11 @@ import torch.multiprocessing as mp
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
 
+def _need(world: int) -> None:
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
@@ -43,13 +48,13 @@ def _worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_fused_optimizer_step_matches_nccl():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_optimizer_step_matches_nccl(world):
+    _need(world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29700 + os.getpid() % 200
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
@@ -167,17 +172,17 @@ def _tp_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tensor_parallel_fused_ag_rs_gemms():
-    """TP=2 + sequence parallel decoder layer, forward and backward, with the
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_fused_ag_rs_gemms(world):
+    """TP + sequence parallel decoder layer, forward and backward, with the
     all-gather and reduce-scatter fused into tcgen05 GEMMs over NVLink; the
     result must match the unsharded bf16 layer about as closely as the NCCL
     path does."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    _need(world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29980 + os.getpid() % 9
-    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29980 + os.getpid() % 9 + world
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
@@ -217,15 +222,15 @@ def _cp_worker(rank, world, port, out_q):
     dist.destroy_process_group()
 
 
-def test_context_parallel_ring_attention():
-    """CP=2 zigzag ring attention (flash blocks + LSE merge, K/V over NCCL p2p)
+@pytest.mark.parametrize("world", [2, 4])
+def test_context_parallel_ring_attention(world):
+    """CP zigzag ring attention (flash blocks + LSE merge, K/V over NCCL p2p)
     against full causal attention, forward and backward, bf16."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    _need(world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29970 + os.getpid() % 9
-    procs = [ctx.Process(target=_cp_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29970 + os.getpid() % 9 + world
+    procs = [ctx.Process(target=_cp_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
@@ -250,16 +255,16 @@ def _ep_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_expert_parallel_nvlink_dispatch_combine():
-    """EP=2 MoE part: count exchange, dispatch and combine by peer stores,
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_nvlink_dispatch_combine(world):
+    """EP MoE part: count exchange, dispatch and combine by peer stores,
     grouped tcgen05 expert GEMMs; forward and backward against all experts on
     one rank, as close as the NCCL all-to-all path."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    _need(world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29960 + os.getpid() % 9
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    port = 29960 + os.getpid() % 9 + world
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
@@ -327,3 +332,90 @@ def test_p2p_weight_sync_to_separate_rollout_gpu():
     for p in procs:
         p.join(timeout=60)
     assert len(res[1]) == 3 and max(res[1]) == 0.0, res[1]
+
+
+def _sep_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.core.config import LumenRLConfig
+    from lumenrl_b200.models.config import tiny_qwen3_moe
+    from lumenrl_b200.parallel.dist import ParallelState, init_distributed
+    from lumenrl_b200.trainer.rl_trainer import RLRunSpec
+    from lumenrl_b200.trainer.separated_trainer import SeparatedRLTrainer
+    st = init_distributed()
+    cfg = LumenRLConfig.from_dict({"algorithm": {"name": "grpo", "grpo": {"num_generations": 4}},
+                                   "policy": {"learning_rate": 1e-5}, "num_training_steps": 2, "seed": 0})
+    spec = RLRunSpec(prompts_per_step=4, prompt_len=64, max_new_tokens=32, reward="parity", eos_token_id=None)
+    tr = SeparatedRLTrainer(cfg, tiny_qwen3_moe(), spec, st, num_rollout=1).setup()
+    hist = [tr.step() for _ in range(2)]
+    torch.cuda.synchronize()
+    flat = tr.model.flat.clone()
+    other = torch.empty_like(flat)
+    if rank == 0:
+        dist.send(flat, 1)
+        q.put((rank, hist[-1].get("actor/grad_norm"), hist[-1].get("weight_sync/push_GBps"), None))
+    else:
+        dist.recv(other, 0)
+        q.put((rank, None, hist[-1].get("weight_sync/push_GBps"), bool(torch.equal(other, flat))))
+    dist.barrier()
+    tr.close()
+    dist.destroy_process_group()
+
+
+def test_separated_trainer_and_rollout_gpus():
+    """Separated mode on 2 GPUs: a tiny MoE GRPO step on the trainer GPU, the
+    rollout on the other; the weights reach the rollout GPU by peer stores
+    (P2PWeightSync) and equal the trainer's after every step."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29940 + os.getpid() % 9
+    procs = [ctx.Process(target=_sep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (g, bw, same) for r, g, bw, same in (q.get(timeout=300) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0][0] == res[0][0] and res[0][0] > 0      # finite, non-zero grad norm
+    assert res[1][2] is True                             # rollout weights == trainer weights
+
+
+def _sddd_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    import dataclasses
+    from lumenrl_b200.models.config import tiny_qwen3
+    from lumenrl_b200.parallel.dist import init_distributed
+    from lumenrl_b200.trainer.spec_distill_trainer import SDDDTrainer, SpecDistillSpec
+    st = init_distributed()
+    spec = SpecDistillSpec(aux_layers=(0, 1, 2), draft_vocab=256, ttt_length=3, seq_len=128, batch_per_rank=2,
+                           draft_heads=4, draft_kv_heads=2, draft_ffn=256)
+    tr = SDDDTrainer(dataclasses.replace(tiny_qwen3(), num_layers=3), spec, st, num_teacher=world - 1, seed=3)
+    outs = [tr.step() for _ in range(3)]
+    torch.cuda.synchronize()
+    tr.check()
+    q.put((rank, [o.get("loss") for o in outs]))
+    dist.barrier()
+    tr.close()
+    dist.destroy_process_group()
+
+
+def test_sddd_teacher_streams_hidden_states_to_draft_gpu():
+    """SDDD on 2 GPUs: the teacher GPU pushes ids + hidden states into the
+    draft GPU's ring slots over NVLink; the draft trains on them."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29930 + os.getpid() % 9
+    procs = [ctx.Process(target=_sddd_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    losses = res[1]
+    assert len(losses) == 3 and all(l == l and l > 0 for l in losses)

@@ -97,6 +97,12 @@ torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits);
 torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> c,
                       int64_t epi, int64_t bn);
 int64_t gemm2sm_status();
+void rs_norm_mc(int64_t mc_grads, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+                torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
+void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+                 torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
+                 double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
+                 torch::Tensor norm_out, int64_t wait_cycles);
 std::vector<torch::Tensor> gemm2sm_logprob(torch::Tensor h, torch::Tensor w, torch::Tensor targets, double inv_t);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
@@ -186,6 +192,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2sm", &lrl::gemm2sm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0);
   m.def("gemm2sm_status", &lrl::gemm2sm_status);
+  m.def("rs_norm_mc", &lrl::rs_norm_mc);
+  m.def("adamw_ag_mc", &lrl::adamw_ag_mc);
   m.def("gemm2sm_logprob", &lrl::gemm2sm_logprob);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);

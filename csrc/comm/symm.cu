@@ -19,6 +19,12 @@
 //              -> bf16 values stored into EVERY rank's weight buffer at this
 //              rank's offset (the trainer -> rollout weight sync and the
 //              parameter all-gather in one pass) -> completion barrier.
+//   rs_norm_mc / adamw_ag_mc: the same two steps through an NVLink-SHARP
+//              (NVLS) multicast mapping of the gradient and weight buffers:
+//              one multimem.ld_reduce returns the sum of an element over every
+//              GPU (the reduction runs in the NVSwitch), one multimem.st writes
+//              a value into every GPU's copy, so each byte crosses a GPU's
+//              NVLink ports once instead of once per peer.
 #include "../common.cuh"
 
 namespace lrl {
@@ -182,6 +188,118 @@ __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig
   }
 }
 
+
+// ---- NVLS multicast variants -----------------------------------------------------
+__device__ __forceinline__ float4 mc_ld_reduce_add_v4(const float* mc_addr) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(mc_addr)
+               : "memory");
+  return r;
+}
+
+// 8 bytes (4 bf16) to the same offset of every GPU's buffer
+__device__ __forceinline__ void mc_st_v2(void* mc_addr, uint2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};\n" ::"l"(mc_addr), "f"(__uint_as_float(v.x)),
+               "f"(__uint_as_float(v.y))
+               : "memory");
+}
+
+__global__ void rs_norm_mc_kernel(float* mc_grads, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t lo,
+                                  int64_t n, float* __restrict__ out, uint32_t epoch, int* status,
+                                  long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles)) return;
+  __shared__ float red[32];
+  float ss = 0.f;
+  const int64_t n4 = n / 4;
+  const float* src = mc_grads + lo;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 acc = mc_ld_reduce_add_v4(src + 4 * i);
+    reinterpret_cast<float4*>(out)[i] = acc;
+    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) {
+    atomicAdd(reinterpret_cast<float*>(my_sig + kSigNorms + kMaxRanks), ss);
+    __threadfence();
+    const unsigned int done = atomicAdd(my_sig + kSigNorms + kMaxRanks + 1, 1u);
+    if (done == gridDim.x - 1) {
+      const float total = atomicExch(reinterpret_cast<float*>(my_sig + kSigNorms + kMaxRanks), 0.f);
+      my_sig[kSigNorms + kMaxRanks + 1] = 0u;
+      for (int r = 0; r < W; ++r)
+        reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigNorms)[rank] = total;
+      __threadfence_system();
+    }
+  }
+}
+
+__global__ void adamw_ag_mc_kernel(__nv_bfloat16* mc_weights, PeerPtrs sig, uint32_t* my_sig, int rank, int W,
+                                   int64_t lo, int64_t n, float* __restrict__ p, const float* __restrict__ g,
+                                   float* __restrict__ m, float* __restrict__ v, float lr, float b1, float b2, float eps,
+                                   float wd, float bc1, float bc2, float max_norm, uint32_t epoch, int* status,
+                                   float* norm_out, long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles)) return;
+  float sq = 0.f;
+  for (int r = 0; r < W; ++r) sq += reinterpret_cast<volatile float*>(my_sig + kSigNorms)[r];
+  const float norm = sqrtf(sq);
+  const bool finite = isfinite(norm);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *norm_out = norm;
+  if (finite) {
+    const float clip = max_norm > 0.f ? fminf(1.f, max_norm / (norm + 1e-6f)) : 1.f;
+    const int64_t n4 = n / 4;
+    __nv_bfloat16* dst = mc_weights + lo;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+      float4 pp = reinterpret_cast<float4*>(p)[i];
+      const float4 gg = reinterpret_cast<const float4*>(g)[i];
+      float4 mm = reinterpret_cast<float4*>(m)[i];
+      float4 vv = reinterpret_cast<float4*>(v)[i];
+      float* pa = &pp.x;
+      const float* ga = &gg.x;
+      float* ma = &mm.x;
+      float* va = &vv.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gr = ga[j] * clip;
+        ma[j] = b1 * ma[j] + (1.f - b1) * gr;
+        va[j] = b2 * va[j] + (1.f - b2) * gr * gr;
+        pa[j] = pa[j] * (1.f - lr * wd) - lr * (ma[j] / bc1) / (sqrtf(va[j] / bc2) + eps);
+      }
+      reinterpret_cast<float4*>(p)[i] = pp;
+      reinterpret_cast<float4*>(m)[i] = mm;
+      reinterpret_cast<float4*>(v)[i] = vv;
+      uint2 packed;
+      __nv_bfloat162 lo2 = __floats2bfloat162_rn(pp.x, pp.y), hi2 = __floats2bfloat162_rn(pp.z, pp.w);
+      packed.x = *reinterpret_cast<uint32_t*>(&lo2);
+      packed.y = *reinterpret_cast<uint32_t*>(&hi2);
+      mc_st_v2(dst + 4 * i, packed);   // every GPU's resident weights at once
+    }
+  }
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // multicast stores before the unicast flag writes below (different virtual aliases)
+    asm volatile("fence.proxy.alias;\n" ::: "memory");
+    __threadfence_system();
+    last = atomicAdd(my_sig + kSigNorms + kMaxRanks + 2, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    my_sig[kSigNorms + kMaxRanks + 2] = 0u;
+    for (int r = 0; r < W; ++r)
+      st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 2 * kMaxRanks + rank, epoch);
+    const long long t0 = clock64();
+    for (int r = 0; r < W; ++r) {
+      while (ld_acquire_sys(my_sig + kSigFlags + 2 * kMaxRanks + r) < epoch) {
+        if (clock64() - t0 > wait_cycles) {
+          atomicCAS(status, 0, 102);
+          break;
+        }
+      }
+    }
+  }
+}
+
 PeerPtrs to_peers(const std::vector<int64_t>& ptrs) {
   TORCH_CHECK((int)ptrs.size() <= kMaxRanks, "at most ", kMaxRanks, " ranks");
   PeerPtrs pp{};
@@ -249,6 +367,33 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
       g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
       (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(), norm_out.data_ptr<float>(),
       (long long)wait_cycles);
+}
+
+// NVLS: mc_grads / mc_weights are the multicast addresses of the symmetric
+// gradient and weight buffers (same layout on every rank)
+void rs_norm_mc(int64_t mc_grads, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+                torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles) {
+  TORCH_CHECK(n % 4 == 0 && lo % 4 == 0 && mc_grads % 16 == 0, "rs_norm_mc: 16-byte aligned shards");
+  const int W = sig_ptrs.size();
+  uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
+  rs_norm_mc_kernel<<<comm_grid(), 512, 0, stream()>>>(reinterpret_cast<float*>(mc_grads), to_peers(sig_ptrs), my_sig,
+                                                       (int)rank, W, lo, n, out.data_ptr<float>(), (uint32_t)epoch,
+                                                       status.data_ptr<int>(), (long long)wait_cycles);
+}
+
+void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
+                 torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
+                 double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
+                 torch::Tensor norm_out, int64_t wait_cycles) {
+  TORCH_CHECK(n % 4 == 0 && lo % 4 == 0 && mc_weights % 16 == 0, "adamw_ag_mc: aligned shards");
+  const int W = sig_ptrs.size();
+  uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
+  const float bc1 = 1.f - powf((float)b1, (float)step), bc2 = 1.f - powf((float)b2, (float)step);
+  adamw_ag_mc_kernel<<<comm_grid(), 512, 0, stream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(mc_weights), to_peers(sig_ptrs), my_sig, (int)rank, W, lo, n,
+      p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1,
+      (float)b2, (float)eps, (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(),
+      norm_out.data_ptr<float>(), (long long)wait_cycles);
 }
 
 }  // namespace lrl

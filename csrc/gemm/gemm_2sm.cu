@@ -50,7 +50,7 @@ using namespace tc2;
 
 namespace {
 
-constexpr int kPairM = 256, kBK = 64, kGroupM = 8, kThreads = 192;
+constexpr int kPairM = 256, kBK = 64, kThreads = 192;
 
 enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3, kE2LogProb = 4 };
 
@@ -79,11 +79,13 @@ struct Pair {
   static constexpr int kSmem = kStages * kStageBytes + kStagingBytes + 1024 + 256;
 };
 
-__device__ __forceinline__ void pair_tile(int t, int num_m, int num_n, int& mb, int& nb) {
-  const int per_group = kGroupM * num_n;
+// grouped raster: `group_m` consecutive 256-row tiles share every B panel of
+// the group while the wave sweeps N, so A and B panels are re-read from L2
+__device__ __forceinline__ void pair_tile(int t, int num_m, int num_n, int group_m, int& mb, int& nb) {
+  const int per_group = group_m * num_n;
   const int g = t / per_group;
-  const int first = g * kGroupM;
-  const int gm = min(num_m - first, kGroupM);
+  const int first = g * group_m;
+  const int gm = min(num_m - first, group_m);
   const int r = t % per_group;
   mb = first + r % gm;
   nb = r / gm;
@@ -144,7 +146,7 @@ template <int BN, bool AMN, bool BMN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, void* C, int M, int N, int K, int64_t ldc, int vec,
-                   int tma_c, LogProbArgs lp, int* err_out) {
+                   int tma_c, LogProbArgs lp, int group_m, uint32_t wait_hint, int* err_out) {
   using G = Pair<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,12 +199,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = cid; t < tiles && ok; t += ncl) {
         int mb, nb;
-        pair_tile(t, num_m, num_n, mb, nb);
+        pair_tile(t, num_m, num_n, group_m, mb, nb);
         const int am = mb * kPairM + rank * 128;
         const int bn = nb * BN + rank * (BN / 2);
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % G::kStages;
-          if (!mbar_wait(&empty[s], ((it / G::kStages) & 1) ^ 1, err, kErrProducer)) {
+          if (!mbar_wait_sleep(&empty[s], ((it / G::kStages) & 1) ^ 1, err, kErrProducer, wait_hint)) {
             ok = false;
             break;
           }
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = cid; t < tiles && ok; t += ncl, ++tc) {
         const int buf = tc & 1;
-        if (!mbar_wait(&tempty[buf], ((tc >> 1) & 1) ^ 1, err, kErrMma)) {
+        if (!mbar_wait_sleep(&tempty[buf], ((tc >> 1) & 1) ^ 1, err, kErrMma, wait_hint)) {
           ok = false;
           break;
         }
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem + buf * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % G::kStages;
-          if (!mbar_wait(&full[s], (it / G::kStages) & 1, err, kErrMma)) {
+          if (!mbar_wait_sleep(&full[s], (it / G::kStages) & 1, err, kErrMma, wait_hint)) {
             ok = false;
             break;
           }
@@ -292,9 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int tc = 0, nst = 0;
     for (int t = cid; t < tiles; t += ncl, ++tc) {
       int mb, nb;
-      pair_tile(t, num_m, num_n, mb, nb);
+      pair_tile(t, num_m, num_n, group_m, mb, nb);
       const int buf = tc & 1;
-      if (!mbar_wait(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue)) break;
+      if (!mbar_wait_sleep(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue, wait_hint)) break;
       tc_fence_after();
       const int row0 = mb * kPairM + rank * 128 + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
@@ -457,8 +459,18 @@ void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc
   }
   const int tiles = ((M + kPairM - 1) / kPairM) * ((N + BN - 1) / BN);
   cfg.gridDim = dim3(2 * std::min(tiles, max_clusters));
-  C10_CUDA_CHECK(
-      cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, lp, err_word()));
+  // tuning knobs for same-box experiments (defaults are the measured choice)
+  static const int group_m = [] {
+    const char* e = getenv("LRL_GEMM_GROUP_M");
+    const int v = e ? atoi(e) : 8;
+    return v > 0 ? v : 8;
+  }();
+  static const uint32_t wait_hint = [] {
+    const char* e = getenv("LRL_GEMM_WAIT_HINT_NS");
+    return (uint32_t)(e ? atoi(e) : 0);
+  }();
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, lp, group_m,
+                                    wait_hint, err_word()));
 }
 
 }  // namespace

@@ -131,6 +131,34 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32_major(int M, int N, bool a
 }
 
 
+// try_wait with a suspend-time hint (ns): a waiting warp sleeps until the
+// phase completes or the hint expires, instead of re-polling every short
+// system-defined window
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// bounded wait (see tc::mbar_wait) that sleeps between polls when hint_ns > 0
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* err, int code,
+                                                uint32_t hint_ns) {
+  if (hint_ns == 0) return tc::mbar_wait(bar, parity, err, code);
+  const long long t0 = clock64();
+  while (!mbar_try_wait_hint(bar, parity, hint_ns)) {
+    if (*err != tc::kErrNone) return false;
+    if (clock64() - t0 > tc::kWaitCycles) {
+      *err = code;
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---- epilogue: TMA bulk stores from shared memory --------------------------------
 // tcgen05.ld without the wait (issue several, then one tcgen05.wait::ld)
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {

@@ -18,12 +18,20 @@ optimizer step as two fused kernels:
    weight buffer -- the parameter all-gather and the trainer -> rollout
    weight sync in the same pass -- then a completion barrier.
 
+With ``nvls`` (default: when the GPUs support NVLink SHARP multicast) the
+weight and gradient buffers come from PyTorch's symmetric memory, which also
+maps them into one NVLS multicast object; the kernels then use
+``multimem.ld_reduce`` (the gradient sum of an element over all GPUs, reduced
+in the NVSwitch) and ``multimem.st`` (one store into every GPU's weights), so
+each byte crosses a GPU's NVLink ports once.
+
 Waits are bounded in the kernels; ``check()`` raises ``CommTimeout`` when a
 kernel recorded an expired wait (a dead or stalled rank).
 """
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -65,16 +73,62 @@ class SymmetricBuffer:
             self.local_ptr = 0
 
 
+class MulticastBuffer:
+    """Same-sized buffer on every rank from PyTorch's symmetric memory (cuMem
+    allocations mapped into every peer) plus its NVLS multicast address
+    ``mc`` (0 when the GPUs have no multicast support)."""
+
+    def __init__(self, numel: int, dtype: torch.dtype, group=None) -> None:
+        import torch.distributed._symmetric_memory as symm
+        g = group if group is not None else dist.group.WORLD
+        try:
+            symm.enable_symm_mem_for_group(g.group_name)
+        except Exception:
+            pass
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.tensor = symm.empty(numel, dtype=dtype, device=dev)
+        self.tensor.zero_()
+        self.handle = symm.rendezvous(self.tensor, g.group_name)
+        self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.mc = int(self.handle.multicast_ptr)
+
+    def close(self) -> None:
+        self.handle = None
+
+
+def nvls_supported() -> bool:
+    try:
+        import torch.distributed._symmetric_memory as symm
+        from torch._C._distributed_c10d import _SymmetricMemory
+        return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA,
+                                                           torch.cuda.current_device()))
+    except Exception:
+        return False
+
+
 class NVLinkOptimizerComm:
-    """Fused reduce-scatter / AdamW / all-gather over NVLink peer memory."""
+    """Fused reduce-scatter / AdamW / all-gather over NVLink peer memory, or
+    over NVLS multicast (``nvls``: True, False, or None = when supported)."""
 
     def __init__(self, numel: int, rank: int, world: int, weight_dtype=torch.bfloat16, group=None,
-                 wait_seconds: float = 10.0) -> None:
+                 wait_seconds: float = 10.0, nvls: Optional[bool] = None) -> None:
         self.rank, self.world, self.group = rank, world, group
         # in-kernel spin bound, in SM clock cycles at boost clock
         self.wait_cycles = int(wait_seconds * 2.0e9)
-        self.weights = SymmetricBuffer(numel, weight_dtype, rank, world, group)
-        self.grads = SymmetricBuffer(numel, torch.float32, rank, world, group)
+        if nvls is None:   # LRL_NVLS=1 opts in; the unicast peer path is the default
+            nvls = os.environ.get("LRL_NVLS", "0") == "1"
+        use_mc = bool(nvls) and nvls_supported()
+        self.nvls = False
+        if use_mc:
+            self.weights = MulticastBuffer(numel, weight_dtype, group)
+            self.grads = MulticastBuffer(numel, torch.float32, group)
+            self.nvls = self.weights.mc != 0 and self.grads.mc != 0
+            if not self.nvls:
+                self.weights.close()
+                self.grads.close()
+        if not self.nvls:
+            self.weights = SymmetricBuffer(numel, weight_dtype, rank, world, group)
+            self.grads = SymmetricBuffer(numel, torch.float32, rank, world, group)
         self.signals = SymmetricBuffer(int(ext().symm_signal_words()), torch.int32, rank, world, group)
         dev = self.weights.tensor.device
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -95,12 +149,19 @@ class NVLinkOptimizerComm:
             dist.all_reduce(self._rendezvous, group=self.group)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record()
-        e.rs_norm(self.grads.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, grad_shard, self.epoch,
-                  self.status, self.wait_cycles)
+        if self.nvls:
+            e.rs_norm_mc(self.grads.mc, self.signals.ptrs, self.rank, shard_lo, shard_n, grad_shard, self.epoch,
+                         self.status, self.wait_cycles)
+        else:
+            e.rs_norm(self.grads.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, grad_shard, self.epoch,
+                      self.status, self.wait_cycles)
         ev[1].record()
-        e.adamw_ag(self.weights.ptrs, self.signals.ptrs, self.rank, shard_lo, shard_n, master, grad_shard, m, v, lr,
-                   betas[0], betas[1], eps, wd, step, max_norm if max_norm else 0.0, self.epoch, self.status,
-                   self.norm, self.wait_cycles)
+        args = (self.signals.ptrs, self.rank, shard_lo, shard_n, master, grad_shard, m, v, lr, betas[0], betas[1], eps,
+                wd, step, max_norm if max_norm else 0.0, self.epoch, self.status, self.norm, self.wait_cycles)
+        if self.nvls:
+            e.adamw_ag_mc(self.weights.mc, *args)
+        else:
+            e.adamw_ag(self.weights.ptrs, *args)
         ev[2].record()
         vals = torch.cat([self.norm, self.status.float()]).cpu()   # one device->host read per step
         # device time of the two kernels (the read above waited for both)
@@ -157,7 +218,8 @@ def replica_agreement(model_flat: torch.Tensor, master: torch.Tensor, lo: int, g
             "master_mismatches": sum(r[2] for r in rows)}
 
 
-def fused_vs_nccl_max_err(numel: int, rank: int, world: int, steps: int = 1, group=None, seed: int = 0) -> dict:
+def fused_vs_nccl_max_err(numel: int, rank: int, world: int, steps: int = 1, group=None, seed: int = 0,
+                          nvls: Optional[bool] = None) -> dict:
     """One (or more) fused NVLink optimizer steps (rs_norm + adamw_ag) against
     NCCL reduce_scatter_tensor + the AdamW kernel + all_gather_into_tensor on
     the same gradients; returns the largest differences of the resulting bf16
@@ -167,7 +229,7 @@ def fused_vs_nccl_max_err(numel: int, rank: int, world: int, steps: int = 1, gro
     dev = torch.device("cuda", torch.cuda.current_device())
     g0 = torch.Generator(device=dev).manual_seed(seed)
     w0 = torch.randn(n, device=dev, generator=g0).to(torch.bfloat16)
-    comm = NVLinkOptimizerComm(n, rank, world, group=group)
+    comm = NVLinkOptimizerComm(n, rank, world, group=group, nvls=nvls)
     try:
         comm.weights.tensor.copy_(w0)
         kw = dict(lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
@@ -186,7 +248,7 @@ def fused_vs_nccl_max_err(numel: int, rank: int, world: int, steps: int = 1, gro
                             (fused.master - plain.master).abs().max().item(), norm_err], device=dev)
         dist.all_reduce(out, op=dist.ReduceOp.MAX, group=group)
         return {"weights_max_err": float(out[0]), "master_max_err": float(out[1]), "grad_norm_rel_err": float(out[2]),
-                "numel": n}
+                "numel": n, "nvls": comm.nvls}
     finally:
         torch.cuda.synchronize()
         dist.barrier(group=group)

@@ -17,7 +17,7 @@ def _need(world: int) -> None:
         pytest.skip(f"needs {world} GPUs")
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, nvls=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -27,7 +27,7 @@ def _worker(rank, world, port, q):
     n = 128 * world * 1000
     torch.manual_seed(0)
     w0 = torch.randn(n, device="cuda").to(torch.bfloat16)
-    comm = NVLinkOptimizerComm(n, rank, world)
+    comm = NVLinkOptimizerComm(n, rank, world, nvls=nvls)
     comm.weights.tensor.copy_(w0)
     fused = ShardedFlatAdamW(comm.weights.tensor, world, rank, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1,
                              max_grad_norm=1.0, comm=comm)
@@ -43,24 +43,30 @@ def _worker(rank, world, port, q):
         norms.append((a["grad_norm"], b["grad_norm"]))
     torch.cuda.synchronize()
     err = (comm.weights.tensor.float() - plain_w.float()).abs().max().item()
-    q.put((rank, err, norms))
+    q.put((rank, err, norms, comm.nvls))
+    dist.barrier()
     comm.close()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("nvls", [True, False])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_fused_optimizer_step_matches_nccl(world):
+def test_fused_optimizer_step_matches_nccl(world, nvls):
+    """Fused step (nvls=True: NVLS multimem when the GPUs support it; False:
+    peer loads and stores) against NCCL reduce-scatter + AdamW + all-gather."""
     _need(world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29700 + os.getpid() % 200
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port + (0 if nvls else 50), q, nvls))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
-    for rank, err, norms in res:
+    print("nvls path:", [r[3] for r in res])
+    for rank, err, norms, _ in res:
         assert err <= 1e-2, (rank, err)
         for a, b in norms:
             assert abs(a - b) <= 1e-3 * max(1.0, b), (a, b)
@@ -73,7 +79,8 @@ def _dead_peer_worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     from lumenrl_b200.parallel.symm import CommTimeout, NVLinkOptimizerComm
     n = 128 * world * 64
-    comm = NVLinkOptimizerComm(n, rank, world, wait_seconds=0.5)
+    # plain peer loads / stores: no rank's memory is bound to an NVLS multicast object
+    comm = NVLinkOptimizerComm(n, rank, world, wait_seconds=0.5, nvls=False)
     shard = n // world
     master = torch.zeros(shard, device="cuda")
     gs, m, v = torch.zeros_like(master), torch.zeros_like(master), torch.zeros_like(master)

@@ -67,3 +67,43 @@ def test_separated_matches_colocated_moe_with_routing_replay():
     assert torch.allclose(sep_w, single.actor.model.flat, atol=1e-6)
     # the rollout rank holds the trainer's latest weights
     assert torch.equal(res[1][1], sep_w)
+
+
+def _async_worker(rank, world, port, q, lag):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from lumenrl_b200.trainer.separated_trainer import SeparatedRLTrainer
+    torch.manual_seed(0)
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["num_training_steps=3", "policy.learning_rate=3e-3"])
+    from lumenrl_b200.models.config import tiny_llama
+    tr = SeparatedRLTrainer(cfg, tiny_llama(), _spec(), ParallelState(rank=rank, world_size=world), num_rollout=1,
+                            async_lag=lag).setup()
+    hist = [tr.step() for _ in range(3)]
+    tr.finish()
+    q.put((rank, [m.get("rollout_corr/kl") for m in hist] if not tr.is_rollout else None, tr.model.flat.clone()))
+    dist.barrier()
+    tr.close()
+    dist.destroy_process_group()
+
+
+def test_async_separated_is_one_step_stale():
+    """async_lag=1: the rollout generates batch s+1 while batch s trains, so
+    from the second step on the trainer sees rollout log-probs of the previous
+    policy (non-zero rollout/training KL); synchronous runs see none.  After
+    finish() the rollout holds the trainer's final weights in both modes."""
+    ctx = mp.get_context("spawn")
+    kls = {}
+    for lag in (0, 1):
+        q = ctx.Queue()
+        port = 29650 + os.getpid() % 150 + 7 * lag
+        procs = [ctx.Process(target=_async_worker, args=(r, 2, port, q, lag)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = {r: (k, w) for r, k, w in (q.get(timeout=300) for _ in procs)}
+        for p in procs:
+            p.join(timeout=60)
+        kls[lag] = res[0][0]
+        assert torch.equal(res[0][1], res[1][1])
+    assert all(abs(k) < 1e-4 for k in kls[0]), kls
+    assert abs(kls[1][0]) < 1e-4 and all(abs(k) > 1e-5 for k in kls[1][1:]), kls

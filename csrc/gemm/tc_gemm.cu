@@ -260,9 +260,17 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int64_t ld
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
+  // L2 sector promotion of the TMA loads (LRL_TMA_L2_PROMOTION=0..3: none, 64, 128, 256 bytes)
+  static const CUtensorMapL2promotion promo = [] {
+    const char* e = getenv("LRL_TMA_L2_PROMOTION");
+    const int v = e ? atoi(e) : 3;
+    return v == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                  : v == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                           : v == 2 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  }();
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   LRL_CHECK_FMT(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d): dims %lld x %lld, stride %lld B, box %d x %d",
                 (int)r, (long long)K, (long long)rows, (long long)(ld * 2), kBK, box_rows);
   return m;

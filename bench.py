@@ -49,7 +49,30 @@ def parse():
     ap.add_argument("--micro", type=int, default=4)
     ap.add_argument("--recompute", choices=["auto", "on", "off"], default="auto")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--recipe", choices=["grpo", "dapo-fp8"], default="grpo",
+                    help="grpo: the headline bf16 GRPO config; dapo-fp8: DAPO with W8A8 FP8 rollout, FP8 KV "
+                         "cache and hybrid FP8 training linears (E4M3 forward, E5M2 gradients)")
     return ap.parse_args()
+
+
+def recipe_config(args, model_name: str) -> dict:
+    """Trainer config of the chosen recipe (the YAML schema of ``configs/``)."""
+    vllm = {"temperature": 1.0, "top_p": 1.0}
+    cfg = {"policy": {"model_name": model_name, "learning_rate": 1e-6, "lr_warmup_steps": 0,
+                      "lr_decay_style": "constant", "train_micro_batch_size": args.micro,
+                      "max_grad_norm": 1.0, "weight_decay": 0.01, "generation": {"vllm_cfg": vllm}},
+           "algorithm": {"name": "grpo", "grpo": {"num_generations": args.group, "kl_coeff": 0.0,
+                                                  "clip_ratio": 0.2}},
+           "num_training_steps": args.warmup + 2 * args.steps, "seed": 1234}
+    if args.recipe == "dapo-fp8":
+        vllm.update(kv_cache_dtype="fp8", quantization="fp8_per_block", calculate_log_probs=True)
+        cfg["algorithm"] = {"name": "dapo", "dapo": {
+            "num_generations": args.group, "clip_ratio_low": 0.2, "clip_ratio_high": 0.28,
+            "token_level_pg": True, "filter_groups": {"enable": True}}}
+        cfg["quantization"] = {"rollout": {"precision": "fp8"},
+                               "training": {"fp8": "hybrid", "fp8_recipe": "blockwise"},
+                               "rollout_correction": {"rollout_is": "token", "rollout_is_threshold": 2.0}}
+    return cfg
 
 
 def reference_arm(args) -> None:
@@ -153,13 +176,7 @@ def main() -> None:
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
     margs = resolve_model(args.model)
     recompute = {"on": True, "off": False, "auto": "auto"}[args.recompute]
-    cfg = LumenRLConfig.from_dict({
-        "policy": {"model_name": margs.name, "learning_rate": 1e-6, "lr_warmup_steps": 0,
-                   "lr_decay_style": "constant", "train_micro_batch_size": args.micro,
-                   "max_grad_norm": 1.0, "weight_decay": 0.01,
-                   "generation": {"vllm_cfg": {"temperature": 1.0, "top_p": 1.0}}},
-        "algorithm": {"name": "grpo", "grpo": {"num_generations": args.group, "kl_coeff": 0.0, "clip_ratio": 0.2}},
-        "num_training_steps": args.warmup + 2 * args.steps, "seed": 1234})
+    cfg = LumenRLConfig.from_dict(recipe_config(args, margs.name))
     spec = RLRunSpec(prompts_per_step=args.prompts_per_gpu * world, prompt_len=args.prompt_len, prompt_low=0,
                      prompt_high=151643, max_new_tokens=args.max_new, eos_token_id=151645, reward="parity",
                      rows_per_micro=args.micro, use_cuda_graph=not args.no_graph,
@@ -225,14 +242,16 @@ def main() -> None:
         out = {
             "metric": METRIC, "value": toks / dev_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dev_s / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.recipe == "grpo" else "fp8 (E4M3 fwd / E5M2 grads, bf16 weights)",
             "data": "synthetic: uniform-random prompt ids [0,151643) by seed, random-init weights N(0,0.02)",
             "config": {"model": "Qwen3-8B (36L, h4096, 32q/8kv, hd128, ffn12288, vocab151936, qk-norm)",
                        "global_batch": B * world, "prompts": args.prompts_per_gpu * world, "group": args.group,
                        "seq_len": args.prompt_len + args.max_new, "prompt_len": args.prompt_len,
                        "max_new_tokens": args.max_new, "micro_batch": args.micro,
                        "parallelism": f"dp{world} (sharded AdamW, resident bf16 weights; rollout TP=1 per GPU)",
-                       "recompute": recompute, "cache": "inputs larger than L2 (16 GB of weights per step)"},
+                       "recompute": recompute, "recipe": args.recipe,
+                       "cache": "inputs larger than L2 (16 GB of weights per step)"},
             "clocks": clk,
             "e2e": {"value": toks_e2e / wall, "unit": "tokens/s", "h2d_bytes_per_step": tr.io_bytes["h2d"] * world,
                     "d2h_bytes_per_step": tr.io_bytes.get("d2h", 0) * world},
@@ -243,6 +262,8 @@ def main() -> None:
             "weight_sync_GBps": last.get("weight_sync/GBps"),
             "gen_tokens_per_s": last.get("perf/gen_tokens_per_s"),
             "mean_response_len": last.get("response_length/mean"),
+            **({k: last[k] for k in ("dapo/gen_rounds", "dapo/kept_frac", "rollout_corr/kl") if k in last}
+               if args.recipe != "grpo" else {}),
             **checks,
         }
         print(json.dumps(out))

@@ -104,6 +104,13 @@ void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank
                  double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
                  torch::Tensor norm_out, int64_t wait_cycles);
 std::vector<torch::Tensor> gemm2sm_logprob(torch::Tensor h, torch::Tensor w, torch::Tensor targets, double inv_t);
+std::vector<torch::Tensor> ttt_diag_fwd(torch::Tensor q, torch::Tensor o0, torch::Tensor lse0,
+                                        std::vector<torch::Tensor> kd, std::vector<torch::Tensor> vd, double scale);
+std::vector<torch::Tensor> ttt_diag_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor out, torch::Tensor lse,
+                                        std::vector<torch::Tensor> kd, std::vector<torch::Tensor> vd,
+                                        torch::Tensor dq, double scale);
+std::vector<torch::Tensor> fkl_fwd(torch::Tensor zt, torch::Tensor zd);
+void row_scale_(torch::Tensor x, torch::Tensor g);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
 void symm_close(int64_t ptr);
@@ -195,6 +202,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_norm_mc", &lrl::rs_norm_mc);
   m.def("adamw_ag_mc", &lrl::adamw_ag_mc);
   m.def("gemm2sm_logprob", &lrl::gemm2sm_logprob);
+  m.def("ttt_diag_fwd", &lrl::ttt_diag_fwd);
+  m.def("ttt_diag_bwd", &lrl::ttt_diag_bwd);
+  m.def("fkl_fwd", &lrl::fkl_fwd);
+  m.def("row_scale_", &lrl::row_scale_);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);
   m.def("symm_close", &lrl::symm_close);

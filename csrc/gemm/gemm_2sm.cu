@@ -146,7 +146,7 @@ template <int BN, bool AMN, bool BMN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, void* C, int M, int N, int K, int64_t ldc, int vec,
-                   int tma_c, LogProbArgs lp, int group_m, uint32_t wait_hint, int* err_out) {
+                   int tma_c, LogProbArgs lp, int group_m, uint32_t wait_hint, int l2_hints, int* err_out) {
   using G = Pair<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t full0 = map_to_rank(smem_addr(&full[0]), 0);  // the even CTA's full[0]
+      const uint64_t pol_a = l2_policy(l2_hints & 3), pol_b = l2_policy((l2_hints >> 2) & 3);
       int it = 0;
       bool ok = true;
       for (int t = cid; t < tiles && ok; t += ncl) {
@@ -213,16 +214,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + s * G::kStageBytes;
           uint8_t* sb = sa + G::kABytes;
           if constexpr (AMN) {
-            tma_load_2d_pair(sa, &tmA, fb, am, kb * kBK);
-            tma_load_2d_pair(sa + 8192, &tmA, fb, am + 64, kb * kBK);
+            tma_load_2d_pair_hint(sa, &tmA, fb, am, kb * kBK, pol_a);
+            tma_load_2d_pair_hint(sa + 8192, &tmA, fb, am + 64, kb * kBK, pol_a);
           } else {
-            tma_load_2d_pair(sa, &tmA, fb, kb * kBK, am);
+            tma_load_2d_pair_hint(sa, &tmA, fb, kb * kBK, am, pol_a);
           }
           if constexpr (BMN) {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, fb, bn + 64 * j, kb * kBK);
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair_hint(sb + j * 8192, &tmB, fb, bn + 64 * j, kb * kBK, pol_b);
           } else {
-            tma_load_2d_pair(sb, &tmB, fb, kb * kBK, bn);
+            tma_load_2d_pair_hint(sb, &tmB, fb, kb * kBK, bn, pol_b);
           }
         }
       }
@@ -292,6 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunks = BN / kCols;
     uint8_t* mybuf = staging + (warp - 2) * 2 * kStageChunk;
     int tc = 0, nst = 0;
+    const uint64_t pol_c = l2_policy((l2_hints >> 4) & 3);
     for (int t = cid; t < tiles; t += ncl, ++tc) {
       int mb, nb;
       pair_tile(t, num_m, num_n, group_m, mb, nb);
@@ -385,8 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && row0 < M && col0 < N) {
-            if constexpr (EPI == kE2AccF32) tma_reduce_add_2d(&tmC, sb, col0, row0);
-            else tma_store_2d(&tmC, sb, col0, row0);
+            if constexpr (EPI == kE2AccF32) tma_reduce_add_2d_hint(&tmC, sb, col0, row0, pol_c);
+            else tma_store_2d_hint(&tmC, sb, col0, row0, pol_c);
             bulk_commit();
           }
           ++nst;
@@ -469,8 +472,13 @@ void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc
     const char* e = getenv("LRL_GEMM_WAIT_HINT_NS");
     return (uint32_t)(e ? atoi(e) : 0);
   }();
+  // L2 policies, 2 bits each for A, B and C: 0 evict_normal, 1 evict_last, 2 evict_first
+  static const int l2_hints = [] {
+    const char* e = getenv("LRL_GEMM_L2_HINTS");
+    return e ? atoi(e) : 0;
+  }();
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, c, M, N, K, ldc, (int)vec, (int)tma_c, lp, group_m,
-                                    wait_hint, err_word()));
+                                    wait_hint, l2_hints, err_word()));
 }
 
 }  // namespace

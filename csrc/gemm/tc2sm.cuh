@@ -110,6 +110,29 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// L2 eviction policy for one access (PTX `createpolicy`): code 1 keeps the
+// lines (evict_last), 2 lets them go first (evict_first), 0 is evict_normal.
+__device__ __forceinline__ uint64_t l2_policy(int code) {
+  uint64_t p;
+  if (code == 1)
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+  else if (code == 2)
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  else
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
+// tma_load_2d_pair with an L2 cache policy
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                      int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4}], [%2], %5;\n" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
 // MN-major operand tile (128-byte swizzle): 64 MN elements (128 B) per row,
 // rows along K, 8-row swizzle atoms 1024 B apart (SBO), 64-wide MN slabs
 // `lbo` bytes apart (LBO).
@@ -193,6 +216,23 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                    map),
                "r"(smem_addr(src)), "r"(c0), "r"(c1)
                : "memory");
+}
+
+// tma_store_2d / tma_reduce_add_2d with an L2 cache policy
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int c0, int c1,
+                                                  uint64_t policy) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;\n"
+               ::"l"(map), "r"(smem_addr(src)), "r"(c0), "r"(c1), "l"(policy)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d_hint(const CUtensorMap* map, const void* src, int c0, int c1,
+                                                       uint64_t policy) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], "
+      "%4;\n" ::"l"(map),
+      "r"(smem_addr(src)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }

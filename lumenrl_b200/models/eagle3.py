@@ -34,6 +34,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 from torch import Tensor
 
+from lumenrl_b200 import ops
 from lumenrl_b200.ops import reference as ref
 
 
@@ -44,6 +45,8 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: Tensor) -> Tensor:
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16:
+            return ops.rmsnorm(x, self.weight, self.eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight.float()).to(x.dtype)
 
@@ -66,15 +69,25 @@ class Eagle3Layer(nn.Module):
         self.wo = nn.Linear(heads * head_dim, hidden, bias=False)
         self.w13 = nn.Linear(hidden, 2 * ffn, bias=False)
         self.w2 = nn.Linear(ffn, hidden, bias=False)
-        self.register_buffer("inv_freq", inv_freq, persistent=False)
+        # fp32 RoPE frequencies, kept out of the module's buffers so that a
+        # cast of the module to bf16 does not round them
+        self._inv_freq = inv_freq.float()
         self.scale = 1.0 / math.sqrt(head_dim)
+        self.eps = eps
+
+    def inv_freq(self, device) -> Tensor:
+        if self._inv_freq.device != device:
+            self._inv_freq = self._inv_freq.to(device)
+        return self._inv_freq
 
     def _rope(self, x: Tensor, pos: Tensor) -> Tensor:
-        ang = pos.float().unsqueeze(-1) * self.inv_freq.to(x.device).unsqueeze(0)
+        ang = pos.float().unsqueeze(-1) * self.inv_freq(x.device).unsqueeze(0)
         return ref.apply_rope(x, ang.cos(), ang.sin())
 
-    def forward(self, emb: Tensor, h: Tensor, pos: Tensor, cu: Tensor, cache: list) -> Tensor:
+    def forward(self, emb: Tensor, h: Tensor, pos: Tensor, cu: Tensor, cache: list, max_len: int = 0) -> Tensor:
         T = h.shape[0]
+        if h.is_cuda and h.dtype == torch.bfloat16 and self.hd == 128 and max_len > 0:
+            return self._forward_kernels(emb, h, pos, cu, cache, max_len)
         x = torch.cat([self.input_norm(emb), self.hidden_norm(h)], -1)
         qkv = self.wqkv(x)
         q = qkv[:, : self.nh * self.hd].view(T, self.nh, self.hd)
@@ -89,6 +102,23 @@ class Eagle3Layer(nn.Module):
         gu = self.w13(self.post_norm(h))
         f = gu.shape[-1] // 2
         return h + self.w2(F.silu(gu[:, :f]) * gu[:, f:])
+
+    def _forward_kernels(self, emb: Tensor, h: Tensor, pos: Tensor, cu: Tensor, cache: list, max_len: int) -> Tensor:
+        """Same layer on this package's kernels: RMSNorm, CTA-pair GEMMs,
+        RoPE, TTT attention (flash + diagonal merge), SwiGLU."""
+        from lumenrl_b200.ops.eagle import ttt_attention
+        T = h.shape[0]
+        x = torch.cat([ops.rmsnorm(emb, self.input_norm.weight, self.eps),
+                       ops.rmsnorm(h, self.hidden_norm.weight, self.eps)], -1)
+        qkv = ops.linear(x, self.wqkv.weight)
+        step = len(cache)
+        q, k, v = ops.qk_norm_rope(qkv, None, None, pos + step, self.inv_freq(h.device), self.nh, self.nkv,
+                                   self.hd, self.eps)
+        cache.append((k, v))
+        o = ttt_attention(q, cache, cu, max_len, self.scale)
+        h = h + ops.linear(o.reshape(T, -1), self.wo.weight)
+        gu = ops.linear(ops.rmsnorm(h, self.post_norm.weight, self.eps), self.w13.weight)
+        return h + ops.linear(ops.swiglu(gu), self.w2.weight)
 
 
 def cached_tree_attention(q: Tensor, cache: list, cu: Tensor, scale: float, block: int = 1024) -> Tensor:
@@ -153,9 +183,12 @@ class Eagle3Model(nn.Module):
         T = input_ids.shape[0]
         cu = cu_seqlens
         lens = (cu[1:] - cu[:-1])
-        pos = torch.cat([torch.arange(int(n), device=input_ids.device) for n in lens.tolist()])
+        lens_h = lens.tolist()
+        max_len = max(lens_h) if lens_h else 0
+        pos = torch.cat([torch.arange(int(n), device=input_ids.device) for n in lens_h])
         seq_id = torch.repeat_interleave(torch.arange(len(lens), device=input_ids.device), lens)
-        h = self.fc(aux_hidden)
+        kernels = aux_hidden.is_cuda and aux_hidden.dtype == torch.bfloat16
+        h = ops.linear(aux_hidden, self.fc.weight) if kernels else self.fc(aux_hidden)
         ids, mask = input_ids, loss_mask.float()
         w_teacher = teacher_lm_head.index_select(0, self.d2t.to(teacher_lm_head.device))
         caches: list[list] = [[] for _ in self.layers]
@@ -164,7 +197,7 @@ class Eagle3Model(nn.Module):
         for step in range(self.length):
             emb = F.embedding(ids, embed_weight)
             for li, layer in enumerate(self.layers):
-                h = layer(emb, h, pos, cu, caches[li])
+                h = layer(emb, h, pos, cu, caches[li], max_len)
             # teacher hidden `step` positions ahead (same sequence only)
             tgt_idx = torch.arange(T, device=h.device) + step
             valid = (tgt_idx < T)
@@ -172,8 +205,14 @@ class Eagle3Model(nn.Module):
             valid = valid & (seq_id[tgt_idx] == seq_id) & (mask > 0)
             idx = valid.nonzero(as_tuple=True)[0]
             if idx.numel():
-                kl, acc = self._fkl(self.out_norm(h).index_select(0, idx), target_hidden.index_select(0, tgt_idx[idx]),
-                                    w_teacher, chunk)
+                dh = self.out_norm(h).index_select(0, idx)
+                th = target_hidden.index_select(0, tgt_idx[idx])
+                if kernels:
+                    from lumenrl_b200.ops.eagle import forward_kl
+                    kl_rows, hit = forward_kl(dh, self.lm_head.weight, th, w_teacher)
+                    kl, acc = kl_rows.sum() / idx.numel(), hit.sum() / idx.numel()
+                else:
+                    kl, acc = self._fkl(dh, th, w_teacher, chunk)
                 losses.append(kl)
                 accs.append(acc)
                 total = total + (decay ** step) * kl

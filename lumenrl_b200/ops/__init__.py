@@ -110,7 +110,9 @@ class _Linear(torch.autograd.Function):
                 # gradient buffer: no bf16 weight-grad tensor is ever allocated.
                 mm_tn_acc(mg, dy2, x2)
             else:
-                _accum_main_grad(wh, dy2.t().float() @ x2.float())
+                acc = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+                mm_tn_acc(acc, dy2, x2.contiguous())
+                _accum_main_grad(wh, acc)
             return dx, None, None
         dx = dy @ w
         _accum_main_grad(wh, dy2.t().float() @ x2.float())
@@ -584,7 +586,7 @@ def skinny_linear(x: Tensor, w: Tensor, ksplit: int = 0) -> Tensor:
 # of cuBLAS in isolation at M=64: 12.4 vs 18.2 us on 4096x4096, 15.3 vs 17.9
 # on 6144x4096; inside the CUDA-graph decode step "auto" measured 1.4 % slower
 # than all-cuBLAS, 5.72 vs 5.64 ms per step, hence the default)
-DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "cublas")
+DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "auto")
 
 
 def decode_linear(x: Tensor, w: Tensor) -> Tensor:

@@ -15,6 +15,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 
 import torch
 
@@ -44,6 +45,19 @@ def _time(fn, steps: int, warmup: int) -> float:
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / steps
+
+
+def _time_sustained(fn, steps: int, warmup: int, sustain_ms: float) -> float:
+    """_time after ``sustain_ms`` of back-to-back calls, so that the clocks
+    have settled where the power limit holds them for a long kernel stream."""
+    if sustain_ms > 0:
+        import time
+        t0 = time.perf_counter()
+        while (time.perf_counter() - t0) * 1e3 < sustain_ms:
+            for _ in range(8):
+                fn()
+            torch.cuda.synchronize()
+    return _time(fn, steps, warmup)
 
 
 def bench_decode(ns) -> dict:
@@ -302,8 +316,8 @@ def bench_gemm2(ns) -> dict:
                 ("dgrad", lambda: ext().gemm2sm(dy, False, w, True, None, 0, ns.bn), lambda: dy @ w),
                 ("wgrad", lambda: ext().gemm2sm(dy, True, x, True, mg, 2, ns.bn),
                  lambda: torch.addmm(mg, dy.t(), x, out_dtype=torch.float32, out=mg))]:
-            t_own = _time(own, ns.steps, ns.warmup)
-            t_lib = _time(lib, ns.steps, ns.warmup)
+            t_own = _time_sustained(own, ns.steps, ns.warmup, ns.sustain_ms)
+            t_lib = _time_sustained(lib, ns.steps, ns.warmup, ns.sustain_ms)
             tot["own"] += t_own
             tot["cublas"] += t_lib
             r[kind] = {"own_tflops": round(fl / t_own / 1e9, 1), "cublas_tflops": round(fl / t_lib / 1e9, 1),
@@ -314,6 +328,99 @@ def bench_gemm2(ns) -> dict:
         del x, w, dy, mg
     out["sum_ms"] = {k: round(v, 3) for k, v in tot.items()}
     out["status"] = int(ext().gemm2sm_status())
+    return out
+
+
+def _nvml_handle():
+    """NVML handle of the GPU this process runs on (first visible device)."""
+    import pynvml
+    pynvml.nvmlInit()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[0].strip()
+    if vis.startswith("GPU-"):
+        return pynvml.nvmlDeviceGetHandleByUUID(vis)
+    return pynvml.nvmlDeviceGetHandleByIndex(int(vis) if vis else 0)
+
+
+def bench_gemm2energy(ns) -> dict:
+    """Energy per FLOP of the training GEMMs: each GEMM runs back to back for
+    --sustain-ms (clocks settle under the power limit), then for ~2 s more
+    while NVML's energy counter and CUDA events are read; reports TFLOP/s,
+    joules per PFLOP and the mean SM clock for the pair GEMM at 256- and
+    128-wide tiles and for cuBLAS."""
+    import time
+
+    import pynvml
+    from lumenrl_b200.ops.ext import ext
+    h = _nvml_handle()
+    a = _model_args(ns.model)
+    T = ns.rows * ns.seq
+    shapes = {"qkv": (a.qkv_dim, a.hidden_size), "w13": (2 * a.intermediate_size, a.hidden_size),
+              "w2": (a.hidden_size, a.intermediate_size)}
+    out = {"op": "gemm_energy", "tokens": T}
+    for name, (N, K) in shapes.items():
+        x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        dy = (torch.randn(T, N, device="cuda") / 8).to(torch.bfloat16)
+        fl = 2 * T * N * K
+        r = {}
+        for tag, fn in [("own256_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 256)),
+                        ("own128_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 128)),
+                        ("cublas_fwd", lambda: x @ w.t()),
+                        ("own256_dgrad", lambda: ext().gemm2sm(dy, False, w, True, None, 0, 256)),
+                        ("cublas_dgrad", lambda: dy @ w)]:
+            _time_sustained(fn, 1, 0, ns.sustain_ms)
+            n, clk = 0, []
+            e0 = pynvml.nvmlDeviceGetTotalEnergyConsumption(h)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < 2.0:
+                for _ in range(16):
+                    fn()
+                n += 16
+                clk.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                torch.cuda.synchronize()
+            ev1.record()
+            torch.cuda.synchronize()
+            e1 = pynvml.nvmlDeviceGetTotalEnergyConsumption(h)
+            ms = ev0.elapsed_time(ev1)
+            r[tag] = {"tflops": round(fl * n / ms / 1e9, 1), "J_per_PFLOP": round((e1 - e0) / 1e3 / (fl * n / 1e15), 1),
+                      "W": round((e1 - e0) / ms, 1), "sm_mhz": round(sum(clk) / len(clk))}
+        out[name] = r
+        del x, w, dy
+    out["status"] = int(ext().gemm2sm_status())
+    return out
+
+
+def bench_fp8gemm(ns) -> dict:
+    """Block-scaled FP8 tcgen05 GEMM (csrc/gemm/fp8_gemm.cu) on the forward
+    GEMMs of the Qwen3-8B training linears (E4M3 x E4M3, 1x128 activation
+    and 128x128 weight scales), against the bf16 CTA-pair GEMM and cuBLAS bf16
+    on the same shapes; plus the E5M2-gradient dgrad shape.  Quantisation is
+    outside the timed region (weights are quantised once per optimizer step)."""
+    from lumenrl_b200.ops.ext import ext
+    from lumenrl_b200.quant import fp8 as q8
+    a = _model_args(ns.model)
+    T = ns.rows * ns.seq
+    shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
+              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size)}
+    out = {"op": "fp8_gemm", "tokens": T}
+    for name, (N, K) in shapes.items():
+        x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16)
+        qx, sx = q8.quant_act_1x128(x)
+        qw, sw = q8.quant_weight_128x128(w)
+        fl = 2 * T * N * K
+        t8 = _time(lambda: q8.fp8_matmul(qx, sx, qw, sw), ns.steps, ns.warmup)
+        t16 = _time(lambda: ext().gemm2sm(x, False, w, False, None, 0, 0), ns.steps, ns.warmup)
+        tcb = _time(lambda: x @ w.t(), ns.steps, ns.warmup)
+        ref = q8.dequant_1x128(qx[:256], sx[:256]) @ q8.dequant_128x128(qw, sw).t()
+        err = (q8.fp8_matmul(qx[:256].contiguous(), sx[:256].contiguous(), qw, sw).float() - ref).abs().max().item()
+        out[name] = {"fp8_tflops": round(fl / t8 / 1e9, 1), "bf16_pair_tflops": round(fl / t16 / 1e9, 1),
+                     "cublas_bf16_tflops": round(fl / tcb / 1e9, 1), "fp8_ms": round(t8, 4),
+                     "max_err_vs_dequant": err}
+        del x, w, qx, sx, qw, sw
+    out["status"] = int(q8.fp8_gemm_status())
     return out
 
 
@@ -388,7 +495,7 @@ def bench_comm(ns) -> dict:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
-                                     "dgemm", "gemm2", "gemm2probe"])
+                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -406,10 +513,12 @@ def main(argv=None) -> None:
     ap.add_argument("--mnk", default="", help="gemm2probe shape M,N,K")
     ap.add_argument("--case", default="", help="gemm2probe operand layout: kk, kn, nn or nk")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--sustain-ms", type=float, default=0.0,
+                    help="gemm2: run each GEMM back to back this long before timing it (power-limited clocks)")
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "gemm2energy": bench_gemm2energy,
           "comm": bench_comm, "gemm2": bench_gemm2,
           "gemm2probe": bench_gemm2probe}[ns.what]
     res = fn(ns)

@@ -51,6 +51,9 @@ class SamplingParams:
     seed: int = 0
     eos_token_id: Optional[int] = 2
     stop_at_eos: bool = True
+    # global index of this call's first row: a replica that serves a slice of
+    # a larger batch draws exactly the samples one engine would draw for it
+    row_offset: int = 0
 
 
 @dataclass
@@ -198,7 +201,7 @@ class RolloutEngine:
         eos = sp.eos_token_id if sp.stop_at_eos else None
         alloc = self.cache.allocator
         g = self._graph(S, sp, None)
-        base_seed = sp.seed * 1_000_003
+        base_seed = sp.seed * 1_000_003 + sp.row_offset
         # outputs (one trash row at the end absorbs the writes of idle slots)
         out_tok = torch.full((total + 1, max_new), self.pad_token_id, dtype=torch.long, device=dev)
         out_lp = torch.zeros(total + 1, max_new, dtype=torch.float32, device=dev)
@@ -420,7 +423,7 @@ class RolloutEngine:
             share = (group, max_prefix, max_suffix)
         g = self._graph(B, sp, share)
         ev2 = self._ev()
-        g.row_seed.copy_(torch.arange(B, device=dev) + (sp.seed * 1_000_003 + prompt_offset * n) )
+        g.row_seed.copy_(torch.arange(B, device=dev) + (sp.seed * 1_000_003 + sp.row_offset + prompt_offset * n))
         g.step.fill_(0)
         from lumenrl_b200 import ops
         tok, lp = ops.sample_tokens_device(row_logits, sp.temperature, sp.top_p, g.row_seed, g.step)

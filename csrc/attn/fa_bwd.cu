@@ -1,6 +1,7 @@
 // Causal varlen flash-attention backward on the 5th-generation tensor cores
 // (head dim 128, bf16, GQA), the backward of fa_fwd.cu.  Reference call site:
-// the packed varlen attention of `engine/training/packing.py:363-421`.
+// the packed varlen attention of `engine/training/packing.py:363-421`.  Like
+// the forward, a runtime flag drops the causal mask (ring-attention blocks).
 //
 // With P = exp(S * scale - lse) (lse from the forward), D = rowsum(dO o O):
 //   dP = dO V^T,  dS = P o (dP - D),  dQ = scale dS K,  dK = scale dS^T Q,  dV = P^T dO.
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     fa_bwd_dq_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                      int nseq, int max_tiles, int Hq, int Hk, float scale_log2, float scale,
                      const float* __restrict__ lse2p, const float* __restrict__ dpad, int Tpad,
-                     __nv_bfloat16* __restrict__ dq, int* err_out) {
+                     __nv_bfloat16* __restrict__ dq, int causal, int* err_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
   if (qt >= ntiles) return;  // uniform for the CTA: nothing allocated yet
   const int hk = h / (Hq / Hk);
   const int q0 = qt * kBQ;
-  const int nblocks = qt + 1;  // causal: key blocks 0 .. qt
+  const int nblocks = causal ? qt + 1 : ntiles;  // causal: key blocks 0 .. qt
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qrow = q0 + r;
-    const int lim = min(qrow + 1, len);
+    const int lim = causal ? min(qrow + 1, len) : len;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     // padded per-row statistics: rows past the sequence read lse2 = +inf (P = 0)
     const int64_t pidx = (int64_t)h * Tpad + poff[sidx] + qrow;
@@ -237,7 +238,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       if (!ok) break;
       tc_fence_after();
       const int k0 = j * kBK;
-      const bool need_mask = k0 + kBK > q0 + 1 || k0 + kBK > len;
+      const bool need_mask = (causal && k0 + kBK > q0 + 1) || k0 + kBK > len;
       if constexpr (kTm) {
         // dS for keys [64 hh, 64 hh + 64) into score columns [32 hh, 32 hh + 32), already read
 #pragma unroll 1
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ BwdMaps maps, const int* __restrict__ cu,
                        const int* __restrict__ poff, int nseq, int max_tiles, int Hq, int Hk, float scale_log2,
                        float scale, const float* __restrict__ lse2p, const float* __restrict__ dpad, int Tpad,
-                       __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int* err_out) {
+                       __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int causal, int* err_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -395,7 +396,9 @@ __global__ void __launch_bounds__(kThreadsB, 1)
   volatile int* err = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int G = Hq / Hk;
-  const int nqi = ntiles - kt;  // query tiles kt .. ntiles-1 see this key tile
+  // causal: query tiles kt .. ntiles-1 see this key tile; non-causal: all of them
+  const int qfirst = causal ? kt : 0;
+  const int nqi = ntiles - qfirst;
   const int nit = G * nqi;
   const int k0 = kt * kBK;
 
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       }
       int L = 0, it = 0;  // ring: Q_i, dO_i, dO^T_i, Q^T_i per iteration
       for (; it < nit && *err == kErrNone; ++it) {
-        const int h = hk * G + it / nqi, i = kt + it % nqi;
+        const int h = hk * G + it / nqi, i = qfirst + it % nqi;
         const int col = poff[sidx] + i * kBQ;  // padded column of the query tile
         const int sb = it & 1;
         if (!mbar_wait(&small_empty[sb], ((it >> 1) & 1) ^ 1, err, kErrProducer)) break;
@@ -551,7 +554,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
       ok = __all_sync(0xffffffffu, w1 && mbar_wait(s_full, it & 1, err, kErrEpilogue));
       if (!ok) break;
       tc_fence_after();
-      const bool diag = (kt + it % nqi) == kt;
+      const bool diag = causal && (qfirst + it % nqi) == kt;
       const float* sl = small + sb * 256;
       if constexpr (kTm) {
         // P^T / dS^T for queries [64 hh, 64 hh + 64) into columns [32 hh, 32 hh + 32)
@@ -704,7 +707,7 @@ int64_t fa_bwd_status() {
 // (dq, dk, dv) in bf16.
 std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                   torch::Tensor out, torch::Tensor lse, torch::Tensor cu, int64_t max_seqlen,
-                                  double scale, int64_t streams, int64_t variant) {
+                                  double scale, int64_t streams, int64_t variant, bool causal) {
   for (auto* t : {&dout, &q, &k, &v, &out}) {
     LRL_CHECK((*t));
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 3 && t->size(2) == kD, "fa_bwd: bf16 [T, H, 128]");
@@ -760,7 +763,7 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
   const float sl2 = (float)(scale * 1.4426950408889634);
   dq_kern<<<(unsigned)(max_tiles * nseq * Hq), kThreadsB, kSmemDQ, stream()>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
-      lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dq.data_ptr(),
+      lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dq.data_ptr(), causal ? 1 : 0,
       bwd_err_word().data_ptr<int>());
   // the dK/dV grid can run beside the dQ grid (independent outputs): each
   // fills the SMs the other's tail leaves idle
@@ -779,7 +782,7 @@ std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Te
   kv_kern<<<(unsigned)(max_tiles * nseq * Hk), kThreadsB, kSmemKV, kv_stream>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_tiles, (int)Hq, (int)Hk, sl2, (float)scale,
       lse2p.data_ptr<float>(), dpad.data_ptr<float>(), (int)Tpad, (__nv_bfloat16*)dk.data_ptr(),
-      (__nv_bfloat16*)dv.data_ptr(), bwd_err_word().data_ptr<int>());
+      (__nv_bfloat16*)dv.data_ptr(), causal ? 1 : 0, bwd_err_word().data_ptr<int>());
   if (kv_stream != main) {  // the caller's stream waits for both grids
     cudaEventRecord(ev_join, kv_stream);
     cudaStreamWaitEvent(main, ev_join, 0);

@@ -1,7 +1,9 @@
 // Causal varlen flash-attention forward on the 5th-generation tensor cores
 // (training forward, old-log-prob scoring and prefill; head dim 128, bf16,
 // GQA).  Reference call sites: the packed varlen attention of
-// `engine/training/packing.py:363-421`.
+// `engine/training/packing.py:363-421`.  A runtime flag turns the causal mask
+// off (every query sees every key of its sequence) for the off-diagonal
+// blocks of context-parallel ring attention.
 //
 // One CTA per (query head, pair of 128-query tiles A and B of one sequence),
 // 320 threads:
@@ -131,7 +133,7 @@ template <bool kTwoPass, bool kPoly, bool kPTmem = false>
 __global__ void __launch_bounds__(kThreadsFA, 1)
     fa_fwd_kernel(const __grid_constant__ FAMaps maps, const int* __restrict__ cu, const int* __restrict__ poff,
                   int nseq, int max_pairs, int Hq, int Hk, float scale_log2, __nv_bfloat16* __restrict__ out,
-                  float* __restrict__ lse, int T, int* err_out) {
+                  float* __restrict__ lse, int T, int causal, int* err_out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;                              // Q_A, Q_B
@@ -159,8 +161,11 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
   if (pi >= npairs) return;  // uniform for the CTA: nothing allocated yet
   const int hk = h / (Hq / Hk);
   const int qa0 = 2 * pi * kBQ;                    // first query of tile A (tile B follows)
-  const int nA = 2 * pi + 1;                       // causal key blocks of tile A
-  const int nB = min(2 * pi + 2, nkb);             // ... of tile B (tile B past the end repeats A's)
+  // causal: key blocks 0 .. 2 pi of tile A, 0 .. 2 pi + 1 of tile B (tile B past
+  // the end repeats A's); non-causal (the off-diagonal blocks of ring
+  // attention): every key block for both tiles
+  const int nA = causal ? 2 * pi + 1 : nkb;
+  const int nB = causal ? min(2 * pi + 2, nkb) : nkb;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -291,7 +296,7 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qrow = qa0 + X * kBQ + r;            // query index inside the sequence
-    const int lim = min(qrow + 1, len);            // keys [0, lim) are visible to this row
+    const int lim = causal ? min(qrow + 1, len) : len;  // keys [0, lim) are visible to this row
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t t_s = tmem + lane_off + X * 128, t_o = tmem + lane_off + 256 + X * 128;
     uint8_t* px = sp + X * kTile;
@@ -306,7 +311,7 @@ __global__ void __launch_bounds__(kThreadsFA, 1)
       tc_fence_after();
       const int k0 = j * kBK;
       // only the diagonal block and a sequence's last block need the mask
-      const bool need_mask = k0 + kBK > tile_end - kBQ + 1 || k0 + kBK > len;
+      const bool need_mask = (causal && k0 + kBK > tile_end - kBQ + 1) || k0 + kBK > len;
       float sm[4] = {0.f, 0.f, 0.f, 0.f};
       float alpha = 1.f;
       if constexpr (!kTwoPass) {
@@ -455,9 +460,9 @@ int64_t fa_fwd_status() {
 // q [T, Hq, 128], k/v [T, Hk, 128] bf16 contiguous, cu [nseq + 1] int32 on
 // the device, max_seqlen a host upper bound of the longest sequence (a
 // smaller value leaves query tiles out and sets the status word).  Returns (out [T, Hq, 128] bf16,
-// lse [Hq, T] fp32 natural log).
+// lse [Hq, T] fp32 natural log).  causal = false: no causal mask.
 std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu,
-                                  int64_t max_seqlen, double scale, int64_t variant) {
+                                  int64_t max_seqlen, double scale, int64_t variant, bool causal) {
   LRL_CHECK(q);
   LRL_CHECK(k);
   LRL_CHECK(v);
@@ -496,7 +501,7 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   const int var = variant >= 0 ? (int)variant : env_variant;
   TORCH_CHECK(var >= 0 && var < 5, "fa_fwd: variant 0..4");
   using Kern = void (*)(const FAMaps, const int*, const int*, int, int, int, int, float, __nv_bfloat16*, float*, int,
-                        int*);
+                        int, int*);
   static const Kern kerns[5] = {fa_fwd_kernel<false, false>, fa_fwd_kernel<true, false>,
                                 fa_fwd_kernel<false, true>, fa_fwd_kernel<true, true>,
                                 fa_fwd_kernel<true, false, true>};
@@ -510,7 +515,7 @@ std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tenso
   kerns[var]<<<(unsigned)blocks, kThreadsFA, kSmemFA, stream()>>>(
       maps, cu.data_ptr<int>(), poff.data_ptr<int>(), nseq, (int)max_pairs, (int)Hq, (int)Hk,
       (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), lse.data_ptr<float>(), (int)T,
-      fa_err_word().data_ptr<int>());
+      causal ? 1 : 0, fa_err_word().data_ptr<int>());
   return {out, lse};
 }
 

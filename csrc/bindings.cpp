@@ -83,11 +83,11 @@ torch::Tensor paged_decode_attn_shared_tma(torch::Tensor q, torch::Tensor kc, to
                                            int64_t max_prefix_hint, int64_t max_suffix_hint);
 int64_t decode_tma_status();
 std::vector<torch::Tensor> fa_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu,
-                                  int64_t max_seqlen, double scale, int64_t variant);
+                                  int64_t max_seqlen, double scale, int64_t variant, bool causal);
 int64_t fa_fwd_status();
 std::vector<torch::Tensor> fa_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                   torch::Tensor out, torch::Tensor lse, torch::Tensor cu, int64_t max_seqlen,
-                                  double scale, int64_t streams, int64_t variant);
+                                  double scale, int64_t streams, int64_t variant, bool causal);
 int64_t fa_bwd_status();
 void kv_append(torch::Tensor k, torch::Tensor v, torch::Tensor kc, torch::Tensor vc, torch::Tensor slots,
                double inv_ks, double inv_vs);
@@ -186,10 +186,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attn_shared_tma", &lrl::paged_decode_attn_shared_tma);
   m.def("decode_tma_status", &lrl::decode_tma_status);
   m.def("fa_fwd", &lrl::fa_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"), py::arg("max_seqlen"),
-        py::arg("scale"), py::arg("variant") = -1);
+        py::arg("scale"), py::arg("variant") = -1, py::arg("causal") = true);
   m.def("fa_fwd_status", &lrl::fa_fwd_status);
   m.def("fa_bwd", &lrl::fa_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"),
-        py::arg("lse"), py::arg("cu"), py::arg("max_seqlen"), py::arg("scale"), py::arg("streams") = 1, py::arg("variant") = -1);
+        py::arg("lse"), py::arg("cu"), py::arg("max_seqlen"), py::arg("scale"), py::arg("streams") = 1, py::arg("variant") = -1,
+        py::arg("causal") = true);
   m.def("fa_bwd_status", &lrl::fa_bwd_status);
   m.def("kv_append", &lrl::kv_append);
   m.def("tc_gemm", &lrl::tc_gemm, py::arg("a"), py::arg("b"), py::arg("c") = py::none(), py::arg("epi") = 0,

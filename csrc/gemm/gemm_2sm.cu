@@ -18,10 +18,11 @@
 // 32 KB of operands for 2 x 128 x 256 x 64 FLOPs, half the L2 traffic of a
 // single-SM 128 x 256 tile.
 //
-// Warp roles per CTA (192 threads):
+// Warp roles per CTA (192 threads; 320 for the 512-wide tile, whose epilogue
+// has eight warps):
 //   warp 0     TMA producer: one lane streams A / B slabs into a kStages ring;
 //              the bytes of both CTAs are counted on the even CTA's barrier
-//   warp 1     allocates TMEM (pair-wide, two accumulator buffers); in the
+//   warp 1     allocates TMEM (pair-wide, one or two accumulator buffers); in the
 //              even CTA one lane issues the MMAs and commits each stage back
 //              to both producers and each finished tile to both epilogues
 //   warps 2-5  epilogue: tcgen05.ld of this CTA's 128 rows (32 per warp),
@@ -31,7 +32,9 @@
 //              in L2 (no read-modify-write by the SM).  Each warp double-
 //              buffers its staging chunk; TMEM is released as soon as the
 //              tile's last columns are in registers.
-// Two TMEM buffers let the epilogue of tile i overlap the MMAs of tile i+1.
+// With BN <= 256, two TMEM buffers let the epilogue of tile i overlap the
+// MMAs of tile i+1; the 512-wide tile (the default for N >= 512) fills TMEM
+// with one buffer and drains it with eight epilogue warps (see Pair).
 // Rows / columns of C whose stride is not 16-byte aligned fall back to
 // per-thread stores.
 // Every mbarrier wait is bounded and reports a status word instead of hanging.
@@ -50,7 +53,7 @@ using namespace tc2;
 
 namespace {
 
-constexpr int kPairM = 256, kBK = 64, kThreads = 192;
+constexpr int kPairM = 256, kBK = 64;
 
 enum Epi2 : int { kE2BF16 = 0, kE2F32 = 1, kE2AccF32 = 2, kE2None = 3, kE2LogProb = 4 };
 
@@ -67,16 +70,32 @@ struct LogProbArgs {
 };
 
 constexpr int kStageChunk = 32 * 128;               // one warp's 32 rows x 128 bytes of C
-constexpr int kStagingBytes = 4 * 2 * kStageChunk;  // 4 epilogue warps, double-buffered
 
+// Tile shapes.  BN 128 / 256: one MMA of N = BN per 16-wide K step, two TMEM
+// accumulator buffers (the epilogue of tile i overlaps the MMAs of tile i+1),
+// four epilogue warps with double-buffered staging.  BN 512: two MMAs of N =
+// 256 per K step that share the A slab, so a 64-wide K step brings 48 KB per
+// SM for 2 x 128 x 512 x 64 FLOPs -- three quarters of the 256-wide tile's L2
+// traffic per FLOP, which under the power limit is what sets the clock -- but
+// the 512 accumulator columns fill TMEM: one buffer, drained by eight
+// epilogue warps (two per TMEM lane quarter, one column half each).
 template <int BN>
 struct Pair {
+  static constexpr int kBHalves = BN == 512 ? 2 : 1;  // MMAs per 16-wide K step
+  static constexpr int kMmaN = BN / kBHalves;          // N of each MMA
   static constexpr int kABytes = 128 * kBK * 2;       // this CTA's 128 rows of A
   static constexpr int kBBytes = (BN / 2) * kBK * 2;  // this CTA's BN/2 rows of B
+  static constexpr int kBHalfBytes = kBBytes / kBHalves;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN == 256 ? 6 : 8;
-  static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmem = kStages * kStageBytes + kStagingBytes + 1024 + 256;
+  static constexpr int kStages = BN == 512 ? 4 : (BN == 256 ? 6 : 8);
+  static constexpr int kBufs = BN == 512 ? 1 : 2;      // TMEM accumulator buffers
+  static constexpr int kTmemCols = kBufs * BN;
+  static constexpr int kEpiWarps = BN == 512 ? 8 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kStagingBufs = BN == 512 ? 1 : 2;  // staging chunks per epilogue warp
+  static constexpr int kStaging = kEpiWarps * kStagingBufs * kStageChunk;
+  static constexpr int kSmem = kStages * kStageBytes + kStaging + 1024 + 256;
+  static_assert(kSmem <= 232448, "pair GEMM: shared memory over the per-CTA limit");
 };
 
 // grouped raster: `group_m` consecutive 256-row tiles share every B panel of
@@ -143,15 +162,16 @@ __device__ __forceinline__ void store32(void* C, int row, int col, int N, int64_
 }
 
 template <int BN, bool AMN, bool BMN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Pair<BN>::kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, void* C, int M, int N, int K, int64_t ldc, int vec,
                    int tma_c, LogProbArgs lp, int group_m, uint32_t wait_hint, int l2_hints, int* err_out) {
   using G = Pair<BN>;
+  static_assert(EPI != kE2LogProb || BN <= 256, "the log-prob epilogue reduces a tile with four warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + G::kStages * G::kStageBytes;   // 1024-aligned (stage sizes are multiples of 1 KB)
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + G::kStaging);
   uint64_t* empty = full + G::kStages;
   uint64_t* tfull = empty + G::kStages;
   uint64_t* tempty = tfull + 2;
@@ -174,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs
+      mbar_init(&tempty[b], 2 * G::kEpiWarps);  // every epilogue warp of both CTAs
     }
     mbar_init(mdone, 1);
     *err = kErrNone;
@@ -202,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int mb, nb;
         pair_tile(t, num_m, num_n, group_m, mb, nb);
         const int am = mb * kPairM + rank * 128;
-        const int bn = nb * BN + rank * (BN / 2);
+        const int bn = nb * BN + rank * (G::kMmaN / 2);  // + hh * kMmaN for B half hh
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int s = it % G::kStages;
           if (!mbar_wait_sleep(&empty[s], ((it / G::kStages) & 1) ^ 1, err, kErrProducer, wait_hint)) {
@@ -219,12 +239,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d_pair_hint(sa, &tmA, fb, kb * kBK, am, pol_a);
           }
-          if constexpr (BMN) {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tma_load_2d_pair_hint(sb + j * 8192, &tmB, fb, bn + 64 * j, kb * kBK, pol_b);
-          } else {
-            tma_load_2d_pair_hint(sb, &tmB, fb, kb * kBK, bn, pol_b);
+          for (int hh = 0; hh < G::kBHalves; ++hh) {
+            if constexpr (BMN) {
+#pragma unroll
+              for (int j = 0; j < G::kMmaN / 128; ++j)
+                tma_load_2d_pair_hint(sb + hh * G::kBHalfBytes + j * 8192, &tmB, fb, bn + hh * G::kMmaN + 64 * j,
+                                      kb * kBK, pol_b);
+            } else {
+              tma_load_2d_pair_hint(sb + hh * G::kBHalfBytes, &tmB, fb, kb * kBK, bn + hh * G::kMmaN, pol_b);
+            }
           }
         }
       }
@@ -244,12 +268,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32_major(kPairM, BN, AMN, BMN);
+      constexpr uint32_t idesc = idesc_bf16_f32_major(kPairM, G::kMmaN, AMN, BMN);
       int it = 0, tc = 0;
       bool ok = true;
       for (int t = cid; t < tiles && ok; t += ncl, ++tc) {
-        const int buf = tc & 1;
-        if (!mbar_wait_sleep(&tempty[buf], ((tc >> 1) & 1) ^ 1, err, kErrMma, wait_hint)) {
+        const int buf = tc % G::kBufs;
+        if (!mbar_wait_sleep(&tempty[buf], ((tc / G::kBufs) & 1) ^ 1, err, kErrMma, wait_hint)) {
           ok = false;
           break;
         }
@@ -267,8 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = AMN ? sw128_mnmajor_desc(a0 + k * 2048, 8192) : sw128_kmajor_desc(a0 + k * 32);
-            const uint64_t bd = BMN ? sw128_mnmajor_desc(b0 + k * 2048, 8192) : sw128_kmajor_desc(b0 + k * 32);
-            umma_bf16_pair(d, ad, bd, idesc, (kb | k) != 0);
+#pragma unroll
+            for (int hh = 0; hh < G::kBHalves; ++hh) {
+              const uint32_t bh = b0 + hh * G::kBHalfBytes;
+              const uint64_t bd = BMN ? sw128_mnmajor_desc(bh + k * 2048, 8192) : sw128_kmajor_desc(bh + k * 32);
+              umma_bf16_pair(d + hh * G::kMmaN, ad, bd, idesc, (kb | k) != 0);
+            }
           }
           umma_commit_pair(&empty[s], 3);
         }
@@ -279,8 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!wait_drain(mdone, 0)) *err = kErrDrain;
       if (ok && *err == kErrNone) {
         // the other CTA's epilogue arrivals on tempty have landed
-        for (int j = tc; j < tc + 2; ++j)
-          if (!wait_drain(&tempty[j & 1], ((j >> 1) & 1) ^ 1)) {
+        for (int j = tc; j < tc + G::kBufs; ++j)
+          if (!wait_drain(&tempty[j % G::kBufs], ((j / G::kBufs) & 1) ^ 1)) {
             *err = kErrDrain;
             break;
           }
@@ -292,14 +320,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // bf16: 64 columns (128 B) per staged chunk; fp32: 32 columns
     constexpr int kCols = (EPI == kE2BF16 || EPI == kE2None) ? 64 : 32;
     constexpr int kChunks = BN / kCols;
-    uint8_t* mybuf = staging + (warp - 2) * 2 * kStageChunk;
+    uint8_t* mybuf = staging + (warp - 2) * G::kStagingBufs * kStageChunk;
+    // with eight epilogue warps, warps 2-5 drain the first column half, 6-9 the second
+    constexpr int kParts = G::kEpiWarps / 4;
+    const int c_lo = ((warp - 2) >> 2) * (kChunks / kParts), c_hi = c_lo + kChunks / kParts;
     int tc = 0, nst = 0;
     const uint64_t pol_c = l2_policy((l2_hints >> 4) & 3);
     for (int t = cid; t < tiles; t += ncl, ++tc) {
       int mb, nb;
       pair_tile(t, num_m, num_n, group_m, mb, nb);
-      const int buf = tc & 1;
-      if (!mbar_wait_sleep(&tfull[buf], (tc >> 1) & 1, err, kErrEpilogue, wait_hint)) break;
+      const int buf = tc % G::kBufs;
+      if (!mbar_wait_sleep(&tfull[buf], (tc / G::kBufs) & 1, err, kErrEpilogue, wait_hint)) break;
       tc_fence_after();
       const int row0 = mb * kPairM + rank * 128 + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
@@ -346,12 +377,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c) {
+      for (int c = c_lo; c < c_hi; ++c) {
         uint32_t r0[32], r1[32];
         tmem_ld32_nowait(tbase + c * kCols, r0);
         if constexpr (kCols == 64) tmem_ld32_nowait(tbase + c * kCols + 32, r1);
         tmem_ld_wait();
-        if (c == kChunks - 1) {
+        if (c == c_hi - 1) {
           // every accumulator column of this tile is in registers: give the
           // TMEM buffer back to the MMA warp before the stores
           tc_fence_before();
@@ -365,8 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (tma_c) {
           // stage 32 rows x 128 B in this warp's buffer (128-byte swizzle:
           // 16-byte unit j of row r sits at unit j ^ (r & 7)), then one bulk store
-          uint8_t* sb = mybuf + (nst & 1) * kStageChunk;
-          if (lane == 0) bulk_wait_read<1>();   // the store that used this buffer has read it
+          uint8_t* sb = mybuf + (nst % G::kStagingBufs) * kStageChunk;
+          if (lane == 0) bulk_wait_read<G::kStagingBufs - 1>();   // the store that used this buffer has read it
           __syncwarp();
           uint4* rowp = reinterpret_cast<uint4*>(sb + lane * 128);
 #pragma unroll
@@ -445,7 +476,7 @@ void launch2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(Pair<BN>::kThreads);
   cfg.dynamicSmemBytes = Pair<BN>::kSmem;
   cfg.stream = stream();
   cfg.attrs = attr;
@@ -552,15 +583,23 @@ torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c1
   }
   c10::cuda::CUDAGuard guard(a.device());
   if (bn == 0) {
-    // 256-wide tiles: a 256 x 128 pair tile needs 96 B of operands per SM
-    // clock, more than L2 delivers, so it only pays for N <= 128
-    bn = N <= 128 ? 128 : 256;
+    // 256 x 128 pair tiles need 96 B of operands per SM clock, more than L2
+    // delivers, so they only pay for N <= 128.  512-wide tiles carry a quarter
+    // less L2 traffic per FLOP than 256-wide ones; under the power limit that
+    // measured 0.965 of cuBLAS over the Qwen3-8B training GEMMs against 0.934
+    // (LRL_GEMM_BN=256 selects the double-buffered 256-wide tile)
+    static const int pref = [] {
+      const char* e = getenv("LRL_GEMM_BN");
+      return e ? atoi(e) : 512;
+    }();
+    bn = N <= 128 ? 128 : (pref == 512 && N >= 512 ? 512 : 256);
   }
-  TORCH_CHECK(bn == 128 || bn == 256, "gemm2sm: bn must be 128 or 256");
+  TORCH_CHECK(bn == 128 || bn == 256 || bn == 512, "gemm2sm: bn must be 128, 256 or 512");
+  const int b_box = (int)(bn == 512 ? 128 : bn / 2);   // B rows per CTA and MMA
   const CUtensorMap ma = a_mn ? make_kmajor_map(a.data_ptr(), K, M, a.stride(0), 64)
                               : make_kmajor_map(a.data_ptr(), M, K, a.stride(0), 128);
   const CUtensorMap mb = b_mn ? make_kmajor_map(b.data_ptr(), K, N, b.stride(0), 64)
-                              : make_kmajor_map(b.data_ptr(), N, K, b.stride(0), (int)(bn / 2));
+                              : make_kmajor_map(b.data_ptr(), N, K, b.stride(0), b_box);
   const int64_t ldc = out.stride(0);
   const int esz = (epi == kE2F32 || epi == kE2AccF32) ? 4 : 2;
   const bool vec = (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0) && ((ldc * esz) % 16 == 0);
@@ -574,8 +613,8 @@ torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c1
     if (epi == kE2BF16) GO(BNV, AM, BM, kE2BF16);                     \
     else if (epi == kE2F32) GO(BNV, AM, BM, kE2F32);                  \
     else if (epi == kE2AccF32) GO(BNV, AM, BM, kE2AccF32);            \
-    else if (BNV == 256) GO(256, AM, BM, kE2None);                    \
-    else TORCH_CHECK(false, "gemm2sm: the timing probe needs bn 256"); \
+    else if (BNV != 128) GO(BNV == 128 ? 256 : BNV, AM, BM, kE2None); \
+    else TORCH_CHECK(false, "gemm2sm: the timing probe needs bn 256 or 512"); \
   } while (0)
 #define MAJ(BNV)                                   \
   do {                                             \
@@ -584,7 +623,8 @@ torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c1
     else if (a_mn && b_mn) EPIS(BNV, true, true);  \
     else EPIS(BNV, true, false);                   \
   } while (0)
-  if (bn == 256) MAJ(256);
+  if (bn == 512) MAJ(512);
+  else if (bn == 256) MAJ(256);
   else MAJ(128);
 #undef MAJ
 #undef EPIS

@@ -18,9 +18,12 @@ differentiable all-reduce).
 * ``gather_seq`` / ``scatter_seq``: put per-rank token tensors back in
   sequence order (all-gather) differentiably, e.g. for log-probs.
 
-Block math: on CUDA the per-block forward/backward are PyTorch's varlen
-flash-attention kernels (native GQA, LSE returned and accepted back); on CPU
-an fp32 restatement is used.
+Block math: on CUDA with bf16 and head dim 128 every block runs on this
+package's tcgen05 flash kernels (``csrc/attn/fa_fwd.cu`` / ``fa_bwd.cu``,
+causal for the diagonal blocks, unmasked for the others; the forward returns
+the block's LSE, the backward takes the merged output and LSE); other CUDA
+shapes use PyTorch's varlen flash-attention kernels; on CPU an fp32
+restatement is used.
 """
 
 from __future__ import annotations
@@ -54,6 +57,8 @@ def _expand(k: Tensor, hq: int) -> Tensor:
 def _block_fwd(q: Tensor, k: Tensor, v: Tensor, causal: bool, scale: float) -> tuple[Tensor, Tensor]:
     """q [B,H,Tq,D], k/v [B,Hk,Tk,D] -> (o [B,H,Tq,D] in q's dtype, lse [B,H,Tq] fp32)."""
     H = q.shape[1]
+    if _tc_ok(q):
+        return _tc_fwd(q, k, v, causal, scale)
     if q.is_cuda:
         return _varlen_fwd(q, k, v, causal, scale)
     k, v = _expand(k, H), _expand(v, H)
@@ -70,6 +75,8 @@ def _block_bwd(do: Tensor, q: Tensor, k: Tensor, v: Tensor, o: Tensor, lse: Tens
                scale: float) -> tuple[Tensor, Tensor, Tensor]:
     """Gradients of one block given the GLOBAL output ``o`` and ``lse``."""
     H, Hk = q.shape[1], k.shape[1]
+    if _tc_ok(q):
+        return _tc_bwd(do, q, k, v, o, lse, causal, scale)
     if q.is_cuda:
         return _varlen_bwd(do, q, k, v, o, lse, causal, scale)
     ke, ve = _expand(k, H), _expand(v, H)
@@ -135,6 +142,29 @@ def _varlen_bwd(do, q, k, v, o, lse, causal, scale):
 
 
 _LSE_LAYOUT = [2]
+
+
+def _tc_ok(q: Tensor) -> bool:
+    from lumenrl_b200.ops.attention import TRAIN_ATTN
+    return TRAIN_ATTN == "tc" and q.is_cuda and q.dtype == torch.bfloat16 and q.shape[-1] == 128
+
+
+def _tc_fwd(q, k, v, causal, scale):
+    """One block on the tcgen05 forward: (o [B,H,T,D] bf16, lse [B,H,T] fp32)."""
+    from lumenrl_b200.ops.ext import ext
+    B, H, Tq, D = q.shape
+    out, lse = ext().fa_fwd(_to_thd(q), _to_thd(k), _to_thd(v), _cu(B, Tq, q.device), Tq, scale, causal=causal)
+    return _from_thd(out, B), lse.view(H, B, Tq).permute(1, 0, 2)
+
+
+def _tc_bwd(do, q, k, v, o, lse, causal, scale):
+    """Block gradients on the tcgen05 backward from the GLOBAL output and LSE."""
+    from lumenrl_b200.ops.ext import ext
+    B, H, Tq, D = q.shape
+    lse_in = lse.permute(1, 0, 2).reshape(H, B * Tq).contiguous().float()
+    dq, dk, dv = ext().fa_bwd(_to_thd(do.to(q.dtype)), _to_thd(q), _to_thd(k), _to_thd(v), _to_thd(o.to(q.dtype)),
+                              lse_in, _cu(B, Tq, q.device), Tq, scale, causal=causal)
+    return _from_thd(dq, B).float(), _from_thd(dk, B).float(), _from_thd(dv, B).float()
 
 
 def _merge(o: Optional[Tensor], lse: Optional[Tensor], ob: Tensor, lb: Tensor) -> tuple[Tensor, Tensor]:

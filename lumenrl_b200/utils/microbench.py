@@ -363,7 +363,9 @@ def bench_gemm2energy(ns) -> dict:
         dy = (torch.randn(T, N, device="cuda") / 8).to(torch.bfloat16)
         fl = 2 * T * N * K
         r = {}
-        for tag, fn in [("own256_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 256)),
+        for tag, fn in [("own512_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 512)),
+                        ("own512_dgrad", lambda: ext().gemm2sm(dy, False, w, True, None, 0, 512)),
+                        ("own256_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 256)),
                         ("own128_fwd", lambda: ext().gemm2sm(x, False, w, False, None, 0, 128)),
                         ("cublas_fwd", lambda: x @ w.t()),
                         ("own256_dgrad", lambda: ext().gemm2sm(dy, False, w, True, None, 0, 256)),
@@ -509,7 +511,7 @@ def main(argv=None) -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--recompute", action="store_true")
-    ap.add_argument("--bn", type=int, default=0, help="pair GEMM tile width (0 = auto, 128, 256)")
+    ap.add_argument("--bn", type=int, default=0, help="pair GEMM tile width (0 = auto, 128, 256, 512)")
     ap.add_argument("--mnk", default="", help="gemm2probe shape M,N,K")
     ap.add_argument("--case", default="", help="gemm2probe operand layout: kk, kn, nn or nk")
     ap.add_argument("--no-graph", action="store_true")

@@ -25,7 +25,7 @@ def _operands(M, N, K, a_mn, b_mn, dev):
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])
 def test_gemm2sm_bf16(cuda, M, N, K, a_mn, b_mn, bn):
     if (a_mn and M % 8) or (b_mn and N % 8):
         pytest.skip("MN-major operands need a multiple of 8 along M / N")
@@ -39,12 +39,13 @@ def test_gemm2sm_bf16(cuda, M, N, K, a_mn, b_mn, bn):
 
 
 @pytest.mark.parametrize("M,N,K", [(384, 768, 1024), (4096, 1032, 6144), (136, 256, 104)])
-def test_gemm2sm_fp32_and_accumulate(cuda, M, N, K):
+@pytest.mark.parametrize("bn", [0, 512])
+def test_gemm2sm_fp32_and_accumulate(cuda, M, N, K, bn):
     A, B, a, b = _operands(M, N, K, True, True, cuda)
     c = torch.randn(M, N, device=cuda)
     c0 = c.clone()
-    ext().gemm2sm(a, True, b, True, c, 2, 0)          # wgrad form: c += A . B^T
-    f = ext().gemm2sm(A, False, B, False, None, 1, 0)  # fp32 out
+    ext().gemm2sm(a, True, b, True, c, 2, bn)          # wgrad form: c += A . B^T
+    f = ext().gemm2sm(A, False, B, False, None, 1, bn)  # fp32 out
     torch.cuda.synchronize()
     assert ext().gemm2sm_status() == 0
     ref = A.float() @ B.float().t()

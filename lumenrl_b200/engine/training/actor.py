@@ -70,6 +70,12 @@ class ActorEngine:
             self.model.init_weights(seed)
         self.model.gradient_checkpointing = gradient_checkpointing is True
         self.recompute_policy = "auto" if gradient_checkpointing == "auto" else None
+        # context parallelism: this rank scores its zigzag share of every
+        # sequence; the optimizer still reduces over all ranks (a CP group's
+        # ranks hold the same rows, so they add up like data-parallel ranks)
+        self.cp, self.cp_rank, self.cp_group = state.cp_size, state.cp_rank, state.cp_group
+        if self.cp > 1:
+            self.model.cp_group = state.cp_group
         self.trainable = trainable
         self.opt: Optional[ShardedFlatAdamW] = None
         self.sched: Optional[LRSchedule] = None
@@ -97,7 +103,7 @@ class ActorEngine:
         ent = torch.zeros(B, R, dtype=torch.float32, device=self.device) if want_entropy else None
         for rows in make_micro_batches(lens, token_budget=token_budget):
             pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
-                                self.device)
+                                self.device, self.cp, self.cp_rank)
             self._set_replay(batch, pb)
             lp, e = self._forward_scored(pb, temperature, want_entropy)
             rows_t = torch.as_tensor(rows, device=self.device)[pb.out_row]
@@ -105,6 +111,10 @@ class ActorEngine:
             if want_entropy:
                 ent[rows_t, pb.out_col] = e
         self.model.routing_replay = None
+        if self.cp > 1:   # each CP rank scored its own positions; the others are zero
+            torch.distributed.all_reduce(logp, group=self.cp_group)
+            if want_entropy:
+                torch.distributed.all_reduce(ent, group=self.cp_group)
         return logp, ent
 
     def _set_replay(self, batch: DataProto, pb: PackedBatch) -> None:
@@ -141,7 +151,8 @@ class ActorEngine:
             for m0 in range(0, B, mini_size):
                 mini_rows = list(range(m0, min(B, m0 + mini_size)))
                 local_tok = float(mask_grid[mini_rows].sum())
-                global_tok = max(all_reduce_sum(local_tok), 1.0)
+                # the ranks of a CP group hold the same rows: count them once
+                global_tok = max(all_reduce_sum(local_tok, self.state) / self.cp, 1.0)
                 micro = make_micro_batches([lens[r] for r in mini_rows], rows_per_micro=rows_per_micro,
                                            token_budget=token_budget)
                 t0 = time.perf_counter()
@@ -187,7 +198,7 @@ class ActorEngine:
                     global_tok: float, temperature: float) -> dict[str, float]:
         t = batch.tensors
         pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
-                            self.device)
+                            self.device, self.cp, self.cp_rank)
         self._set_replay(batch, pb)
         logp, _ = self._forward_scored(pb, temperature, want_entropy=False)
         r_idx = torch.as_tensor(rows, device=self.device)[pb.out_row]

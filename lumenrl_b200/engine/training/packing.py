@@ -67,12 +67,54 @@ def pack_rows(prompts: list[Tensor], responses: list[Tensor], device, rows: list
         num_rows=len(prompts))
 
 
+def pack_rows_cp(prompts: list[Tensor], responses: list[Tensor], device, rows: list[int] | None, cp: int,
+                 cp_rank: int) -> PackedBatch:
+    """Context-parallel pack: every sequence is right-padded to one length L
+    (a multiple of 2 * cp) and this rank keeps its two zigzag chunks of each
+    (chunks ``cp_rank`` and ``2 cp - 1 - cp_rank`` of ``2 cp``), so the pack is
+    B equal segments of 2 L / (2 cp) tokens at their global positions.  Only
+    the response tokens scored by this rank's positions appear in
+    ``score_index`` / ``targets`` / ``out_row`` / ``out_col``; pad tokens are
+    attended by nothing real (they sit after every real token)."""
+    from lumenrl_b200.parallel.context_parallel import zigzag_indices
+    lens = [int(p.numel()) + int(a.numel()) for p, a in zip(prompts, responses)]
+    L = max(lens) if lens else 0
+    L = max(2 * cp, -(-L // (2 * cp)) * (2 * cp))
+    loc = zigzag_indices(L, cp, cp_rank)                  # global positions kept here
+    two_c = int(loc.numel())
+    where = torch.full((L,), -1, dtype=torch.long)
+    where[loc] = torch.arange(two_c)
+    ids, score, tgt, orow, ocol = [], [], [], [], []
+    for r, (p, a) in enumerate(zip(prompts, responses)):
+        lp, la = int(p.numel()), int(a.numel())
+        seq = torch.zeros(L, dtype=torch.long)
+        seq[: lp + la] = torch.cat([p, a]).long()
+        ids.append(seq[loc])
+        if la > 0:
+            g = torch.arange(lp - 1, lp + la - 1)         # positions that score response tokens
+            keep = where[g] >= 0
+            score.append(r * two_c + where[g[keep]])
+            tgt.append(a[keep].long())
+            orow.append(torch.full((int(keep.sum()),), r, dtype=torch.long))
+            ocol.append(torch.arange(la)[keep])
+    B = len(prompts)
+    cat = lambda xs: (torch.cat(xs) if xs else torch.zeros(0, dtype=torch.long)).to(device)  # noqa: E731
+    return PackedBatch(
+        input_ids=cat(ids), positions=loc.repeat(B).to(device),
+        cu_seqlens=torch.arange(0, B * two_c + 1, two_c, dtype=torch.int32, device=device), max_seqlen=two_c,
+        score_index=cat(score), targets=cat(tgt), out_row=cat(orow), out_col=cat(ocol),
+        rows=list(rows) if rows is not None else list(range(B)), num_rows=B)
+
+
 def pack_from_grid(prompt_ids: Tensor, prompt_lens: Tensor, responses: Tensor, response_lens: Tensor,
-                   rows: list[int], device) -> PackedBatch:
-    """Rows of right-padded prompt/response grids -> PackedBatch."""
+                   rows: list[int], device, cp: int = 1, cp_rank: int = 0) -> PackedBatch:
+    """Rows of right-padded prompt/response grids -> PackedBatch (with
+    ``cp`` > 1: this context-parallel rank's zigzag share, ``pack_rows_cp``)."""
     pl, rl = prompt_lens.tolist(), response_lens.tolist()
     ps = [prompt_ids[r, : pl[r]] for r in rows]
     rs = [responses[r, : rl[r]] for r in rows]
+    if cp > 1:
+        return pack_rows_cp(ps, rs, device, rows, cp, cp_rank)
     return pack_rows(ps, rs, device, rows)
 
 

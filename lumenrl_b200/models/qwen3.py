@@ -151,6 +151,7 @@ class Qwen3Model(nn.Module):
         self.routing_replay = None   # set by moe.r3 for rollout routing replay
         self.aux_losses: list[Tensor] = []
         self.fp8_training = None     # quant.fp8.FP8TrainingManager: FP8 decoder linears when set
+        self.cp_group = None         # context-parallel group: attention runs as a ring over it
 
     # -- parameter access ------------------------------------------------------
     def p(self, name: str) -> nn.Parameter:
@@ -200,8 +201,22 @@ class Qwen3Model(nn.Module):
         kn = P.get(f"layers.{i}.k_norm")
         q, k, v = ops.qk_norm_rope(qkv, qn, kn, positions, self.inv_freq, a.num_heads, a.num_kv_heads, a.head_dim,
                                    a.rms_norm_eps)
-        o = ops.attention_varlen(q, k, v, cu, max_len, causal=True, scale=1.0 / math.sqrt(a.head_dim))
+        if self.cp_group is not None:
+            o = self._ring_attention(q, k, v, max_len)
+        else:
+            o = ops.attention_varlen(q, k, v, cu, max_len, causal=True, scale=1.0 / math.sqrt(a.head_dim))
         return self._linear(f"layers.{i}.wo", o.reshape(o.shape[0], -1))
+
+    def _ring_attention(self, q: Tensor, k: Tensor, v: Tensor, seg: int) -> Tensor:
+        """Context parallelism: the pack is B segments of ``seg`` tokens, each
+        this rank's zigzag share of one sequence; attention over the whole
+        sequences runs as a ring over the CP group."""
+        from lumenrl_b200.parallel.context_parallel import ring_attention
+        T = q.shape[0]
+        B = T // seg
+        to_bhtd = lambda x: x.reshape(B, seg, x.shape[1], x.shape[2]).transpose(1, 2).contiguous()  # noqa: E731
+        o = ring_attention(to_bhtd(q), to_bhtd(k), to_bhtd(v), self.cp_group, 1.0 / math.sqrt(self.args.head_dim))
+        return o.transpose(1, 2).reshape(T, q.shape[1], q.shape[2])
 
     def _mlp_block(self, i: int, h: Tensor) -> Tensor:
         P = self._params

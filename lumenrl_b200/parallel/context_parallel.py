@@ -36,6 +36,22 @@ import torch.distributed as dist
 from torch import Tensor
 
 
+def make_dp_cp_groups(cp: int):
+    """Context-parallel groups of ``cp`` consecutive ranks (every rank calls
+    this, same order).  Returns this rank's CP group; with ``set_state`` the
+    rank's ``ParallelState`` gets ``cp_size``, ``cp_rank`` and ``cp_group``,
+    which ``ActorEngine`` and ``SFTTrainer`` read."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if world % cp:
+        raise ValueError(f"world {world} is not a multiple of cp {cp}")
+    mine = None
+    for g0 in range(0, world, cp):
+        g = dist.new_group(list(range(g0, g0 + cp)))
+        if g0 <= rank < g0 + cp:
+            mine = g
+    return mine
+
+
 def zigzag_indices(S: int, cp: int, rank: int, device=None) -> Tensor:
     if S % (2 * cp):
         raise ValueError(f"sequence length {S} must be a multiple of 2 * cp = {2 * cp}")
@@ -184,7 +200,7 @@ def _ring_exchange(tensors: list, group, rank: int, cp: int) -> list:
     nxt, prv = (rank + 1) % cp, (rank - 1) % cp
     g_nxt = dist.get_global_rank(group, nxt) if group is not None else nxt
     g_prv = dist.get_global_rank(group, prv) if group is not None else prv
-    recv = [torch.empty_like(t) for t in tensors]
+    recv = [torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in tensors]
     ops = [dist.P2POp(dist.isend, t.contiguous(), g_nxt, group) for t in tensors]
     ops += [dist.P2POp(dist.irecv, r, g_prv, group) for r in recv]
     reqs = dist.batch_isend_irecv(ops)

@@ -28,6 +28,10 @@ class ParallelState:
     ep_size: int = 1
     pp_size: int = 1
     cp_size: int = 1
+    # context parallelism: ranks of one CP group hold the same rows and split
+    # every sequence into zigzag chunks (parallel/context_parallel.py)
+    cp_group: Optional[object] = None
+    cp_rank: int = 0
 
     @property
     def dp_size(self) -> int:
@@ -96,11 +100,14 @@ def all_reduce_max(x: float) -> float:
     return float(t.item())
 
 
-def all_reduce_sum(x: float) -> float:
-    if not dist.is_initialized():
+def all_reduce_sum(x: float, state: Optional[ParallelState] = None) -> float:
+    """Sum of ``x`` over the data-parallel group of ``state`` (default: the
+    process-wide state); a single-rank state sums nothing."""
+    st = state if state is not None else _STATE
+    if not dist.is_initialized() or (state is not None and state.world_size == 1):
         return x
-    t = torch.tensor([x], dtype=torch.float64, device=_STATE.device if _STATE.device.type == "cuda" else "cpu")
-    dist.all_reduce(t, group=_STATE.dp_group)
+    t = torch.tensor([x], dtype=torch.float64, device=st.device if st.device.type == "cuda" else "cpu")
+    dist.all_reduce(t, group=st.dp_group)
     return float(t.item())
 
 

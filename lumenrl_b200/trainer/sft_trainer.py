@@ -36,12 +36,15 @@ class SFTTrainer:
         t = batch.tensors
         dev = self.state.device
         mask = t.get("loss_mask", t["response_mask"]).float()
-        total = max(all_reduce_sum(float(mask.sum())), 1.0)
+        cp = self.engine.cp
+        # the ranks of a context-parallel group hold the same rows: count them once
+        total = max(all_reduce_sum(float(mask.sum()), self.state) / cp, 1.0)
         lens = (t["prompt_lengths"] + t["response_lengths"]).tolist()
         nll = 0.0
         t0 = time.perf_counter()
         for rows in make_micro_batches(lens, rows_per_micro=self.config.policy.train_micro_batch_size):
-            pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows, dev)
+            pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows, dev,
+                                cp, self.engine.cp_rank)
             lp, _ = self.engine._forward_scored(pb, 1.0, want_entropy=False)
             r_idx = torch.as_tensor(rows, device=dev)[pb.out_row]
             w = mask[r_idx, pb.out_col]

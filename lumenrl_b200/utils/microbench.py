@@ -446,7 +446,7 @@ def bench_gemm2probe(ns) -> dict:
         if ns.case and name != ns.case:
             continue
         for epi, tag in ((0, "bf16"), (3, "none")):
-            t = _time(lambda: ext().gemm2sm(x, xm, y, ym, None, epi, 256), ns.steps, ns.warmup)
+            t = _time(lambda: ext().gemm2sm(x, xm, y, ym, None, epi, ns.bn or 256), ns.steps, ns.warmup)
             out[f"{name}_{tag}_tflops"] = round(fl / t / 1e9, 1)
     if not ns.case:
         t = _time(lambda: A @ B.t(), ns.steps, ns.warmup)

@@ -110,6 +110,8 @@ std::vector<torch::Tensor> ttt_diag_bwd(torch::Tensor dout, torch::Tensor q, tor
                                         std::vector<torch::Tensor> kd, std::vector<torch::Tensor> vd,
                                         torch::Tensor dq, double scale);
 std::vector<torch::Tensor> fkl_fwd(torch::Tensor zt, torch::Tensor zd);
+torch::Tensor skinny_sk(torch::Tensor x, torch::Tensor w, int64_t grid);
+int64_t skinny_sk_status();
 void row_scale_(torch::Tensor x, torch::Tensor g);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
@@ -206,6 +208,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ttt_diag_fwd", &lrl::ttt_diag_fwd);
   m.def("ttt_diag_bwd", &lrl::ttt_diag_bwd);
   m.def("fkl_fwd", &lrl::fkl_fwd);
+  m.def("skinny_sk", &lrl::skinny_sk, py::arg("x"), py::arg("w"), py::arg("grid") = 0);
+  m.def("skinny_sk_status", &lrl::skinny_sk_status);
   m.def("row_scale_", &lrl::row_scale_);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);

@@ -590,13 +590,21 @@ DECODE_GEMM = os.environ.get("LRL_DECODE_GEMM", "auto")
 
 
 def decode_linear(x: Tensor, w: Tensor) -> Tensor:
-    """No-grad linear of the rollout decode step (M = live sequences)."""
+    """No-grad linear of the rollout decode step (M = live sequences).
+    ``LRL_DECODE_GEMM``: ``sk`` the persistent stream-K weight-streaming
+    kernel (csrc/gemm/skinny_sk.cu), ``skinny`` the one-tile-per-CTA kernel
+    (skinny_gemm.cu), ``cublas``, or ``auto``: the stream-K kernel for the
+    LM head (N >= 64 K rows: 208.7 us vs cuBLAS 211.6 at M = 64), the
+    one-tile kernel up to 64 M weight elements (qkv, o, w2), cuBLAS between
+    (w13: its split tiles make the stream-K tail cost more than it saves)."""
     mode = DECODE_GEMM
     if mode == "auto":
-        mode = "skinny" if w.numel() <= (64 << 20) else "cublas"
-    if (mode == "skinny" and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-            and x.dim() == 2 and x.shape[0] <= 256 and x.shape[1] % 8 == 0 and x.is_contiguous()
-            and w.is_contiguous()):
+        mode = "sk" if w.shape[0] >= 65536 else ("skinny" if w.numel() <= (64 << 20) else "cublas")
+    ok = (x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+          and x.shape[1] % 8 == 0 and x.is_contiguous() and w.is_contiguous())
+    if mode == "sk" and ok and x.shape[0] <= 128:
+        return ext().skinny_sk(x, w, 0)
+    if mode in ("skinny", "sk") and ok and x.shape[0] <= 256:
         return ext().skinny_gemm(x, w, 0)
     return x @ w.t()
 

@@ -17,7 +17,7 @@ LAUNCHES = [0]   # kernels of this extension launched (graph replays add their c
 
 # host-only entry points (no kernel) and ops that launch two kernels
 _NO_KERNEL = {"symm_malloc", "symm_open", "symm_close", "symm_free", "symm_tensor", "symm_signal_words",
-              "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "grouped_gemm_status", "decode_tma_status",
+              "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "skinny_sk_status", "grouped_gemm_status", "decode_tma_status",
               "fa_fwd_status", "fa_bwd_status", "gemm2sm_status", "install_segv_backtrace"}
 _TWO_KERNELS = {"fa_fwd", "paged_decode_attn_shared", "paged_decode_attn_tma", "paged_decode_attn_shared_tma", "gemm_rs"}
 

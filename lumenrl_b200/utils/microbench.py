@@ -215,7 +215,8 @@ def bench_dgemm(ns) -> dict:
     from lumenrl_b200 import ops
     a = _model_args(ns.model)
     shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
-              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size)}
+              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size),
+              "lm_head": (a.vocab_size, a.hidden_size)}
     out = {"op": "decode_linears", "M": ns.batch, "cache": "weights rotate through > 300 MB of copies (HBM, not L2)"}
     for name, (N, K) in shapes.items():
         x = torch.randn(ns.batch, K, device="cuda").to(torch.bfloat16)
@@ -229,6 +230,9 @@ def bench_dgemm(ns) -> dict:
         res = {"weight_MB": round(N * K * 2 / 1e6, 1)}
         res["linear_us"] = round(_time(lambda: torch.nn.functional.linear(x, nxt()), ns.steps, ns.warmup) * 1e3, 1)
         res["skinny_us"] = round(_time(lambda: ops.skinny_linear(x, nxt()), ns.steps, ns.warmup) * 1e3, 1)
+        from lumenrl_b200.ops.ext import ext
+        res["stream_k_us"] = round(_time(lambda: ext().skinny_sk(x, nxt(), 0), ns.steps, ns.warmup) * 1e3, 1)
+        res["stream_k_TBps"] = round(N * K * 2 / res["stream_k_us"] / 1e6, 2)
         out[name] = res
         del ws
     return out

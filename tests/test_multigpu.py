@@ -426,3 +426,55 @@ def test_sddd_teacher_streams_hidden_states_to_draft_gpu():
         p.join(timeout=60)
     losses = res[1]
     assert len(losses) == 3 and all(l == l and l > 0 for l in losses)
+
+
+def _cp_actor_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from lumenrl_b200.core.protocol import DataProto
+        from lumenrl_b200.engine.training.actor import ActorEngine
+        from lumenrl_b200.models.config import tiny_qwen3
+        from lumenrl_b200.parallel.context_parallel import make_dp_cp_groups
+        from lumenrl_b200.parallel.dist import ParallelState
+        dev = torch.device("cuda", rank)
+        g = make_dp_cp_groups(world)
+        st = ParallelState(world_size=world, rank=rank, local_rank=rank, device=dev, cp_size=world, cp_rank=rank,
+                           cp_group=g)
+        cp_eng = ActorEngine(tiny_qwen3(), st, seed=3, trainable=False)
+        ref_eng = ActorEngine(tiny_qwen3(), ParallelState(device=dev), seed=3, trainable=False)
+        gen = torch.Generator().manual_seed(0)
+        B, P, R = 4, 300, 200
+        plen, rlen = torch.tensor([300, 128, 257, 64]), torch.tensor([200, 77, 131, 200])
+        b = DataProto({"prompt_ids": torch.randint(3, 2048, (B, P), generator=gen), "prompt_lengths": plen,
+                       "responses": torch.randint(3, 2048, (B, R), generator=gen), "response_lengths": rlen,
+                       "response_mask": (torch.arange(R).unsqueeze(0) < rlen.unsqueeze(1)).float()})
+        lp_cp, _ = cp_eng.compute_log_probs(b, want_entropy=False)
+        lp_ref, _ = ref_eng.compute_log_probs(b, want_entropy=False)
+        m = b.tensors["response_mask"].to(dev) > 0
+        q.put((rank, float((lp_cp - lp_ref)[m].abs().max())))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_context_parallel_actor_scoring_on_gpus():
+    """The training engine with CP = 2 over two GPUs (zigzag shares, ring
+    attention on the tcgen05 flash kernels, K/V over NCCL p2p) scores the
+    same log-probs as one GPU with the whole sequences."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29890 + os.getpid() % 50
+    procs = [ctx.Process(target=_cp_actor_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err in res:
+        assert isinstance(err, float), (rank, err)
+        assert err < 5e-2, (rank, err)     # bf16 logits, log-prob difference in nats

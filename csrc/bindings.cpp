@@ -111,6 +111,9 @@ std::vector<torch::Tensor> ttt_diag_bwd(torch::Tensor dout, torch::Tensor q, tor
                                         torch::Tensor dq, double scale);
 std::vector<torch::Tensor> fkl_fwd(torch::Tensor zt, torch::Tensor zd);
 torch::Tensor skinny_sk(torch::Tensor x, torch::Tensor w, int64_t grid);
+std::vector<torch::Tensor> moe_route(torch::Tensor logits, int64_t k, bool norm, c10::optional<torch::Tensor> replay);
+torch::Tensor moe_route_bwd(torch::Tensor probs, torch::Tensor ids, torch::Tensor w, torch::Tensor dw,
+                            c10::optional<torch::Tensor> dprobs, bool norm);
 int64_t skinny_sk_status();
 void row_scale_(torch::Tensor x, torch::Tensor g);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
@@ -210,6 +213,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fkl_fwd", &lrl::fkl_fwd);
   m.def("skinny_sk", &lrl::skinny_sk, py::arg("x"), py::arg("w"), py::arg("grid") = 0);
   m.def("skinny_sk_status", &lrl::skinny_sk_status);
+  m.def("moe_route", &lrl::moe_route, py::arg("logits"), py::arg("k"), py::arg("norm"), py::arg("replay") = py::none());
+  m.def("moe_route_bwd", &lrl::moe_route_bwd, py::arg("probs"), py::arg("ids"), py::arg("w"), py::arg("dw"),
+        py::arg("dprobs") = py::none(), py::arg("norm") = true);
   m.def("row_scale_", &lrl::row_scale_);
   m.def("symm_malloc", &lrl::symm_malloc);
   m.def("symm_open", &lrl::symm_open);

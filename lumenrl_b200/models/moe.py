@@ -117,6 +117,38 @@ class _NullCtx:
         pass
 
 
+class _RouteDevice(torch.autograd.Function):
+    """Softmax + top-k (+ replay) + expert permutation on the device
+    (csrc/ops/moe_route.cu); gradients reach the logits through the routing
+    weights and the probabilities (aux loss)."""
+
+    @staticmethod
+    def forward(ctx, logits, k, norm, replay):
+        from lumenrl_b200.ops.ext import ext
+        probs, ids, w, order, token_of, offsets, counts = ext().moe_route(logits.contiguous(), k, norm, replay)
+        ctx.save_for_backward(probs, ids, w)
+        ctx.norm = norm
+        ctx.mark_non_differentiable(ids, order, token_of, offsets, counts)
+        return w, probs, ids, order, token_of, offsets, counts
+
+    @staticmethod
+    def backward(ctx, dw, dprobs, *_):
+        from lumenrl_b200.ops.ext import ext
+        probs, ids, w = ctx.saved_tensors
+        if dw is None:
+            dw = torch.zeros_like(w)
+        return ext().moe_route_bwd(probs, ids, w, dw, dprobs, ctx.norm), None, None, None
+
+
+def route_device(h: Tensor, router_w: Tensor, top_k: int, norm_topk: bool, replay_ids: Optional[Tensor] = None):
+    """Device routing: (ids [T,k], weights [T,k], probs [T,E], order, token_of,
+    offsets int32 [E+1], counts [E]) -- the permutation the grouped GEMMs use."""
+    logits = ops.linear_fp32(h, router_w)
+    rep = replay_ids.long().to(h.device).contiguous() if replay_ids is not None else None
+    w, probs, ids, order, token_of, offsets, counts = _RouteDevice.apply(logits, int(top_k), bool(norm_topk), rep)
+    return ids, w, probs, order, token_of, offsets, counts
+
+
 def route(h: Tensor, router_w: Tensor, top_k: int, norm_topk: bool,
           replay_ids: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     """Returns (expert ids [T,k] int64, weights [T,k] fp32, full probs [T,E])."""
@@ -148,20 +180,27 @@ def moe_forward(model, layer: int, h: Tensor) -> tuple[Tensor, Optional[Tensor]]
     rr = getattr(model, "routing_replay", None)
     if rr is not None:
         replay = rr.lookup(layer, h.shape[0])
-    ids, w, probs = route(h, P[pre + "router"], a.num_experts_per_tok, a.norm_topk_prob, replay)
+    w13, w2 = P[pre + "experts_w13"], P[pre + "experts_w2"]
+    if _use_tc_grouped(h, w13, w2) and a.num_experts <= 1024 and a.num_experts_per_tok <= 16:
+        ids, w, probs, order, token_of, offs, counts = route_device(
+            h, P[pre + "router"], a.num_experts_per_tok, a.norm_topk_prob, replay)
+    else:
+        ids, w, probs = route(h, P[pre + "router"], a.num_experts_per_tok, a.norm_topk_prob, replay)
+        offs = None
     rec = getattr(model, "routing_recorder", None)
     if rec is not None:
         rec.record(layer, ids)
     T, k = ids.shape
-    flat_ids = ids.reshape(-1)
-    order = torch.argsort(flat_ids, stable=True)
-    counts = torch.bincount(flat_ids, minlength=a.num_experts)
-    token_of = order // k
+    if offs is None:
+        flat_ids = ids.reshape(-1)
+        order = torch.argsort(flat_ids, stable=True)
+        counts = torch.bincount(flat_ids, minlength=a.num_experts)
+        token_of = order // k
     xs = h[token_of]
-    w13, w2 = P[pre + "experts_w13"], P[pre + "experts_w2"]
     if _use_tc_grouped(h, w13, w2):
-        offs = torch.zeros(a.num_experts + 1, dtype=torch.int32, device=h.device)
-        offs[1:] = torch.cumsum(counts, 0)
+        if offs is None:
+            offs = torch.zeros(a.num_experts + 1, dtype=torch.int32, device=h.device)
+            offs[1:] = torch.cumsum(counts, 0)
         gu = grouped_linear_device(xs, w13, offs)
         ys = grouped_linear_device(ops.swiglu(gu), w2, offs)
     else:

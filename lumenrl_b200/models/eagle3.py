@@ -27,6 +27,7 @@ needs a [T, T] matrix per extra step.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -37,6 +38,10 @@ from torch import Tensor
 from lumenrl_b200 import ops
 from lumenrl_b200.ops import reference as ref
 
+# bf16 CUDA tensors take this package's kernels (TTT attention, forward KL,
+# GEMMs, norms); LRL_EAGLE_KERNELS=0 keeps the PyTorch path for comparisons
+_KERNELS = os.environ.get("LRL_EAGLE_KERNELS", "1") != "0"
+
 
 class RMSNorm(nn.Module):
     def __init__(self, dim: int, eps: float = 1e-6) -> None:
@@ -45,7 +50,7 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x: Tensor) -> Tensor:
-        if x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16:
+        if _KERNELS and x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16:
             return ops.rmsnorm(x, self.weight, self.eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight.float()).to(x.dtype)
@@ -86,7 +91,7 @@ class Eagle3Layer(nn.Module):
 
     def forward(self, emb: Tensor, h: Tensor, pos: Tensor, cu: Tensor, cache: list, max_len: int = 0) -> Tensor:
         T = h.shape[0]
-        if h.is_cuda and h.dtype == torch.bfloat16 and self.hd == 128 and max_len > 0:
+        if _KERNELS and h.is_cuda and h.dtype == torch.bfloat16 and self.hd == 128 and max_len > 0:
             return self._forward_kernels(emb, h, pos, cu, cache, max_len)
         x = torch.cat([self.input_norm(emb), self.hidden_norm(h)], -1)
         qkv = self.wqkv(x)
@@ -187,7 +192,7 @@ class Eagle3Model(nn.Module):
         max_len = max(lens_h) if lens_h else 0
         pos = torch.cat([torch.arange(int(n), device=input_ids.device) for n in lens_h])
         seq_id = torch.repeat_interleave(torch.arange(len(lens), device=input_ids.device), lens)
-        kernels = aux_hidden.is_cuda and aux_hidden.dtype == torch.bfloat16
+        kernels = _KERNELS and aux_hidden.is_cuda and aux_hidden.dtype == torch.bfloat16
         h = ops.linear(aux_hidden, self.fc.weight) if kernels else self.fc(aux_hidden)
         ids, mask = input_ids, loss_mask.float()
         w_teacher = teacher_lm_head.index_select(0, self.d2t.to(teacher_lm_head.device))

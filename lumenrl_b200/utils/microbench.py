@@ -398,6 +398,34 @@ def bench_gemm2energy(ns) -> dict:
     return out
 
 
+def bench_eagle(ns) -> dict:
+    """One Eagle3 draft training step (forward over the 7 TTT steps + backward)
+    at Qwen3-8B width on --rows sequences of --seq tokens: teacher hidden
+    states random, draft vocabulary 32000.  Run once with the package's
+    kernels and once with LRL_EAGLE_KERNELS=0 (PyTorch path) to compare."""
+    from lumenrl_b200.models import eagle3
+    a = _model_args(ns.model)
+    T = ns.rows * ns.seq
+    torch.manual_seed(0)
+    m = eagle3.Eagle3Model(a.hidden_size, a.vocab_size, 32000, a.num_heads, a.num_kv_heads, a.head_dim,
+                           a.intermediate_size, 1, 7, a.rms_norm_eps, a.rope_theta).cuda().to(torch.bfloat16)
+    ids = torch.randint(0, a.vocab_size, (T,), device="cuda")
+    aux = (torch.randn(T, 3 * a.hidden_size, device="cuda") * 0.5).to(torch.bfloat16)
+    tgt = (torch.randn(T, a.hidden_size, device="cuda") * 0.5).to(torch.bfloat16)
+    emb = (torch.randn(a.vocab_size, a.hidden_size, device="cuda") * 0.02).to(torch.bfloat16)
+    head = (torch.randn(a.vocab_size, a.hidden_size, device="cuda") * 0.02).to(torch.bfloat16)
+    cu = torch.arange(0, T + 1, ns.seq, dtype=torch.int32, device="cuda")
+    mask = torch.ones(T, device="cuda")
+
+    def step():
+        out = m(ids, aux, tgt, emb, head, cu, mask)
+        out["loss"].backward()
+        m.zero_grad(set_to_none=True)
+    ms = _time(step, ns.steps, ns.warmup)
+    return {"op": "eagle3_draft_step", "tokens": T, "ttt_steps": 7, "kernels": eagle3._KERNELS, "ms": ms,
+            "tokens_per_s": T / ms * 1e3, "peak_mem_GB": torch.cuda.max_memory_allocated() / 1e9}
+
+
 def bench_fp8gemm(ns) -> dict:
     """Block-scaled FP8 tcgen05 GEMM (csrc/gemm/fp8_gemm.cu) on the forward
     GEMMs of the Qwen3-8B training linears (E4M3 x E4M3, 1x128 activation
@@ -501,7 +529,7 @@ def bench_comm(ns) -> dict:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
-                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy"])
+                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy", "eagle"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -524,7 +552,7 @@ def main(argv=None) -> None:
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "gemm2energy": bench_gemm2energy,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "eagle": bench_eagle, "gemm2energy": bench_gemm2energy,
           "comm": bench_comm, "gemm2": bench_gemm2,
           "gemm2probe": bench_gemm2probe}[ns.what]
     res = fn(ns)

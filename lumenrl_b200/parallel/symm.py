@@ -18,7 +18,8 @@ optimizer step as two fused kernels:
    weight buffer -- the parameter all-gather and the trainer -> rollout
    weight sync in the same pass -- then a completion barrier.
 
-With ``nvls`` (default: when the GPUs support NVLink SHARP multicast) the
+With ``nvls`` (opt-in: ``nvls=True`` or ``LRL_NVLS=1``, used when the GPUs
+support NVLink SHARP multicast) the
 weight and gradient buffers come from PyTorch's symmetric memory, which also
 maps them into one NVLS multicast object; the kernels then use
 ``multimem.ld_reduce`` (the gradient sum of an element over all GPUs, reduced
@@ -108,7 +109,8 @@ def nvls_supported() -> bool:
 
 class NVLinkOptimizerComm:
     """Fused reduce-scatter / AdamW / all-gather over NVLink peer memory, or
-    over NVLS multicast (``nvls``: True, False, or None = when supported)."""
+    over NVLS multicast (``nvls``: True, False, or None = ``LRL_NVLS`` == "1";
+    either way only when the GPUs support it)."""
 
     def __init__(self, numel: int, rank: int, world: int, weight_dtype=torch.bfloat16, group=None,
                  wait_seconds: float = 10.0, nvls: Optional[bool] = None) -> None:

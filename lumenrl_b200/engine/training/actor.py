@@ -101,9 +101,9 @@ class ActorEngine:
         lens = (t["prompt_lengths"] + t["response_lengths"]).tolist()
         logp = torch.zeros(B, R, dtype=torch.float32, device=self.device)
         ent = torch.zeros(B, R, dtype=torch.float32, device=self.device) if want_entropy else None
+        pl_h, rl_h = t["prompt_lengths"].tolist(), t["response_lengths"].tolist()
         for rows in make_micro_batches(lens, token_budget=token_budget):
-            pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
-                                self.device, self.cp, self.cp_rank)
+            pb = pack_from_grid(t["prompt_ids"], pl_h, t["responses"], rl_h, rows, self.device, self.cp, self.cp_rank)
             self._set_replay(batch, pb)
             lp, e = self._forward_scored(pb, temperature, want_entropy)
             rows_t = torch.as_tensor(rows, device=self.device)[pb.out_row]
@@ -142,7 +142,9 @@ class ActorEngine:
             rows = rows_per_micro or B
             tok = max(sum(sorted(lens, reverse=True)[:rows]), 1)
             metrics["actor/recompute_layers"] = float(self.plan_recompute(tok))
-        sums = {"pg_loss": 0.0, "ppo_kl": 0.0, "clipfrac": 0.0, "tok": 0.0, "entropy": 0.0}
+        # per-micro-batch statistics stay on the device until the end
+        sums: dict = {"pg_loss": 0.0, "ppo_kl": 0.0, "clipfrac": 0.0, "tok": 0.0, "entropy": 0.0}
+        lens_h = (t["prompt_lengths"].tolist(), t["response_lengths"].tolist())
         t_fwd_bwd = 0.0
         opt_stats = {}
         opt_t = {"opt_rs_s": 0.0, "opt_bcast_s": 0.0}
@@ -158,7 +160,8 @@ class ActorEngine:
                 t0 = time.perf_counter()
                 for mb in micro:
                     rows = [mini_rows[i] for i in mb]
-                    stats = self._micro_step(batch, rows, mask_grid, algo_cfg, algorithm, global_tok, temperature)
+                    stats = self._micro_step(batch, rows, mask_grid, algo_cfg, algorithm, global_tok, temperature,
+                                             lens_h)
                     for k in sums:
                         sums[k] += stats.get(k, 0.0)
                 t_fwd_bwd += time.perf_counter() - t0
@@ -170,6 +173,7 @@ class ActorEngine:
                     opt_t[k] += self.opt.last_timing.get(k, 0.0)
                 if self.sched:
                     self.sched.step()
+        sums = {k: float(v) for k, v in sums.items()}
         tok = max(sums["tok"], 1.0)
         metrics.update({
             "actor/pg_loss": sums["pg_loss"], "actor/ppo_kl": sums["ppo_kl"] / tok,
@@ -195,10 +199,10 @@ class ActorEngine:
         return n
 
     def _micro_step(self, batch: DataProto, rows: list[int], mask_grid: Tensor, algo_cfg, algorithm: str,
-                    global_tok: float, temperature: float) -> dict[str, float]:
+                    global_tok: float, temperature: float, lens_h=None) -> dict:
         t = batch.tensors
-        pb = pack_from_grid(t["prompt_ids"], t["prompt_lengths"], t["responses"], t["response_lengths"], rows,
-                            self.device, self.cp, self.cp_rank)
+        pl, rl = lens_h if lens_h is not None else (t["prompt_lengths"], t["response_lengths"])
+        pb = pack_from_grid(t["prompt_ids"], pl, t["responses"], rl, rows, self.device, self.cp, self.cp_rank)
         self._set_replay(batch, pb)
         logp, _ = self._forward_scored(pb, temperature, want_entropy=False)
         r_idx = torch.as_tensor(rows, device=self.device)[pb.out_row]
@@ -219,15 +223,15 @@ class ActorEngine:
             ref_lp = t["ref_log_probs"][r_idx, c_idx].float()
             loss = loss + kl_c * ((ref_lp - logp) * mask).sum() / global_tok
         for aux in self.model.aux_losses:
-            loss = loss + aux * (float(mask.sum()) / global_tok)
+            loss = loss + aux * (mask.sum() / global_tok)
         loss.backward()
         self.model.routing_replay = None
         with torch.no_grad():
             d = logp.detach() - old
             ratio = torch.exp(d.clamp(-20, 20))
             clipped = ((ratio < 1 - lo) | (ratio > 1 + hi)).float()
-            return {"pg_loss": float(loss.detach()), "ppo_kl": float(((-d) * mask).sum()),
-                    "clipfrac": float((clipped * mask).sum()), "tok": float(mask.sum())}
+            return {"pg_loss": loss.detach(), "ppo_kl": ((-d) * mask).sum(), "clipfrac": (clipped * mask).sum(),
+                    "tok": mask.sum()}
 
     # ------------------------------------------------------------------ state
     def state_dict(self) -> dict[str, Any]:

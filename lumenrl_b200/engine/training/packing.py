@@ -41,6 +41,14 @@ class PackedBatch:
         return grid[self.out_row, self.out_col]
 
 
+def _to_device(x: Tensor, device) -> Tensor:
+    """Host index tensors reach the GPU through pinned memory without a
+    stream synchronisation (a pageable copy would wait for the queue)."""
+    if x.device.type == "cpu" and torch.device(device).type == "cuda":
+        return x.pin_memory().to(device, non_blocking=True)
+    return x.to(device)
+
+
 def pack_rows(prompts: list[Tensor], responses: list[Tensor], device, rows: list[int] | None = None) -> PackedBatch:
     """prompts/responses: 1-D token tensors per row (no padding)."""
     ids, pos, cu = [], [], [0]
@@ -58,10 +66,10 @@ def pack_rows(prompts: list[Tensor], responses: list[Tensor], device, rows: list
             ocol.append(torch.arange(la))
         off += lp + la
         cu.append(off)
-    cat = lambda xs, dt=torch.long: (torch.cat(xs) if xs else torch.zeros(0, dtype=dt)).to(device)  # noqa: E731
+    cat = lambda xs, dt=torch.long: _to_device(torch.cat(xs) if xs else torch.zeros(0, dtype=dt), device)  # noqa: E731
     lens = [cu[i + 1] - cu[i] for i in range(len(cu) - 1)]
     return PackedBatch(
-        input_ids=cat(ids), positions=cat(pos), cu_seqlens=torch.tensor(cu, dtype=torch.int32, device=device),
+        input_ids=cat(ids), positions=cat(pos), cu_seqlens=_to_device(torch.tensor(cu, dtype=torch.int32), device),
         max_seqlen=max(lens) if lens else 0, score_index=cat(score), targets=cat(tgt), out_row=cat(orow),
         out_col=cat(ocol), rows=list(rows) if rows is not None else list(range(len(prompts))),
         num_rows=len(prompts))
@@ -98,19 +106,22 @@ def pack_rows_cp(prompts: list[Tensor], responses: list[Tensor], device, rows: l
             orow.append(torch.full((int(keep.sum()),), r, dtype=torch.long))
             ocol.append(torch.arange(la)[keep])
     B = len(prompts)
-    cat = lambda xs: (torch.cat(xs) if xs else torch.zeros(0, dtype=torch.long)).to(device)  # noqa: E731
+    cat = lambda xs: _to_device(torch.cat(xs) if xs else torch.zeros(0, dtype=torch.long), device)  # noqa: E731
     return PackedBatch(
-        input_ids=cat(ids), positions=loc.repeat(B).to(device),
+        input_ids=cat(ids), positions=_to_device(loc.repeat(B), device),
         cu_seqlens=torch.arange(0, B * two_c + 1, two_c, dtype=torch.int32, device=device), max_seqlen=two_c,
         score_index=cat(score), targets=cat(tgt), out_row=cat(orow), out_col=cat(ocol),
         rows=list(rows) if rows is not None else list(range(B)), num_rows=B)
 
 
-def pack_from_grid(prompt_ids: Tensor, prompt_lens: Tensor, responses: Tensor, response_lens: Tensor,
+def pack_from_grid(prompt_ids: Tensor, prompt_lens, responses: Tensor, response_lens,
                    rows: list[int], device, cp: int = 1, cp_rank: int = 0) -> PackedBatch:
     """Rows of right-padded prompt/response grids -> PackedBatch (with
-    ``cp`` > 1: this context-parallel rank's zigzag share, ``pack_rows_cp``)."""
-    pl, rl = prompt_lens.tolist(), response_lens.tolist()
+    ``cp`` > 1: this context-parallel rank's zigzag share, ``pack_rows_cp``).
+    The lengths may be tensors or host lists (lists save a device read per
+    micro-batch)."""
+    pl = prompt_lens if isinstance(prompt_lens, list) else prompt_lens.tolist()
+    rl = response_lens if isinstance(response_lens, list) else response_lens.tolist()
     ps = [prompt_ids[r, : pl[r]] for r in rows]
     rs = [responses[r, : rl[r]] for r in rows]
     if cp > 1:

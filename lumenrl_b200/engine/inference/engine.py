@@ -137,8 +137,8 @@ class RolloutEngine:
         if flat is not None and flat.data_ptr() != self.model.flat.data_ptr():
             self.model.flat.copy_(flat, non_blocking=True)
         if self.runner.fp8 is not None:
+            # re-quantised in place: the captured graphs read the same buffers
             self.runner.fp8.quantize_model(self.model)
-            self._graphs.clear()   # graphs hold the previous quantised buffers
         self.weight_version = self.weight_version + 1 if version is None else version
 
     # -- generation ------------------------------------------------------------------

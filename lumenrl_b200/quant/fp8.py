@@ -165,13 +165,21 @@ class FP8RolloutQuantizer:
         return c.num_first_layers_in_bf16 <= i < self.num_layers - c.num_last_layers_in_bf16
 
     def quantize_model(self, model) -> dict:
-        """(Re)quantise every eligible linear weight of ``model`` (used after each weight sync)."""
+        """(Re)quantise every eligible linear weight of ``model`` (used after
+        each weight sync).  A re-quantisation writes into the tensors of the
+        first one, so decode graphs captured against them stay valid."""
         for name, p in model.named_flat_params():
             if not any(name.endswith(s) for s in ("wqkv", "wo", "w13", "w2")):
                 continue
             layer = int(name.split(".")[1])
             if self.layer_in_fp8(layer):
-                self.weights[name] = quant_weight_128x128(p.detach())
+                qw, sw = quant_weight_128x128(p.detach())
+                old = self.weights.get(name)
+                if old is not None and old[0].shape == qw.shape and old[1].shape == sw.shape:
+                    old[0].copy_(qw)
+                    old[1].copy_(sw)
+                else:
+                    self.weights[name] = (qw, sw)
         return {"fp8/quantized_tensors": len(self.weights)}
 
     def linear(self, name: str, x: Tensor, w_bf16: Tensor) -> Tensor:

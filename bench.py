@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--micro", type=int, default=4)
     ap.add_argument("--recompute", choices=["auto", "on", "off"], default="auto")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--placement", choices=["colocated", "separated", "async"], default="colocated",
+                    help="colocated: every GPU generates and trains; separated: half the GPUs generate, half "
+                         "train, in lockstep; async: the same split with the rollout one step ahead")
     ap.add_argument("--recipe", choices=["grpo", "dapo-fp8"], default="grpo",
                     help="grpo: the headline bf16 GRPO config; dapo-fp8: DAPO with W8A8 FP8 rollout, FP8 KV "
                          "cache and hybrid FP8 training linears (E4M3 forward, E5M2 gradients)")
@@ -177,11 +180,20 @@ def main() -> None:
     margs = resolve_model(args.model)
     recompute = {"on": True, "off": False, "auto": "auto"}[args.recompute]
     cfg = LumenRLConfig.from_dict(recipe_config(args, margs.name))
-    spec = RLRunSpec(prompts_per_step=args.prompts_per_gpu * world, prompt_len=args.prompt_len, prompt_low=0,
+    colocated = args.placement == "colocated"
+    n_roll = world if colocated else world // 2     # GPUs that generate
+    if not colocated and world < 2:
+        raise SystemExit("--placement separated / async needs at least 2 GPUs")
+    spec = RLRunSpec(prompts_per_step=args.prompts_per_gpu * n_roll, prompt_len=args.prompt_len, prompt_low=0,
                      prompt_high=151643, max_new_tokens=args.max_new, eos_token_id=151645, reward="parity",
                      rows_per_micro=args.micro, use_cuda_graph=not args.no_graph,
                      gradient_checkpointing=recompute)
-    tr = RLTrainer(cfg, margs, spec, st).setup()
+    if colocated:
+        tr = RLTrainer(cfg, margs, spec, st).setup()
+    else:
+        from lumenrl_b200.trainer.separated_trainer import SeparatedRLTrainer
+        tr = SeparatedRLTrainer(cfg, margs, spec, st, num_rollout=n_roll,
+                                async_lag=1 if args.placement == "async" else 0).setup()
 
     def sync():
         if dist.is_initialized():
@@ -203,7 +215,7 @@ def main() -> None:
     for _ in range(args.steps):
         m = tr.step()
         hist.append(m)
-        toks += m["perf/total_num_tokens"]
+        toks += m.get("perf/total_num_tokens", 0.0)   # rank 0 trains in every placement
     e1.record()
     sync()
     launches = LAUNCHES[0] - l0
@@ -219,7 +231,7 @@ def main() -> None:
     toks_e2e = 0.0
     for _ in range(args.steps):
         m = tr.step()           # copies the pinned prompt batch H2D inside
-        toks_e2e += float(m["perf/total_num_tokens"])   # metrics are host values (D2H inside step)
+        toks_e2e += float(m.get("perf/total_num_tokens", 0.0))   # metrics are host values (D2H inside step)
     sync()
     wall = time.perf_counter() - w0
     tw = torch.tensor([wall], device=st.device, dtype=torch.float64)
@@ -228,8 +240,15 @@ def main() -> None:
     wall = float(tw.item())
     # ---- multi-GPU correctness, outside the timed regions: replicas agree
     # bit for bit, and one fused NVLink optimizer step equals the NCCL path ----
+    # host<->device bytes per step, summed over the ranks that move them
+    io = torch.tensor([float(tr.io_bytes.get("h2d", 0)), float(tr.io_bytes.get("d2h", 0))], device=st.device,
+                      dtype=torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(io)
     checks = {}
-    if world > 1:
+    if not colocated:
+        tr.finish()             # async: the rollout side takes the last pushed update
+    if world > 1 and colocated:
         from lumenrl_b200.parallel.symm import fused_vs_nccl_max_err, replica_agreement
         opt = tr.actor.opt
         checks.update(replica_agreement(tr.actor.model.flat, opt.master, opt.lo))
@@ -249,12 +268,17 @@ def main() -> None:
                        "global_batch": B * world, "prompts": args.prompts_per_gpu * world, "group": args.group,
                        "seq_len": args.prompt_len + args.max_new, "prompt_len": args.prompt_len,
                        "max_new_tokens": args.max_new, "micro_batch": args.micro,
-                       "parallelism": f"dp{world} (sharded AdamW, resident bf16 weights; rollout TP=1 per GPU)",
+                       "parallelism": (f"dp{world} (sharded AdamW, resident bf16 weights; rollout TP=1 per GPU)"
+                                       if colocated else
+                                       f"separated: {world - n_roll} trainer GPU(s) (sharded AdamW) + {n_roll} "
+                                       f"rollout GPU(s), weights pushed by NVLink peer stores"
+                                       + (", rollout one step ahead" if args.placement == "async" else "")),
+                       "placement": args.placement,
                        "recompute": recompute, "recipe": args.recipe,
                        "cache": "inputs larger than L2 (16 GB of weights per step)"},
             "clocks": clk,
-            "e2e": {"value": toks_e2e / wall, "unit": "tokens/s", "h2d_bytes_per_step": tr.io_bytes["h2d"] * world,
-                    "d2h_bytes_per_step": tr.io_bytes.get("d2h", 0) * world},
+            "e2e": {"value": toks_e2e / wall, "unit": "tokens/s", "h2d_bytes_per_step": int(io[0]),
+                    "d2h_bytes_per_step": int(io[1])},
             "gpu_launches": launches,
             "breakdown_s": {k.replace("timing/", ""): v for k, v in last.items() if k.startswith("timing/")},
             "recompute_layers": last.get("actor/recompute_layers"),

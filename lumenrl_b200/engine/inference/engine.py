@@ -83,7 +83,7 @@ class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
                  use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True,
-                 fp8_rollout=None, continuous_batching: bool = True) -> None:
+                 fp8_rollout=None, continuous_batching: bool = True, vocab_limit: Optional[int] = None) -> None:
         self.model = model
         self.args = model.args
         self.device = model.flat.device
@@ -103,6 +103,10 @@ class RolloutEngine:
         self.cache = PagedKVCache(spec, nblocks, self.device)
         self.runner = ModelRunner(model, self.cache)
         self.runner.max_len = max_model_len
+        if vocab_limit is not None:
+            if not 0 < vocab_limit <= self.args.vocab_size:
+                raise ValueError(f"vocab_limit {vocab_limit} outside (0, {self.args.vocab_size}]")
+            self.runner.vocab_limit = int(vocab_limit)
         if fp8_rollout is not None and fp8_rollout.is_fp8_enabled():
             # W8A8 blockwise rollout (128x128 E4M3 weight blocks, 1x128 activation
             # blocks); requantised from the bf16 weights at every weight sync

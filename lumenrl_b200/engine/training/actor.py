@@ -138,6 +138,12 @@ class ActorEngine:
         if "dapo_sample_mask" in t:
             mask_grid = mask_grid * t["dapo_sample_mask"].float().reshape(-1, 1)
         metrics: dict[str, float] = {}
+        rstats = getattr(self.model, "router_stats", None)
+        if rstats is None and self.args.num_experts:
+            from lumenrl_b200.moe.diagnostics import attach_router_stats
+            rstats = attach_router_stats(self.model, self.device)
+        if rstats is not None:
+            rstats.reset()
         if self.recompute_policy == "auto" and self.device.type == "cuda":
             rows = rows_per_micro or B
             tok = max(sum(sorted(lens, reverse=True)[:rows]), 1)
@@ -182,6 +188,8 @@ class ActorEngine:
             "timing/fwd_bwd_s": t_fwd_bwd,
             "timing/opt_rs_s": opt_t["opt_rs_s"], "timing/opt_bcast_s": opt_t["opt_bcast_s"],
         })
+        if rstats is not None:
+            metrics.update(rstats.summary("moe/"))   # router entropy and expert load of this update
         return metrics
 
     def plan_recompute(self, tokens_per_micro: int, margin_bytes: int = 8 << 30) -> int:

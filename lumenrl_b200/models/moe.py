@@ -190,6 +190,9 @@ def moe_forward(model, layer: int, h: Tensor) -> tuple[Tensor, Optional[Tensor]]
     rec = getattr(model, "routing_recorder", None)
     if rec is not None:
         rec.record(layer, ids)
+    stats = getattr(model, "router_stats", None)
+    if stats is not None and torch.is_grad_enabled():   # training steps only
+        stats.observe(layer, probs, ids)
     T, k = ids.shape
     if offs is None:
         flat_ids = ids.reshape(-1)

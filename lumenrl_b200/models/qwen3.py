@@ -331,6 +331,11 @@ class Qwen3Model(nn.Module):
         if self.args.tie_word_embeddings and "lm_head.weight" in sd and "model.embed_tokens.weight" not in sd:
             targets["model.embed_tokens.weight"].copy_(sd["lm_head.weight"])
             missing = [m for m in missing if m != "model.embed_tokens.weight"]
-        if strict and missing:
-            raise KeyError(f"missing keys in state dict: {missing[:8]}{'...' if len(missing) > 8 else ''}")
+        if strict:
+            # sync coverage: every parameter loaded, and no tensor of the
+            # state dict silently dropped (a renamed or foreign key)
+            extra = [k for k in sd if k not in targets and not (k == "lm_head.weight" and self.args.tie_word_embeddings)]
+            if missing or extra:
+                raise KeyError(f"weight sync coverage: missing {missing[:8]}{'...' if len(missing) > 8 else ''}, "
+                               f"unexpected {extra[:8]}{'...' if len(extra) > 8 else ''}")
         return missing

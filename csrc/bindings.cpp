@@ -115,6 +115,12 @@ std::vector<torch::Tensor> moe_route(torch::Tensor logits, int64_t k, bool norm,
 torch::Tensor moe_route_bwd(torch::Tensor probs, torch::Tensor ids, torch::Tensor w, torch::Tensor dw,
                             c10::optional<torch::Tensor> dprobs, bool norm);
 int64_t skinny_sk_status();
+torch::Tensor skinny_fp8(torch::Tensor x, torch::Tensor qw, torch::Tensor sw, int64_t grid);
+int64_t skinny_fp8_status();
+void nvlink_allreduce(std::vector<int64_t> buf_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n,
+                      double scale, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
+void nvlink_allreduce_mc(int64_t mc_buf, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n, double scale,
+                         int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 void row_scale_(torch::Tensor x, torch::Tensor g);
 std::vector<int64_t> symm_malloc(int64_t nbytes);
 int64_t symm_open(std::vector<int64_t> handle_words);
@@ -213,6 +219,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fkl_fwd", &lrl::fkl_fwd);
   m.def("skinny_sk", &lrl::skinny_sk, py::arg("x"), py::arg("w"), py::arg("grid") = 0);
   m.def("skinny_sk_status", &lrl::skinny_sk_status);
+  m.def("skinny_fp8", &lrl::skinny_fp8, py::arg("x"), py::arg("qw"), py::arg("sw"), py::arg("grid") = 0);
+  m.def("skinny_fp8_status", &lrl::skinny_fp8_status);
+  m.def("nvlink_allreduce", &lrl::nvlink_allreduce);
+  m.def("nvlink_allreduce_mc", &lrl::nvlink_allreduce_mc);
   m.def("moe_route", &lrl::moe_route, py::arg("logits"), py::arg("k"), py::arg("norm"), py::arg("replay") = py::none());
   m.def("moe_route_bwd", &lrl::moe_route_bwd, py::arg("probs"), py::arg("ids"), py::arg("w"), py::arg("dw"),
         py::arg("dprobs") = py::none(), py::arg("norm") = true);

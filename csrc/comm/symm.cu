@@ -307,6 +307,87 @@ PeerPtrs to_peers(const std::vector<int64_t>& ptrs) {
   return pp;
 }
 
+// ---- replicated data parallel: all-reduce of a symmetric fp32 buffer -------------
+// Two-shot over NVLink in one kernel: after a start barrier, rank r owns the
+// r-th contiguous slice of the buffer, sums that slice over every rank's copy
+// (peer loads), scales it (1/W for a mean) and stores the result into EVERY
+// rank's copy (peer stores).  Slices are disjoint and each element is read on
+// all ranks before it is written, so the ranks never race; a completion
+// barrier keeps every rank in the kernel until all slices have landed.
+// Signal slots 4 (start) and 5 (completion) and counter word kArCounter keep
+// it independent of the optimizer kernels' slots.
+constexpr int kArCounter = kSigNorms + kMaxRanks + 3;
+
+__device__ void ar_completion(const PeerPtrs& sig, uint32_t* my_sig, int rank, int W, uint32_t epoch, int* status,
+                              long long wait_cycles) {
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    last = atomicAdd(my_sig + kArCounter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    my_sig[kArCounter] = 0u;
+    for (int r = 0; r < W; ++r)
+      st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 5 * kMaxRanks + rank, epoch);
+    const long long t0 = clock64();
+    for (int r = 0; r < W; ++r) {
+      while (ld_acquire_sys(my_sig + kSigFlags + 5 * kMaxRanks + r) < epoch) {
+        if (clock64() - t0 > wait_cycles) {
+          atomicCAS(status, 0, 105);
+          return;
+        }
+      }
+    }
+  }
+}
+
+__global__ void allreduce_kernel(PeerPtrs bufs, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t n,
+                                 float scale, uint32_t epoch, int* status, long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles)) return;
+  const int64_t n4 = n / 4, per = (n4 + W - 1) / W;
+  const int64_t a = rank * per, b = min(n4, a + per);
+  for (int64_t i = a + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= W) break;
+      const float4 v = reinterpret_cast<const float4*>(bufs.p[r])[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    acc.x *= scale;
+    acc.y *= scale;
+    acc.z *= scale;
+    acc.w *= scale;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= W) break;
+      reinterpret_cast<float4*>(bufs.p[r])[i] = acc;
+    }
+  }
+  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles);
+}
+
+// NVLS: one multimem.ld_reduce returns the sum over every GPU's copy (reduced
+// in the NVSwitch), one multimem.st writes the result into every copy
+__global__ void allreduce_mc_kernel(float* mc, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t n,
+                                    float scale, uint32_t epoch, int* status, long long wait_cycles) {
+  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles)) return;
+  const int64_t n4 = n / 4, per = (n4 + W - 1) / W;
+  const int64_t a = rank * per, b = min(n4, a + per);
+  for (int64_t i = a + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = mc_ld_reduce_add_v4(mc + 4 * i);
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(mc + 4 * i),
+                 "f"(acc.x * scale), "f"(acc.y * scale), "f"(acc.z * scale), "f"(acc.w * scale)
+                 : "memory");
+  }
+  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles);
+}
+
 int comm_grid() { return num_sms(); }  // one 512-thread block per SM: all blocks co-resident
 
 }  // namespace
@@ -394,6 +475,34 @@ void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1,
       (float)b2, (float)eps, (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(),
       norm_out.data_ptr<float>(), (long long)wait_cycles);
+}
+
+// ---- replicated data-parallel all-reduce ------------------------------------------
+// buf_ptrs: every rank's copy of the same-sized fp32 symmetric buffer; the
+// first n elements (n % 4 == 0) are replaced on every rank by their sum over
+// ranks times `scale`.
+void nvlink_allreduce(std::vector<int64_t> buf_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n,
+                      double scale, int64_t epoch, torch::Tensor status, int64_t wait_cycles) {
+  TORCH_CHECK(n % 4 == 0, "nvlink_allreduce: element count must be a multiple of 4");
+  const int W = buf_ptrs.size();
+  TORCH_CHECK(W >= 1 && W <= kMaxRanks && (int)sig_ptrs.size() == W, "nvlink_allreduce: 1..8 ranks");
+  uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
+  allreduce_kernel<<<comm_grid(), 512, 0, stream()>>>(to_peers(buf_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W,
+                                                      n, (float)scale, (uint32_t)epoch, status.data_ptr<int>(),
+                                                      (long long)wait_cycles);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void nvlink_allreduce_mc(int64_t mc_buf, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n, double scale,
+                         int64_t epoch, torch::Tensor status, int64_t wait_cycles) {
+  TORCH_CHECK(n % 4 == 0 && mc_buf % 16 == 0, "nvlink_allreduce_mc: 16-byte aligned buffer, n % 4 == 0");
+  const int W = sig_ptrs.size();
+  TORCH_CHECK(W >= 1 && W <= kMaxRanks, "nvlink_allreduce_mc: 1..8 ranks");
+  uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
+  allreduce_mc_kernel<<<comm_grid(), 512, 0, stream()>>>(reinterpret_cast<float*>(mc_buf), to_peers(sig_ptrs), my_sig,
+                                                         (int)rank, W, n, (float)scale, (uint32_t)epoch,
+                                                         status.data_ptr<int>(), (long long)wait_cycles);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace lrl

@@ -33,12 +33,22 @@ class ModelRunner:
         self.routing_recorder = None
         self.max_len = 0   # static bound on context length (set by the engine)
         self.fp8 = None    # FP8RolloutQuantizer: W8A8 blockwise linears when set
+        # token ids >= vocab_limit (the padded rows of the embedding / LM head
+        # that no tokenizer id maps to) are never sampled: the LM head is
+        # applied to its first vocab_limit rows only, which is the same as
+        # masking the out-of-vocabulary logits to -inf before the softmax
+        self.vocab_limit: Optional[int] = None
 
     def _lin(self, x: Tensor, name: str, decode: bool) -> Tensor:
         w = self._w(name)
         if self.fp8 is not None and name in self.fp8.weights:
-            return self.fp8.linear(name, x, w)
+            return self.fp8.linear(name, x, w, decode)
         return ops.decode_linear(x, w) if decode else ops.linear(x, w)
+
+    def _lm_head(self) -> Tensor:
+        w = self.model.lm_head.detach()
+        v = self.vocab_limit
+        return w if v is None or v >= w.shape[0] else w[:v]
 
     def _w(self, name: str) -> Tensor:
         return self.model.p(name).detach()
@@ -77,7 +87,7 @@ class ModelRunner:
             x = self._mlp(i, h)
         last = cu_seqlens[1:] - 1
         h, _ = ops.add_rmsnorm(x[last], res[last], self._w("norm"), a.rms_norm_eps)
-        return ops.linear(h, self.model.lm_head.detach())
+        return ops.linear(h, self._lm_head())
 
     @torch.no_grad()
     def decode(self, ids: Tensor, positions: Tensor, slots: Tensor, block_table: Tensor, seq_lens: Tensor,
@@ -101,7 +111,7 @@ class ModelRunner:
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h, True)
         h, _ = ops.add_rmsnorm(x, res, self._w("norm"), a.rms_norm_eps)
-        return ops.decode_linear(h, self.model.lm_head.detach())
+        return ops.decode_linear(h, self._lm_head())
 
 
 class DecodeGraph:

@@ -636,6 +636,24 @@ def fp8_gemm_blockwise(x: Tensor, qw: Tensor, sw: Tensor, qx: Optional[Tensor] =
     return out.view(*x.shape[:-1], qw.shape[0]) if x is not None else out
 
 
+FP8_DECODE_GEMM = os.environ.get("LRL_FP8_DECODE_GEMM", "stream")
+
+
+def fp8_decode_linear(x: Tensor, qw: Tensor, sw: Tensor) -> Tensor:
+    """W8A8 linear of the FP8 rollout's decode step (M = live sequences <= 64):
+    one activation-quantiser launch (1x128 E4M3 blocks, the rule of
+    ``quant_act_1x128``) and the persistent stream-K weight-streaming kernel
+    (csrc/gemm/skinny_fp8.cu), which reads the E4M3 weights once.
+    ``LRL_FP8_DECODE_GEMM=gemm`` (or shapes it does not take) use the
+    compute-shaped block-scaled GEMM after the separate quantiser."""
+    ok = (FP8_DECODE_GEMM == "stream" and x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2
+          and 1 <= x.shape[0] <= 64 and x.shape[1] % 128 == 0 and x.stride(1) == 1 and x.stride(0) % 4 == 0
+          and qw.is_contiguous())
+    if ok:
+        return ext().skinny_fp8(x, qw, sw.contiguous(), 0)
+    return fp8_gemm_blockwise(x, qw, sw)
+
+
 def fp8_gemm_status() -> int:
     v = 0
     for t in _FP8_ERR.values():

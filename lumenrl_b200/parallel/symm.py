@@ -185,6 +185,71 @@ class NVLinkOptimizerComm:
             b.close()
 
 
+class NVLinkAllReduce:
+    """All-reduce for replicated data parallel (the draft model of the SDDD
+    layout, DDP-style replicas) on this package's NVLink kernel instead of
+    NCCL: the bucket is staged in an fp32 symmetric buffer, one kernel sums
+    every rank's copy slice by slice over peer memory and writes the result
+    into every copy (``nvls``: the NVLS multimem variant, opt-in like the
+    optimizer's), and the result is read back.  Sums run in fp32 whatever the
+    gradient dtype.  Every cross-rank wait is bounded: a dead or late peer
+    raises ``CommTimeout``."""
+
+    def __init__(self, capacity: int, rank: int, world: int, group=None, wait_seconds: float = 10.0,
+                 nvls: Optional[bool] = None) -> None:
+        self.capacity = (capacity + 3) // 4 * 4
+        self.rank, self.world, self.group = rank, world, group
+        self.wait_cycles = int(wait_seconds * 2.0e9)
+        if nvls is None:
+            nvls = os.environ.get("LRL_NVLS", "0") == "1"
+        self.nvls = False
+        if nvls and nvls_supported():
+            self.buf = MulticastBuffer(self.capacity, torch.float32, group)
+            self.nvls = self.buf.mc != 0
+            if not self.nvls:
+                self.buf.close()
+        if not self.nvls:
+            self.buf = SymmetricBuffer(self.capacity, torch.float32, rank, world, group)
+        self.signals = SymmetricBuffer(int(ext().symm_signal_words()), torch.int32, rank, world, group)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.buf.tensor.device)
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def all_reduce_(self, flat: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
+        """In place: ``flat`` (1-D, any float dtype) <- scale * sum over ranks.
+        Buckets larger than the buffer go through it in pieces."""
+        n = flat.numel()
+        for a in range(0, n, self.capacity):
+            b = min(n, a + self.capacity)
+            m = b - a
+            m4 = (m + 3) // 4 * 4
+            stage = self.buf.tensor[:m4]
+            stage[:m].copy_(flat[a:b])
+            if m4 != m:
+                stage[m:].zero_()
+            self.epoch += 1
+            if self.nvls:
+                ext().nvlink_allreduce_mc(self.buf.mc, self.signals.ptrs, self.rank, m4, scale, self.epoch,
+                                          self.status, self.wait_cycles)
+            else:
+                ext().nvlink_allreduce(self.buf.ptrs, self.signals.ptrs, self.rank, m4, scale, self.epoch,
+                                       self.status, self.wait_cycles)
+            flat[a:b].copy_(stage[:m])
+        return flat
+
+    def check(self) -> None:
+        """Raise ``CommTimeout`` if a cross-rank wait of an earlier call expired
+        (one device->host read)."""
+        s = int(self.status.item())
+        if s:
+            raise CommTimeout(f"NVLink all-reduce: a cross-rank wait expired (code {s}); a peer rank is dead or stalled")
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.buf.close()
+        self.signals.close()
+
+
 # ---------------------------------------------------------------------------
 # correctness checks of the data-parallel replicas (used by bench.py at N > 1
 # and by the multi-GPU tests)

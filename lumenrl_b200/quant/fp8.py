@@ -182,13 +182,15 @@ class FP8RolloutQuantizer:
                     self.weights[name] = (qw, sw)
         return {"fp8/quantized_tensors": len(self.weights)}
 
-    def linear(self, name: str, x: Tensor, w_bf16: Tensor) -> Tensor:
+    def linear(self, name: str, x: Tensor, w_bf16: Tensor, decode: bool = False) -> Tensor:
+        """``decode``: x holds one token per live sequence; the weight-streaming
+        W8A8 kernel serves it (the weights are read once)."""
         if name not in self.weights:
             return x @ w_bf16.t()
         qw, sw = self.weights[name]
         if x.is_cuda:
-            from lumenrl_b200.ops import fp8_gemm_blockwise
-            return fp8_gemm_blockwise(x, qw, sw)
+            from lumenrl_b200.ops import fp8_decode_linear, fp8_gemm_blockwise
+            return fp8_decode_linear(x, qw, sw) if decode else fp8_gemm_blockwise(x, qw, sw)
         qx, sx = quant_1x128_ref(x)
         return (dequant_1x128(qx, sx) @ dequant_128x128(qw, sw).t()).to(x.dtype)
 

@@ -23,6 +23,7 @@ final hidden state, or the last ``num_target_layers`` aux taps).
 
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass
 from typing import Optional
@@ -117,7 +118,7 @@ class SpecDistillTrainer:
     def lm_head_weight(self) -> torch.Tensor:
         return self.teacher.lm_head.detach()
 
-    def draft_update(self, batches: list, group=None, world: int = 1) -> dict:
+    def draft_update(self, batches: list, group=None, world: int = 1, comm=None) -> dict:
         """One optimizer step of the draft over ``batches`` = [(ids, aux,
         last), ...]: the loss is the mean over batches (gradients accumulate),
         then gradients are averaged over ``world`` draft replicas."""
@@ -129,7 +130,7 @@ class SpecDistillTrainer:
             total += float(loss.detach()) / len(batches)
             accs.append(acc)
         if world > 1:
-            allreduce_mean_grads(list(self.draft.parameters()), world, group=group)
+            allreduce_mean_grads(list(self.draft.parameters()), world, group=group, comm=comm)
         o = self.opt.step()
         self.step_count += 1
         mean_acc = [sum(a[i] for a in accs) / len(accs) for i in range(len(accs[0]))]
@@ -201,6 +202,15 @@ class SDDDTrainer(SpecDistillTrainer):
             self._lm_head = self._embed if a.tie_word_embeddings else torch.empty(a.vocab_size, a.hidden_size,
                                                                                  dtype=dtype, device=dev)
             self._build_draft(dev, dtype, total_steps)
+        # the draft replicas average gradients with the NVLink all-reduce kernel
+        # (LRL_DRAFT_ALLREDUCE=nccl keeps NCCL); every draft rank builds it
+        self.ar_comm = None
+        if (not self.is_teacher and self.num_draft > 1 and dev.type == "cuda"
+                and os.environ.get("LRL_DRAFT_ALLREDUCE", "nvlink") != "nccl"):
+            from lumenrl_b200.parallel.symm import NVLinkAllReduce
+            n_grad = sum(p.numel() for p in self.draft.parameters())
+            self.ar_comm = NVLinkAllReduce(min(n_grad, 64 << 20), rank - num_teacher, self.num_draft,
+                                           group=self.draft_group)
         if rank in [0] + list(range(num_teacher, world)):
             dist.broadcast(self._embed, src=0, group=self.weights_group)
             if not a.tie_word_embeddings:
@@ -263,7 +273,9 @@ class SDDDTrainer(SpecDistillTrainer):
             payload = self.rings[t].get((self.payload_bytes,), torch.uint8, device=dev)
             batches.append(self._unpack(payload))
             held.append(t)
-        out = self.draft_update(batches, group=self.draft_group, world=self.num_draft)
+        out = self.draft_update(batches, group=self.draft_group, world=self.num_draft, comm=self.ar_comm)
+        if self.ar_comm is not None:
+            self.ar_comm.check()
         for t in held:
             self.rings[t].release()
         out.update(role="draft", step_s=time.perf_counter() - t0, tokens=tokens)
@@ -276,11 +288,16 @@ class SDDDTrainer(SpecDistillTrainer):
     def close(self) -> None:
         for r in self.rings.values():
             r.close()
+        if self.ar_comm is not None:
+            self.ar_comm.close()
+            self.ar_comm = None
 
 
-def allreduce_mean_grads(params: list, world: int, bucket_bytes: int = 256 << 20, group=None) -> None:
+def allreduce_mean_grads(params: list, world: int, bucket_bytes: int = 256 << 20, group=None, comm=None) -> None:
     """Replicated data parallel: average gradients across ranks with a few
-    large flat all-reduces (one per dtype bucket) instead of one per tensor."""
+    large flat all-reduces (one per dtype bucket) instead of one per tensor.
+    ``comm``: an ``NVLinkAllReduce`` (this package's peer-memory kernel, fp32
+    sums); without it the buckets go through NCCL."""
     grads = [p.grad for p in params if p.grad is not None]
     by_dtype: dict = {}
     for g in grads:
@@ -293,8 +310,11 @@ def allreduce_mean_grads(params: list, world: int, bucket_bytes: int = 256 << 20
                 size += gs[j].numel() * gs[j].element_size()
                 j += 1
             flat = torch.cat([g.reshape(-1) for g in gs[i:j]])
-            dist.all_reduce(flat, group=group)
-            flat /= world
+            if comm is not None and flat.is_cuda:
+                comm.all_reduce_(flat, scale=1.0 / world)
+            else:
+                dist.all_reduce(flat, group=group)
+                flat /= world
             off = 0
             for g in gs[i:j]:
                 g.copy_(flat[off: off + g.numel()].view_as(g))

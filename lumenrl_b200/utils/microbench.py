@@ -66,7 +66,12 @@ def bench_decode(ns) -> dict:
     from lumenrl_b200 import ops
     m = _model(ns.model, False)
     B, ctx = ns.batch, ns.ctx
-    eng = RolloutEngine(m, max_num_seqs=B, max_model_len=ctx + 64, use_cuda_graph=not ns.no_graph)
+    fp8 = None
+    if ns.fp8:
+        from lumenrl_b200.quant.fp8 import FP8Config
+        fp8 = FP8Config(precision="fp8")
+    eng = RolloutEngine(m, max_num_seqs=B, max_model_len=ctx + 64, use_cuda_graph=not ns.no_graph,
+                        kv_dtype=torch.float8_e4m3fn if ns.fp8_kv else torch.bfloat16, fp8_rollout=fp8)
     bs = eng.block_size
     n, P = ns.group, (ns.prefix // bs) * bs    # rows of a group share a P-token prompt (in ctx)
     grp = ops.shared_prefix_group(n, m.args.num_heads // m.args.num_kv_heads) if n > 1 and P > 0 else 1
@@ -87,9 +92,12 @@ def bench_decode(ns) -> dict:
     g.tokens.random_(0, m.args.vocab_size)
     ms = _time(g.run, ns.steps, ns.warmup)
     wbytes = m.flat.numel() * 2
-    kvbytes = B * ctx * m.args.kv_bytes_per_token()
+    if fp8 is not None:   # E4M3 copies replace the bf16 decoder linears in the step
+        wbytes -= sum(qw.numel() for qw, _ in eng.runner.fp8.weights.values())
+    kvbytes = B * ctx * m.args.kv_bytes_per_token() // (2 if ns.fp8_kv else 1)
     return {"op": "decode_step", "batch": B, "ctx": ctx, "shared_prefix": pb * bs, "group": grp,
-            "attn": ops.DECODE_ATTN, "gemm": ops.DECODE_GEMM, "ms": ms,
+            "attn": ops.DECODE_ATTN, "gemm": ops.DECODE_GEMM, "ms": ms, "fp8_weights": bool(ns.fp8),
+            "fp8_kv": bool(ns.fp8_kv), "fp8_decode_gemm": ops.FP8_DECODE_GEMM if ns.fp8 else None,
             "weights_GB": wbytes / 1e9, "kv_GB": kvbytes / 1e9, "achieved_TBps": (wbytes + kvbytes) / ms / 1e9}
 
 
@@ -235,6 +243,46 @@ def bench_dgemm(ns) -> dict:
         res["stream_k_TBps"] = round(N * K * 2 / res["stream_k_us"] / 1e6, 2)
         out[name] = res
         del ws
+    return out
+
+
+def bench_fp8dgemm(ns) -> dict:
+    """FP8 rollout decode linears (M = --batch rows, E4M3 weights with 128x128
+    scales): the weight-streaming W8A8 path (quantiser + stream-K kernel)
+    against the two-kernel path (1x128 activation quantiser + block-scaled
+    GEMM) and the bf16 cuBLAS linear; weights rotate through > 300 MB of
+    copies so every call streams them from HBM."""
+    from lumenrl_b200 import ops
+    from lumenrl_b200.ops.ext import ext
+    from lumenrl_b200.quant.fp8 import quant_weight_128x128
+    a = _model_args(ns.model)
+    shapes = {"qkv": (a.qkv_dim, a.hidden_size), "o": (a.hidden_size, a.q_dim),
+              "w13": (2 * a.intermediate_size, a.hidden_size), "w2": (a.hidden_size, a.intermediate_size)}
+    out = {"op": "fp8_decode_linears", "M": ns.batch, "cache": "weights rotate through > 300 MB of copies"}
+    total = {"stream_us": 0.0, "two_kernel_us": 0.0, "bf16_cublas_us": 0.0}
+    for name, (N, K) in shapes.items():
+        x = torch.randn(ns.batch, K, device="cuda").to(torch.bfloat16)
+        copies = max(2, -(-300_000_000 // (N * K)))
+        qs = [quant_weight_128x128((torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16))
+              for _ in range(copies)]
+        wb = [(torch.randn(N, K, device="cuda") / K ** 0.5).to(torch.bfloat16) for _ in range(max(2, copies // 2))]
+        it = [0]
+
+        def nxt(pool):
+            it[0] = (it[0] + 1) % len(pool)
+            return pool[it[0]]
+        res = {"weight_MB": round(N * K / 1e6, 1)}
+        res["stream_us"] = round(_time(lambda: ext().skinny_fp8(x, *nxt(qs), 0), ns.steps, ns.warmup) * 1e3, 1)
+        res["two_kernel_us"] = round(_time(lambda: ops.fp8_gemm_blockwise(x, *nxt(qs)), ns.steps, ns.warmup) * 1e3, 1)
+        res["bf16_cublas_us"] = round(_time(lambda: torch.nn.functional.linear(x, nxt(wb)), ns.steps,
+                                            ns.warmup) * 1e3, 1)
+        res["stream_TBps"] = round(N * K / res["stream_us"] / 1e6, 2)
+        res["status"] = int(ext().skinny_fp8_status())
+        for k in total:
+            total[k] += res[k]
+        out[name] = res
+        del qs, wb
+    out["per_layer_us"] = {k: round(v, 1) for k, v in total.items()}
     return out
 
 
@@ -529,7 +577,7 @@ def bench_comm(ns) -> dict:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
-                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy", "eagle"])
+                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy", "eagle", "fp8dgemm"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -547,12 +595,14 @@ def main(argv=None) -> None:
     ap.add_argument("--mnk", default="", help="gemm2probe shape M,N,K")
     ap.add_argument("--case", default="", help="gemm2probe operand layout: kk, kn, nn or nk")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--fp8", action="store_true", help="decode: W8A8 FP8 rollout linears (128x128 weight blocks)")
+    ap.add_argument("--fp8-kv", action="store_true", help="decode: E4M3 KV cache")
     ap.add_argument("--sustain-ms", type=float, default=0.0,
                     help="gemm2: run each GEMM back to back this long before timing it (power-limited clocks)")
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "eagle": bench_eagle, "gemm2energy": bench_gemm2energy,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "fp8dgemm": bench_fp8dgemm, "eagle": bench_eagle, "gemm2energy": bench_gemm2energy,
           "comm": bench_comm, "gemm2": bench_gemm2,
           "gemm2probe": bench_gemm2probe}[ns.what]
     res = fn(ns)

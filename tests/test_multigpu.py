@@ -72,6 +72,59 @@ def test_fused_optimizer_step_matches_nccl(world, nvls):
             assert abs(a - b) <= 1e-3 * max(1.0, b), (a, b)
 
 
+def _allreduce_worker(rank, world, port, q, nvls):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    from lumenrl_b200.parallel.symm import NVLinkAllReduce
+    from lumenrl_b200.trainer.spec_distill_trainer import allreduce_mean_grads
+    comm = NVLinkAllReduce(4000, rank, world, nvls=nvls)          # small: buckets go through in pieces
+    errs = []
+    for step, (n, dt) in enumerate([(10003, torch.float32), (6001, torch.bfloat16), (8, torch.float32)]):
+        g = torch.Generator(device="cuda").manual_seed(100 * step + rank)
+        x = torch.randn(n, device="cuda", generator=g).to(dt)
+        want = x.float().clone()
+        dist.all_reduce(want)
+        got = comm.all_reduce_(x.clone(), scale=1.0 / world).float()
+        errs.append((got - want / world).abs().max().item())
+    # the replicated-DP gradient path of the draft trainer
+    lin = torch.nn.Linear(64, 48, device="cuda")
+    lin.weight.grad = torch.full_like(lin.weight, float(rank + 1))
+    lin.bias.grad = torch.full_like(lin.bias, float(2 * rank))
+    allreduce_mean_grads(list(lin.parameters()), world, comm=comm)
+    errs.append((lin.weight.grad - (world + 1) / 2).abs().max().item())
+    errs.append((lin.bias.grad - (world - 1)).abs().max().item())
+    comm.check()
+    torch.cuda.synchronize()
+    q.put((rank, errs, comm.nvls))
+    dist.barrier()
+    comm.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("nvls", [False, True])
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nvlink_allreduce_matches_nccl(world, nvls):
+    """Replicated-DP all-reduce on the peer-memory kernel (nvls=True: NVLS
+    multimem when supported) against NCCL all_reduce, fp32 and bf16 buckets
+    larger and smaller than the staging buffer."""
+    _need(world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28700 + os.getpid() % 150 + (0 if nvls else 200)
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, port, q, nvls)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    print("nvls path:", [r[2] for r in res])
+    for rank, errs, _ in res:
+        assert errs[0] <= 1e-5 and errs[1] <= 2e-2 and errs[2] <= 1e-5, (rank, errs)
+        assert errs[3] <= 1e-6 and errs[4] <= 1e-6, (rank, errs)
+
+
 def _dead_peer_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")

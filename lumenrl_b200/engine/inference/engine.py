@@ -83,7 +83,13 @@ class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
                  use_cuda_graph: bool = True, pad_token_id: int = 0, shared_prefix_attention: bool = True,
-                 fp8_rollout=None, continuous_batching: bool = True, vocab_limit: Optional[int] = None) -> None:
+                 fp8_rollout=None, continuous_batching: bool = True, vocab_limit: Optional[int] = None,
+                 tp_group=None) -> None:
+        """``tp_group``: a process group of size T > 1 serves the model with
+        tensor parallelism (``runner.TPShards``): every member calls
+        ``generate`` with the same prompts and sampling parameters and gets the
+        same samples, each GPU holding 1/T of the decoder linears' reads and of
+        the KV cache."""
         self.model = model
         self.args = model.args
         self.device = model.flat.device
@@ -94,14 +100,24 @@ class RolloutEngine:
         self.shared_prefix_attention = shared_prefix_attention
         self.continuous_batching = continuous_batching
         self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda" and self.args.num_experts == 0
-        spec = KVSpec(self.args.num_layers, self.args.num_kv_heads, self.args.head_dim, block_size, kv_dtype)
+        tp = None
+        if tp_group is not None:
+            import torch.distributed as dist
+            if dist.get_world_size(tp_group) > 1:
+                from lumenrl_b200.engine.inference.runner import TPShards
+                tp = TPShards(model, tp_group, dist.get_rank(tp_group), dist.get_world_size(tp_group))
+                if fp8_rollout is not None and fp8_rollout.is_fp8_enabled():
+                    raise ValueError("rollout TP with FP8 rollout weights is not supported: use TP=1 per GPU")
+        self.tp = tp
+        kv_heads = tp.num_kv_heads if tp is not None else self.args.num_kv_heads
+        spec = KVSpec(self.args.num_layers, kv_heads, self.args.head_dim, block_size, kv_dtype)
         self.max_blocks_per_seq = math.ceil(max_model_len / block_size) + 1
         if kv_cache_bytes is None:
             nblocks = max_num_seqs * self.max_blocks_per_seq + 1
         else:
             nblocks = PagedKVCache.blocks_for_budget(spec, kv_cache_bytes)
         self.cache = PagedKVCache(spec, nblocks, self.device)
-        self.runner = ModelRunner(model, self.cache)
+        self.runner = ModelRunner(model, self.cache, tp)
         self.runner.max_len = max_model_len
         if vocab_limit is not None:
             if not 0 < vocab_limit <= self.args.vocab_size:
@@ -143,6 +159,8 @@ class RolloutEngine:
         if self.runner.fp8 is not None:
             # re-quantised in place: the captured graphs read the same buffers
             self.runner.fp8.quantize_model(self.model)
+        if self.tp is not None:
+            self.tp.refresh()      # this rank's slices, copied in place
         self.weight_version = self.weight_version + 1 if version is None else version
 
     # -- generation ------------------------------------------------------------------

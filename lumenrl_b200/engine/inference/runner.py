@@ -24,10 +24,79 @@ from lumenrl_b200.engine.inference.kv_cache import PagedKVCache
 from lumenrl_b200.models.qwen3 import Qwen3Model
 
 
+class TPShards:
+    """Tensor-parallel rollout (Megatron layout) for one rank of a TP group:
+    this rank's slice of every decoder linear, rebuilt from the full bf16
+    weights at each weight sync (``refresh``).
+
+    * ``wqkv``: the q rows of heads [t Hq/T, (t+1) Hq/T) and the k / v rows of
+      kv heads [t Hk/T, (t+1) Hk/T) (column parallel: no reduction);
+    * ``wo``: the matching input columns (row parallel: partial sums);
+    * ``w13``: rows [t F/T, (t+1) F/T) of gate and of up (column parallel);
+    * ``w2``: the matching input columns (row parallel).
+
+    Norm weights, the embedding and the LM head stay replicated, so after the
+    two all-reduces of a layer every rank holds the same residual stream and
+    samples the same tokens.  The KV cache of a rank holds its kv heads only."""
+
+    SHARDED = ("wqkv", "wo", "w13", "w2")
+
+    def __init__(self, model: Qwen3Model, group, rank: int, size: int) -> None:
+        a = model.args
+        if a.num_heads % size or a.num_kv_heads % size or a.intermediate_size % size:
+            raise ValueError(f"rollout TP={size} must divide heads ({a.num_heads} q / {a.num_kv_heads} kv) and "
+                             f"the FFN width ({a.intermediate_size})")
+        if a.num_experts:
+            raise ValueError("rollout TP serves dense models; MoE rollouts shard experts instead")
+        self.model, self.group, self.rank, self.size = model, group, rank, size
+        self.num_heads, self.num_kv_heads = a.num_heads // size, a.num_kv_heads // size
+        self.weights: dict[str, Tensor] = {}
+        self.refresh()
+
+    @torch.no_grad()
+    def _slice(self, kind: str, w: Tensor) -> Tensor:
+        a, t, T = self.model.args, self.rank, self.size
+        D = a.head_dim
+        if kind == "wqkv":
+            qh, kh = self.num_heads * D, self.num_kv_heads * D
+            q0, k0 = a.num_heads * D, a.num_heads * D + a.num_kv_heads * D
+            return torch.cat([w[t * qh:(t + 1) * qh], w[q0 + t * kh: q0 + (t + 1) * kh],
+                              w[k0 + t * kh: k0 + (t + 1) * kh]])
+        if kind == "wo":
+            qh = self.num_heads * D
+            return w[:, t * qh:(t + 1) * qh]
+        F, f = a.intermediate_size, a.intermediate_size // T
+        if kind == "w13":
+            return torch.cat([w[t * f:(t + 1) * f], w[F + t * f: F + (t + 1) * f]])
+        return w[:, t * f:(t + 1) * f]    # w2
+
+    @torch.no_grad()
+    def refresh(self) -> None:
+        """Copy this rank's slices out of the model's (full, current) weights,
+        into the same buffers every time (captured decode graphs stay valid)."""
+        for name, p in self.model.named_flat_params():
+            kind = name.rsplit(".", 1)[-1]
+            if kind not in self.SHARDED:
+                continue
+            sl = self._slice(kind, p.detach())
+            dst = self.weights.get(name)
+            if dst is None:
+                self.weights[name] = sl.contiguous().clone()
+            else:
+                dst.copy_(sl)
+
+    def reduce(self, x: Tensor) -> Tensor:
+        """Sum the row-parallel partial outputs over the TP group (in place)."""
+        import torch.distributed as dist
+        dist.all_reduce(x, group=self.group)
+        return x
+
+
 class ModelRunner:
-    def __init__(self, model: Qwen3Model, cache: PagedKVCache) -> None:
+    def __init__(self, model: Qwen3Model, cache: PagedKVCache, tp: Optional[TPShards] = None) -> None:
         self.model = model
         self.cache = cache
+        self.tp = tp
         self.args = model.args
         self.scale = 1.0 / math.sqrt(self.args.head_dim)
         self.routing_recorder = None
@@ -51,7 +120,18 @@ class ModelRunner:
         return w if v is None or v >= w.shape[0] else w[:v]
 
     def _w(self, name: str) -> Tensor:
+        if self.tp is not None and name in self.tp.weights:
+            return self.tp.weights[name]
         return self.model.p(name).detach()
+
+    def _heads(self) -> tuple[int, int]:
+        if self.tp is not None:
+            return self.tp.num_heads, self.tp.num_kv_heads
+        return self.args.num_heads, self.args.num_kv_heads
+
+    def _row_parallel(self, x: Tensor, name: str, decode: bool) -> Tensor:
+        y = self._lin(x, name, decode)
+        return self.tp.reduce(y) if self.tp is not None else y
 
     def _mlp(self, i: int, h: Tensor, decode: bool = False) -> Tensor:
         if self.args.is_moe_layer(i):
@@ -63,14 +143,15 @@ class ModelRunner:
             finally:
                 self.model.routing_recorder = prev
             return out
-        return self._lin(ops.swiglu(self._lin(h, f"layers.{i}.w13", decode)), f"layers.{i}.w2", decode)
+        return self._row_parallel(ops.swiglu(self._lin(h, f"layers.{i}.w13", decode)), f"layers.{i}.w2", decode)
 
     def _qkv(self, i: int, h: Tensor, positions: Tensor, slots: Tensor, decode: bool = False):
         a, c = self.args, self.cache
         qkv = self._lin(h, f"layers.{i}.wqkv", decode)
         qn = self._w(f"layers.{i}.q_norm") if a.qk_norm else None
         kn = self._w(f"layers.{i}.k_norm") if a.qk_norm else None
-        return ops.qk_norm_rope_cache(qkv, qn, kn, positions, self.model.inv_freq, a.num_heads, a.num_kv_heads,
+        nh, nkv = self._heads()
+        return ops.qk_norm_rope_cache(qkv, qn, kn, positions, self.model.inv_freq, nh, nkv,
                                       a.head_dim, a.rms_norm_eps, c.k[i], c.v[i], slots, c.k_scale[i], c.v_scale[i])
 
     @torch.no_grad()
@@ -82,7 +163,7 @@ class ModelRunner:
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln1"), a.rms_norm_eps)
             q, k, v = self._qkv(i, h, positions, slots)
             o = ops.attention_varlen(q, k, v, cu_seqlens, max_len, causal=True, scale=self.scale)
-            x = self._lin(o.reshape(o.shape[0], -1), f"layers.{i}.wo", False)
+            x = self._row_parallel(o.reshape(o.shape[0], -1), f"layers.{i}.wo", False)
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h)
         last = cu_seqlens[1:] - 1
@@ -107,7 +188,7 @@ class ModelRunner:
             else:
                 o = ops.paged_decode_attention(q, c.k[i], c.v[i], block_table, seq_lens, self.scale,
                                                c.k_scale[i], c.v_scale[i], self.max_len)
-            x = self._lin(o.reshape(o.shape[0], -1), f"layers.{i}.wo", True)
+            x = self._row_parallel(o.reshape(o.shape[0], -1), f"layers.{i}.wo", True)
             h, res = ops.add_rmsnorm(x, res, self._w(f"layers.{i}.ln2"), a.rms_norm_eps)
             x = self._mlp(i, h, True)
         h, _ = ops.add_rmsnorm(x, res, self._w("norm"), a.rms_norm_eps)

@@ -69,6 +69,19 @@ class RLRunSpec:
     gradient_checkpointing: object = False   # True (every layer), False, or "auto" (memory-budgeted)
 
 
+def _keep_groups(out, n: int, T: int, member: int):
+    """Rows of every T-th prompt group (starting at ``member``) of a
+    generation result: whole GRPO groups, so group statistics stay local."""
+    from dataclasses import replace
+    P = out.responses.shape[0] // n
+    keep_p = torch.arange(member, P, T, device=out.responses.device)
+    rows = (keep_p.unsqueeze(1) * n + torch.arange(n, device=keep_p.device)).reshape(-1)
+    prompts = out.prompts[rows] if isinstance(out.prompts, torch.Tensor) else [out.prompts[i] for i in rows.tolist()]
+    return replace(out, prompts=prompts, responses=out.responses[rows], response_lengths=out.response_lengths[rows],
+                   logprobs=out.logprobs[rows], prompt_index=out.prompt_index[rows],
+                   routed_experts=[out.routed_experts[i] for i in rows.tolist()] if out.routed_experts else [])
+
+
 class RLTrainer:
     def __init__(self, config: LumenRLConfig, model_args: Optional[ModelArgs] = None,
                  spec: Optional[RLRunSpec] = None, state: Optional[ParallelState] = None) -> None:
@@ -155,11 +168,23 @@ class RLTrainer:
         max_len = self.spec.prompt_len + self.spec.max_new_tokens
         prompts_per_rank = max(1, self.spec.prompts_per_step // rollout_ranks)
         self.prompts_per_rank = prompts_per_rank
+        # rollout tensor parallelism: TP groups of consecutive ranks generate
+        # the same prompts together; each member then keeps every T-th GRPO
+        # group of the result, so training stays data parallel over all ranks
+        T = int(getattr(vc, "tensor_parallel_size", 1) or 1)
+        self.tp_size, self.tp_member, self.tp_group = T, 0, None
+        if T > 1:
+            import torch.distributed as dist
+            W, r = self.state.world_size, self.state.rank
+            if W % T:
+                raise ValueError(f"rollout tensor_parallel_size={T} must divide the {W} rollout ranks")
+            groups = [dist.new_group(list(range(g * T, (g + 1) * T))) for g in range(W // T)]  # every rank, same order
+            self.tp_group, self.tp_member = groups[r // T], r % T
         kv_dtype = torch.float8_e4m3fn if str(vc.kv_cache_dtype).startswith("fp8") else torch.bfloat16
-        self.rollout = RolloutEngine(model, max_num_seqs=prompts_per_rank * self.group,
+        self.rollout = RolloutEngine(model, max_num_seqs=prompts_per_rank * T * self.group,
                                      max_model_len=max_len, kv_cache_bytes=self.spec.kv_cache_bytes,
                                      use_cuda_graph=self.spec.use_cuda_graph, kv_dtype=kv_dtype,
-                                     fp8_rollout=self._fp8_rollout_config(c))
+                                     fp8_rollout=self._fp8_rollout_config(c), tp_group=self.tp_group)
 
     @staticmethod
     def _fp8_rollout_config(c):
@@ -174,17 +199,21 @@ class RLTrainer:
     # ------------------------------------------------------------------ step
     def _rollout(self, step: int, round_idx: int = 0) -> DataProto:
         st, sp = self.state, self.spec
-        host = self.data.batch_tensor(self.prompts_per_rank, step, st.rank, pin=st.device.type == "cuda",
+        T = getattr(self, "tp_size", 1)
+        src = st.rank // T          # the members of a rollout TP group draw the same prompts and samples
+        host = self.data.batch_tensor(self.prompts_per_rank * T, step, src, pin=st.device.type == "cuda",
                                       round=round_idx)
         prompts = host.to(st.device, non_blocking=True)
         self.io_bytes["h2d"] = host.numel() * host.element_size()
         params = SamplingParams(max_new_tokens=sp.max_new_tokens, temperature=self.temperature, top_p=self.top_p,
                                 n=self.group,
-                                seed=self.config.seed * 7919 + step * 131 + st.rank + round_idx * 1_000_033,
+                                seed=self.config.seed * 7919 + step * 131 + src + round_idx * 1_000_033,
                                 eos_token_id=sp.eos_token_id)
         self.rollout.wake()
         out = self.rollout.generate(prompts, params)
         self.rollout.sleep()
+        if T > 1:
+            out = _keep_groups(out, self.group, T, self.tp_member)
         dev = st.device
         B = out.responses.shape[0]
         pgrid = out.prompts
@@ -202,6 +231,16 @@ class RLTrainer:
             batch.ragged["routed_experts"] = out.routed_experts
         return batch
 
+    def _tp_total(self, n: int) -> int:
+        """``n`` summed over this rank's rollout TP group (a generation round is
+        collective inside the group, so its members decide refills together)."""
+        if getattr(self, "tp_size", 1) <= 1:
+            return n
+        import torch.distributed as dist
+        t = torch.tensor([float(n)], device=self.state.device)
+        dist.all_reduce(t, group=self.tp_group)
+        return int(t.item())
+
     def _score(self, batch: DataProto) -> None:
         rewards = self.reward_fn(batch["responses"], None, lengths=batch["response_lengths"], **self.spec.reward_kwargs)
         batch["rewards"] = rewards.to(self.state.device).float()
@@ -218,7 +257,7 @@ class RLTrainer:
         from lumenrl_b200.algorithms.dapo_sampling import filter_groups_keep_mask
         max_rounds = int(fg.max_num_gen_batches) if int(fg.max_num_gen_batches) > 0 else 10_000
         parts, uids, stats, kept, rounds, seen = [], [], {}, 0, 0, 0
-        while kept < self.prompts_per_rank and rounds < max_rounds:
+        while self._tp_total(kept) < self.prompts_per_rank * getattr(self, "tp_size", 1) and rounds < max_rounds:
             b = self._rollout(step, rounds)
             self._score(b)
             keep, kept_uids = filter_groups_keep_mask(b["rewards"].float().cpu(), b.meta["uid"])

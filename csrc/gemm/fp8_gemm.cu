@@ -15,10 +15,13 @@
 // warp already fills the other buffer with the next K block.  At the end of a
 // tile the registers are written as bf16.
 //
-// Roles per CTA (192 threads): warp 0 TMA producer (128x128-byte A and B
+// Roles per CTA (320 threads): warp 0 TMA producer (128x128-byte A and B
 // boxes, 128-byte swizzle, kStages ring), warp 1 TMEM owner + single-thread
 // tcgen05.mma issuer (M=128, N=128, K=32 per instruction, 4 per K block),
-// warps 2-5 promotion + epilogue (one TMEM lane / output row per thread).
+// warps 2-9 promotion + epilogue (two warps per TMEM lane quarter, each
+// owning 64 of the tile's 128 columns of its 32 rows: both 32-column TMEM
+// loads of a K block are issued before one wait, and the accumulator buffer
+// is released to the MMA warp as soon as it is in registers).
 // All mbarrier waits are bounded (tc_gemm.cuh).
 #include "../common.cuh"
 #include "tc_gemm.cuh"
@@ -34,7 +37,8 @@ constexpr int kFStages = 6;
 constexpr int kFABytes = kFBM * kFBK, kFBBytes = kFBN * kFBK;
 constexpr int kFStageBytes = kFABytes + kFBBytes;  // 32 KB
 constexpr int kFSmem = kFStages * kFStageBytes + 1024 + 256;
-constexpr int kFThreads = 192;
+constexpr int kFThreads = 320;   // producer, MMA, 8 promotion / epilogue warps
+constexpr int kHalf = 64;         // tile columns per promotion warp
 
 __host__ __device__ constexpr uint32_t idesc_f8_f32(int M, int N, int afmt, int bfmt) {
   // c_format F32 (bit 4); A format at [7,10), B format at [10,13) (E4M3 = 0,
@@ -50,6 +54,31 @@ __device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t adesc, uint64_
       " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns into r[0..31] WITHOUT waiting: the
+// caller issues several loads, then one tcgen05.wait::ld before using them
+__device__ __forceinline__ void tmem_ld_x32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Ties 32 registers written by an asynchronous tcgen05.ld to the wait that
+// precedes this call: the empty asm "rewrites" them, so no use can be moved
+// above the wait by the compiler.
+__device__ __forceinline__ void regs_ready(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
 }
 
 template <int AF, int BF, bool B_ROW, bool ACC>
@@ -80,7 +109,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&kfull[b], 1);
-      mbar_init(&kempty[b], 128);
+      mbar_init(&kempty[b], 8);   // one arrival per promotion warp
     }
     *err = kErrNone;
     fence_barrier_init();
@@ -143,16 +172,19 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
       }
     }
-  } else {
-    const int q = warp & 3;
+  } else if (warp >= 2) {
+    // promotion + epilogue: 8 warps, two per TMEM lane quarter; warp w owns
+    // rows [32 (w % 4), +32) and columns [64 hf, 64 hf + 64) of the tile
+    const int q = warp & 3, hf = (warp - 2) >> 2;
+    const int col0 = hf * kHalf;
     int kc = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       const int mb = t % num_m, nb = t / num_m;
       const int row = mb * kFBM + q * 32 + lane;
       const int rs = row < M ? row : M - 1;
-      float acc[kFBN];
+      float acc[kHalf];
 #pragma unroll
-      for (int i = 0; i < kFBN; ++i) acc[i] = 0.f;
+      for (int i = 0; i < kHalf; ++i) acc[i] = 0.f;
       bool ok = true;
       for (int kb = 0; kb < kblocks; ++kb, ++kc) {
         const int buf = kc & 1;
@@ -161,47 +193,47 @@ __global__ void __launch_bounds__(kFThreads, 1)
           break;
         }
         tc_fence_after();
+        // both 32-column loads in flight before one wait
+        uint32_t r[kHalf];
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + col0;
+        tmem_ld_x32_nowait(ta, r);
+        tmem_ld_x32_nowait(ta + 32, r + 32);
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+        regs_ready(r);
+        regs_ready(r + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kempty[buf]);   // the accumulator is in registers now
         if constexpr (B_ROW) {
           // per-column scales of this K block: sb is K-block-major [kblocks,
-          // Npad] (Npad a multiple of 128), so the 128 scales of the tile are
+          // Npad] (Npad a multiple of 128), so the warp's 64 scales are
           // contiguous and every thread reads the same addresses (broadcast)
           const float sr = sa[(int64_t)rs * kblocks + kb];
           const int npad = (N + kFBN - 1) / kFBN * kFBN;
-          const float4* sc = reinterpret_cast<const float4*>(sb + (int64_t)kb * npad + nb * kFBN);
+          const float4* sc = reinterpret_cast<const float4*>(sb + (int64_t)kb * npad + nb * kFBN + col0);
 #pragma unroll
-          for (int c = 0; c < kFBN / 32; ++c) {
-            float v[32];
-            tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 f = __ldg(sc + c * 8 + i);
-              acc[c * 32 + 4 * i] += v[4 * i] * (sr * f.x);
-              acc[c * 32 + 4 * i + 1] += v[4 * i + 1] * (sr * f.y);
-              acc[c * 32 + 4 * i + 2] += v[4 * i + 2] * (sr * f.z);
-              acc[c * 32 + 4 * i + 3] += v[4 * i + 3] * (sr * f.w);
-            }
+          for (int i = 0; i < kHalf / 4; ++i) {
+            const float4 f = __ldg(sc + i);
+            acc[4 * i] += __uint_as_float(r[4 * i]) * (sr * f.x);
+            acc[4 * i + 1] += __uint_as_float(r[4 * i + 1]) * (sr * f.y);
+            acc[4 * i + 2] += __uint_as_float(r[4 * i + 2]) * (sr * f.z);
+            acc[4 * i + 3] += __uint_as_float(r[4 * i + 3]) * (sr * f.w);
           }
         } else {
           const float scale = sa[(int64_t)rs * kblocks + kb] * sb[(int64_t)nb * kblocks + kb];
 #pragma unroll
-          for (int c = 0; c < kFBN / 32; ++c) {
-            float v[32];
-            tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + buf * kFBN + c * 32, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c * 32 + i] += v[i] * scale;
-          }
+          for (int i = 0; i < kHalf; ++i) acc[i] += __uint_as_float(r[i]) * scale;
         }
-        tc_fence_before();
-        mbar_arrive(&kempty[buf]);
       }
       if (!ok) break;
       if (row < M) {
-        const int ncols = min(kFBN, N - nb * kFBN);
+        const int ncols = min(kHalf, N - nb * kFBN - col0);
+        if (ncols <= 0) continue;
         if constexpr (ACC) {
-          float* p = reinterpret_cast<float*>(Cv) + (int64_t)row * ldc + nb * kFBN;
-          if (ncols == kFBN && (ldc % 4) == 0) {
+          float* p = reinterpret_cast<float*>(Cv) + (int64_t)row * ldc + nb * kFBN + col0;
+          if (ncols == kHalf && (ldc % 4) == 0) {
 #pragma unroll
-            for (int i = 0; i < kFBN / 4; ++i) {
+            for (int i = 0; i < kHalf / 4; ++i) {
               float4 o = reinterpret_cast<float4*>(p)[i];
               o.x += acc[4 * i];
               o.y += acc[4 * i + 1];
@@ -211,14 +243,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < kFBN; ++i)
+            for (int i = 0; i < kHalf; ++i)
               if (i < ncols) p[i] += acc[i];
           }
         } else {
-          __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(Cv) + (int64_t)row * ldc + nb * kFBN;
-          if (ncols == kFBN && (ldc % 8) == 0) {
+          __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(Cv) + (int64_t)row * ldc + nb * kFBN + col0;
+          if (ncols == kHalf && (ldc % 8) == 0) {
 #pragma unroll
-            for (int i = 0; i < kFBN / 8; ++i) {
+            for (int i = 0; i < kHalf / 8; ++i) {
               float tmp[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) tmp[j] = acc[8 * i + j];
@@ -226,7 +258,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < kFBN; ++i)
+            for (int i = 0; i < kHalf; ++i)
               if (i < ncols) p[i] = __float2bfloat16(acc[i]);
           }
         }

@@ -79,7 +79,10 @@ def _async_worker(rank, world, port, q, lag):
     from lumenrl_b200.models.config import tiny_llama
     tr = SeparatedRLTrainer(cfg, tiny_llama(), _spec(), ParallelState(rank=rank, world_size=world), num_rollout=1,
                             async_lag=lag).setup()
-    hist = [tr.step() for _ in range(3)]
+    hist = []
+    for _ in range(3):
+        hist.append(tr.step())
+        dist.barrier()      # a barrier between steps (bench.py's timed-region boundary) must not deadlock
     tr.finish()
     q.put((rank, [m.get("rollout_corr/kl") for m in hist] if not tr.is_rollout else None, tr.model.flat.clone()))
     dist.barrier()

@@ -29,11 +29,12 @@
 //     block, and the epilogue warps "promote" each one: tcgen05.ld, scale by
 //     sw * sx[m], add into fp32 registers.
 //
-// Warps of the GEMM (192 threads): 0 TMA producer (the first stages' weights
+// Warps of the GEMM (320 threads): 0 TMA producer (the first stages' weights
 // are prefetched into L2 before the dependency wait, every shared-memory load
-// is issued after it), 1 TMEM owner + MMA issuer, 2-5 promotion + output (one
-// TMEM lane = one weight row per thread).  Every mbarrier wait is bounded and
-// reports a status word.
+// is issued after it), 1 TMEM owner + MMA issuer, 2-9 promotion + output (two
+// warps per TMEM lane quarter, each owning half of the token columns; one
+// TMEM wait per unit, the weight scale loaded one unit ahead).  Every
+// mbarrier wait is bounded and reports a status word.
 #include <cstdlib>
 #include <mutex>
 
@@ -49,7 +50,7 @@ namespace {
 constexpr int kQBM = 128;              // weight rows per tile = one weight-scale block
 constexpr int kQBK = 128;              // K per work unit = one scale block
 constexpr int kQWBytes = kQBM * kQBK;  // 16 KB of E4M3 per unit
-constexpr int kQThreads = 192;
+constexpr int kQThreads = 320;   // producer, MMA, 8 promotion / output warps
 constexpr int kQBufs = 4;              // TMEM accumulators
 
 template <int MP>  // padded token count: the MMA's N (32 or 64)
@@ -94,6 +95,39 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+// 32 lanes x N consecutive fp32 TMEM columns (N = 16 or 32) into r[] WITHOUT
+// waiting: the caller waits once (tcgen05.wait::ld) and then calls regs_ready
+template <int N>
+__device__ __forceinline__ void tmem_ld_nowait(uint32_t taddr, uint32_t* r) {
+  if constexpr (N == 32) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+  } else {
+    static_assert(N == 16, "tmem_ld_nowait: 16 or 32 columns");
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+  }
+}
+
+// Ties registers written by an asynchronous tcgen05.ld to the wait before
+// this call: the empty asm "rewrites" them, so no use moves above the wait.
+template <int N>
+__device__ __forceinline__ void regs_ready(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; i += 8)
+    asm volatile("" : "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]), "+r"(r[i + 5]),
+                 "+r"(r[i + 6]), "+r"(r[i + 7]));
 }
 
 __device__ __forceinline__ int64_t owner(int64_t x, int64_t U, int64_t G) { return ((x + 1) * G - 1) / U; }
@@ -152,11 +186,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + 4);  // the MMA commit + the four promotion warps (scale row read)
+      mbar_init(&empty[s], 1 + 8);  // the MMA commit + the eight promotion warps (scale row read)
     }
     for (int b = 0; b < kQBufs; ++b) {
       mbar_init(&kfull[b], 1);
-      mbar_init(&kempty[b], 4);
+      mbar_init(&kempty[b], 8);
     }
     *err = kErrNone;
     fence_barrier_init();
@@ -217,17 +251,25 @@ __global__ void __launch_bounds__(kQThreads, 1)
       }
     }
   } else {
-    // ---- promotion + output: warp q owns TMEM lanes [32 q, 32 q + 32)
-    const int q = warp & 3;
+    // ---- promotion + output: 8 warps, two per TMEM lane quarter; warp w owns
+    // weight rows [32 (w % 4), +32) of the tile and token columns
+    // [hf MP/2, (hf + 1) MP/2)
+    constexpr int HM = MP / 2;
+    const int q = warp & 3, hf = (warp - 2) >> 2;
+    const int m0 = hf * HM;
     pdl_wait();  // before the first global write
-    float acc[MP];
+    float acc[HM];
 #pragma unroll
-    for (int j = 0; j < MP; ++j) acc[j] = 0.f;
+    for (int j = 0; j < HM; ++j) acc[j] = 0.f;
+    // sw is [tiles, kblocks] contiguous, so unit u's weight scale is sw[u];
+    // it is loaded one unit ahead
+    float s_w = __ldg(sw + u0);
     for (int i = 0; i < nu; ++i) {
       const int64_t u = u0 + i;
       const int64_t tile = u / kblocks;
       const int kb = (int)(u % kblocks);
       const int s = i % NS, b = i % kQBufs;
+      const float s_w_next = i + 1 < nu ? __ldg(sw + u + 1) : 0.f;
       // kfull: this unit's accumulator is in TMEM (so its stage has landed too);
       // full[s]: the same completed phase, which acquires the TMA-written scale
       // row for these threads (the stage cannot be refilled before they release it)
@@ -235,77 +277,77 @@ __global__ void __launch_bounds__(kQThreads, 1)
                                        mbar_wait(&full[s], (i / NS) & 1, err, kErrEpilogue)))
         break;
       tc_fence_after();
-      const float s_w = __ldg(sw + tile * kblocks + kb);
-      const float4* sx4 = reinterpret_cast<const float4*>(smem + s * C::kStageStride + kQWBytes + C::kXBytes);
-#pragma unroll
-      for (int c = 0; c < MP; c += 32) {
-        float v[32];
-        tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + b * MP + c, v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 f = sx4[c / 4 + j];
-          acc[c + 4 * j] += v[4 * j] * (f.x * s_w);
-          acc[c + 4 * j + 1] += v[4 * j + 1] * (f.y * s_w);
-          acc[c + 4 * j + 2] += v[4 * j + 2] * (f.z * s_w);
-          acc[c + 4 * j + 3] += v[4 * j + 3] * (f.w * s_w);
-        }
-      }
+      uint32_t r[HM];
+      tmem_ld_nowait<HM>(tmem + ((uint32_t)(q * 32) << 16) + b * MP + m0, r);
+      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+      regs_ready<HM>(r);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&kempty[b]);
-        mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&kempty[b]);   // the accumulator is in registers
+      const float4* sx4 = reinterpret_cast<const float4*>(smem + s * C::kStageStride + kQWBytes + C::kXBytes) + m0 / 4;
+#pragma unroll
+      for (int j = 0; j < HM / 4; ++j) {
+        const float4 f = sx4[j];
+        acc[4 * j] += __uint_as_float(r[4 * j]) * (f.x * s_w);
+        acc[4 * j + 1] += __uint_as_float(r[4 * j + 1]) * (f.y * s_w);
+        acc[4 * j + 2] += __uint_as_float(r[4 * j + 2]) * (f.z * s_w);
+        acc[4 * j + 3] += __uint_as_float(r[4 * j + 3]) * (f.w * s_w);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);    // scale row read
+      s_w = s_w_next;
       if (kb != kblocks - 1 && i != nu - 1) continue;
       // ---- end of this CTA's segment of `tile`.  The accumulators go to this
       // thread's own column of the staging buffer, so the global stores below
-      // run in rolled loops (one running address instead of MP of them).
+      // run in rolled loops (one running address instead of HM of them).
       const int n = (int)tile * kQBM + q * 32 + lane;
       float* stc = stage + q * 32 + lane;
 #pragma unroll
-      for (int mm = 0; mm < MP; ++mm) stc[mm * kQBM] = acc[mm];
+      for (int mm = 0; mm < HM; ++mm) stc[(m0 + mm) * kQBM] = acc[mm];
+      const int mend = min(M, m0 + HM);
       const int64_t tstart = tile * kblocks, tend = tstart + kblocks;
       const int64_t first_c = owner(tstart, U, G), last_c = owner(tend - 1, U, G);
       if (first_c == last_c) {
         if (n < N) {
-          __nv_bfloat16* yp = Y + n;
+          __nv_bfloat16* yp = Y + (int64_t)m0 * N + n;
 #pragma unroll 4
-          for (int mm = 0; mm < M; ++mm, yp += N) *yp = __float2bfloat16(stc[mm * kQBM]);
+          for (int mm = m0; mm < mend; ++mm, yp += N) *yp = __float2bfloat16(stc[mm * kQBM]);
         }
       } else {
         if (n < N) {
-          float* wp = ws + n;
+          float* wp = ws + (int64_t)m0 * N + n;
 #pragma unroll 4
-          for (int mm = 0; mm < M; ++mm, wp += N) atomicAdd(wp, stc[mm * kQBM]);
+          for (int mm = m0; mm < mend; ++mm, wp += N) atomicAdd(wp, stc[mm * kQBM]);
         }
         __threadfence();
         __syncwarp();
+        int* ctr = &cnt[tile * 8 + q * 2 + hf];   // one counter per (lane quarter, column half)
         int lastw = 0;
-        if (lane == 0) lastw = atomicAdd(&cnt[tile * 4 + q], 1) == (int)(last_c - first_c);
+        if (lane == 0) lastw = atomicAdd(ctr, 1) == (int)(last_c - first_c);
         lastw = __shfl_sync(0xffffffffu, lastw, 0);
         if (lastw) {
           __threadfence();
           if (n < N) {
-            float* wp = ws + n;
-            __nv_bfloat16* yp = Y + n;
-            for (int m0 = 0; m0 < M; m0 += 8, wp += 8 * (int64_t)N, yp += 8 * (int64_t)N) {
+            float* wp = ws + (int64_t)m0 * N + n;
+            __nv_bfloat16* yp = Y + (int64_t)m0 * N + n;
+            for (int mb = m0; mb < mend; mb += 8, wp += 8 * (int64_t)N, yp += 8 * (int64_t)N) {
               float t[8];  // eight independent loads in flight, then the stores
 #pragma unroll
-              for (int j = 0; j < 8; ++j) t[j] = m0 + j < M ? __ldcg(wp + (int64_t)j * N) : 0.f;
+              for (int j = 0; j < 8; ++j) t[j] = mb + j < mend ? __ldcg(wp + (int64_t)j * N) : 0.f;
 #pragma unroll
               for (int j = 0; j < 8; ++j)
-                if (m0 + j < M) {
+                if (mb + j < mend) {
                   yp[(int64_t)j * N] = __float2bfloat16(t[j]);
                   __stcg(wp + (int64_t)j * N, 0.f);
                 }
             }
           }
           __syncwarp();
-          if (lane == 0) cnt[tile * 4 + q] = 0;
+          if (lane == 0) *ctr = 0;
         }
       }
 #pragma unroll
-      for (int j = 0; j < MP; ++j) acc[j] = 0.f;
+      for (int j = 0; j < HM; ++j) acc[j] = 0.f;
     }
   }
   __syncthreads();
@@ -455,7 +497,7 @@ torch::Tensor skinny_fp8(torch::Tensor x, torch::Tensor qw, torch::Tensor sw, in
   const int mp = M <= 32 ? 32 : 64;
   // Xq [mp rows x K] then its scales [kblocks x mp], 256-byte aligned
   const int64_t xq_part = (mp * K + 255) / 256 * 256;
-  QWorkspace& ws = qf8_workspace(N * M, tiles * 4, xq_part + kblocks * mp * 4);
+  QWorkspace& ws = qf8_workspace(N * M, tiles * 8, xq_part + kblocks * mp * 4);
   auto* xq = reinterpret_cast<__nv_fp8_e4m3*>(ws.xq);
   float* sT = reinterpret_cast<float*>(ws.xq + xq_part);
   {

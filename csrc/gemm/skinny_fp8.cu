@@ -163,7 +163,8 @@ template <int MP>
 __global__ void __launch_bounds__(kQThreads, 1)
     skinny_fp8_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                       const float* __restrict__ sT, const float* __restrict__ sw, __nv_bfloat16* __restrict__ Y,
-                      float* __restrict__ ws, int* __restrict__ cnt, int M, int N, int K, int* err_out) {
+                      float* __restrict__ ws, int* __restrict__ cnt, int M, int N, int K, int flags,
+                      int* err_out) {
   using C = QCfg<MP>;
   constexpr int NS = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -244,8 +245,10 @@ __global__ void __launch_bounds__(kQThreads, 1)
         const uint8_t* st = smem + s * C::kStageStride;
         const uint64_t ad = sw128_kmajor_desc(smem_addr(st));
         const uint64_t bd = sw128_kmajor_desc(smem_addr(st + kQWBytes));
+        if (!(flags & 2)) {  // probe bit 1: no MMAs (only the commits)
 #pragma unroll
-        for (int k = 0; k < kQBK / 32; ++k) umma_e4m3(tmem + b * MP, ad + 2 * k, bd + 2 * k, idesc, k != 0);
+          for (int k = 0; k < kQBK / 32; ++k) umma_e4m3(tmem + b * MP, ad + 2 * k, bd + 2 * k, idesc, k != 0);
+        }
         umma_commit(&empty[s]);
         umma_commit(&kfull[b]);
       }
@@ -278,8 +281,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
         break;
       tc_fence_after();
       uint32_t r[HM];
-      tmem_ld_nowait<HM>(tmem + ((uint32_t)(q * 32) << 16) + b * MP + m0, r);
-      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+      if (!(flags & 1)) {  // probe bit 0: no TMEM read (the promotion adds zeros)
+        tmem_ld_nowait<HM>(tmem + ((uint32_t)(q * 32) << 16) + b * MP + m0, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+      } else {
+#pragma unroll
+        for (int j = 0; j < HM; ++j) r[j] = 0u;
+      }
       regs_ready<HM>(r);
       tc_fence_before();
       __syncwarp();
@@ -455,7 +463,14 @@ void launch_qf8(const CUtensorMap& mw, const CUtensorMap& mx, const float* sT, c
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mw, mx, sT, sw, y, w.ws, w.cnt, M, N, K, qf8_err_word()));
+  // probe knob for same-box experiments: LRL_FP8_SK_FLAGS bit 0 = no TMEM
+  // read in the promotion, bit 1 = no MMAs (results are then wrong)
+  static const int env_flags = [] {
+    const char* e = std::getenv("LRL_FP8_SK_FLAGS");
+    return e ? std::atoi(e) : 0;
+  }();
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mw, mx, sT, sw, y, w.ws, w.cnt, M, N, K, env_flags,
+                                    qf8_err_word()));
 }
 
 }  // namespace

@@ -145,7 +145,9 @@ class ShardedParamActorEngine(ActorEngine):
     def __init__(self, args: ModelArgs, state: ParallelState, *, lr: float = 1e-6, betas=(0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 0.01, max_grad_norm: float = 1.0, seed: int = 0,
                  dtype: Optional[torch.dtype] = None, total_steps: int = 1000, warmup_steps: int = 0,
-                 lr_style: str = "constant", min_lr_ratio: float = 0.0) -> None:
+                 lr_style: str = "constant", min_lr_ratio: float = 0.0, gradient_checkpointing=None) -> None:
+        # gradient_checkpointing is accepted for ActorEngine's signature: every
+        # layer is recomputed here anyway
         if state.cp_size > 1:
             raise ValueError("parameter sharding is not combined with context parallelism")
         self.args, self.state, self.device = args, state, state.device
@@ -314,14 +316,23 @@ class ShardedParamActorEngine(ActorEngine):
 
     # ------------------------------------------------------------------ whole model
     @torch.no_grad()
-    def full_flat(self) -> Tensor:
+    def full_flat(self, numel: Optional[int] = None) -> Tensor:
         """The whole bf16 model in ``Qwen3Model``'s flat layout (a transient
-        buffer): for weight pushes to rollout GPUs and exports."""
+        buffer, zero-padded to ``numel``): for weight pushes to rollout GPUs
+        and exports.  Collective over the data-parallel group."""
         layout = FlatLayout(param_specs(self.args))
-        flat = torch.zeros(layout.numel, dtype=self.dtype, device=self.device)
+        flat = torch.zeros(max(layout.numel, numel or 0), dtype=self.dtype, device=self.device)
         tmp = torch.empty(max(u.numel for u in self.units), dtype=self.dtype, device=self.device)
         for u in self.units:
             full = self._gather(u, tmp)
             for n, (o, shape) in u.entries.items():
                 layout.view(flat, n).copy_(full[o: o + math.prod(shape)].view(shape))
         return flat
+
+
+def wants_param_sharding(config) -> bool:
+    """``policy.training.fsdp_cfg.reshard_after_forward``: FSDP2's full
+    sharding, i.e. this engine (where the trainer's weights are not also the
+    colocated rollout's)."""
+    fc = getattr(getattr(getattr(config, "policy", None), "training", None), "fsdp_cfg", None) or {}
+    return bool(fc.get("reshard_after_forward", False)) if isinstance(fc, dict) else False

@@ -114,7 +114,11 @@ class RLTrainer:
         self.algo_cfg = getattr(c.algorithm, algo)
         self.group = int(getattr(self.algo_cfg, "num_generations", 1) or 1)
         p = c.policy
-        self.actor = ActorEngine(
+        engine_cls = ActorEngine
+        if self._shard_params():
+            from lumenrl_b200.engine.training.fsdp import ShardedParamActorEngine
+            engine_cls = ShardedParamActorEngine
+        self.actor = engine_cls(
             self.model_args, st, lr=p.learning_rate, betas=(p.adam_beta1, p.adam_beta2), eps=p.adam_eps,
             weight_decay=p.weight_decay, max_grad_norm=p.max_grad_norm, seed=c.seed,
             gradient_checkpointing=self.spec.gradient_checkpointing, total_steps=c.num_training_steps,
@@ -135,7 +139,7 @@ class RLTrainer:
                                              c.algorithm.kl_horizon)
         if kl_coeff > 0 or self.kl_ctrl is not None:
             self.ref = ActorEngine(self.model_args, st, seed=c.seed, trainable=False, init=False)
-            self.ref.model.flat.copy_(self.actor.model.flat)
+            self.ref.model.flat.copy_(self._actor_flat(self.ref.model.flat.numel()))
         self.critic = None
         if algo == "ppo" or c.algorithm.adv_estimator == "gae" or c.critic.enabled:
             from lumenrl_b200.engine.training.critic import CriticEngine
@@ -145,6 +149,18 @@ class RLTrainer:
                                        gradient_checkpointing=self.spec.gradient_checkpointing,
                                        total_steps=c.num_training_steps)
         self._setup_common()
+
+    def _shard_params(self) -> bool:
+        """Colocated: the trainer's resident weights are the rollout engine's,
+        so they are never sharded (see ``ShardedParamActorEngine``)."""
+        return False
+
+    def _actor_flat(self, numel: Optional[int] = None) -> torch.Tensor:
+        """The actor's whole bf16 model as one flat buffer (assembled from the
+        shards when the weights are sharded)."""
+        if self.actor.model.flat is not None:
+            return self.actor.model.flat
+        return self.actor.full_flat(numel)
 
     def _setup_common(self) -> None:
         c, st = self.config, self.state
@@ -374,8 +390,9 @@ class RLTrainer:
         sync_s = all_reduce_max(float(tm.get("timing/opt_bcast_s", 0.0)) + times["weight_sync"])
         m["timing/weight_sync_s"] = sync_s
         m["weight_sync/ms"] = sync_s * 1e3
-        m["weight_sync/GBps"] = self.actor.model.flat.numel() * self.actor.model.flat.element_size() / max(
-            sync_s, 1e-9) / 1e9
+        wbytes = sum(p.numel() for _, p in self.actor.model.named_flat_params()) * (
+            2 if self.actor.model.p("embed").dtype == torch.bfloat16 else 4)
+        m["weight_sync/GBps"] = wbytes / max(sync_s, 1e-9) / 1e9
         for k in ("prefill_ms", "setup_ms", "decode_ms"):
             if k in batch.meta.get("gen_stats", {}):
                 m[f"timing/gen_{k}"] = batch.meta["gen_stats"][k]

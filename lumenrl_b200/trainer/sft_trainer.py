@@ -25,7 +25,11 @@ class SFTTrainer:
     def __init__(self, config, model_args: ModelArgs, state: ParallelState) -> None:
         p = config.policy
         self.config = config
-        self.engine = ActorEngine(model_args, state, lr=p.learning_rate, weight_decay=p.weight_decay,
+        from lumenrl_b200.engine.training.fsdp import ShardedParamActorEngine, wants_param_sharding
+        # SFT has no rollout engine sharing the weights, so FSDP2-style full
+        # sharding (policy.training.fsdp_cfg.reshard_after_forward) is honoured
+        engine_cls = ShardedParamActorEngine if wants_param_sharding(config) else ActorEngine
+        self.engine = engine_cls(model_args, state, lr=p.learning_rate, weight_decay=p.weight_decay,
                                   max_grad_norm=p.max_grad_norm, seed=config.seed,
                                   total_steps=config.num_training_steps, warmup_steps=p.lr_warmup_steps,
                                   lr_style=p.lr_decay_style)

@@ -88,3 +88,31 @@ def test_sharded_params_match_unsharded_engine():
         # Adam's first step is ~lr * sign(g): weights whose gradient is at the
         # rounding level may differ by a fraction of one step, no more
         assert float((res[r]["w1"][:n] - ref.model.flat[:n]).abs().max()) < 0.1 * moved
+
+
+def test_sft_with_fsdp_cfg_uses_sharded_engine_and_matches():
+    """policy.training.fsdp_cfg.reshard_after_forward selects the sharded engine
+    in SFT; two steps give the losses of the resident-weight engine."""
+    from lumenrl_b200.core.config import LumenRLConfig
+    from lumenrl_b200.core.protocol import DataProto
+    from lumenrl_b200.engine.training.fsdp import ShardedParamActorEngine
+    from lumenrl_b200.models.config import tiny_llama
+    from lumenrl_b200.parallel.dist import ParallelState
+    from lumenrl_b200.trainer.sft_trainer import SFTTrainer
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    b = DataProto({"prompt_ids": torch.randint(3, 2048, (4, 8), generator=torch.Generator().manual_seed(0)),
+                   "prompt_lengths": torch.full((4,), 8),
+                   "responses": torch.randint(3, 2048, (4, 6), generator=torch.Generator().manual_seed(1)),
+                   "response_lengths": torch.tensor([6, 5, 4, 6]),
+                   "response_mask": (torch.arange(6).unsqueeze(0) < torch.tensor([6, 5, 4, 6]).unsqueeze(1)).float()})
+    losses = {}
+    for shard in (False, True):
+        cfg = LumenRLConfig.from_yaml(os.path.join(here, "configs", "grpo_tiny_cpu.yaml"),
+                                      ["policy.learning_rate=1e-3"])
+        if shard:
+            cfg.policy.training.fsdp_cfg = {"reshard_after_forward": True}
+        sft = SFTTrainer(cfg, tiny_llama(), ParallelState())
+        assert isinstance(sft.engine, ShardedParamActorEngine) == shard
+        losses[shard] = [sft.step(b)["sft/loss"] for _ in range(2)]
+    for a, c in zip(losses[False], losses[True]):
+        assert abs(a - c) < 1e-5 * max(1.0, abs(a)), losses

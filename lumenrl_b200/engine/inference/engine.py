@@ -109,6 +109,10 @@ class RolloutEngine:
                 if fp8_rollout is not None and fp8_rollout.is_fp8_enabled():
                     raise ValueError("rollout TP with FP8 rollout weights is not supported: use TP=1 per GPU")
         self.tp = tp
+        if tp is not None:
+            # no collective inside a captured decode graph: under TP the decode
+            # step runs eagerly (its all-reduces are ordinary NCCL calls)
+            self.use_cuda_graph = False
         kv_heads = tp.num_kv_heads if tp is not None else self.args.num_kv_heads
         spec = KVSpec(self.args.num_layers, kv_heads, self.args.head_dim, block_size, kv_dtype)
         self.max_blocks_per_seq = math.ceil(max_model_len / block_size) + 1

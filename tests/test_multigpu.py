@@ -531,3 +531,121 @@ def test_context_parallel_actor_scoring_on_gpus():
     for rank, err in res:
         assert isinstance(err, float), (rank, err)
         assert err < 5e-2, (rank, err)     # bf16 logits, log-prob difference in nats
+
+
+def _sharded_engine_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from lumenrl_b200.core.config import GRPOConfig
+        from lumenrl_b200.core.protocol import DataProto
+        from lumenrl_b200.engine.training.actor import ActorEngine
+        from lumenrl_b200.engine.training.fsdp import ShardedParamActorEngine
+        from lumenrl_b200.models.config import tiny_qwen3
+        from lumenrl_b200.parallel.dist import ParallelState
+        dev = torch.device("cuda", rank)
+        g = torch.Generator().manual_seed(rank)
+        B, P, R = 4, 40, 24
+        rlen = torch.randint(8, R + 1, (B,), generator=g)
+        b = DataProto({"prompt_ids": torch.randint(3, 2048, (B, P), generator=g), "prompt_lengths": torch.full((B,), P),
+                       "responses": torch.randint(3, 2048, (B, R), generator=g), "response_lengths": rlen,
+                       "response_mask": (torch.arange(R).unsqueeze(0) < rlen.unsqueeze(1)).float(),
+                       "old_log_probs": -torch.rand(B, R, generator=g) * 8,
+                       "advantages": torch.randn(B, generator=g)}).to(dev)
+        sh = ShardedParamActorEngine(tiny_qwen3(), ParallelState(world_size=world, rank=rank, device=dev),
+                                     lr=1e-3, seed=3)
+        # the resident-weight engine on the same two ranks (plain NCCL collectives)
+        ref = ActorEngine(tiny_qwen3(), ParallelState(world_size=world, rank=rank, device=dev), lr=1e-3, seed=3,
+                          fused_comm=False)
+        n = ref.model.layout.numel
+        w_eq = bool(torch.equal(sh.full_flat()[:n], ref.model.flat[:n]))
+        lp_s, _ = sh.compute_log_probs(b)
+        lp_r, _ = ref.compute_log_probs(b)
+        m = b.tensors["response_mask"] > 0
+        lp_err = float((lp_s - lp_r)[m].abs().max())
+        gs = sh.update_policy(b, GRPOConfig(), "grpo", rows_per_micro=2)["actor/grad_norm"]
+        gr = ref.update_policy(b, GRPOConfig(), "grpo", rows_per_micro=2)["actor/grad_norm"]
+        w1 = sh.full_flat()[:n].float()
+        dw = float((w1 - ref.model.flat[:n].float()).abs().max())
+        q.put((rank, {"w_eq": w_eq, "lp_err": lp_err, "gs": gs, "gr": gr, "dw": dw}))
+    except Exception as e:
+        import traceback
+        q.put((rank, {"error": traceback.format_exc()[-2000:] + repr(e)}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_param_engine_matches_resident_on_gpus():
+    """Parameter-sharded engine (NCCL gathers / reduce-scatters) against the
+    resident-weight engine on the same 2 GPUs: equal weights, equal scores,
+    the same gradient norm and an update within bf16 rounding."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28300 + os.getpid() % 150
+    procs = [ctx.Process(target=_sharded_engine_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert "error" not in v, v["error"]
+        assert v["w_eq"], r
+        assert v["lp_err"] < 2e-2, (r, v)
+        assert abs(v["gs"] - v["gr"]) < 2e-2 * v["gr"], (r, v)
+        assert v["dw"] < 5e-3, (r, v)        # lr 1e-3: one Adam step moves weights by ~1e-3
+
+
+def _rollout_tp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from lumenrl_b200.engine.inference.engine import RolloutEngine, SamplingParams
+        from lumenrl_b200.models.config import tiny_qwen3
+        from lumenrl_b200.models.qwen3 import Qwen3Model
+        dev = torch.device("cuda", rank)
+        m = Qwen3Model(tiny_qwen3(), device=dev, dtype=torch.bfloat16, requires_grad=False)
+        m.init_weights(5)
+        sp = SamplingParams(max_new_tokens=24, n=4, seed=3, stop_at_eos=False)
+        prompts = [[5 + i for i in range(70)], [11 + i for i in range(33)]]
+        tp = RolloutEngine(m, max_num_seqs=8, max_model_len=160, tp_group=dist.group.WORLD)
+        assert not tp.use_cuda_graph          # TP decode runs eagerly
+        out = tp.generate(prompts, sp)
+        one = RolloutEngine(m, max_num_seqs=8, max_model_len=160, use_cuda_graph=True).generate(prompts, sp)
+        toks = out.responses.cpu()
+        both = [torch.zeros_like(toks) for _ in range(world)]
+        dist.all_gather(both, out.responses)
+        q.put((rank, {"ranks_agree": all(torch.equal(both[0].cpu(), t.cpu()) for t in both),
+                      "same_as_tp1": float((toks == one.responses.cpu()).float().mean()),
+                      "lp_gap": float((out.logprobs - one.logprobs).abs()[:, :1].max())}))
+    except Exception as e:
+        import traceback
+        q.put((rank, {"error": traceback.format_exc()[-2000:] + repr(e)}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_rollout_tp2_on_gpus():
+    """TP=2 rollout on 2 GPUs (eager decode step, NCCL all-reduces): both ranks
+    draw the same samples, which agree with one GPU's up to bf16
+    reduction-order ties."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28450 + os.getpid() % 150
+    procs = [ctx.Process(target=_rollout_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert "error" not in v, v["error"]
+        assert v["ranks_agree"], r
+        assert v["same_as_tp1"] > 0.8, (r, v)
+        assert v["lp_gap"] < 5e-2, (r, v)

@@ -553,6 +553,10 @@ def bench_comm(ns) -> dict:
         fused.comm.fused_step(fused.lo, fused.shard, fused.master, fused.grad_shard, fused.m, fused.v, 1e-6,
                               fused.betas, fused.eps, fused.wd, 1, 1.0)
     t_f = _time(fstep, ns.steps, ns.warmup)
+    fstep()
+    split = dict(comm.last_timing)          # device time of the two kernels of one step
+    sp = torch.tensor([split.get("opt_rs_s", 0.0), split.get("opt_bcast_s", 0.0)], device="cuda",
+                      dtype=torch.float64)
     del fused
     plain_w = torch.zeros(n, dtype=torch.bfloat16, device="cuda")
     plain = ShardedFlatAdamW(plain_w, W, r, lr=1e-6)
@@ -568,16 +572,61 @@ def bench_comm(ns) -> dict:
     t_p = _time(pstep, ns.steps, ns.warmup)
     t = torch.tensor([t_f, t_p], device="cuda", dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(sp, op=dist.ReduceOp.MAX)
+    nvls = comm.nvls
     comm.close()
     grad_bytes, w_bytes = n * 4, n * 2
-    return {"op": "optimizer_collective", "world": W, "numel": n, "fused_ms": float(t[0]), "nccl_ms": float(t[1]),
-            "nvlink_bytes_per_gpu": (W - 1) / W * (grad_bytes + w_bytes)}
+    rs_link = (W - 1) / W * grad_bytes       # fp32 gradients a rank pulls from its peers
+    ag_link = (W - 1) / W * w_bytes          # bf16 weights a rank pushes to its peers
+    return {"op": "optimizer_collective", "world": W, "numel": n, "nvls": nvls, "fused_ms": float(t[0]),
+            "nccl_ms": float(t[1]), "rs_norm_ms": float(sp[0]) * 1e3, "adamw_ag_ms": float(sp[1]) * 1e3,
+            "rs_link_GBps": rs_link / max(float(sp[0]), 1e-12) / 1e9,
+            "ag_link_GBps": ag_link / max(float(sp[1]), 1e-12) / 1e9,
+            "nvlink_bytes_per_gpu": rs_link + ag_link}
+
+
+def bench_allreduce(ns) -> dict:
+    """Replicated-DP gradient all-reduce (launch under torchrun): this
+    package's NVLink kernel (peer two-shot; NVLS with LRL_NVLS=1) against
+    NCCL ``all_reduce`` on an fp32 buffer of --numel elements already in the
+    symmetric staging buffer (so only the collective is timed).  Bus bytes per
+    GPU = 2 (W-1)/W x size, the all-reduce convention."""
+    import torch.distributed as dist
+    from lumenrl_b200.ops.ext import ext
+    from lumenrl_b200.parallel.dist import init_distributed
+    from lumenrl_b200.parallel.symm import NVLinkAllReduce
+    st = init_distributed()
+    W, r = st.world_size, st.rank
+    n = ns.numel // 4 * 4
+    comm = NVLinkAllReduce(n, r, W)
+    buf = comm.buf.tensor[:n]
+    buf.normal_()
+
+    def own():
+        comm.epoch += 1
+        if comm.nvls:
+            ext().nvlink_allreduce_mc(comm.buf.mc, comm.signals.ptrs, r, n, 1.0, comm.epoch, comm.status,
+                                      comm.wait_cycles)
+        else:
+            ext().nvlink_allreduce(comm.buf.ptrs, comm.signals.ptrs, r, n, 1.0, comm.epoch, comm.status,
+                                   comm.wait_cycles)
+    x = torch.randn(n, device="cuda")
+    t_own = _time(own, ns.steps, ns.warmup)
+    comm.check()
+    t_nccl = _time(lambda: dist.all_reduce(x), ns.steps, ns.warmup)
+    t = torch.tensor([t_own, t_nccl], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    comm.close()
+    bus = 2 * (W - 1) / W * n * 4
+    return {"op": "allreduce_fp32", "world": W, "numel": n, "nvls": comm.nvls, "own_ms": float(t[0]),
+            "nccl_ms": float(t[1]), "own_busbw_GBps": bus / float(t[0]) / 1e6,
+            "nccl_busbw_GBps": bus / float(t[1]) / 1e6}
 
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["decode", "attn", "attn_train", "skinny", "train", "logprob", "gemm", "comm",
-                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy", "eagle", "fp8dgemm"])
+                                     "dgemm", "gemm2", "gemm2probe", "fp8gemm", "gemm2energy", "eagle", "fp8dgemm", "allreduce"])
     ap.add_argument("--blas", choices=["default", "cublas", "cublaslt"], default="default",
                     help="torch's preferred BLAS library for the library GEMMs")
     ap.add_argument("--group", type=int, default=8)
@@ -602,7 +651,7 @@ def main(argv=None) -> None:
     ns = ap.parse_args(argv)
     if ns.blas != "default":
         torch.backends.cuda.preferred_blas_library(ns.blas)
-    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "fp8dgemm": bench_fp8dgemm, "eagle": bench_eagle, "gemm2energy": bench_gemm2energy,
+    fn = {"decode": bench_decode, "attn": bench_attn, "skinny": bench_skinny, "attn_train": bench_attn_train, "train": bench_train, "dgemm": bench_dgemm, "logprob": bench_logprob, "gemm": bench_gemm, "fp8gemm": bench_fp8gemm, "fp8dgemm": bench_fp8dgemm, "allreduce": bench_allreduce, "eagle": bench_eagle, "gemm2energy": bench_gemm2energy,
           "comm": bench_comm, "gemm2": bench_gemm2,
           "gemm2probe": bench_gemm2probe}[ns.what]
     res = fn(ns)

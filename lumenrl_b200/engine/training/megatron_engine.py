@@ -90,14 +90,46 @@ class _Stage:
     def loss(self, mb: MicroBatch, x: Tensor) -> Tensor:
         e = self.e
         h = ops.rmsnorm(x, e.norm, e.args.rms_norm_eps)
+        if e.vocab_parallel:
+            # vocabulary-parallel LM head: every TP rank scores all tokens of the
+            # micro-batch against its slice of the vocabulary; the value returned
+            # is this rank's token share (so the TP sum is the loss) while the
+            # gradient is that of the full loss, which every rank needs for the
+            # vocabulary-parallel backward
+            from lumenrl_b200.parallel.vocab_parallel import vocab_parallel_token_logprob
+            hf = _GatherTokens.apply(h, e.tpc)
+            logp, _ = vocab_parallel_token_logprob(hf, e.lm_head, mb.targets, e.vocab_start, group=e.g["tp"])
+            full = -(logp * mb.weights).sum()
+            local = -(self._local(logp) * self._local(mb.weights)).sum()
+            return local.detach() + (full - full.detach())
         logp, _ = ops.token_logprob(h, e.lm_head, self._local(mb.targets), want_entropy=False)
         return -(logp * self._local(mb.weights)).sum()
+
+
+class _GatherTokens(torch.autograd.Function):
+    """All-gather of the sequence-parallel token shards; the backward takes
+    this rank's rows of a gradient that is already the same on every rank
+    (the vocabulary-parallel backward sums it over the group)."""
+
+    @staticmethod
+    def forward(ctx, x, tpc):
+        ctx.tpc = tpc
+        return tpc.all_gather(x) if tpc.world > 1 else x
+
+    @staticmethod
+    def backward(ctx, dy):
+        tpc = ctx.tpc
+        n = dy.shape[0] // tpc.world
+        return dy[tpc.rank * n:(tpc.rank + 1) * n].contiguous(), None
 
 
 class MegatronEngine:
     def __init__(self, args, tp: int = 1, pp: int = 1, device: Optional[torch.device] = None,
                  dtype: torch.dtype = torch.float32, seed: int = 0, lr: float = 1e-4, fused: Optional[bool] = None,
-                 groups: Optional[dict] = None) -> None:
+                 groups: Optional[dict] = None, vocab_parallel: bool = False) -> None:
+        """``vocab_parallel``: the LM head is split by rows over the TP group
+        (Megatron's vocabulary-parallel output layer; untied embeddings) and
+        the token log-probs come from ``parallel.vocab_parallel``."""
         if args.num_experts:
             raise ValueError("MegatronEngine covers dense decoders; MoE layers use parallel.expert_parallel")
         self.args = args
@@ -119,8 +151,18 @@ class MegatronEngine:
         first, last = self.g["stage"] == 0, self.g["stage"] == self.g["pp_size"] - 1
         self.embed = P(full.p("embed")) if first or (last and args.tie_word_embeddings) else None
         self.norm = P(full.p("norm")) if self.g["stage"] == self.g["pp_size"] - 1 else None
+        self.vocab_parallel = bool(vocab_parallel) and self.g["tp_size"] > 1
+        self.vocab_start = 0
+        if self.vocab_parallel and args.tie_word_embeddings:
+            raise ValueError("vocab_parallel needs untied embeddings (the embedding is not split by vocabulary)")
         if self.g["stage"] == self.g["pp_size"] - 1:
-            self.lm_head = self.embed if args.tie_word_embeddings else P(full.lm_head)
+            if self.vocab_parallel:
+                from lumenrl_b200.parallel.vocab_parallel import vocab_slice
+                a, b = vocab_slice(args.vocab_size, self.g["t"], self.g["tp_size"])
+                self.vocab_start = a
+                self.lm_head = P(full.lm_head[a:b])
+            else:
+                self.lm_head = self.embed if args.tie_word_embeddings else P(full.lm_head)
         else:
             self.lm_head = None
         del full
@@ -140,7 +182,7 @@ class MegatronEngine:
         ps = []
         for layer in self.layers:
             ps += [layer.ln1, layer.ln2] + [p for p in (layer.q_norm, layer.k_norm) if p is not None]
-        for p in (self.embed, self.norm, self.lm_head):
+        for p in (self.embed, self.norm, None if self.vocab_parallel else self.lm_head):
             if p is not None and all(p is not q for q in ps):
                 ps.append(p)
         return ps

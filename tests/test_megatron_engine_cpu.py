@@ -24,18 +24,19 @@ def _batches(vocab, n_mb, seed=0):
     return out
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, vocab_parallel=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from lumenrl_b200.engine.training.megatron_engine import MegatronEngine
     from lumenrl_b200.models.config import tiny_qwen3
     from lumenrl_b200.parallel.tensor_parallel import shard_cols, shard_gate_up, shard_qkv
     args = tiny_qwen3(layers=4)
-    eng = MegatronEngine(args, tp=2, pp=2, seed=5)
+    eng = MegatronEngine(args, tp=2, pp=2, seed=5, vocab_parallel=vocab_parallel)
     loss = eng.forward_backward(_batches(args.vocab_size, 3))
     eng.sync_grads()
     g = eng.g
-    out = {"loss": loss, "stage": g["stage"], "t": g["t"], "lo": eng.layer_range[0], "grads": {}}
+    out = {"loss": loss, "stage": g["stage"], "t": g["t"], "lo": eng.layer_range[0], "grads": {},
+           "vocab": (eng.vocab_start, eng.vocab_start + (eng.lm_head.shape[0] if eng.lm_head is not None else 0))}
     for j, layer in enumerate(eng.layers):
         for name in ("wqkv", "wo", "w13", "w2", "ln1", "ln2", "q_norm", "k_norm"):
             out["grads"][f"{eng.layer_range[0] + j}.{name}"] = getattr(layer, name).grad.numpy().copy()
@@ -48,11 +49,16 @@ def _worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tp2_pp2_matches_single_process():
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("vocab_parallel", [False, True])
+def test_tp2_pp2_matches_single_process(vocab_parallel):
+    """vocab_parallel=True: the LM head split by rows over the TP group."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29100 + os.getpid() % 90
-    procs = [ctx.Process(target=_worker, args=(r, 4, port, q)) for r in range(4)]
+    port = 29100 + os.getpid() % 90 + (300 if vocab_parallel else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 4, port, q, vocab_parallel)) for r in range(4)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in procs)
@@ -86,6 +92,8 @@ def test_tp2_pp2_matches_single_process():
                     ref = shard[name](ref, out["t"])
             else:
                 ref = m.p(key).grad if key != "lm_head" else m.lm_head.grad
+                if key == "lm_head" and vocab_parallel:
+                    ref = ref[out["vocab"][0]: out["vocab"][1]]
             assert np.allclose(got, ref.numpy(), atol=2e-5, rtol=1e-4), (r, key, np.abs(got - ref.numpy()).max())
             seen.add(key)
     assert {f"{i}.wqkv" for i in range(4)} <= seen and {"embed", "norm", "lm_head"} <= seen

@@ -36,7 +36,7 @@ import torch
 from torch import Tensor
 
 from lumenrl_b200.engine.inference.kv_cache import KVSpec, PagedKVCache
-from lumenrl_b200.engine.inference.runner import DecodeGraph, ModelRunner
+from lumenrl_b200.engine.inference.runner import DecodeGraph, ModelRunner, RoutingRecorder
 from lumenrl_b200.models.qwen3 import Qwen3Model
 
 logger = logging.getLogger(__name__)
@@ -67,18 +67,6 @@ class GenerationOutput:
     stats: dict = field(default_factory=dict)
 
 
-class _RoutingRecorder:
-    def __init__(self, layers: list[int]) -> None:
-        self.layers = layers
-        self.buf: dict[int, Tensor] = {}
-
-    def record(self, layer: int, ids: Tensor) -> None:
-        self.buf[layer] = ids.to(torch.int16)
-
-    def take(self) -> Tensor:
-        return torch.stack([self.buf[l] for l in self.layers], dim=1)  # [B, layers, k]
-
-
 class RolloutEngine:
     def __init__(self, model: Qwen3Model, max_num_seqs: int = 64, max_model_len: int = 2048,
                  kv_cache_bytes: Optional[int] = None, block_size: int = 64, kv_dtype: torch.dtype = torch.bfloat16,
@@ -99,7 +87,11 @@ class RolloutEngine:
         self.pad_token_id = pad_token_id
         self.shared_prefix_attention = shared_prefix_attention
         self.continuous_batching = continuous_batching
-        self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda" and self.args.num_experts == 0
+        # MoE decode steps are captured too when their routing and expert GEMMs
+        # run on the device (no host read of the routes inside the step)
+        from lumenrl_b200.models.moe import moe_graph_ok
+        self.use_cuda_graph = (use_cuda_graph and self.device.type == "cuda"
+                               and (self.args.num_experts == 0 or moe_graph_ok(model)))
         tp = None
         if tp_group is not None:
             import torch.distributed as dist
@@ -418,7 +410,7 @@ class RolloutEngine:
         recorder = None
         moe_layers = [i for i in range(self.args.num_layers) if self.args.is_moe_layer(i)]
         if moe_layers:
-            recorder = _RoutingRecorder(moe_layers)
+            recorder = RoutingRecorder(moe_layers)
             self.runner.routing_recorder = recorder
         logits = self.runner.prefill(ids, pos, cu, int(lens.max()), slots)
         ev1 = self._ev()
@@ -478,7 +470,7 @@ class RolloutEngine:
             g.step.fill_(t)
             tok, lp = g.run()
             if recorder:
-                step_routes = recorder.take()
+                step_routes = g.recorder.take()     # the routes of the step just replayed
                 for r in range(B):
                     routes_rows[r].append(step_routes[r])
             out_tok[:, t] = tok

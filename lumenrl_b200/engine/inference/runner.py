@@ -195,6 +195,23 @@ class ModelRunner:
         return ops.decode_linear(h, self._lm_head())
 
 
+class RoutingRecorder:
+    """Expert ids chosen by every MoE layer in the last forward (rollout
+    routing replay, R3): ``record`` keeps the layer's id tensor as int16, so
+    inside a captured decode graph the recorded tensors are graph buffers
+    that every replay rewrites; ``take`` stacks them into a new tensor."""
+
+    def __init__(self, layers: list[int]) -> None:
+        self.layers = layers
+        self.buf: dict[int, Tensor] = {}
+
+    def record(self, layer: int, ids: Tensor) -> None:
+        self.buf[layer] = ids.to(torch.int16)
+
+    def take(self) -> Tensor:
+        return torch.stack([self.buf[l] for l in self.layers], dim=1)  # [B, layers, k]
+
+
 class DecodeGraph:
     """Static-shape decode step + sampling, captured into one CUDA graph.
 
@@ -218,6 +235,11 @@ class DecodeGraph:
         self.prefix_len = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.share = share
         self.temperature, self.top_p = temperature, top_p
+        # MoE models: this step's routes, recorded by the graph's own recorder
+        # (a recorder created per generate() call would not see a cached
+        # graph's replays)
+        moe_layers = [i for i in range(runner.args.num_layers) if runner.args.is_moe_layer(i)]
+        self.recorder = RoutingRecorder(moe_layers) if moe_layers else None
         self.out_tokens: Optional[Tensor] = None
         self.out_logp: Optional[Tensor] = None
         self.graph = None
@@ -230,7 +252,12 @@ class DecodeGraph:
         slots = blk * self.bs + pos % self.bs
         seq_lens = (pos + 1).to(torch.int32)
         shared = (self.prefix_len, *self.share) if self.share is not None else None
-        logits = self.runner.decode(self.tokens, pos, slots, self.block_table, seq_lens, shared)
+        prev = self.runner.routing_recorder
+        self.runner.routing_recorder = self.recorder if self.recorder is not None else prev
+        try:
+            logits = self.runner.decode(self.tokens, pos, slots, self.block_table, seq_lens, shared)
+        finally:
+            self.runner.routing_recorder = prev
         tok, lp = ops.sample_tokens_device(logits, self.temperature, self.top_p, self.row_seed, self.step)
         if self.out_tokens is None:
             self.out_tokens, self.out_logp = tok, lp

@@ -112,6 +112,25 @@ def _use_tc_grouped(h: Tensor, w13: Tensor, w2: Tensor) -> bool:
             and w13.shape[2] % 8 == 0 and w2.shape[2] % 8 == 0 and w13.shape[0] <= 512)
 
 
+def moe_graph_ok(model) -> bool:
+    """True when every MoE layer of ``model`` takes the device path (kernel
+    routing and the tcgen05 grouped GEMMs with device offsets), i.e. a decode
+    step makes no host read of the routes and can be captured in a graph."""
+    a = model.args
+    if not a.num_experts:
+        return True
+    if a.num_experts > 512 or a.num_experts_per_tok > 16:
+        return False
+    P = model._params
+    for i in range(a.num_layers):
+        if a.is_moe_layer(i):
+            w13, w2 = P[f"layers.{i}.experts_w13"], P[f"layers.{i}.experts_w2"]
+            probe = w13.new_empty(0)
+            if not _use_tc_grouped(probe, w13, w2):
+                return False
+    return True
+
+
 class _NullCtx:
     def save_for_backward(self, *a):
         pass

@@ -207,6 +207,121 @@ def _ring_exchange(tensors: list, group, rank: int, cp: int) -> list:
     return recv, reqs
 
 
+_FREE = 64          # signal words: [0, 64) ready flags of my slots, [64, 128) free flags of the next rank's slots
+_EPOCH_STRIDE = 8   # ready epochs of a slot's lap L are L*8 + 1 .. L*8 + K (K <= 8 tensors per exchange), so
+                    # they grow monotonically whatever K each exchange has (2 forward, 4 backward)
+
+
+def _r256(n: int) -> int:
+    return (n + 255) // 256 * 256
+
+
+class _NVLinkRing:
+    """Ring exchange over NVLink for the CP group (instead of NCCL send/recv).
+
+    Every rank owns ``nslots`` receive slots in a CUDA-IPC symmetric buffer.
+    ``exchange`` pushes this rank's tensors into the next rank's slot with
+    ``p2p_push`` (plain peer stores; push k of the slot's lap L publishes
+    epoch 8 L + k + 1 in the slot's ready flag, so the last push's epoch
+    implies all) on a side stream, so the transfer overlaps the caller's attention work, and
+    waits on the current stream for the previous rank's pushes into this
+    rank's slot.  ``release`` hands the slot back (stream-ordered after every
+    reader of it, including this rank's own push of its contents) by writing
+    the lap into the previous rank's free flag; a push waits for that flag
+    before reusing a slot.  Every wait is bounded and reports a status code
+    (``check`` raises ``CommTimeout``)."""
+
+    def __init__(self, group, slot_bytes: int, nslots: int = 2, wait_seconds: float = 10.0) -> None:
+        from lumenrl_b200.ops.ext import ext
+        from lumenrl_b200.parallel.symm import SymmetricBuffer
+        self.group = group
+        self.cp, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.nxt, self.prv = (self.rank + 1) % self.cp, (self.rank - 1) % self.cp
+        self.slot_bytes, self.nslots = _r256(slot_bytes), nslots
+        self._e = ext()
+        self.data = SymmetricBuffer(self.slot_bytes * nslots // 4, torch.int32, self.rank, self.cp, group)
+        self.sig = SymmetricBuffer(128, torch.int32, self.rank, self.cp, group)
+        dev = self.data.tensor.device
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.wait_cycles = int(wait_seconds * 2.0e9)
+        self.count = 0
+        self.side = torch.cuda.Stream(device=dev)
+        dist.barrier(group=group)
+
+    def exchange(self, tensors: list) -> tuple[list, tuple]:
+        e = self._e
+        i, K = self.count, len(tensors)
+        if K > _EPOCH_STRIDE:
+            raise ValueError("CP ring exchange: at most 8 tensors per exchange")
+        self.count += 1
+        slot, lap = i % self.nslots, i // self.nslots
+        base = slot * self.slot_bytes
+        tensors = [t.contiguous() for t in tensors]
+        main = torch.cuda.current_stream()
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            if lap > 0:   # the next rank has released this slot's previous contents
+                e.p2p_wait(self.sig.ptrs[self.rank] + 4 * (_FREE + slot), lap, self.status, 1, self.wait_cycles)
+            off = 0
+            for k, t in enumerate(tensors):
+                t.record_stream(self.side)
+                e.p2p_push(t.view(-1), self.data.ptrs[self.nxt] + base + off, self.sig.ptrs[self.nxt] + 4 * slot,
+                           lap * _EPOCH_STRIDE + k + 1, self.counter)
+                off += _r256(t.numel() * t.element_size())
+        # the previous rank's pushes into this rank's slot (the last one implies all)
+        e.p2p_wait(self.sig.ptrs[self.rank] + 4 * slot, lap * _EPOCH_STRIDE + K, self.status, 2, self.wait_cycles)
+        mem = self.data.tensor.view(torch.uint8)
+        out, off = [], 0
+        for t in tensors:
+            nb = t.numel() * t.element_size()
+            out.append(mem[base + off: base + off + nb].view(t.dtype).view(t.shape))
+            off += _r256(nb)
+        return out, (slot, lap)
+
+    def release(self, ticket: tuple) -> None:
+        torch.cuda.current_stream().wait_stream(self.side)   # this rank's push of the slot has finished
+        slot, lap = ticket
+        self._e.p2p_signal(self.sig.ptrs[self.prv] + 4 * (_FREE + slot), lap + 1)
+
+    def check(self) -> None:
+        s = int(self.status.item())
+        if s:
+            from lumenrl_b200.parallel.symm import CommTimeout
+            raise CommTimeout(f"CP ring exchange: a bounded wait expired (code {s})")
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.data.close()
+        self.sig.close()
+
+
+_RINGS: dict = {}
+
+
+def _nvlink_ring(group, payload_bytes: int) -> Optional[_NVLinkRing]:
+    """The group's NVLink ring channel (grown to the payload collectively:
+    every rank asks for the same size at the same call), or None when the
+    exchange runs over the process group (CPU / gloo, or LRL_CP_RING=pg)."""
+    import os
+    if os.environ.get("LRL_CP_RING", "nvlink") != "nvlink" or not torch.cuda.is_available():
+        return None
+    if dist.get_backend(group) != "nccl":
+        return None
+    key = id(group) if group is not None else 0
+    ring = _RINGS.get(key)
+    if ring is None or ring.slot_bytes < payload_bytes:
+        if ring is not None:
+            ring.close()
+        ring = _NVLinkRing(group, max(payload_bytes, 1 << 20))
+        _RINGS[key] = ring
+    return ring
+
+
+def _payload(tensors: list) -> int:
+    return sum(_r256(t.numel() * t.element_size()) for t in tensors)
+
+
 def _pairs(cp: int, rank: int, src: int):
     """(local q chunk slot, kv chunk slot of `src`, causal?) for every
     (query chunk, key chunk) pair that is not fully masked."""
@@ -232,20 +347,29 @@ class _RingAttention(torch.autograd.Function):
         o = [None, None]
         lse = [None, None]
         kv = (k, v)
+        ring = _nvlink_ring(group, 3 * _payload([k, v])) if k.is_cuda else None   # 3x: the backward's payload
+        ticket = None
         for step in range(cp):
             src = (rank - step) % cp
             reqs = None
+            nt = None
             if step < cp - 1:
-                nxt_kv, reqs = _ring_exchange(list(kv), group, rank, cp)
+                if ring is not None:
+                    nxt_kv, nt = ring.exchange(list(kv))
+                else:
+                    nxt_kv, reqs = _ring_exchange(list(kv), group, rank, cp)
             kk, vv = kv
             ks, vs = [kk[:, :, :c], kk[:, :, c:]], [vv[:, :, :c], vv[:, :, c:]]
             for qi, ki, causal in _pairs(cp, rank, src):
                 ob, lb = _block_fwd(qs[qi], ks[ki], vs[ki], causal, scale)
                 o[qi], lse[qi] = _merge(o[qi], lse[qi], ob, lb)
+            if ring is not None and ticket is not None:
+                ring.release(ticket)          # the slot just computed from (and pushed on)
             if reqs is not None:
                 for r in reqs:
                     r.wait()
-                kv = tuple(nxt_kv)
+            if step < cp - 1:
+                kv, ticket = tuple(nxt_kv), nt
         out = torch.cat([o[0], o[1]], 2).to(q.dtype)
         L = torch.cat([lse[0], lse[1]], 2)
         ctx.save_for_backward(q, k, v, out, L)
@@ -265,6 +389,8 @@ class _RingAttention(torch.autograd.Function):
         kk, vv = k, v
         dk = torch.zeros(k.shape, dtype=torch.float32, device=k.device)
         dv = torch.zeros(v.shape, dtype=torch.float32, device=v.device)
+        ring = _nvlink_ring(group, _payload([k, v, dk, dv])) if k.is_cuda else None
+        ticket = None
         for step in range(cp):
             src = (rank - step) % cp
             for qi, ki, causal in _pairs(cp, rank, src):
@@ -274,11 +400,20 @@ class _RingAttention(torch.autograd.Function):
                 dk[:, :, sl[ki]] += gk
                 dv[:, :, sl[ki]] += gv
             # pass (K, V, dK, dV) on; after cp steps every block is home again
-            recv, reqs = _ring_exchange([kk, vv, dk, dv], group, rank, cp)
-            for r in reqs:
-                r.wait()
+            if ring is not None:
+                recv, nt = ring.exchange([kk, vv, dk, dv])
+                if ticket is not None:
+                    ring.release(ticket)
+                ticket = nt
+            else:
+                recv, reqs = _ring_exchange([kk, vv, dk, dv], group, rank, cp)
+                for r in reqs:
+                    r.wait()
             kk, vv, dk, dv = recv
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
+        grads = dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+        if ring is not None and ticket is not None:
+            ring.release(ticket)             # after the copies above read the home slot
+        return (*grads, None, None)
 
 
 def ring_attention(q: Tensor, k: Tensor, v: Tensor, group=None, scale: Optional[float] = None) -> Tensor:

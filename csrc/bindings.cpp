@@ -1,6 +1,8 @@
 // Python bindings of the lumenrl_b200._C extension.
 #include <torch/extension.h>
 
+#include "comm/comm_api.h"
+
 #include <execinfo.h>
 #include <fcntl.h>
 #include <signal.h>
@@ -97,12 +99,6 @@ torch::Tensor tc_gemm_splitk(torch::Tensor a, torch::Tensor b, int64_t splits);
 torch::Tensor gemm2sm(torch::Tensor a, bool a_mn, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> c,
                       int64_t epi, int64_t bn);
 int64_t gemm2sm_status();
-void rs_norm_mc(int64_t mc_grads, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-                torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
-void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-                 torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
-                 double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
-                 torch::Tensor norm_out, int64_t wait_cycles);
 std::vector<torch::Tensor> gemm2sm_logprob(torch::Tensor h, torch::Tensor w, torch::Tensor targets, double inv_t);
 std::vector<torch::Tensor> ttt_diag_fwd(torch::Tensor q, torch::Tensor o0, torch::Tensor lse0,
                                         std::vector<torch::Tensor> kd, std::vector<torch::Tensor> vd, double scale);
@@ -117,45 +113,17 @@ torch::Tensor moe_route_bwd(torch::Tensor probs, torch::Tensor ids, torch::Tenso
 int64_t skinny_sk_status();
 torch::Tensor skinny_fp8(torch::Tensor x, torch::Tensor qw, torch::Tensor sw, int64_t grid);
 int64_t skinny_fp8_status();
-void nvlink_allreduce(std::vector<int64_t> buf_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n,
-                      double scale, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
-void nvlink_allreduce_mc(int64_t mc_buf, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t n, double scale,
-                         int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 void row_scale_(torch::Tensor x, torch::Tensor g);
-std::vector<int64_t> symm_malloc(int64_t nbytes);
-int64_t symm_open(std::vector<int64_t> handle_words);
-void symm_close(int64_t ptr);
-void symm_free(int64_t ptr);
-torch::Tensor symm_tensor(int64_t ptr, int64_t numel, torch::ScalarType dtype);
-int64_t symm_signal_words();
-void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_t epoch, torch::Tensor counter);
-void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles);
-void p2p_signal(int64_t flag_ptr, int64_t epoch);
 torch::Tensor skinny_gemm(torch::Tensor x, torch::Tensor w, int64_t ksplit);
 int64_t skinny_gemm_status();
 torch::Tensor grouped_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor offsets);
 int64_t grouped_gemm_status();
-int64_t ep_flag_slots();
-void ep_exchange_counts(torch::Tensor counts, std::vector<int64_t> table_ptrs, std::vector<int64_t> sig_ptrs,
-                        int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
-void ep_scatter_rows(torch::Tensor src, c10::optional<torch::Tensor> src_row, torch::Tensor dst_rank,
-                     torch::Tensor dst_row, std::vector<int64_t> buf_ptrs, int64_t cap,
-                     std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch, torch::Tensor counter,
-                     torch::Tensor status);
-void ep_wait_all(int64_t my_sig_ptr, int64_t W, int64_t slot, int64_t epoch, torch::Tensor status,
-                 int64_t wait_cycles);
 void tp_publish(std::vector<int64_t> sig_ptrs, int64_t rank, int64_t slot, int64_t epoch);
 torch::Tensor ag_gemm(std::vector<int64_t> shard_ptrs, int64_t Ml, torch::Tensor b, std::vector<int64_t> sig_ptrs,
                       int64_t rank, int64_t slot, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
 torch::Tensor gemm_rs(torch::Tensor a, torch::Tensor b, std::vector<int64_t> recv_ptrs,
                       std::vector<int64_t> sig_ptrs, torch::Tensor counter, int64_t rank, int64_t slot, int64_t epoch,
                       torch::Tensor status, int64_t wait_cycles);
-void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-             torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles);
-void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
-              torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1, double b2,
-              double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
-              torch::Tensor norm_out, int64_t wait_cycles);
 std::vector<torch::Tensor> quant_act_1x128(torch::Tensor x, bool e5m2);
 std::vector<torch::Tensor> quant_weight_128x128(torch::Tensor w, bool e5m2);
 std::vector<torch::Tensor> quant_t_1x128(torch::Tensor x, bool e5m2, bool kb_major);
@@ -165,6 +133,7 @@ torch::Tensor fp8_gemm(torch::Tensor a, torch::Tensor sa, torch::Tensor b, torch
 }  // namespace lrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  lrl::def_comm_ops(m);
   m.doc() = "lumenrl_b200 sm_100a kernels";
   m.def("install_segv_backtrace", &install_segv_backtrace, py::arg("path") = "");
   m.def("rmsnorm_fwd", &lrl::rmsnorm_fwd);
@@ -211,8 +180,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm2sm", &lrl::gemm2sm, py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"),
         py::arg("c") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0);
   m.def("gemm2sm_status", &lrl::gemm2sm_status);
-  m.def("rs_norm_mc", &lrl::rs_norm_mc);
-  m.def("adamw_ag_mc", &lrl::adamw_ag_mc);
   m.def("gemm2sm_logprob", &lrl::gemm2sm_logprob);
   m.def("ttt_diag_fwd", &lrl::ttt_diag_fwd);
   m.def("ttt_diag_bwd", &lrl::ttt_diag_bwd);
@@ -221,34 +188,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("skinny_sk_status", &lrl::skinny_sk_status);
   m.def("skinny_fp8", &lrl::skinny_fp8, py::arg("x"), py::arg("qw"), py::arg("sw"), py::arg("grid") = 0);
   m.def("skinny_fp8_status", &lrl::skinny_fp8_status);
-  m.def("nvlink_allreduce", &lrl::nvlink_allreduce);
-  m.def("nvlink_allreduce_mc", &lrl::nvlink_allreduce_mc);
   m.def("moe_route", &lrl::moe_route, py::arg("logits"), py::arg("k"), py::arg("norm"), py::arg("replay") = py::none());
   m.def("moe_route_bwd", &lrl::moe_route_bwd, py::arg("probs"), py::arg("ids"), py::arg("w"), py::arg("dw"),
         py::arg("dprobs") = py::none(), py::arg("norm") = true);
   m.def("row_scale_", &lrl::row_scale_);
-  m.def("symm_malloc", &lrl::symm_malloc);
-  m.def("symm_open", &lrl::symm_open);
-  m.def("symm_close", &lrl::symm_close);
-  m.def("symm_free", &lrl::symm_free);
-  m.def("symm_tensor", &lrl::symm_tensor);
-  m.def("symm_signal_words", &lrl::symm_signal_words);
-  m.def("p2p_push", &lrl::p2p_push);
-  m.def("p2p_wait", &lrl::p2p_wait);
-  m.def("p2p_signal", &lrl::p2p_signal);
   m.def("skinny_gemm", &lrl::skinny_gemm, py::arg("x"), py::arg("w"), py::arg("ksplit") = 0);
   m.def("skinny_gemm_status", &lrl::skinny_gemm_status);
   m.def("grouped_gemm", &lrl::grouped_gemm);
   m.def("grouped_gemm_status", &lrl::grouped_gemm_status);
-  m.def("ep_flag_slots", &lrl::ep_flag_slots);
-  m.def("ep_exchange_counts", &lrl::ep_exchange_counts);
-  m.def("ep_scatter_rows", &lrl::ep_scatter_rows);
-  m.def("ep_wait_all", &lrl::ep_wait_all);
   m.def("tp_publish", &lrl::tp_publish);
   m.def("ag_gemm", &lrl::ag_gemm);
   m.def("gemm_rs", &lrl::gemm_rs);
-  m.def("rs_norm", &lrl::rs_norm);
-  m.def("adamw_ag", &lrl::adamw_ag);
   m.def("quant_act_1x128", &lrl::quant_act_1x128);
   m.def("quant_weight_128x128", &lrl::quant_weight_128x128);
   m.def("quant_t_1x128", &lrl::quant_t_1x128, py::arg("x"), py::arg("e5m2") = false, py::arg("kb_major") = false);

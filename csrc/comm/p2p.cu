@@ -17,6 +17,7 @@
 // Everything is stream-ordered: work queued after p2p_wait on the same
 // stream sees the pushed data.
 #include "../common.cuh"
+#include "bounds.cuh"
 
 namespace lrl {
 
@@ -32,32 +33,37 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
 }
 
 __global__ void p2p_push_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t n16,
-                                uint32_t* __restrict__ ready_flag, uint32_t epoch, unsigned int* __restrict__ counter) {
+                                uint32_t* __restrict__ ready_flag, uint32_t epoch, unsigned int* __restrict__ counter,
+                                Span dst_sp, Span flag_sp, int* bstat) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // bounds build: one check of the whole destination range, then no stores
+  // at all when it does not fit (the ordinary build skips the check)
+  const bool fits = span_ok(dst_sp, dst, 16 * n16, bstat, 905);
   // 4 independent 16-byte loads in flight per thread
-  for (; i + 3 * stride < n16; i += 4 * stride) {
+  for (; fits && i + 3 * stride < n16; i += 4 * stride) {
     const uint4 a = src[i], b = src[i + stride], c = src[i + 2 * stride], d = src[i + 3 * stride];
     dst[i] = a;
     dst[i + stride] = b;
     dst[i + 2 * stride] = c;
     dst[i + 3 * stride] = d;
   }
-  for (; i < n16; i += stride) dst[i] = src[i];
+  for (; fits && i < n16; i += stride) dst[i] = src[i];
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned int done = atomicAdd(counter, 1u);
     if (done == gridDim.x - 1) {
       __threadfence_system();
-      st_release_sys_u32(ready_flag, epoch);
+      if (span_ok(flag_sp, ready_flag, 4, bstat, 906)) st_release_sys_u32(ready_flag, epoch);
       *counter = 0u;  // the next push on this stream starts from zero
     }
   }
 }
 
 __global__ void p2p_wait_kernel(const uint32_t* __restrict__ flag, uint32_t epoch, int* __restrict__ status, int tag,
-                                long long wait_cycles) {
+                                long long wait_cycles, Span flag_sp, int* bstat) {
+  if (!span_ok(flag_sp, flag, 4, bstat, 906)) return;
   const long long t0 = clock64();
   while (ld_acquire_sys_u32(flag) < epoch) {
     if (clock64() - t0 > wait_cycles) {
@@ -67,9 +73,9 @@ __global__ void p2p_wait_kernel(const uint32_t* __restrict__ flag, uint32_t epoc
   }
 }
 
-__global__ void p2p_signal_kernel(uint32_t* flag, uint32_t epoch) {
+__global__ void p2p_signal_kernel(uint32_t* flag, uint32_t epoch, Span flag_sp, int* bstat) {
   __threadfence_system();
-  st_release_sys_u32(flag, epoch);
+  if (span_ok(flag_sp, flag, 4, bstat, 906)) st_release_sys_u32(flag, epoch);
 }
 
 }  // namespace
@@ -85,17 +91,20 @@ void p2p_push(torch::Tensor src, int64_t dst_ptr, int64_t ready_flag_ptr, int64_
   p2p_push_kernel<<<blocks, 256, 0, stream()>>>(reinterpret_cast<const uint4*>(src.data_ptr()),
                                                reinterpret_cast<uint4*>(dst_ptr), n16,
                                                reinterpret_cast<uint32_t*>(ready_flag_ptr), (uint32_t)epoch,
-                                               reinterpret_cast<unsigned int*>(counter.data_ptr<int>()));
+                                               reinterpret_cast<unsigned int*>(counter.data_ptr<int>()),
+                                               span_of(dst_ptr), span_of(ready_flag_ptr), bounds_status_ptr());
 }
 
 void p2p_wait(int64_t flag_ptr, int64_t epoch, torch::Tensor status, int64_t tag, int64_t wait_cycles) {
   TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "p2p_wait: int32 status");
   p2p_wait_kernel<<<1, 1, 0, stream()>>>(reinterpret_cast<const uint32_t*>(flag_ptr), (uint32_t)epoch,
-                                         status.data_ptr<int>(), (int)tag, (long long)wait_cycles);
+                                         status.data_ptr<int>(), (int)tag, (long long)wait_cycles, span_of(flag_ptr),
+                                         bounds_status_ptr());
 }
 
 void p2p_signal(int64_t flag_ptr, int64_t epoch) {
-  p2p_signal_kernel<<<1, 1, 0, stream()>>>(reinterpret_cast<uint32_t*>(flag_ptr), (uint32_t)epoch);
+  p2p_signal_kernel<<<1, 1, 0, stream()>>>(reinterpret_cast<uint32_t*>(flag_ptr), (uint32_t)epoch, span_of(flag_ptr),
+                                           bounds_status_ptr());
 }
 
 }  // namespace lrl

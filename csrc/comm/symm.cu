@@ -26,6 +26,7 @@
 //              a value into every GPU's copy, so each byte crosses a GPU's
 //              NVLink ports once instead of once per peer.
 #include "../common.cuh"
+#include "bounds.cuh"
 
 namespace lrl {
 
@@ -55,14 +56,16 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
 // peer's row for `slot`; every block's thread 0 waits (bounded) until all W
 // announcements for this epoch are visible in the local row.
 __device__ bool rank_barrier(const PeerPtrs& sig, uint32_t* my_sig, int rank, int W, int slot, uint32_t epoch,
-                             int* status, long long wait_cycles) {
+                             int* status, long long wait_cycles, const Checks& chk) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     ok = 1;
     if (blockIdx.x == 0) {
       __threadfence_system();
-      for (int r = 0; r < W; ++r)
-        st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + slot * kMaxRanks + rank, epoch);
+      for (int r = 0; r < W; ++r) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + slot * kMaxRanks + rank;
+        if (span_ok(chk.sig.s[r], f, 4, chk.bstat, 910)) st_release_sys(f, epoch);
+      }
     }
     const long long t0 = clock64();
     for (int r = 0; r < W && ok; ++r) {
@@ -81,8 +84,8 @@ __device__ bool rank_barrier(const PeerPtrs& sig, uint32_t* my_sig, int rank, in
 
 __global__ void rs_norm_kernel(PeerPtrs grads, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t lo,
                                int64_t n, float* __restrict__ out, uint32_t epoch, int* status,
-                               long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles)) return;
+                               long long wait_cycles, const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles, chk)) return;
   __shared__ float red[32];
   float ss = 0.f;
   const int64_t n4 = n / 4;
@@ -91,7 +94,9 @@ __global__ void rs_norm_kernel(PeerPtrs grads, PeerPtrs sig, uint32_t* my_sig, i
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
       if (r >= W) break;
-      const float4 v = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[r]) + lo)[i];
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[r]) + lo) + i;
+      if (!span_ok(chk.data.s[r], src, 16, chk.bstat, 907)) continue;
+      const float4 v = *src;
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
@@ -109,8 +114,10 @@ __global__ void rs_norm_kernel(PeerPtrs grads, PeerPtrs sig, uint32_t* my_sig, i
     if (done == gridDim.x - 1) {
       const float total = atomicExch(reinterpret_cast<float*>(my_sig + kSigNorms + kMaxRanks), 0.f);
       my_sig[kSigNorms + kMaxRanks + 1] = 0u;
-      for (int r = 0; r < W; ++r)
-        reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigNorms)[rank] = total;
+      for (int r = 0; r < W; ++r) {
+        float* dst = reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigNorms) + rank;
+        if (span_ok(chk.sig.s[r], dst, 4, chk.bstat, 910)) *dst = total;
+      }
       __threadfence_system();
     }
   }
@@ -120,8 +127,8 @@ __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig
                                 int64_t n, float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                                 float* __restrict__ v, float lr, float b1, float b2, float eps, float wd, float bc1,
                                 float bc2, float max_norm, uint32_t epoch, int* status, float* norm_out,
-                                long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles)) return;
+                                long long wait_cycles, const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles, chk)) return;
   float sq = 0.f;
   for (int r = 0; r < W; ++r) sq += reinterpret_cast<volatile float*>(my_sig + kSigNorms)[r];
   const float norm = sqrtf(sq);
@@ -157,7 +164,8 @@ __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig
 #pragma unroll
       for (int r = 0; r < kMaxRanks; ++r) {
         if (r >= W) break;
-        reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(weights.p[r]) + lo)[i] = packed;
+        uint2* dst = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(weights.p[r]) + lo) + i;
+        if (span_ok(chk.data.s[r], dst, 8, chk.bstat, 908)) *dst = packed;
       }
     }
   }
@@ -173,8 +181,10 @@ __global__ void adamw_ag_kernel(PeerPtrs weights, PeerPtrs sig, uint32_t* my_sig
     if (threadIdx.x == 0) my_sig[kSigNorms + kMaxRanks + 2] = 0u;
     // reuse the barrier with a dedicated slot; only this block participates
     if (threadIdx.x == 0) {
-      for (int r = 0; r < W; ++r)
-        st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 2 * kMaxRanks + rank, epoch);
+      for (int r = 0; r < W; ++r) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 2 * kMaxRanks + rank;
+        if (span_ok(chk.sig.s[r], f, 4, chk.bstat, 910)) st_release_sys(f, epoch);
+      }
       const long long t0 = clock64();
       for (int r = 0; r < W; ++r) {
         while (ld_acquire_sys(my_sig + kSigFlags + 2 * kMaxRanks + r) < epoch) {
@@ -208,8 +218,8 @@ __device__ __forceinline__ void mc_st_v2(void* mc_addr, uint2 v) {
 
 __global__ void rs_norm_mc_kernel(float* mc_grads, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t lo,
                                   int64_t n, float* __restrict__ out, uint32_t epoch, int* status,
-                                  long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles)) return;
+                                  long long wait_cycles, const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 0, epoch, status, wait_cycles, chk)) return;
   __shared__ float red[32];
   float ss = 0.f;
   const int64_t n4 = n / 4;
@@ -227,8 +237,10 @@ __global__ void rs_norm_mc_kernel(float* mc_grads, PeerPtrs sig, uint32_t* my_si
     if (done == gridDim.x - 1) {
       const float total = atomicExch(reinterpret_cast<float*>(my_sig + kSigNorms + kMaxRanks), 0.f);
       my_sig[kSigNorms + kMaxRanks + 1] = 0u;
-      for (int r = 0; r < W; ++r)
-        reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigNorms)[rank] = total;
+      for (int r = 0; r < W; ++r) {
+        float* dst = reinterpret_cast<float*>(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigNorms) + rank;
+        if (span_ok(chk.sig.s[r], dst, 4, chk.bstat, 910)) *dst = total;
+      }
       __threadfence_system();
     }
   }
@@ -238,8 +250,8 @@ __global__ void adamw_ag_mc_kernel(__nv_bfloat16* mc_weights, PeerPtrs sig, uint
                                    int64_t lo, int64_t n, float* __restrict__ p, const float* __restrict__ g,
                                    float* __restrict__ m, float* __restrict__ v, float lr, float b1, float b2, float eps,
                                    float wd, float bc1, float bc2, float max_norm, uint32_t epoch, int* status,
-                                   float* norm_out, long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles)) return;
+                                   float* norm_out, long long wait_cycles, const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 1, epoch, status, wait_cycles, chk)) return;
   float sq = 0.f;
   for (int r = 0; r < W; ++r) sq += reinterpret_cast<volatile float*>(my_sig + kSigNorms)[r];
   const float norm = sqrtf(sq);
@@ -286,8 +298,10 @@ __global__ void adamw_ag_mc_kernel(__nv_bfloat16* mc_weights, PeerPtrs sig, uint
   __syncthreads();
   if (last && threadIdx.x == 0) {
     my_sig[kSigNorms + kMaxRanks + 2] = 0u;
-    for (int r = 0; r < W; ++r)
-      st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 2 * kMaxRanks + rank, epoch);
+    for (int r = 0; r < W; ++r) {
+      uint32_t* f = reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 2 * kMaxRanks + rank;
+      if (span_ok(chk.sig.s[r], f, 4, chk.bstat, 910)) st_release_sys(f, epoch);
+    }
     const long long t0 = clock64();
     for (int r = 0; r < W; ++r) {
       while (ld_acquire_sys(my_sig + kSigFlags + 2 * kMaxRanks + r) < epoch) {
@@ -319,7 +333,7 @@ PeerPtrs to_peers(const std::vector<int64_t>& ptrs) {
 constexpr int kArCounter = kSigNorms + kMaxRanks + 3;
 
 __device__ void ar_completion(const PeerPtrs& sig, uint32_t* my_sig, int rank, int W, uint32_t epoch, int* status,
-                              long long wait_cycles) {
+                              long long wait_cycles, const Checks& chk) {
   __shared__ int last;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -329,8 +343,10 @@ __device__ void ar_completion(const PeerPtrs& sig, uint32_t* my_sig, int rank, i
   __syncthreads();
   if (last && threadIdx.x == 0) {
     my_sig[kArCounter] = 0u;
-    for (int r = 0; r < W; ++r)
-      st_release_sys(reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 5 * kMaxRanks + rank, epoch);
+    for (int r = 0; r < W; ++r) {
+      uint32_t* f = reinterpret_cast<uint32_t*>(sig.p[r]) + kSigFlags + 5 * kMaxRanks + rank;
+      if (span_ok(chk.sig.s[r], f, 4, chk.bstat, 910)) st_release_sys(f, epoch);
+    }
     const long long t0 = clock64();
     for (int r = 0; r < W; ++r) {
       while (ld_acquire_sys(my_sig + kSigFlags + 5 * kMaxRanks + r) < epoch) {
@@ -344,8 +360,9 @@ __device__ void ar_completion(const PeerPtrs& sig, uint32_t* my_sig, int rank, i
 }
 
 __global__ void allreduce_kernel(PeerPtrs bufs, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t n,
-                                 float scale, uint32_t epoch, int* status, long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles)) return;
+                                 float scale, uint32_t epoch, int* status, long long wait_cycles,
+                                 const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles, chk)) return;
   const int64_t n4 = n / 4, per = (n4 + W - 1) / W;
   const int64_t a = rank * per, b = min(n4, a + per);
   for (int64_t i = a + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += (int64_t)gridDim.x * blockDim.x) {
@@ -353,7 +370,9 @@ __global__ void allreduce_kernel(PeerPtrs bufs, PeerPtrs sig, uint32_t* my_sig, 
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
       if (r >= W) break;
-      const float4 v = reinterpret_cast<const float4*>(bufs.p[r])[i];
+      const float4* src = reinterpret_cast<const float4*>(bufs.p[r]) + i;
+      if (!span_ok(chk.data.s[r], src, 16, chk.bstat, 909)) continue;
+      const float4 v = *src;
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
@@ -366,17 +385,19 @@ __global__ void allreduce_kernel(PeerPtrs bufs, PeerPtrs sig, uint32_t* my_sig, 
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r) {
       if (r >= W) break;
-      reinterpret_cast<float4*>(bufs.p[r])[i] = acc;
+      float4* dst = reinterpret_cast<float4*>(bufs.p[r]) + i;
+      if (span_ok(chk.data.s[r], dst, 16, chk.bstat, 909)) *dst = acc;
     }
   }
-  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles);
+  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles, chk);
 }
 
 // NVLS: one multimem.ld_reduce returns the sum over every GPU's copy (reduced
 // in the NVSwitch), one multimem.st writes the result into every copy
 __global__ void allreduce_mc_kernel(float* mc, PeerPtrs sig, uint32_t* my_sig, int rank, int W, int64_t n,
-                                    float scale, uint32_t epoch, int* status, long long wait_cycles) {
-  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles)) return;
+                                    float scale, uint32_t epoch, int* status, long long wait_cycles,
+                                    const __grid_constant__ Checks chk) {
+  if (!rank_barrier(sig, my_sig, rank, W, 4, epoch, status, wait_cycles, chk)) return;
   const int64_t n4 = n / 4, per = (n4 + W - 1) / W;
   const int64_t a = rank * per, b = min(n4, a + per);
   for (int64_t i = a + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < b; i += (int64_t)gridDim.x * blockDim.x) {
@@ -385,7 +406,7 @@ __global__ void allreduce_mc_kernel(float* mc, PeerPtrs sig, uint32_t* my_sig, i
                  "f"(acc.x * scale), "f"(acc.y * scale), "f"(acc.z * scale), "f"(acc.w * scale)
                  : "memory");
   }
-  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles);
+  ar_completion(sig, my_sig, rank, W, epoch, status, wait_cycles, chk);
 }
 
 int comm_grid() { return num_sms(); }  // one 512-thread block per SM: all blocks co-resident
@@ -397,6 +418,7 @@ std::vector<int64_t> symm_malloc(int64_t nbytes) {
   void* ptr = nullptr;
   C10_CUDA_CHECK(cudaMalloc(&ptr, nbytes));
   C10_CUDA_CHECK(cudaMemset(ptr, 0, nbytes));
+  bounds_register(reinterpret_cast<int64_t>(ptr), nbytes);
   cudaIpcMemHandle_t h;
   C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, ptr));
   std::vector<int64_t> out{reinterpret_cast<int64_t>(ptr)};
@@ -414,8 +436,14 @@ int64_t symm_open(std::vector<int64_t> handle_words) {
   return reinterpret_cast<int64_t>(ptr);
 }
 
-void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
-void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+void symm_close(int64_t ptr) {
+  bounds_unregister(ptr);
+  cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+}
+void symm_free(int64_t ptr) {
+  bounds_unregister(ptr);
+  cudaFree(reinterpret_cast<void*>(ptr));
+}
 
 torch::Tensor symm_tensor(int64_t ptr, int64_t numel, torch::ScalarType dtype) {
   return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, [](void*) {},
@@ -428,11 +456,14 @@ int64_t symm_signal_words() { return kSigWords; }
 void rs_norm(std::vector<int64_t> grad_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
              torch::Tensor out, int64_t epoch, torch::Tensor status, int64_t wait_cycles) {
   TORCH_CHECK(n % 4 == 0 && lo % 4 == 0, "rs_norm: 16-byte aligned shards");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= n,
+              "rs_norm: out must be a contiguous fp32 CUDA tensor of at least n elements");
   const int W = grad_ptrs.size();
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   rs_norm_kernel<<<comm_grid(), 512, 0, stream()>>>(to_peers(grad_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W, lo,
                                                     n, out.data_ptr<float>(), (uint32_t)epoch,
-                                                    status.data_ptr<int>(), (long long)wait_cycles);
+                                                    status.data_ptr<int>(), (long long)wait_cycles,
+                                                    checks_of(grad_ptrs, sig_ptrs));
 }
 
 void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
@@ -440,6 +471,9 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
               double eps, double wd, int64_t step, double max_norm, int64_t epoch, torch::Tensor status,
               torch::Tensor norm_out, int64_t wait_cycles) {
   TORCH_CHECK(n % 4 == 0 && lo % 4 == 0, "adamw_ag: aligned shards");
+  for (const auto& t : {p, g, m, v})
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() >= n,
+                "adamw_ag: p, g, m and v must be contiguous fp32 CUDA tensors of at least n elements");
   const int W = weight_ptrs.size();
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   const float bc1 = 1.f - powf((float)b1, (float)step), bc2 = 1.f - powf((float)b2, (float)step);
@@ -447,7 +481,7 @@ void adamw_ag(std::vector<int64_t> weight_ptrs, std::vector<int64_t> sig_ptrs, i
       to_peers(weight_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W, lo, n, p.data_ptr<float>(),
       g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
       (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(), norm_out.data_ptr<float>(),
-      (long long)wait_cycles);
+      (long long)wait_cycles, checks_of(weight_ptrs, sig_ptrs));
 }
 
 // NVLS: mc_grads / mc_weights are the multicast addresses of the symmetric
@@ -459,7 +493,8 @@ void rs_norm_mc(int64_t mc_grads, std::vector<int64_t> sig_ptrs, int64_t rank, i
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   rs_norm_mc_kernel<<<comm_grid(), 512, 0, stream()>>>(reinterpret_cast<float*>(mc_grads), to_peers(sig_ptrs), my_sig,
                                                        (int)rank, W, lo, n, out.data_ptr<float>(), (uint32_t)epoch,
-                                                       status.data_ptr<int>(), (long long)wait_cycles);
+                                                       status.data_ptr<int>(), (long long)wait_cycles,
+                                                       checks_of({}, sig_ptrs));
 }
 
 void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank, int64_t lo, int64_t n,
@@ -474,7 +509,7 @@ void adamw_ag_mc(int64_t mc_weights, std::vector<int64_t> sig_ptrs, int64_t rank
       reinterpret_cast<__nv_bfloat16*>(mc_weights), to_peers(sig_ptrs), my_sig, (int)rank, W, lo, n,
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1,
       (float)b2, (float)eps, (float)wd, bc1, bc2, (float)max_norm, (uint32_t)epoch, status.data_ptr<int>(),
-      norm_out.data_ptr<float>(), (long long)wait_cycles);
+      norm_out.data_ptr<float>(), (long long)wait_cycles, checks_of({}, sig_ptrs));
 }
 
 // ---- replicated data-parallel all-reduce ------------------------------------------
@@ -489,7 +524,7 @@ void nvlink_allreduce(std::vector<int64_t> buf_ptrs, std::vector<int64_t> sig_pt
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   allreduce_kernel<<<comm_grid(), 512, 0, stream()>>>(to_peers(buf_ptrs), to_peers(sig_ptrs), my_sig, (int)rank, W,
                                                       n, (float)scale, (uint32_t)epoch, status.data_ptr<int>(),
-                                                      (long long)wait_cycles);
+                                                      (long long)wait_cycles, checks_of(buf_ptrs, sig_ptrs));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -501,7 +536,8 @@ void nvlink_allreduce_mc(int64_t mc_buf, std::vector<int64_t> sig_ptrs, int64_t 
   uint32_t* my_sig = reinterpret_cast<uint32_t*>(sig_ptrs[rank]);
   allreduce_mc_kernel<<<comm_grid(), 512, 0, stream()>>>(reinterpret_cast<float*>(mc_buf), to_peers(sig_ptrs), my_sig,
                                                          (int)rank, W, n, (float)scale, (uint32_t)epoch,
-                                                         status.data_ptr<int>(), (long long)wait_cycles);
+                                                         status.data_ptr<int>(), (long long)wait_cycles,
+                                                         checks_of({}, sig_ptrs));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

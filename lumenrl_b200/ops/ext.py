@@ -9,6 +9,7 @@ tensor reaching an op without the extension raises ``RuntimeError``.
 from __future__ import annotations
 
 import importlib
+import os
 
 _MOD = None
 _ERR: Exception | None = None
@@ -17,6 +18,8 @@ LAUNCHES = [0]   # kernels of this extension launched (graph replays add their c
 
 # host-only entry points (no kernel) and ops that launch two kernels
 _NO_KERNEL = {"symm_malloc", "symm_open", "symm_close", "symm_free", "symm_tensor", "symm_signal_words",
+              "bounds_register", "bounds_unregister", "bounds_lookup", "bounds_status", "bounds_reset",
+              "debug_bounds_build",
               "ep_flag_slots", "tc_gemm_status", "skinny_gemm_status", "skinny_sk_status", "grouped_gemm_status", "decode_tma_status",
               "fa_fwd_status", "fa_bwd_status", "gemm2sm_status", "install_segv_backtrace"}
 _TWO_KERNELS = {"fa_fwd", "paged_decode_attn_shared", "paged_decode_attn_tma", "paged_decode_attn_shared_tma", "gemm_rs"}
@@ -40,13 +43,17 @@ def _kernels(name: str, a: tuple) -> int:
 class _Counted:
     """Proxy that counts the kernels the extension launches (an estimate for
     the split decode attention, whose combine pass is skipped when a single
-    split covers the context)."""
+    split covers the context).  With a bounds module (``LRL_DEBUG_BOUNDS=1``)
+    every op that module defines -- the NVLink comm kernels, the symmetric
+    buffer plumbing and the bounds registry -- resolves there."""
 
-    def __init__(self, mod) -> None:
+    def __init__(self, mod, bounds=None) -> None:
         self._mod = mod
+        self._bounds = bounds
 
     def __getattr__(self, name):
-        fn = getattr(self._mod, name)
+        src = self._bounds if self._bounds is not None and hasattr(self._bounds, name) else self._mod
+        fn = getattr(src, name)
         if not callable(fn):
             return fn
 
@@ -62,9 +69,34 @@ def _load():
         return
     try:
         import torch  # noqa: F401  (loads libc10/libtorch for the extension)
-        _MOD = _Counted(importlib.import_module("lumenrl_b200._C"))
+        mod = importlib.import_module("lumenrl_b200._C")
     except Exception as e:  # pragma: no cover - depends on the build
         _ERR = e
+        return
+    bounds = None
+    if debug_bounds_requested():
+        # no fallback: a run that asked for checked kernels must get them
+        bounds = importlib.import_module("lumenrl_b200._C_bounds")
+    _MOD = _Counted(mod, bounds)
+
+
+def debug_bounds_requested() -> bool:
+    """``LRL_DEBUG_BOUNDS=1``: the NVLink comm kernels come from
+    ``lumenrl_b200._C_bounds``, where every peer and signal-area access is
+    checked against its buffer's registered extent; a violation is skipped and
+    recorded (``bounds_error()``) instead of faulting a GPU."""
+    return os.environ.get("LRL_DEBUG_BOUNDS", "0") == "1"
+
+
+def bounds_error() -> int:
+    """Site code of the first out-of-bounds access the checked comm kernels
+    recorded on the current device since the last ``bounds_clear()`` (0 =
+    none, always 0 without ``LRL_DEBUG_BOUNDS=1``).  Synchronises."""
+    return int(ext().bounds_status())
+
+
+def bounds_clear() -> None:
+    ext().bounds_reset()
 
 
 def has_ext() -> bool:

@@ -61,6 +61,7 @@ class SymmetricBuffer:
                 self.ptrs.append(self.local_ptr)
             else:
                 p = int(ext().symm_open(h))
+                ext().bounds_register(p, nbytes)   # extent for the bounds-checked comm kernels
                 self.ptrs.append(p)
                 self._opened.append(p)
         self.tensor = ext().symm_tensor(self.local_ptr, numel, dtype)
@@ -92,8 +93,14 @@ class MulticastBuffer:
         self.handle = symm.rendezvous(self.tensor, g.group_name)
         self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
         self.mc = int(self.handle.multicast_ptr)
+        nbytes = numel * self.tensor.element_size()
+        for p in self.ptrs:
+            ext().bounds_register(p, nbytes)   # extents for the bounds-checked comm kernels
 
     def close(self) -> None:
+        if self.handle is not None:
+            for p in self.ptrs:
+                ext().bounds_unregister(p)
         self.handle = None
 
 

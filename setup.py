@@ -1,7 +1,9 @@
 """Build the sm_100a extension in place:  python setup.py build_ext --inplace
 
 Every .cu under csrc/ is compiled for sm_100a only (Blackwell B200); torch's
-own arch list is bypassed by passing the -gencode explicitly.
+own arch list is bypassed by passing the -gencode explicitly.  Two modules:
+lumenrl_b200._C (every kernel) and lumenrl_b200._C_bounds (the NVLink comm
+kernels with every peer access bounds-checked, -DLRL_DEBUG_BOUNDS).
 """
 
 import glob
@@ -14,7 +16,15 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 
 def cuda_sources():
     srcs = sorted(glob.glob(os.path.join("csrc", "**", "*.cu"), recursive=True))
-    return ["csrc/bindings.cpp"] + srcs
+    return ["csrc/bindings.cpp"] + [s for s in srcs if os.sep + "debug_bounds" + os.sep not in s]
+
+
+def bounds_sources():
+    """The NVLink comm kernels again, compiled with -DLRL_DEBUG_BOUNDS into
+    lumenrl_b200._C_bounds (thin wrappers, so their objects do not collide
+    with the ordinary build's)."""
+    d = os.path.join("csrc", "debug_bounds")
+    return [os.path.join(d, "module.cpp")] + sorted(glob.glob(os.path.join(d, "*.cu")))
 
 
 def ext_modules():
@@ -27,13 +37,23 @@ def ext_modules():
     ]
     if os.environ.get("LRL_PTXAS_VERBOSE"):
         nvcc.append("-Xptxas=-v")
-    return [CUDAExtension(
-        name="lumenrl_b200._C",
-        sources=cuda_sources(),
-        include_dirs=[os.path.join(ROOT, "csrc")],
-        extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc},
-        libraries=["cuda"],
-    )]
+    return [
+        CUDAExtension(
+            name="lumenrl_b200._C",
+            sources=cuda_sources(),
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc},
+            libraries=["cuda"],
+        ),
+        CUDAExtension(
+            name="lumenrl_b200._C_bounds",
+            sources=bounds_sources(),
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17", "-DLRL_DEBUG_BOUNDS"],
+                                "nvcc": nvcc + ["-DLRL_DEBUG_BOUNDS"]},
+            libraries=["cuda"],
+        ),
+    ]
 
 
 def cmdclass():

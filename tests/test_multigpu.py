@@ -3,6 +3,8 @@ norm, clip + AdamW + bf16 peer-store broadcast) against the NCCL path, as
 2 processes on 2 GPUs.  Skips with fewer than 2 GPUs."""
 
 import os
+import random
+import time
 
 import pytest
 import torch
@@ -175,8 +177,13 @@ def _ring_worker(rank, world, port, q):
     T, D = 2048, 4 * 1024   # one 16 MiB batch of bf16 hidden rows
     ring = HiddenStateRing(producer=0, consumer=1, slot_bytes=T * D * 2, nslots=2, wait_seconds=2.0)
     errs = []
-    for i in range(5):   # more batches than slots: the producer waits for released slots
+    # randomised host delays before every launch skew the two ranks' kernels
+    # against each other; the lap-numbered flags must still deliver every
+    # batch intact and in order
+    delay = random.Random(1234 + rank)
+    for i in range(8):   # more batches than slots: the producer waits for released slots
         x = torch.randn(T, D, device="cuda", generator=torch.Generator(device="cuda").manual_seed(i)).to(torch.bfloat16)
+        time.sleep(delay.uniform(0.0, 0.05))
         if rank == 0:
             ring.put(x)
         else:
@@ -215,7 +222,7 @@ def test_hidden_state_ring_nvlink():
     for p in procs:
         p.join(timeout=60)
     errs, timeout = res[1]
-    assert len(errs) == 5 and max(errs) == 0.0
+    assert len(errs) == 8 and max(errs) == 0.0
     assert timeout == "timeout"
 
 

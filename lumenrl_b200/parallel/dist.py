@@ -111,6 +111,26 @@ def all_reduce_sum(x: float, state: Optional[ParallelState] = None) -> float:
     return float(t.item())
 
 
+def _reduce_many(xs: list, op) -> list:
+    if not dist.is_initialized() or not xs:
+        return [float(x) for x in xs]
+    t = torch.tensor([float(x) for x in xs], dtype=torch.float64,
+                     device=_STATE.device if _STATE.device.type == "cuda" else "cpu")
+    dist.all_reduce(t, op=op, group=_STATE.dp_group)
+    return t.tolist()
+
+
+def all_reduce_sum_many(xs: list) -> list:
+    """Element-wise sum over the data-parallel group of several host scalars
+    in ONE collective (and one device->host read)."""
+    return _reduce_many(xs, dist.ReduceOp.SUM)
+
+
+def all_reduce_max_many(xs: list) -> list:
+    """Element-wise max over the data-parallel group in one collective."""
+    return _reduce_many(xs, dist.ReduceOp.MAX)
+
+
 def destroy() -> None:
     if dist.is_initialized():
         dist.destroy_process_group()

@@ -44,7 +44,8 @@ from lumenrl_b200.data.synthetic import SyntheticPrompts
 from lumenrl_b200.engine.inference.engine import RolloutEngine, SamplingParams
 from lumenrl_b200.engine.training.actor import ActorEngine
 from lumenrl_b200.models.config import ModelArgs, resolve_model
-from lumenrl_b200.parallel.dist import ParallelState, all_reduce_max, all_reduce_sum, get_state, init_distributed
+from lumenrl_b200.parallel.dist import (ParallelState, all_reduce_max_many, all_reduce_sum_many, get_state,
+                                        init_distributed)
 from lumenrl_b200.rewards import get_reward_fn
 from lumenrl_b200.utils.timers import PhaseTimer
 
@@ -367,28 +368,31 @@ class RLTrainer:
         self.timer.stop("step")
         times = self.timer.collect()
         m.update(tm)
-        tokens_local = float(batch["prompt_lengths"].sum() + batch["response_lengths"].sum())
-        tokens = all_reduce_sum(tokens_local)
-        step_s = all_reduce_max(times["step"])
-        m.update({f"timing/{k}_s": all_reduce_max(v) for k, v in times.items()})
-        m["perf/total_num_tokens"] = tokens
-        m["perf/step_tokens_per_s"] = tokens / step_s
-        m["perf/throughput"] = tokens / (step_s * st.world_size)
-        m["perf/gen_tokens_per_s"] = all_reduce_sum(float(batch["response_lengths"].sum())) / max(
-            all_reduce_max(times["gen"]), 1e-9)
-        m["reward/mean"] = all_reduce_sum(float(scores.sum())) / all_reduce_sum(float(len(batch)))
-        m["response_length/mean"] = all_reduce_sum(float(batch["response_lengths"].float().sum())) / all_reduce_sum(
-            float(len(batch)))
+        # every cross-rank statistic of the step in two collectives (one sum
+        # vector, one max vector) and two device->host reads
+        resp_local = batch["response_lengths"].sum()
+        tokens_local, resp_tokens, score_sum = (float(v) for v in torch.stack(
+            [batch["prompt_lengths"].sum() + resp_local, resp_local, scores.sum()]).double().cpu())
+        tokens, resp_tokens, score_sum, rows = all_reduce_sum_many(
+            [tokens_local, resp_tokens, score_sum, float(len(batch))])
         # Weight sync = from the reduced gradients to rollout-ready weights: the
         # AdamW kernel that writes bf16 into the resident buffer the engine
         # reads (and, on several GPUs, stores it into every rank's copy over
         # NVLink), plus the engine-side update (fp8 re-quantisation when the
         # rollout runs W8A8; a pointer check otherwise).  Max over ranks.
-        for k in ("timing/opt_rs_s", "timing/opt_bcast_s"):
-            if k in m:
-                m[k] = all_reduce_max(float(m[k]))
-        sync_s = all_reduce_max(float(tm.get("timing/opt_bcast_s", 0.0)) + times["weight_sync"])
-        m["timing/weight_sync_s"] = sync_s
+        opt_keys = [k for k in ("timing/opt_rs_s", "timing/opt_bcast_s") if k in m]
+        max_keys = [f"timing/{k}_s" for k in times] + opt_keys + ["timing/weight_sync_s"]
+        max_vals = list(times.values()) + [float(m[k]) for k in opt_keys] + [
+            float(tm.get("timing/opt_bcast_s", 0.0)) + times["weight_sync"]]
+        m.update(zip(max_keys, all_reduce_max_many(max_vals)))
+        step_s = m["timing/step_s"]
+        m["perf/total_num_tokens"] = tokens
+        m["perf/step_tokens_per_s"] = tokens / step_s
+        m["perf/throughput"] = tokens / (step_s * st.world_size)
+        m["perf/gen_tokens_per_s"] = resp_tokens / max(m["timing/gen_s"], 1e-9)
+        m["reward/mean"] = score_sum / rows
+        m["response_length/mean"] = resp_tokens / rows
+        sync_s = m["timing/weight_sync_s"]
         m["weight_sync/ms"] = sync_s * 1e3
         wbytes = sum(p.numel() for _, p in self.actor.model.named_flat_params()) * (
             2 if self.actor.model.p("embed").dtype == torch.bfloat16 else 4)

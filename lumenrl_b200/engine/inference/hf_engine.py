@@ -59,7 +59,7 @@ class HFEngine:
         model = getattr(transformers, arch)(config)
         eng = cls(model=model, dtype=dtype, device=device, **kw)
         eng.init()
-        eng.update_weights({k: v.detach() for k, v in native.hf_state_dict().items()})
+        eng.update_weights({k: v.detach() for k, v in native.hf_state_dict().items()})   # experts routed in
         return eng
 
     def init(self) -> None:
@@ -121,15 +121,17 @@ class HFEngine:
     def update_weights(self, state_dict: dict[str, Tensor]) -> int:
         """Load HF-named tensors; raises KeyError unless every parameter of
         the module is covered and every tensor is used."""
+        from lumenrl_b200.sync.moe_weights import assert_weight_sync_coverage, route_expert_weights
         m = self.model
         params = dict(m.named_parameters())
         tied = getattr(getattr(m, "config", None), "tie_word_embeddings", False)
-        missing = [k for k in params if k not in state_dict and not (tied and k == "lm_head.weight")]
-        extra = [k for k in state_dict if k not in params and not (tied and k == "lm_head.weight")]
-        bad = [k for k, v in state_dict.items() if k in params and tuple(v.shape) != tuple(params[k].shape)]
-        if missing or extra or bad:
-            raise KeyError(f"HFEngine weight sync coverage: missing {missing[:6]}, unexpected {extra[:6]}, "
-                           f"shape mismatch {bad[:6]}")
+        # per-expert checkpoint tensors <-> the module's fused expert parameters
+        state_dict = route_expert_weights(state_dict, params)
+        try:
+            assert_weight_sync_coverage(state_dict, {k: tuple(p.shape) for k, p in params.items()},
+                                        optional=("lm_head.weight",) if tied else ())
+        except KeyError as e:
+            raise KeyError(f"HFEngine {e.args[0]}") from None
         for k, v in state_dict.items():
             if k in params:
                 params[k].copy_(v.to(device=params[k].device, dtype=params[k].dtype))

@@ -283,8 +283,12 @@ class Qwen3Model(nn.Module):
         return hidden @ self.lm_head.t()
 
     # -- HF format ---------------------------------------------------------------
-    def hf_state_dict(self, flat: Optional[Tensor] = None) -> dict[str, Tensor]:
-        """HF-named tensors (views where possible) of ``flat`` (default: own)."""
+    def hf_state_dict(self, flat: Optional[Tensor] = None, fused_experts: bool = False) -> dict[str, Tensor]:
+        """HF-named tensors (views where possible) of ``flat`` (default: own).
+        MoE experts are spelled per expert (the safetensors checkpoint layout)
+        or, with ``fused_experts``, as the fused ``experts.gate_up_proj``
+        [E, 2F, H] / ``experts.down_proj`` [E, H, F] tensors of
+        ``transformers`` >= 5 modules (the native layout itself)."""
         a = self.args
         src = self.flat if flat is None else flat
         v = lambda n: self.layout.view(src, n)  # noqa: E731
@@ -307,6 +311,10 @@ class Qwen3Model(nn.Module):
                 out[hp + "mlp.gate.weight"] = v(p + "router")
                 w13, w2 = v(p + "experts_w13"), v(p + "experts_w2")
                 F = a.moe_intermediate_size
+                if fused_experts:
+                    out[hp + "mlp.experts.gate_up_proj"] = w13
+                    out[hp + "mlp.experts.down_proj"] = w2
+                    continue
                 for e in range(a.num_experts):
                     out[hp + f"mlp.experts.{e}.gate_proj.weight"] = w13[e, :F]
                     out[hp + f"mlp.experts.{e}.up_proj.weight"] = w13[e, F:]
@@ -321,6 +329,11 @@ class Qwen3Model(nn.Module):
 
     @torch.no_grad()
     def load_hf_state_dict(self, sd: dict[str, Tensor], strict: bool = True) -> list[str]:
+        """Load HF-named tensors, experts in either spelling (per expert or
+        fused); ``strict`` rejects a dict that leaves a parameter unloaded or
+        carries a tensor matching no parameter."""
+        from lumenrl_b200.sync.moe_weights import split_experts
+        sd = split_experts(sd)
         targets = self.hf_state_dict()
         missing = []
         for k, dst in targets.items():

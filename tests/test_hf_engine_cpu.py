@@ -92,3 +92,53 @@ def test_rollout_engine_vocab_limit_never_samples_oov():
     eng = RolloutEngine(m, max_num_seqs=4, max_model_len=64, use_cuda_graph=False, vocab_limit=1000)
     out = eng.generate([[1, 2, 3, 4]], SamplingParams(max_new_tokens=6, n=2, seed=0, stop_at_eos=False))
     assert int(out.responses.max()) < 1000
+
+
+def _native_moe():
+    from lumenrl_b200.models.config import tiny_qwen3_moe
+    from lumenrl_b200.models.qwen3 import Qwen3Model
+    m = Qwen3Model(tiny_qwen3_moe(), dtype=torch.float32, requires_grad=False)
+    m.init_weights(3)
+    return m
+
+
+def test_hf_moe_twin_routes_experts_into_fused_parameters():
+    """transformers' Qwen3-MoE module keeps fused [E, 2F, H] / [E, H, F]
+    expert parameters; the per-expert export is fused on the way in and the
+    twin scores like the native model."""
+    from lumenrl_b200.engine.inference.hf_engine import HFEngine
+    m = _native_moe()
+    eng = HFEngine.from_native(m)
+    ids = torch.randint(0, m.args.vocab_size, (2, 10), generator=torch.Generator().manual_seed(1))
+    lp = eng.compute_log_probs(ids)
+    for r in range(2):
+        h = m.forward_packed(ids[r], torch.arange(10), torch.tensor([0, 10]), 10)
+        ref = torch.log_softmax(m.logits(h).float(), -1)[:-1].gather(-1, ids[r, 1:, None]).squeeze(-1)
+        assert (lp[r] - ref).abs().max().item() < 1e-4
+
+
+def test_expert_spellings_round_trip_and_native_loader_takes_both():
+    from lumenrl_b200.sync.moe_weights import fuse_experts, route_expert_weights, split_experts
+    m = _native_moe()
+    per = m.hf_state_dict()
+    fused = m.hf_state_dict(fused_experts=True)
+    assert any(k.endswith("experts.gate_up_proj") for k in fused)
+    f2 = fuse_experts(per)
+    assert f2.keys() == fused.keys() and all(torch.equal(f2[k], fused[k]) for k in fused)
+    p2 = split_experts(fused)
+    assert p2.keys() == per.keys() and all(torch.equal(p2[k], per[k]) for k in per)
+    assert route_expert_weights(per, fused.keys()).keys() == fused.keys()
+    assert route_expert_weights(fused, per.keys()).keys() == per.keys()
+    # the native loader accepts the fused spelling (strict coverage still holds)
+    m2 = _native_moe()
+    m2.init_weights(11)
+    m2.load_hf_state_dict({k: v.clone() for k, v in fused.items()})
+    assert torch.equal(m2.flat, m.flat)
+
+
+def test_fusing_rejects_a_missing_expert():
+    from lumenrl_b200.sync.moe_weights import fuse_experts
+    per = _native_moe().hf_state_dict()
+    gone = next(k for k in per if ".experts.1.up_proj" in k)
+    with pytest.raises(KeyError):
+        fuse_experts({k: v for k, v in per.items() if k != gone})

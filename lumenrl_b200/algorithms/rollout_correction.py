@@ -268,29 +268,57 @@ def compute_rollout_correction_weights(log_ratio: Tensor, response_mask: Tensor,
 
 def compute_offpolicy_metrics(old_log_prob: Tensor, rollout_log_prob: Optional[Tensor],
                               response_mask: Tensor) -> dict[str, Any]:
-    m: dict[str, Any] = {}
+    """Perplexities and train/rollout divergences, all read back to the host
+    in one transfer."""
     lp_train = _mmean(old_log_prob, response_mask, -1)
-    m["training_ppl"] = torch.exp(-lp_train).mean().item()
-    m["training_log_ppl"] = (-lp_train).mean().item()
-    if rollout_log_prob is None:
-        return m
-    m["kl"] = _mmean(rollout_log_prob - old_log_prob, response_mask).item()
-    lr = old_log_prob - rollout_log_prob
-    m["k3_kl"] = _mmean(torch.exp(lr) - lr - 1, response_mask).item()
-    lp_roll = _mmean(rollout_log_prob, response_mask, -1)
-    m["rollout_ppl"] = torch.exp(-lp_roll).mean().item()
-    m["rollout_log_ppl"] = (-lp_roll).mean().item()
-    d = lp_roll - lp_train
-    m["log_ppl_diff"] = d.mean().item()
-    m["log_ppl_abs_diff"] = d.abs().mean().item()
-    m["log_ppl_diff_max"] = d.max().item()
-    m["log_ppl_diff_min"] = d.min().item()
-    m["ppl_ratio"] = torch.exp(d).mean().item()
-    rho = torch.exp(lr.clamp(-SAFETY_BOUND, SAFETY_BOUND))
-    m["chi2_token"] = (_mmean(rho * rho, response_mask) - 1.0).item()
-    s = _msum(lr, response_mask, -1).clamp(-SAFETY_BOUND, SAFETY_BOUND)
-    m["chi2_seq"] = (torch.exp(2.0 * s).mean() - 1.0).item()
-    return m
+    vals: dict[str, Tensor] = {"training_ppl": torch.exp(-lp_train).mean(), "training_log_ppl": (-lp_train).mean()}
+    if rollout_log_prob is not None:
+        lr = old_log_prob - rollout_log_prob
+        lp_roll = _mmean(rollout_log_prob, response_mask, -1)
+        d = lp_roll - lp_train
+        rho = torch.exp(lr.clamp(-SAFETY_BOUND, SAFETY_BOUND))
+        s = _msum(lr, response_mask, -1).clamp(-SAFETY_BOUND, SAFETY_BOUND)
+        vals.update({
+            "kl": _mmean(-lr, response_mask),
+            "k3_kl": _mmean(torch.exp(lr) - lr - 1, response_mask),
+            "rollout_ppl": torch.exp(-lp_roll).mean(), "rollout_log_ppl": (-lp_roll).mean(),
+            "log_ppl_diff": d.mean(), "log_ppl_abs_diff": d.abs().mean(),
+            "log_ppl_diff_max": d.max(), "log_ppl_diff_min": d.min(),
+            "ppl_ratio": torch.exp(d).mean(),
+            "chi2_token": _mmean(rho * rho, response_mask) - 1.0,
+            "chi2_seq": torch.exp(2.0 * s).mean() - 1.0,
+        })
+    host = torch.stack([v.reshape(()).float() for v in vals.values()]).cpu().tolist()
+    return dict(zip(vals.keys(), host))
+
+
+# train/rollout mismatch beyond the signed mean (reference:
+# ``workers/actor_worker.py:760-792``, ``trainer/rl_trainer.py:3630-3652``):
+# per-rank SUMS with their denominators, so a cross-rank sum gives exact
+# token- and sequence-weighted means
+MISMATCH_TOKEN_KEYS = ("mismatch/abs_diff", "mismatch/k3_kl", "mismatch/chi2_token", "mismatch/frac_abs_gt_0.1")
+
+
+def mismatch_sums(train_log_prob: Tensor, rollout_log_prob: Tensor, response_mask: Tensor) -> Tensor:
+    """[sum |r|, sum (e^r - 1 - r), sum (e^r - 1)^2, count |r| > 0.1, tokens,
+    sum over rows (e^{sum r} - 1)^2, rows] on the device, r = train - rollout
+    log-prob per response token (clamped to +-10 inside the exponentials)."""
+    mask = response_mask.to(train_log_prob.dtype)
+    r = (train_log_prob - rollout_log_prob) * mask
+    w = torch.exp(r.clamp(-10.0, 10.0))
+    w_seq = torch.exp(r.sum(-1).clamp(-10.0, 10.0))
+    return torch.stack([r.abs().sum(), ((w - 1.0 - r) * mask).sum(), ((w - 1.0) ** 2 * mask).sum(),
+                        ((r.abs() > 0.1).to(r.dtype) * mask).sum(), mask.sum(), ((w_seq - 1.0) ** 2).sum(),
+                        torch.tensor(float(r.shape[0]), dtype=r.dtype, device=r.device)]).double()
+
+
+def finalize_mismatch(sums) -> dict[str, float]:
+    """Means from (cross-rank summed) ``mismatch_sums``."""
+    a, k3, c2, tail, tok, c2s, rows = (float(x) for x in sums)
+    out = {k: v / max(tok, 1e-6) for k, v in zip(MISMATCH_TOKEN_KEYS, (a, k3, c2, tail))} if tok else {}
+    if rows:
+        out["mismatch/chi2_seq"] = c2s / max(rows, 1e-6)
+    return out
 
 
 _LEGACY_ALIASES = {"is_weight_mean": "rollout_is_mean", "is_weight_max": "rollout_is_max", "kl": "kl", "k3_kl": "k3_kl"}

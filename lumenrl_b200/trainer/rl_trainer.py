@@ -348,6 +348,8 @@ class RLTrainer:
         else:
             m.update(rc.compute_rollout_corr_metrics_from_logprobs(batch["old_log_probs"], batch["rollout_log_probs"],
                                                                    batch["response_mask"]))
+        mm = rc.mismatch_sums(batch["old_log_probs"], batch["rollout_log_probs"], batch["response_mask"]) \
+            if "old_log_probs" in batch.tensors and "rollout_log_probs" in batch.tensors else None
         self.timer.stop("adv")
         self.timer.start("train")
         pol = c.algorithm.dapo if self.algorithm_name == "dapo" else self.algo_cfg
@@ -371,10 +373,14 @@ class RLTrainer:
         # every cross-rank statistic of the step in two collectives (one sum
         # vector, one max vector) and two device->host reads
         resp_local = batch["response_lengths"].sum()
-        tokens_local, resp_tokens, score_sum = (float(v) for v in torch.stack(
-            [batch["prompt_lengths"].sum() + resp_local, resp_local, scores.sum()]).double().cpu())
-        tokens, resp_tokens, score_sum, rows = all_reduce_sum_many(
-            [tokens_local, resp_tokens, score_sum, float(len(batch))])
+        local = torch.stack([batch["prompt_lengths"].sum() + resp_local, resp_local, scores.sum()]).double()
+        if mm is not None:
+            local = torch.cat([local, mm.to(local.device)])
+        local = local.cpu().tolist()
+        summed = all_reduce_sum_many(local[:3] + [float(len(batch))] + local[3:])
+        tokens, resp_tokens, score_sum, rows = summed[:4]
+        if mm is not None:
+            m.update(rc.finalize_mismatch(summed[4:]))
         # Weight sync = from the reduced gradients to rollout-ready weights: the
         # AdamW kernel that writes bf16 into the resident buffer the engine
         # reads (and, on several GPUs, stores it into every rank's copy over
@@ -384,6 +390,12 @@ class RLTrainer:
         max_keys = [f"timing/{k}_s" for k in times] + opt_keys + ["timing/weight_sync_s"]
         max_vals = list(times.values()) + [float(m[k]) for k in opt_keys] + [
             float(tm.get("timing/opt_bcast_s", 0.0)) + times["weight_sync"]]
+        if st.device.type == "cuda":    # memory high-water marks of this step's process, max over ranks
+            gb = float(1 << 30)
+            max_keys += ["mem/actor_max_reserved_gb", "mem/actor_max_allocated_gb", "mem/actor_reserved_gb",
+                         "mem/actor_allocated_gb"]
+            max_vals += [torch.cuda.max_memory_reserved(st.device) / gb, torch.cuda.max_memory_allocated(st.device) / gb,
+                         torch.cuda.memory_reserved(st.device) / gb, torch.cuda.memory_allocated(st.device) / gb]
         m.update(zip(max_keys, all_reduce_max_many(max_vals)))
         step_s = m["timing/step_s"]
         m["perf/total_num_tokens"] = tokens

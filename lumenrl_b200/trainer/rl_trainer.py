@@ -174,7 +174,10 @@ class RLTrainer:
         self.top_p = float(vc.top_p)
         self.data = SyntheticPrompts(self.spec.prompt_len, self.spec.prompt_low, self.spec.prompt_high, c.seed)
         self.reward_fn = get_reward_fn(self.spec.reward)
-        self.timer = PhaseTimer(st.device)
+        from lumenrl_b200.utils.profiler import DistProfiler
+        self.profiler = DistProfiler(c.profiler, st.rank)
+        # NVTX ranges per phase whenever profiling is on for this rank
+        self.timer = PhaseTimer(st.device, nvtx=self.profiler.enabled)
         self.io_bytes = {"h2d": 0, "d2h": 0}
 
     def _setup_rollout(self, model, rollout_ranks: int) -> None:
@@ -307,6 +310,7 @@ class RLTrainer:
         c, st = self.config, self.state
         step = self.global_step
         m: dict[str, Any] = {}
+        self.profiler.start(step)               # no-op unless profiling this rank and step
         self.timer.start("step")
         self.timer.start("gen")
         batch = self._collect(step, m)
@@ -412,6 +416,7 @@ class RLTrainer:
         for k in ("prefill_ms", "setup_ms", "decode_ms"):
             if k in batch.meta.get("gen_stats", {}):
                 m[f"timing/gen_{k}"] = batch.meta["gen_stats"][k]
+        self.last_trace = self.profiler.stop() or getattr(self, "last_trace", None)   # chrome trace path
         host_result = scores.to("cpu")          # the step's result read back to the host
         self.io_bytes["d2h"] = host_result.numel() * host_result.element_size()
         m["step"] = step + 1

@@ -9,12 +9,20 @@ import torch
 
 
 class PhaseTimer:
-    def __init__(self, device) -> None:
+    """``start(name)`` / ``stop(name)`` bracket a phase.  With ``nvtx`` (on
+    GPU) every phase is also an NVTX range, so an external Nsight capture
+    shows the step's phases on the timeline."""
+
+    def __init__(self, device, nvtx: bool = False) -> None:
         self.cuda = torch.device(device).type == "cuda"
+        self.nvtx = bool(nvtx) and self.cuda
         self._open: dict[str, object] = {}
         self._done: dict[str, tuple] = {}
+        self._ranges: dict[str, int] = {}
 
     def start(self, name: str) -> None:
+        if self.nvtx:
+            self._ranges[name] = torch.cuda.nvtx.range_start(name)
         if self.cuda:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
@@ -23,6 +31,8 @@ class PhaseTimer:
             self._open[name] = time.perf_counter()
 
     def stop(self, name: str) -> None:
+        if self.nvtx and name in self._ranges:
+            torch.cuda.nvtx.range_end(self._ranges.pop(name))
         s = self._open.pop(name)
         if self.cuda:
             e = torch.cuda.Event(enable_timing=True)

@@ -58,3 +58,20 @@ def test_mismatch_sums_are_exact_and_additive():
     halves = rc.mismatch_sums(train[:2], roll[:2], mask[:2]) + rc.mismatch_sums(train[2:], roll[2:], mask[2:])
     whole = rc.finalize_mismatch(halves.tolist())
     assert all(abs(whole[k] - got[k]) < 1e-12 for k in got)
+
+
+def test_profiler_traces_the_selected_step(tmp_path):
+    from lumenrl_b200.core.config import LumenRLConfig
+    from lumenrl_b200.models.config import tiny_llama
+    from lumenrl_b200.parallel.dist import ParallelState
+    from lumenrl_b200.trainer.rl_trainer import RLRunSpec, RLTrainer
+    out = str(tmp_path / "prof")
+    cfg = LumenRLConfig.from_yaml(os.path.join(HERE, "configs", "grpo_tiny_cpu.yaml"),
+                                  ["num_training_steps=2", "profiler.enable=true", "profiler.tool=torch",
+                                   f"profiler.save_path={out}", "profiler.steps=[1]"])
+    spec = RLRunSpec(prompts_per_step=2, prompt_len=8, max_new_tokens=8, reward="contains_token", eos_token_id=None)
+    tr = RLTrainer(cfg, tiny_llama(), spec, ParallelState()).setup()
+    tr.step()
+    assert getattr(tr, "last_trace", None) is None          # step 0 is not profiled
+    tr.step()
+    assert tr.last_trace == os.path.join(out, "trace_rank0_step1.json") and os.path.getsize(tr.last_trace) > 0

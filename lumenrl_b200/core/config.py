@@ -648,6 +648,26 @@ class RuntimeAssemblyConfig:
 
 
 @dataclass
+class KernelsConfig:
+    """B200 kernel and collective selection (no counterpart in the reference,
+    whose kernels come from its inference / training libraries).  Each field
+    mirrors one ``LRL_*`` environment variable; ``None`` keeps the variable's
+    value or the built-in default, a value overrides both
+    (``lumenrl_b200.ops.kernel_flags.apply_kernels_config``)."""
+    train_gemm: Optional[str] = None       # LRL_TRAIN_GEMM: own (CTA-pair tcgen05) | cublas
+    train_attn: Optional[str] = None       # LRL_TRAIN_ATTN: tc (tcgen05 flash) | fa2
+    train_attn_bwd: Optional[str] = None   # LRL_TRAIN_ATTN_BWD: tc | fa2
+    decode_gemm: Optional[str] = None      # LRL_DECODE_GEMM: auto | sk | skinny | cublas
+    fp8_decode_gemm: Optional[str] = None  # LRL_FP8_DECODE_GEMM: stream | gemm
+    decode_attn: Optional[str] = None      # LRL_DECODE_ATTN: tma | cp
+    nvls: Optional[bool] = None            # LRL_NVLS: NVLink-SHARP multicast collectives
+    cp_ring: Optional[str] = None          # LRL_CP_RING: nvlink | pg
+    draft_allreduce: Optional[str] = None  # LRL_DRAFT_ALLREDUCE: nvlink | nccl
+    debug_bounds: Optional[bool] = None    # LRL_DEBUG_BOUNDS: bounds-checked NVLink kernels
+    eagle_kernels: Optional[bool] = None   # LRL_EAGLE_KERNELS: fused Eagle3 draft kernels
+
+
+@dataclass
 class LumenRLConfig:
     cluster: ClusterConfig = field(default_factory=ClusterConfig)
     policy: PolicyConfig = field(default_factory=PolicyConfig)
@@ -666,6 +686,7 @@ class LumenRLConfig:
     assembly: RuntimeAssemblyConfig = field(default_factory=RuntimeAssemblyConfig)
     dataset: DatasetConfig = field(default_factory=DatasetConfig)
     eval: EvalConfig = field(default_factory=EvalConfig)
+    kernels: KernelsConfig = field(default_factory=KernelsConfig)
     num_training_steps: int = 1000
     seed: int = 42
     val_dataset: str = ""

@@ -87,6 +87,8 @@ class RLTrainer:
     def __init__(self, config: LumenRLConfig, model_args: Optional[ModelArgs] = None,
                  spec: Optional[RLRunSpec] = None, state: Optional[ParallelState] = None) -> None:
         self.config = config
+        from lumenrl_b200.ops.kernel_flags import apply_kernels_config
+        apply_kernels_config(getattr(config, "kernels", None))   # config's kernel choices win over LRL_*
         self.spec = spec or RLRunSpec()
         self.model_args = model_args or resolve_model(config.policy.model_name or "tiny-llama")
         self.state = state

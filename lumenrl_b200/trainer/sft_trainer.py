@@ -23,6 +23,8 @@ from lumenrl_b200.parallel.dist import ParallelState, all_reduce_sum
 
 class SFTTrainer:
     def __init__(self, config, model_args: ModelArgs, state: ParallelState) -> None:
+        from lumenrl_b200.ops.kernel_flags import apply_kernels_config
+        apply_kernels_config(getattr(config, "kernels", None))
         p = config.policy
         self.config = config
         from lumenrl_b200.engine.training.fsdp import ShardedParamActorEngine, wants_param_sharding

@@ -43,3 +43,32 @@ def test_threshold_coercion():
     assert c.rollout_is_threshold == "2.0" and c.rollout_rs_threshold == "0.5"
     with pytest.raises(ValueError):
         RolloutCorrectionConfig(rollout_is_seq_reduction="max")
+
+
+def test_kernels_section_overrides_environment(monkeypatch):
+    """The config's ``kernels`` section wins over the LRL_* variables and
+    rewrites the owning module's switch; None fields change nothing."""
+    import importlib
+
+    from lumenrl_b200.core.config import LumenRLConfig
+    from lumenrl_b200.ops.kernel_flags import apply_kernels_config
+    ops = importlib.import_module("lumenrl_b200.ops")
+    attn = importlib.import_module("lumenrl_b200.ops.attention")
+    saved = (ops.DECODE_GEMM, attn.TRAIN_ATTN_BWD)
+    monkeypatch.setenv("LRL_DECODE_GEMM", "sk")
+    monkeypatch.setenv("LRL_CP_RING", "nvlink")
+    try:
+        cfg = LumenRLConfig.from_dict({"kernels": {"decode_gemm": "cublas", "train_attn_bwd": "fa2",
+                                                   "cp_ring": "pg", "nvls": True}})
+        assert cfg.kernels.train_gemm is None
+        applied = apply_kernels_config(cfg.kernels)
+        assert applied == {"LRL_DECODE_GEMM": "cublas", "LRL_TRAIN_ATTN_BWD": "fa2", "LRL_CP_RING": "pg",
+                           "LRL_NVLS": "1"}
+        assert ops.DECODE_GEMM == "cublas" and attn.TRAIN_ATTN_BWD == "fa2"
+        assert os.environ["LRL_CP_RING"] == "pg"
+        with pytest.raises(ValueError):
+            apply_kernels_config(LumenRLConfig.from_dict({"kernels": {"decode_attn": "fast"}}).kernels)
+    finally:
+        ops.DECODE_GEMM, attn.TRAIN_ATTN_BWD = saved
+        for k in ("LRL_TRAIN_ATTN_BWD", "LRL_NVLS"):   # set by apply_kernels_config, not by monkeypatch
+            os.environ.pop(k, None)

@@ -77,6 +77,11 @@ def _load():
     if debug_bounds_requested():
         # no fallback: a run that asked for checked kernels must get them
         bounds = importlib.import_module("lumenrl_b200._C_bounds")
+        import torch
+        if torch.cuda.is_available():
+            # allocates this device's bounds status word now, outside any
+            # CUDA-graph capture (the checked kernels write it)
+            bounds.bounds_reset()
     _MOD = _Counted(mod, bounds)
 
 

@@ -75,3 +75,19 @@ def test_profiler_traces_the_selected_step(tmp_path):
     assert getattr(tr, "last_trace", None) is None          # step 0 is not profiled
     tr.step()
     assert tr.last_trace == os.path.join(out, "trace_rank0_step1.json") and os.path.getsize(tr.last_trace) > 0
+
+
+def test_dashboard_renders_charts_from_metric_logs(tmp_path):
+    import json
+
+    from lumenrl_b200.utils.dashboard import load_records, render_dashboard
+    p = tmp_path / "metrics.jsonl"
+    with open(p, "w") as f:
+        for s in range(1, 6):
+            f.write(json.dumps({"step": s, "reward/mean": 0.1 * s, "timing/step_s": 11.0 + 0.01 * s,
+                                "weight_sync/ms": 41.0}) + "\n")
+    out = tmp_path / "dash.html"
+    drawn = render_dashboard(load_records([str(p)]), str(out))
+    assert drawn == ["reward/mean", "timing/step_s", "weight_sync/ms"]
+    text = out.read_text()
+    assert text.count("<svg") == 3 and "<script" not in text and "0.5" in text

@@ -2,6 +2,7 @@
 norm, clip + AdamW + bf16 peer-store broadcast) against the NCCL path, as
 2 processes on 2 GPUs.  Skips with fewer than 2 GPUs."""
 
+import datetime
 import os
 import random
 import time
@@ -13,6 +14,10 @@ import torch.multiprocessing as mp
 
 pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 
+# short process-group timeout: ranks that wait on a dead or stalled peer end in
+# an error instead of holding the GPUs
+_PG_TIMEOUT = datetime.timedelta(seconds=180)
+
 
 def _need(world: int) -> None:
     if torch.cuda.device_count() < world:
@@ -23,7 +28,8 @@ def _worker(rank, world, port, q, nvls=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.engine.training.optimizer import ShardedFlatAdamW
     from lumenrl_b200.parallel.symm import NVLinkOptimizerComm
     n = 128 * world * 1000
@@ -78,7 +84,8 @@ def _allreduce_worker(rank, world, port, q, nvls):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.symm import NVLinkAllReduce
     from lumenrl_b200.trainer.spec_distill_trainer import allreduce_mean_grads
     comm = NVLinkAllReduce(4000, rank, world, nvls=nvls)          # small: buckets go through in pieces
@@ -131,7 +138,8 @@ def _dead_peer_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.symm import CommTimeout, NVLinkOptimizerComm
     n = 128 * world * 64
     # plain peer loads / stores: no rank's memory is bound to an NVLS multicast object
@@ -171,7 +179,8 @@ def _ring_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.symm import CommTimeout
     from lumenrl_b200.transfer.p2p_ring import HiddenStateRing
     T, D = 2048, 4 * 1024   # one 16 MiB batch of bf16 hidden rows
@@ -230,7 +239,8 @@ def _tp_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.tp_check import tp_layer_errors
     fused = tp_layer_errors("cuda", torch.bfloat16, fused=True, T=1024)
     plain = tp_layer_errors("cuda", torch.bfloat16, fused=False, T=1024)
@@ -267,7 +277,8 @@ def _cp_worker(rank, world, port, out_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.context_parallel import ring_attention, zigzag_indices
     S, H, Hk, D = 4096, 8, 2, 128
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -320,7 +331,8 @@ def _ep_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.parallel.ep_check import ep_errors
     kw = dict(T=512, H=256, F=128, E=8, k=2)
     fused = ep_errors("cuda", torch.bfloat16, fused=True, **kw)
@@ -356,7 +368,8 @@ def _p2p_sync_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.engine.inference.engine import RolloutEngine
     from lumenrl_b200.models.config import tiny_qwen3
     from lumenrl_b200.models.qwen3 import Qwen3Model
@@ -413,7 +426,8 @@ def _sep_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     from lumenrl_b200.core.config import LumenRLConfig
     from lumenrl_b200.models.config import tiny_qwen3_moe
     from lumenrl_b200.parallel.dist import ParallelState, init_distributed
@@ -461,7 +475,8 @@ def _sddd_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     import dataclasses
     from lumenrl_b200.models.config import tiny_qwen3
     from lumenrl_b200.parallel.dist import init_distributed
@@ -500,7 +515,8 @@ def _cp_actor_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     try:
         from lumenrl_b200.core.protocol import DataProto
         from lumenrl_b200.engine.training.actor import ActorEngine
@@ -552,7 +568,8 @@ def _sharded_engine_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     try:
         from lumenrl_b200.core.config import GRPOConfig
         from lumenrl_b200.core.protocol import DataProto
@@ -618,7 +635,8 @@ def _rollout_tp_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=_PG_TIMEOUT)
     try:
         from lumenrl_b200.engine.inference.engine import RolloutEngine, SamplingParams
         from lumenrl_b200.models.config import tiny_qwen3

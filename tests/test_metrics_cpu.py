@@ -91,3 +91,29 @@ def test_dashboard_renders_charts_from_metric_logs(tmp_path):
     assert drawn == ["reward/mean", "timing/step_s", "weight_sync/ms"]
     text = out.read_text()
     assert text.count("<svg") == 3 and "<script" not in text and "0.5" in text
+
+
+def _reduce_worker(rank, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    from lumenrl_b200.parallel.dist import all_reduce_max_many, all_reduce_sum_many, init_distributed
+    init_distributed(backend="gloo", timeout_s=30.0, device="cpu")
+    vals = [1.0 + rank, 10.0 * rank, -3.0 + rank]
+    q.put((rank, all_reduce_sum_many(vals), all_reduce_max_many(vals), all_reduce_sum_many([])))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_vector_reductions_over_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29400 + os.getpid() % 200
+    procs = [ctx.Process(target=_reduce_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (s, m, e) for r, s, m, e in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+    for r in (0, 1):
+        assert res[r] == ([3.0, 10.0, -5.0], [2.0, 10.0, -2.0], [])
